@@ -1,0 +1,573 @@
+"""Benchmark of the dense-contraction hot path on B200 (one JSON line on rank 0).
+
+Metric: "GEMM TFLOP/s & GEMV HBM GB/s per B200, % roofline, at 1/2/4/8 GPUs".
+
+Headline workload -- BASELINE config 2, decode GEMV ``x[1,8192] @ W[8192,8192]^T`` bf16:
+a *step* is one ``rk_gemv`` over one weight matrix (128 MiB).  Steps rotate over several
+weight matrices (4 x 128 MiB > the 126 MB L2) so every step streams its weight from HBM;
+``value`` = weight+activation bytes of all steps on all ranks / the device time of the
+timed region (max over ranks).  With N GPUs every rank streams its own 8192-row block of
+an N x 8192-row weight (N-row sharding, weak scaling, no data-path collective).
+
+``e2e``: the same GEMV through the public ``radeon_kernels.gemv`` call (dispatch, pack
+winner) with the step's activation copied host->device from pinned memory and the result
+copied back every step; at N>1 the per-rank output blocks are all-gathered (NCCL) first,
+as a caller that needs the full output would.
+
+``suite``: the other BASELINE configs measured in the same run (GEMM TFLOP/s with the
+tcgen05 kernel, FFN-down GEMV at M = 1/4/16), each with its roofline fraction.
+
+``--impl reference`` times the reference's own path for the same workload on the host
+CPU cores (``oracle/reference_path.py``: ``torch.mm`` as in providers/torch_fallback.py /
+ops/gemv/reference.py), rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "radeon-kernels_b200"))
+sys.path.insert(0, str(REPO))
+
+METRIC = "GEMM TFLOP/s & GEMV HBM GB/s per B200, % roofline, at 1/2/4/8 GPUs"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+ROTATE = 4  # weight matrices cycled through by the headline loop
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return data, "measured"
+    except (OSError, json.JSONDecodeError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic() -> dict:
+    path = REPO / "profiles" / "traffic.json"
+    try:
+        return json.loads(path.read_text())
+    except (OSError, json.JSONDecodeError):
+        return {}
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self._thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL,
+                text=True,
+            )
+            self._thread = threading.Thread(target=self._drain, daemon=True)
+            self._thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _drain(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self._thread is not None:
+                self._thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, sm_max, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": sm_max,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ------------------------------------------------------------------------ distributed
+class Dist:
+    def __init__(self, n_gpus: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.n_gpus = n_gpus
+        self.pg = None
+
+    def init(self, backend: str = "nccl"):
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        if self.world > 1:
+            if backend == "nccl":
+                torch.cuda.set_device(self.local_rank)
+            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+            self.pg = dist.group.WORLD
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, value: float) -> float:
+        if self.world == 1:
+            return value
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------------ workloads
+def seeded(shape, seed, dist, dtype, device="cuda"):
+    import torch
+
+    gen = torch.Generator(device=device).manual_seed(seed)
+    if dist == "uniform":
+        x = torch.rand(shape, generator=gen, device=device) * 2 - 1
+    elif dist == "uniform16":
+        x = (torch.rand(shape, generator=gen, device=device) * 2 - 1) / 16
+    elif dist == "normal64":
+        x = torch.randn(shape, generator=gen, device=device) / 64
+    elif dist == "normal":
+        x = torch.randn(shape, generator=gen, device=device)
+    else:  # "normal/<fan_in>"
+        x = torch.randn(shape, generator=gen, device=device) / float(dist.split("/")[1]) ** 0.5
+    return x.to({"bf16": torch.bfloat16, "fp16": torch.float16}[dtype])
+
+
+def gemv_bytes(m, n, k):
+    return (n * k + m * k + m * n) * 2
+
+
+def time_loop(fn, steps: int, stream) -> float:
+    """Total device milliseconds of `steps` calls on `stream` (events on that stream)."""
+
+    import torch
+
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(steps):
+        fn(i)
+    stop.record(stream)
+    stop.synchronize()
+    return start.elapsed_time(stop)
+
+
+def headline(args, dist: Dist, ext, peaks, peak_kind):
+    """Config 2 decode GEMV, kernel-only, inputs resident; CUDA graph of the launch loop."""
+
+    import torch
+
+    m, n, k = 1, 8192, 8192
+    dtype = "bf16"
+    weights = [seeded((n, k), 100 + 17 * dist.rank + r, "normal/8192", dtype) for r in range(ROTATE)]
+    x = seeded((m, k), 1, "normal", dtype)
+    out = torch.empty(m, n, dtype=x.dtype, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        ext.gemv_out(x, weights[i % ROTATE], out, 0)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+
+    # Capture a block of launches into a CUDA graph: decode loops replay graphs, and the
+    # graph removes the per-launch host overhead from the measurement of the kernel.
+    block = 40
+    graph = torch.cuda.CUDAGraph()
+    capture_stream = torch.cuda.Stream()
+    capture_stream.wait_stream(stream)
+    with torch.cuda.stream(capture_stream):
+        with torch.cuda.graph(graph, stream=capture_stream):
+            for i in range(block):
+                step(i)
+    stream.wait_stream(capture_stream)
+    torch.cuda.synchronize()
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    replays = max(1, args.steps // block)
+    steps = replays * block
+    dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(replays):
+        graph.replay()
+    stop.record(stream)
+    stop.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms_local = start.elapsed_time(stop)
+    ms = dist.max(ms_local)
+    per_launch_s = ms_local / 1e3 / steps
+    bytes_step = gemv_bytes(m, n, k)
+    value = bytes_step * steps * dist.world / (ms / 1e3) / 1e9
+    achieved = bytes_step / per_launch_s / 1e9
+    del graph
+    return {
+        "value": value,
+        "ms_per_step": ms / steps,
+        "steps": steps,
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": round(achieved / peaks["hbm_gbs"], 4),
+            "peak_source": peak_kind,
+        },
+        "bytes_per_step": bytes_step,
+    }
+
+
+def e2e(args, dist: Dist):
+    """The same GEMV through the public API with host buffers, copies inside the region."""
+
+    import torch
+
+    import radeon_kernels as rk
+
+    m, n, k = 1, 8192, 8192
+    weights = [seeded((n, k), 100 + 17 * dist.rank + r, "normal/8192", "bf16") for r in range(ROTATE)]
+    x_host = seeded((m, k), 1, "normal", "bf16", device="cpu").pin_memory()
+    out_host = torch.empty((m, n * dist.world), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
+    gathered = torch.empty((dist.world, m, n), dtype=torch.bfloat16, device="cuda") if dist.world > 1 else None
+    full = torch.empty((m, n * dist.world), dtype=torch.bfloat16, device="cuda") if dist.world > 1 else None
+    ext = None
+    if dist.world > 1:
+        from radeon_kernels import _native
+
+        ext = _native.extension()
+        import torch.distributed as tdist
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        x_dev.copy_(x_host, non_blocking=True)
+        y = rk.gemv(x_dev, weights[i % ROTATE])
+        if dist.world > 1:
+            tdist.all_gather_into_tensor(gathered, y)
+            ext.gather_column_blocks(gathered, full)
+            out_host.copy_(full, non_blocking=True)
+        else:
+            out_host.copy_(y, non_blocking=True)
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    selected = rk.get_last_dispatch()["selected"]
+    steps = max(args.e2e_steps, 10)
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms = time_loop(step, steps, stream)
+    dist.barrier()
+    ms = dist.max(ms)
+    bytes_step = gemv_bytes(m, n, k)
+    return {
+        "value": round(bytes_step * steps * dist.world / (ms / 1e3) / 1e9, 1),
+        "unit": "GB/s",
+        "h2d_bytes_per_step": m * k * 2,
+        "d2h_bytes_per_step": m * n * dist.world * 2,
+        "ms_per_step": round(ms / steps, 5),
+        "path": f"radeon_kernels.gemv -> {selected}" + (" + NCCL all-gather + rk_gather_column_blocks" if dist.world > 1 else ""),
+    }
+
+
+def suite(args, dist: Dist, ext, peaks):
+    """The other BASELINE configs (kernel-only, events on the launching stream)."""
+
+    import torch
+
+    results = {}
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def gemm_case(name, m, n, k, dtype, dist_name, seed, iters, scaling="replica"):
+        a = seeded((m, k), seed, dist_name, dtype)
+        b = seeded((k, n), seed + 1, dist_name, dtype)
+        c = torch.empty(m, n, dtype=a.dtype, device="cuda")
+        for _ in range(2):
+            ext.gemm_out(a, b, c, 0)
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(iters):
+            flush.zero_()  # L2 flush between timed launches
+            ms = time_loop(lambda i: ext.gemm_out(a, b, c, 0), 1, stream)
+            times.append(ms)
+        dist.barrier()
+        ms = dist.max(statistics.median(times))
+        flops = 2.0 * m * n * k
+        achieved = flops / (ms / 1e3) / 1e12
+        results[name] = {
+            "unit": "TFLOP/s",
+            "value": round(achieved * dist.world, 1),
+            "per_gpu": round(achieved, 1),
+            "ms": round(ms, 4),
+            "roofline_frac": round(achieved / peaks["bf16_tflops"], 4),
+            "scaling": scaling,
+            "shape": [m, n, k],
+            "dtype": dtype,
+        }
+        del a, b, c
+
+    def gemv_case(name, m, n, k, dtype, seed, iters):
+        ws = [seeded((n, k), seed + r, f"normal/{k}", dtype) for r in range(ROTATE)]
+        x = seeded((m, k), seed, "normal", dtype)
+        out = torch.empty(m, n, dtype=x.dtype, device="cuda")
+        for i in range(3):
+            ext.gemv_out(x, ws[i % ROTATE], out, 0)
+        torch.cuda.synchronize()
+        ms = time_loop(lambda i: ext.gemv_out(x, ws[i % ROTATE], out, 0), iters, stream) / iters
+        dist.barrier()
+        ms = dist.max(ms)
+        gbs = gemv_bytes(m, n, k) / (ms / 1e3) / 1e9
+        results[name] = {
+            "unit": "GB/s",
+            "value": round(gbs * dist.world, 1),
+            "per_gpu": round(gbs, 1),
+            "us": round(ms * 1e3, 2),
+            "roofline_frac": round(gbs / peaks["hbm_gbs"], 4),
+            "scaling": "weak",
+        }
+        del ws
+
+    g = dist.world
+    gemm_case("c1_gemm_1024_bf16", 1024, 1024, 1024, "bf16", "uniform", 0, 20)
+    gemm_case("c4_gemm_ffn_up_fp16", 4096, 14336, 4096, "fp16", "normal64", 3, 10)
+    gemm_case(f"c5_gemm_large_bf16_shard{g}", 16384, 57344 // g, 8192, "bf16", "uniform16", 4, 5, scaling="strong")
+    if not args.quick:
+        gemm_case("gemm_8192_bf16", 8192, 8192, 8192, "bf16", "uniform16", 7, 5)
+    for m in (1, 16):
+        gemv_case(f"c2_gemv_decode_bf16_m{m}", m, 8192, 8192, "bf16", 1, 200)
+    for m in (1, 4, 16):
+        gemv_case(f"c3_gemv_ffn_down_fp16_m{m}", m, 4096, 14336, "fp16", 2, 200)
+    del flush
+    return results
+
+
+def cpu_baseline(seconds: float) -> dict:
+    """The reference's CPU path (torch.mm on host tensors), bounded sample of config 2."""
+
+    import torch
+
+    from oracle import reference_path
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn((1, 8192), generator=gen).to(torch.bfloat16)
+    w = (torch.randn((8192, 8192), generator=gen) / 8192**0.5).to(torch.bfloat16)
+    for _ in range(3):
+        reference_path.gemv_fallback(torch, x, w)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        reference_path.gemv_fallback(torch, x, w)
+        calls += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds or calls >= 20000:
+            break
+    gbs = gemv_bytes(1, 8192, 8192) * calls / elapsed / 1e9
+    return {
+        "value": round(gbs, 2),
+        "unit": "GB/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": f"{calls} calls of oracle.reference_path.gemv_fallback (torch.mm, the reference's "
+        f"ops/gemv/reference.py:12-15) on x[1,8192] @ W[8192,8192]^T bf16, {elapsed:.1f} s, {cores} threads",
+        "cpu": _cpu_model(),
+    }
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args) -> int:
+    """--impl reference: the reference's CPU implementation on the host cores (rank 0 only)."""
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+
+    from oracle import reference_path
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn((1, 8192), generator=gen).to(torch.bfloat16)
+    w = (torch.randn((8192, 8192), generator=gen) / 8192**0.5).to(torch.bfloat16)
+    for _ in range(max(args.warmup, 3)):
+        reference_path.gemv_fallback(torch, x, w)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        reference_path.gemv_fallback(torch, x, w)
+    elapsed = time.perf_counter() - t0
+    value = gemv_bytes(1, 8192, 8192) * args.steps / elapsed / 1e9
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed / args.steps * 1e3, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded torch.Generator, BASELINE config 2 distributions)",
+        "config": {"workload": "gemv-decode-bf16-m1-n8192-k8192 (BASELINE config 2)", "l2": "n/a (host CPU)"},
+        "cpu_baseline": {
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "cores": cores,
+            "kind": "port",
+            "sample": f"{args.steps} calls of torch.mm(x, W.T) (ops/gemv/reference.py:12-15 via oracle/reference_path.py), host CPU",
+            "cpu": _cpu_model(),
+        },
+        "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None) -> int:
+    parser = argparse.ArgumentParser(description="B200 GEMM/GEMV hot-path benchmark")
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=40000)
+    parser.add_argument("--warmup", type=int, default=20)
+    parser.add_argument("--e2e-steps", type=int, default=2000)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--quick", action="store_true", help="skip the optional 8192^3 suite entry")
+    parser.add_argument("--no-suite", action="store_true")
+    args = parser.parse_args(argv)
+
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+
+    from radeon_kernels import _native
+
+    dist = Dist(args.gpus)
+    dist.init()
+    torch.cuda.set_device(dist.local_rank)
+    ext = _native.extension()
+    peaks, peak_kind = load_peaks()
+
+    launches_before = _native.library().rk_launch_count()
+    with ClockSampler(dist.local_rank) as clocks:
+        head = headline(args, dist, ext, peaks, peak_kind)
+        end_to_end = e2e(args, dist)
+        extra = {} if args.no_suite else suite(args, dist, ext, peaks)
+    traffic = load_traffic().get("gemv_decode_bf16_m1_n8192_k8192")
+    head["roofline"]["traffic"] = traffic
+    cpu = cpu_baseline(args.cpu_seconds) if dist.rank == 0 and dist.world == 1 else None
+    dist.close()
+    if dist.rank != 0:
+        return 0
+    line = {
+        "metric": METRIC,
+        "value": round(head["value"], 1),
+        "unit": "GB/s",
+        "n_gpus": dist.world,
+        "steps": head["steps"],
+        "warmup": args.warmup,
+        "ms_per_step": round(head["ms_per_step"], 6),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded torch.Generator, BASELINE config 2 distributions: x~N(0,1), W~N(0,1/8192))",
+        "config": {
+            "workload": "gemv-decode-bf16-m1-n8192-k8192 (BASELINE config 2), x @ W^T, N-row shards of 8192 rows per GPU",
+            "m": 1,
+            "n_per_gpu": 8192,
+            "k": 8192,
+            "l2": f"inputs larger than L2: {ROTATE} weight matrices x 128 MiB rotated per step",
+            "launch": "CUDA graph of 40 rk_gemv launches, replayed",
+            "parallelism": f"weight-row shards x{dist.world}",
+        },
+        "roofline": head["roofline"],
+        "e2e": end_to_end,
+        "gpu_launches": head["steps"],
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+        "suite": extra,
+        "library_launches_host_counted": int(_native.library().rk_launch_count() - launches_before),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,155 @@
+/*
+ * rk_kernels.h -- C ABI of the B200 (sm_100a) dense-contraction kernels.
+ *
+ * This is the drop-in boundary for the hot path of radeon-kernels:
+ *   rk.gemm(a, b)      C[M,N] = A[M,K] @ B[K,N]        (row-major "nn")
+ *   rk.gemv(x, weight) out[M,N] = x[M,K] @ weight[N,K]^T (weight layout "nk")
+ * fp16 or bf16 operands, fp32 accumulation, output in the operand dtype,
+ * rounded to nearest-even.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream,
+ * never throws and never allocates device memory.  All launches are
+ * asynchronous on the given stream (NULL = legacy default stream); the
+ * caller owns every buffer.  Nothing here depends on PyTorch.
+ *
+ * Errors are reported in two places:
+ *   - host-side argument and launch errors as the returned rk_status;
+ *   - device-side failures (a bounded wait inside a kernel that ran out)
+ *     in a per-device status word that rk_device_status() reads and clears.
+ *     No kernel traps or spins forever: every wait has a time limit.
+ */
+#ifndef RK_KERNELS_H_
+#define RK_KERNELS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define RK_API __attribute__((visibility("default")))
+#else
+#define RK_API
+#endif
+
+/* CUDA stream handle; identical to cudaStream_t / CUstream. */
+typedef struct CUstream_st* rk_stream_t;
+
+typedef enum rk_status {
+  RK_OK = 0,
+  RK_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, K mismatch, M>32 for GEMV */
+  RK_ERR_UNSUPPORTED = 2,      /* variant cannot run this shape / alignment / device */
+  RK_ERR_CUDA = 3,             /* a CUDA runtime or driver call failed */
+  RK_ERR_TIMEOUT = 4,          /* a device-side bounded wait expired (kernel gave up) */
+  RK_ERR_NO_DEVICE = 5,        /* no usable sm_100 device is current */
+  RK_ERR_TOO_LARGE = 6         /* request exceeds a fixed capacity of the entry point */
+} rk_status;
+
+typedef enum rk_dtype {
+  RK_DTYPE_FP16 = 0,
+  RK_DTYPE_BF16 = 1
+} rk_dtype;
+
+/* GEMM variants (the `variant` launch parameter of the dispatch manifest). */
+enum {
+  RK_GEMM_AUTO = 0,        /* pick from shape, alignment and device */
+  RK_GEMM_SIMT = 1,        /* generic predicated CUDA-core kernel: any shape, any alignment */
+  RK_GEMM_TC_1SM = 2,      /* tcgen05 + TMA, 128x256 tile per SM, persistent */
+  RK_GEMM_TC_2SM = 3,      /* tcgen05 cta_group::2, 256x256 tile per SM pair, persistent */
+  RK_GEMM_VARIANT_COUNT = 4
+};
+
+/* GEMV variants. */
+enum {
+  RK_GEMV_AUTO = 0,        /* pick from M, N, K and alignment */
+  RK_GEMV_SCALAR = 1,      /* generic kernel: any K, any alignment */
+  RK_GEMV_STREAM = 2,      /* 128-bit weight streaming, in-CTA split-K, needs K%8==0 + 16B alignment */
+  RK_GEMV_VARIANT_COUNT = 3
+};
+
+/*
+ * C = A @ B.  A: [M,K] row-major (lda = K), B: [K,N] row-major (ldb = N),
+ * C: [M,N] row-major (ldc = N), all of dtype `dt`.  M, N, K >= 0; when K == 0
+ * C is zero-filled.  Replaces the reference's pybind entry `gemm_out(a, b,
+ * out, variant)` (src/radeon_kernels/ops/gemm/native/wmma_gemm.hip:294-316)
+ * and its variant switch `launch<T>` (wmma_gemm.hip:234-277).  Unlike the
+ * reference kernel it has no divisibility requirement: RK_GEMM_AUTO runs a
+ * tensor-core variant when N%8==0, K%8==0 and the pointers are 16-byte
+ * aligned, and the generic kernel otherwise.
+ */
+RK_API rk_status rk_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                  int64_t K, rk_dtype dt, int variant, rk_stream_t stream);
+
+/*
+ * out = x @ weight^T.  x: [M,K] row-major, weight: [N,K] row-major ("nk"),
+ * out: [M,N] row-major.  1 <= M <= 32 (the reference contract's maximum_m,
+ * contracts/gemv-1.0.json:11), N, K >= 1.  Replaces the reference's
+ * `gemv_impl<OutputsPerWave>` behind the `gemv_wave1/2/4` pybind entries
+ * (benchmarks/gemv/native_gemv.hip:277-297, :343-377); unlike those, the
+ * output buffer is the caller's.  Deterministic: the K reduction order is
+ * fixed by (M, N, K, variant).
+ */
+RK_API rk_status rk_gemv(const void* x, const void* weight, void* out, int64_t M,
+                  int64_t N, int64_t K, rk_dtype dt, int variant,
+                  rk_stream_t stream);
+
+/*
+ * Column-block gather for N-sharded GEMM/GEMV results.  `blocks` holds G
+ * contiguous blocks [G][M][N/G] (the layout an NCCL all-gather of per-rank
+ * C blocks produces); `out` receives the row-major [M, N] matrix.  N % G == 0.
+ * No counterpart in the reference (it has no multi-GPU path).
+ */
+RK_API rk_status rk_gather_column_blocks(const void* blocks, void* out, int64_t G,
+                                  int64_t M, int64_t N, rk_dtype dt,
+                                  rk_stream_t stream);
+
+/* Static description of a status code; never NULL. */
+RK_API const char* rk_status_string(rk_status status);
+
+/* Message of the last CUDA error seen by this thread's calls ("" if none). */
+RK_API const char* rk_last_error(void);
+
+/* Tuning hook for RK_GEMV_STREAM: weight rows per warp (1, 2, 4) and in-CTA
+ * K split (1, 2, 4, 8); 0 restores the built-in heuristic.  Process-wide. */
+RK_API void rk_gemv_set_tuning(int rows_per_warp, int ksplit);
+
+/*
+ * Reads and clears the device-side status word of the current device after
+ * synchronising `stream`.  Returns RK_OK, or RK_ERR_TIMEOUT when a kernel
+ * launched since the previous call gave up on a bounded wait.
+ */
+RK_API rk_status rk_device_status(rk_stream_t stream);
+
+/* Sets the per-wait time limit (nanoseconds, default 1e9) used by kernels
+ * launched after the call.  0 restores the default. */
+RK_API void rk_set_wait_timeout_ns(uint64_t ns);
+
+/* Test hook: when nonzero, the next tensor-core GEMM launch makes its MMA
+ * role wait on a barrier that nothing arrives on, so the bounded wait runs
+ * out and the kernel reports RK_ERR_TIMEOUT.  Resets itself after one launch. */
+RK_API void rk_debug_inject_stall(int enable);
+
+/* Human-readable name of a variant ("gemm:tc_1sm", "gemv:stream", ...). */
+RK_API const char* rk_variant_name(int op /* 0 = gemm, 1 = gemv */, int variant);
+
+/* The variant RK_GEMM_AUTO / RK_GEMV_AUTO would pick for this problem. */
+RK_API int rk_gemm_select_variant(const void* A, const void* B, const void* C,
+                           int64_t M, int64_t N, int64_t K, rk_dtype dt);
+RK_API int rk_gemv_select_variant(const void* x, const void* weight, const void* out,
+                           int64_t M, int64_t N, int64_t K, rk_dtype dt);
+
+/* Number of kernel launches this library issued on any stream since load
+ * (host-side counter, for launch accounting in benchmarks). */
+RK_API uint64_t rk_launch_count(void);
+
+RK_API int rk_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RK_KERNELS_H_ */

@@ -1,0 +1,159 @@
+"""numpy front-end of the C oracle (``rk_oracle.c``) -- TEST INFRASTRUCTURE ONLY.
+
+Arrays of 16-bit values are passed as ``numpy.uint16`` bit patterns (the exact bits of
+the fp16/bf16 tensors), so no conversion happens outside the C code.  Each call returns
+``(rounded_uint16, fp32_sums)``.
+
+Parity pinned by ``tests/test_oracle.py`` against ``tests/golden/*.npz``, which hold the
+outputs of the reference's own functions (see ``tests/golden/make_golden.py``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+ORACLE_DIR = Path(__file__).resolve().parent
+LIBRARY = ORACLE_DIR / "_build" / "librk_oracle.so"
+FP16, BF16 = 0, 1
+_lib: ctypes.CDLL | None = None
+
+
+def build() -> Path:
+    """Compile the oracle with the committed Makefile (needs gcc; seconds)."""
+
+    subprocess.run(["make", "-s", "-C", str(ORACLE_DIR)], check=True)
+    return LIBRARY
+
+
+def _library() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIBRARY.is_file():
+            build()
+        lib = ctypes.CDLL(str(LIBRARY))
+        u16p, f32p, i64, cint = (
+            np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS"),
+            np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS"),
+            ctypes.c_int64,
+            ctypes.c_int,
+        )
+        lib.rk_oracle_gemm.argtypes = [u16p, u16p, u16p, f32p, f32p, i64, i64, i64, cint]
+        lib.rk_oracle_gemm.restype = None
+        lib.rk_oracle_gemv.argtypes = [u16p, u16p, u16p, f32p, f32p, i64, i64, i64, cint]
+        lib.rk_oracle_gemv.restype = None
+        lib.rk_oracle_round.argtypes = [f32p, u16p, i64, cint]
+        lib.rk_oracle_round.restype = None
+        lib.rk_oracle_widen.argtypes = [u16p, f32p, i64, cint]
+        lib.rk_oracle_widen.restype = None
+        _lib = lib
+    return _lib
+
+
+def _code(dtype: str) -> int:
+    if dtype not in ("fp16", "bf16"):
+        raise ValueError(f"unsupported dtype {dtype!r}")
+    return BF16 if dtype == "bf16" else FP16
+
+
+def gemm(a_bits: np.ndarray, b_bits: np.ndarray, dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """C = A @ B on 16-bit bit patterns: A [M,K], B [K,N]."""
+
+    a = np.ascontiguousarray(a_bits, dtype=np.uint16)
+    b = np.ascontiguousarray(b_bits, dtype=np.uint16)
+    (m, k), (k2, n) = a.shape, b.shape
+    if k != k2:
+        raise ValueError("inner dimensions differ")
+    c = np.empty((m, n), np.uint16)
+    acc = np.empty((m, n), np.float32)
+    work = np.empty(k * n + k + 1, np.float32)
+    _library().rk_oracle_gemm(a, b, c, acc, work, m, n, k, _code(dtype))
+    return c, acc
+
+
+def gemv(x_bits: np.ndarray, w_bits: np.ndarray, dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """out = x @ W^T on 16-bit bit patterns: x [M,K], W [N,K]."""
+
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    (m, k), (n, k2) = x.shape, w.shape
+    if k != k2:
+        raise ValueError("K dimensions differ")
+    out = np.empty((m, n), np.uint16)
+    acc = np.empty((m, n), np.float32)
+    work = np.empty(2 * k + 1, np.float32)
+    _library().rk_oracle_gemv(x, w, out, acc, work, m, n, k, _code(dtype))
+    return out, acc
+
+
+def widen(bits: np.ndarray, dtype: str) -> np.ndarray:
+    src = np.ascontiguousarray(bits, dtype=np.uint16)
+    dst = np.empty(src.shape, np.float32)
+    _library().rk_oracle_widen(src.reshape(-1), dst.reshape(-1), src.size, _code(dtype))
+    return dst
+
+
+def round_to(values: np.ndarray, dtype: str) -> np.ndarray:
+    src = np.ascontiguousarray(values, dtype=np.float32)
+    dst = np.empty(src.shape, np.uint16)
+    _library().rk_oracle_round(src.reshape(-1), dst.reshape(-1), src.size, _code(dtype))
+    return dst
+
+
+def parity_error(result: np.ndarray, reference: np.ndarray) -> float:
+    """The north-star metric max|C - C_ref| / max|C_ref| (fp64 arithmetic)."""
+
+    result = np.asarray(result, np.float64)
+    reference = np.asarray(reference, np.float64)
+    scale = float(np.max(np.abs(reference))) if reference.size else 0.0
+    if reference.size == 0:
+        return 0.0
+    diff = float(np.max(np.abs(result - reference)))
+    return diff / scale if scale > 0 else diff
+
+
+# Tolerances of the parity gate, by output dtype (max|C - C_ref| / max|C_ref|).
+TOLERANCE = {"bf16": 4e-3, "fp16": 1e-3}
+
+
+def ulp_distance(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    """Distance in representable steps between two arrays of 16-bit float bit patterns."""
+
+    def ordered(bits: np.ndarray) -> np.ndarray:
+        v = np.asarray(bits, np.int32)
+        return np.where(v & 0x8000, 0x8000 - (v & 0x7FFF), 0x8000 + (v & 0x7FFF))
+
+    return np.abs(ordered(a_bits) - ordered(b_bits))
+
+
+def compare(result_bits: np.ndarray, ref_bits: np.ndarray, ref_fp32: np.ndarray, dtype: str) -> dict[str, float]:
+    """Parity summary of a 16-bit result against the reference's rounded and fp32 outputs.
+
+    * ``parity``    -- max|C - C_ref32| / max|C_ref32| (the gate, TOLERANCE[dtype]);
+    * ``max_steps`` -- largest distance in representable steps from the reference's rounded
+      output over the elements with |C_ref| >= max|C_ref| / 64 (smaller elements are
+      dominated by cancellation, where the fp32 summation order alone moves the result
+      by several steps);
+    * ``equal``     -- fraction of elements bit-identical to the reference's output.
+    """
+
+    if ref_bits.size == 0:
+        return {"parity": 0.0, "max_steps": 0.0, "equal": 1.0}
+    ref32 = np.asarray(ref_fp32, np.float32)
+    big = np.abs(ref32) >= np.abs(ref32).max() / 64
+    steps = ulp_distance(result_bits, ref_bits)
+    return {
+        "parity": parity_error(widen(result_bits, dtype), ref32),
+        "max_steps": float(steps[big].max(initial=0)),
+        "equal": float(np.mean(np.asarray(result_bits) == np.asarray(ref_bits))),
+    }
+
+
+def assert_parity(result_bits: np.ndarray, ref_bits: np.ndarray, ref_fp32: np.ndarray, dtype: str) -> dict[str, float]:
+    summary = compare(result_bits, ref_bits, ref_fp32, dtype)
+    assert summary["parity"] <= TOLERANCE[dtype], f"parity {summary['parity']:.3e} > {TOLERANCE[dtype]} ({dtype})"
+    assert summary["max_steps"] <= 1, f"{summary['max_steps']} representable steps from the reference"
+    return summary

@@ -1,0 +1,36 @@
+"""The reference's own CPU path for rk.gemm / rk.gemv, restated -- TEST INFRASTRUCTURE ONLY.
+
+These are the functions the reference executes when no native winner matches, i.e. the
+path the reference runs on CPU tensors (``rk.gemm`` itself rejects CPU tensors at
+ops/gemm/api.py:62-63, so the baseline calls them directly):
+
+* ``gemm_fallback``  -- providers/torch_fallback.py:6-9
+* ``gemv_fallback``  -- ops/gemv/reference.py:12-15
+* ``gemv_reference`` -- ops/gemv/reference.py:6-9 (the gemv contract's declared oracle)
+
+They are one-line calls of ``torch.mm``; torch is the reference's arithmetic engine (see
+``rk_oracle.c`` for the version note).  ``bench.py --impl reference`` times them on the
+host cores as the reference arm; tests compare the CUDA path against them.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+
+def gemm_fallback(torch_module: Any, a: Any, b: Any, output: Any | None = None) -> Any:
+    return torch_module.mm(a, b) if output is None else torch_module.mm(a, b, out=output)
+
+
+def gemv_fallback(torch_module: Any, x: Any, weight: Any) -> Any:
+    return torch_module.mm(x, weight.transpose(0, 1))
+
+
+def gemv_reference(torch_module: Any, x: Any, weight: Any) -> Any:
+    return torch_module.mm(x.float(), weight.float().transpose(0, 1)).to(dtype=x.dtype)
+
+
+def gemm_reference_fp32(torch_module: Any, a: Any, b: Any) -> Any:
+    """fp32-accumulated product before the final rounding (parity metric denominator)."""
+
+    return torch_module.mm(a.float(), b.float())

@@ -1,0 +1,304 @@
+// gemv.cu -- decode GEMV / skinny GEMM: out[M,N] = x[M,K] @ W[N,K]^T, M <= 32.
+//
+// The weight is the only large operand (N*K*2 bytes, read exactly once), so
+// the kernel is an HBM stream.  Design for B200:
+//   * each warp owns ROWS weight rows and a contiguous slice of K; every lane
+//     issues 128-bit `ld.global.nc.L1::no_allocate` loads, a warp covers 512
+//     contiguous bytes of a row per load, UNROLL x ROWS loads are in flight
+//     per lane before the first FMA (Little's law: ~5 MB must be in flight
+//     across 148 SMs to cover HBM latency);
+//   * x (at most 32 x K x 2 bytes) stays in L2/L1 and is read with __ldg;
+//     one 16-byte x vector feeds ROWS rows;
+//   * fp32 accumulation, warp-shuffle tree reduction;
+//   * split-K inside the CTA: the 8 warps form (8/KS) row groups x KS K-slices
+//     and the KS partial sums are added in a fixed order through shared
+//     memory -- deterministic, no workspace, no second launch.  KS grows when
+//     N is too small to give every SM enough rows.
+// No tensor cores: at M <= 16 the kernel is bound by HBM bandwidth.
+//
+// Role of the reference: replaces gemv_wave_kernel / gemv_packed_kernel /
+// gemv_lds_kernel (benchmarks/gemv/native_gemv.hip:30-203), whose lanes
+// stride K one element at a time (native_gemv.hip:49-58).
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "rk_device.cuh"
+#include "rk_internal.h"
+
+namespace rk {
+
+static std::atomic<int> g_gemv_rows_override{0};
+static std::atomic<int> g_gemv_ks_override{0};
+
+namespace {
+
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T, int MB, int ROWS>
+__device__ __forceinline__ void fma_vec(float (&acc)[MB][ROWS], const uint4 (&w)[ROWS],
+                                        const uint4& xv, int m) {
+  const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const float2 xf = Pack2<T>::to_floats(xs[p]);
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      const uint32_t ws[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+      const float2 wf = Pack2<T>::to_floats(ws[p]);
+      acc[m][r] = fmaf(wf.x, xf.x, acc[m][r]);
+      acc[m][r] = fmaf(wf.y, xf.y, acc[m][r]);
+    }
+  }
+}
+
+template <typename T, int MB, int ROWS, int KS>
+__global__ void __launch_bounds__(GEMV_THREADS)
+    gemv_stream_kernel(const T* __restrict__ x, const T* __restrict__ W, T* __restrict__ out,
+                       int M, int N, int K) {
+  constexpr int RG = GEMV_WARPS / KS;
+  constexpr int UNROLL = (ROWS >= 4) ? 2 : 4;
+  __shared__ float red[KS > 1 ? KS * RG * ROWS * MB : 1];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rg = warp / KS, ks = warp % KS;
+  const int row0 = (blockIdx.x * RG + rg) * ROWS;
+  const int KV = K >> 3;  // 16-byte vectors per row
+  const int v0 = static_cast<int>(static_cast<int64_t>(KV) * ks / KS);
+  const int v1 = static_cast<int>(static_cast<int64_t>(KV) * (ks + 1) / KS);
+
+  const uint4* wrow[ROWS];
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    const int row = min(row0 + r, N - 1);  // rows past N re-read the last row; never stored
+    wrow[r] = reinterpret_cast<const uint4*>(W + static_cast<size_t>(row) * K);
+  }
+  const uint4* xrow = reinterpret_cast<const uint4*>(x);
+
+  float acc[MB][ROWS];
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) acc[m][r] = 0.f;
+
+  int v = v0 + lane;
+  for (; v + 32 * (UNROLL - 1) < v1; v += 32 * UNROLL) {
+    uint4 w[UNROLL][ROWS];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) w[u][r] = ld_stream_v4(wrow[r] + v + 32 * u);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+#pragma unroll
+      for (int m = 0; m < MB; ++m)
+        if (m < M) fma_vec<T, MB, ROWS>(acc, w[u], __ldg(xrow + static_cast<size_t>(m) * KV + v + 32 * u), m);
+  }
+  for (; v < v1; v += 32) {
+    uint4 w[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) w[r] = ld_stream_v4(wrow[r] + v);
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+      if (m < M) fma_vec<T, MB, ROWS>(acc, w, __ldg(xrow + static_cast<size_t>(m) * KV + v), m);
+  }
+
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) acc[m][r] = warp_sum(acc[m][r]);
+
+  if constexpr (KS == 1) {
+    if (lane == 0) {
+#pragma unroll
+      for (int m = 0; m < MB; ++m)
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+          if (m < M && row0 + r < N)
+            out[static_cast<size_t>(m) * N + row0 + r] = from_f32<T>(acc[m][r]);
+    }
+  } else {
+    if (lane == 0) {
+#pragma unroll
+      for (int m = 0; m < MB; ++m)
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) red[((ks * RG + rg) * ROWS + r) * MB + m] = acc[m][r];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < RG * ROWS * MB; i += GEMV_THREADS) {
+      const int m = i % MB, rr = i / MB;  // rr = rg * ROWS + r
+      const int row = blockIdx.x * RG * ROWS + rr;
+      if (m < M && row < N) {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < KS; ++k) s += red[(k * RG * ROWS + rr) * MB + m];
+        out[static_cast<size_t>(m) * N + row] = from_f32<T>(s);
+      }
+    }
+  }
+}
+
+// Generic GEMV: any K, any alignment.  One warp per output row, lanes stride K.
+template <typename T, int MB>
+__global__ void __launch_bounds__(256)
+    gemv_scalar_kernel(const T* __restrict__ x, const T* __restrict__ W, T* __restrict__ out,
+                       int M, int N, int K) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= N) return;
+  const T* w = W + static_cast<size_t>(row) * K;
+  float acc[MB];
+#pragma unroll
+  for (int m = 0; m < MB; ++m) acc[m] = 0.f;
+  for (int k = lane; k < K; k += 32) {
+    const float wf = to_f32(w[k]);
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+      if (m < M) acc[m] = fmaf(wf, to_f32(x[static_cast<size_t>(m) * K + k]), acc[m]);
+  }
+#pragma unroll
+  for (int m = 0; m < MB; ++m) {
+    const float s = warp_sum(acc[m]);
+    if (lane == 0 && m < M) out[static_cast<size_t>(m) * N + row] = from_f32<T>(s);
+  }
+}
+
+using GemvFn = void (*)(const void*, const void*, void*, int, int, int, int, cudaStream_t);
+
+template <typename T, int MB, int ROWS, int KS>
+void launch_stream(const void* x, const void* W, void* out, int M, int N, int K, int grid,
+                   cudaStream_t s) {
+  gemv_stream_kernel<T, MB, ROWS, KS><<<grid, GEMV_THREADS, 0, s>>>(
+      static_cast<const T*>(x), static_cast<const T*>(W), static_cast<T*>(out), M, N, K);
+}
+
+template <typename T, int MB, int ROWS>
+GemvFn pick_ks(int ks) {
+  switch (ks) {
+    case 1: return &launch_stream<T, MB, ROWS, 1>;
+    case 2: return &launch_stream<T, MB, ROWS, 2>;
+    case 4: return &launch_stream<T, MB, ROWS, 4>;
+    default: return &launch_stream<T, MB, ROWS, 8>;
+  }
+}
+
+template <typename T, int MB>
+GemvFn pick_rows(int rows, int ks) {
+  if constexpr (MB <= 4) {
+    if (rows >= 4) return pick_ks<T, MB, 4>(ks);
+  }
+  if constexpr (MB <= 16) {
+    if (rows >= 2) return pick_ks<T, MB, 2>(ks);
+  }
+  return pick_ks<T, MB, 1>(ks);
+}
+
+template <typename T>
+GemvFn pick(int mb, int rows, int ks) {
+  switch (mb) {
+    case 1: return pick_rows<T, 1>(rows, ks);
+    case 2: return pick_rows<T, 2>(rows, ks);
+    case 4: return pick_rows<T, 4>(rows, ks);
+    case 8: return pick_rows<T, 8>(rows, ks);
+    case 16: return pick_rows<T, 16>(rows, ks);
+    default: return pick_rows<T, 32>(rows, ks);
+  }
+}
+
+int bucket_m(int64_t M) {
+  int mb = 1;
+  while (mb < M) mb <<= 1;
+  return mb;
+}
+
+// Rows per warp the kernel instantiations actually provide for an M bucket.
+int clamp_rows(int mb, int rows) {
+  const int cap = mb <= 4 ? 4 : (mb <= 16 ? 2 : 1);
+  int r = 1;
+  while (r * 2 <= rows && r * 2 <= cap) r *= 2;
+  return r;
+}
+
+}  // namespace
+
+bool gemv_stream_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,
+                           int64_t K) {
+  (void)out;
+  if (M < 1 || M > 32 || N < 1 || K < 8) return false;
+  if (K % 8 != 0) return false;
+  if (!aligned16(x) || !aligned16(W)) return false;
+  if (N > (1ll << 31) - 64 || K > (1ll << 31) - 64) return false;
+  return true;
+}
+
+rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,
+                             int64_t K, rk_dtype dt, cudaStream_t s) {
+  if (!gemv_stream_supported(x, W, out, M, N, K)) return RK_ERR_UNSUPPORTED;
+  const int mb = bucket_m(M);
+  int rows = g_gemv_rows_override.load();
+  if (rows <= 0) rows = mb <= 16 ? 2 : 1;
+  rows = clamp_rows(mb, rows);
+  int ks = g_gemv_ks_override.load();
+  if (ks <= 0) {
+    // Enough CTAs that every SM holds several: split K inside the CTA when N is small.
+    const int64_t target = 4ll * device_sm_count();
+    ks = 1;
+    while (ks < 8 && (N + (GEMV_WARPS / ks) * rows - 1) / ((GEMV_WARPS / ks) * rows) < target) ks *= 2;
+    // Each K slice should still stream at least a few KB per row.
+    while (ks > 1 && (K / 8) / ks < 64) ks /= 2;
+  }
+  ks = ks >= 8 ? 8 : (ks >= 4 ? 4 : (ks >= 2 ? 2 : 1));
+  const int rows_per_cta = (GEMV_WARPS / ks) * rows;
+  const int64_t grid = (N + rows_per_cta - 1) / rows_per_cta;
+  GemvFn fn = dt == RK_DTYPE_BF16 ? pick<__nv_bfloat16>(mb, rows, ks) : pick<__half>(mb, rows, ks);
+  fn(x, W, out, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+     static_cast<int>(grid), s);
+  note_launch();
+  return cuda_status(cudaGetLastError());
+}
+
+rk_status gemv_scalar_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,
+                             int64_t K, rk_dtype dt, cudaStream_t s) {
+  if (M < 1 || M > 32 || N < 1 || K < 1) return RK_ERR_INVALID_ARGUMENT;
+  if (N > (1ll << 31) - 64 || K > (1ll << 31) - 64) return RK_ERR_UNSUPPORTED;
+  const unsigned grid = static_cast<unsigned>((N + 7) / 8);
+  const int mb = bucket_m(M);
+#define RK_SCALAR_CASE(MBV)                                                                       \
+  case MBV:                                                                                       \
+    if (dt == RK_DTYPE_BF16)                                                                      \
+      gemv_scalar_kernel<__nv_bfloat16, MBV><<<grid, 256, 0, s>>>(                                \
+          static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(W),             \
+          static_cast<__nv_bfloat16*>(out), int(M), int(N), int(K));                              \
+    else                                                                                          \
+      gemv_scalar_kernel<__half, MBV><<<grid, 256, 0, s>>>(static_cast<const __half*>(x),        \
+                                                           static_cast<const __half*>(W),        \
+                                                           static_cast<__half*>(out), int(M),    \
+                                                           int(N), int(K));                      \
+    break;
+  switch (mb) {
+    RK_SCALAR_CASE(1)
+    RK_SCALAR_CASE(2)
+    RK_SCALAR_CASE(4)
+    RK_SCALAR_CASE(8)
+    RK_SCALAR_CASE(16)
+    RK_SCALAR_CASE(32)
+    default: return RK_ERR_INVALID_ARGUMENT;
+  }
+#undef RK_SCALAR_CASE
+  note_launch();
+  return cuda_status(cudaGetLastError());
+}
+
+void gemv_set_tuning(int rows, int ks) {
+  g_gemv_rows_override.store(rows);
+  g_gemv_ks_override.store(ks);
+}
+
+}  // namespace rk

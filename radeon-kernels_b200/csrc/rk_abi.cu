@@ -1,0 +1,230 @@
+// rk_abi.cu -- the extern "C" boundary of librk_kernels.so (include/rk_kernels.h):
+// argument validation, variant selection, per-device state (status word,
+// SM count), error mapping.  No entry point allocates device memory.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "rk_device.cuh"
+#include "rk_internal.h"
+
+namespace rk {
+void gemv_set_tuning(int rows, int ks);
+}
+
+// One status word per device: kernels atomicOr RK_DEV_ERR_* bits into it when
+// a bounded wait runs out; rk_device_status() reads and clears it.
+__device__ uint32_t rk_device_status_word;
+
+namespace rk {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  uint32_t* status = nullptr;
+  int sm_count = 0;
+  int cc_major = 0;
+  int cc_minor = 0;
+};
+
+DeviceInfo g_devices[kMaxDevices];
+std::atomic<uint64_t> g_timeout_ns{1000000000ull};
+std::atomic<int> g_inject_stall{0};
+std::atomic<uint64_t> g_launches{0};
+thread_local std::string g_last_error;
+
+DeviceInfo* current_device_info() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  DeviceInfo* d = &g_devices[dev];
+  std::call_once(d->once, [d, dev] {
+    cudaDeviceProp prop;
+    cudaError_t e = cudaGetDeviceProperties(&prop, dev);
+    if (e == cudaSuccess) {
+      d->sm_count = prop.multiProcessorCount;
+      d->cc_major = prop.major;
+      d->cc_minor = prop.minor;
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, rk_device_status_word);
+      d->status = static_cast<uint32_t*>(p);
+    }
+    d->err = e;
+  });
+  return d->err == cudaSuccess ? d : nullptr;
+}
+
+bool valid_dtype(rk_dtype dt) { return dt == RK_DTYPE_FP16 || dt == RK_DTYPE_BF16; }
+
+}  // namespace
+
+rk_status cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return RK_OK;
+  g_last_error = cudaGetErrorString(e);
+  return RK_ERR_CUDA;
+}
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int device_sm_count() {
+  DeviceInfo* d = current_device_info();
+  return d ? d->sm_count : 1;
+}
+
+int device_cc_major() {
+  DeviceInfo* d = current_device_info();
+  return d ? d->cc_major : 0;
+}
+
+rk_status launch_ctl(LaunchCtl* ctl) {
+  DeviceInfo* d = current_device_info();
+  if (d == nullptr) return RK_ERR_NO_DEVICE;
+  ctl->status = d->status;
+  ctl->timeout_ns = g_timeout_ns.load();
+  ctl->inject_stall = g_inject_stall.exchange(0);
+  return RK_OK;
+}
+
+rk_status gemm_tc_2sm_launch(const void*, const void*, void*, int64_t, int64_t, int64_t, rk_dtype,
+                             cudaStream_t);
+
+}  // namespace rk
+
+using namespace rk;
+
+extern "C" {
+
+const char* rk_status_string(rk_status status) {
+  switch (status) {
+    case RK_OK: return "ok";
+    case RK_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case RK_ERR_UNSUPPORTED: return "variant does not support this problem";
+    case RK_ERR_CUDA: return "CUDA error";
+    case RK_ERR_TIMEOUT: return "device-side wait timed out";
+    case RK_ERR_NO_DEVICE: return "no usable CUDA device";
+    case RK_ERR_TOO_LARGE: return "request exceeds the entry point's fixed capacity";
+  }
+  return "unknown status";
+}
+
+const char* rk_last_error(void) { return g_last_error.c_str(); }
+
+int rk_abi_version(void) { return RK_ABI_VERSION; }
+
+uint64_t rk_launch_count(void) { return g_launches.load(); }
+
+void rk_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 1000000000ull); }
+
+void rk_debug_inject_stall(int enable) { g_inject_stall.store(enable ? 1 : 0); }
+
+void rk_gemv_set_tuning(int rows, int ksplit) { rk::gemv_set_tuning(rows, ksplit); }
+
+const char* rk_variant_name(int op, int variant) {
+  if (op == 0) {
+    switch (variant) {
+      case RK_GEMM_AUTO: return "gemm:auto";
+      case RK_GEMM_SIMT: return "gemm:simt";
+      case RK_GEMM_TC_1SM: return "gemm:tc_1sm";
+      case RK_GEMM_TC_2SM: return "gemm:tc_2sm";
+    }
+  } else if (op == 1) {
+    switch (variant) {
+      case RK_GEMV_AUTO: return "gemv:auto";
+      case RK_GEMV_SCALAR: return "gemv:scalar";
+      case RK_GEMV_STREAM: return "gemv:stream";
+    }
+  }
+  return "unknown";
+}
+
+int rk_gemm_select_variant(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                           int64_t K, rk_dtype dt) {
+  (void)dt;
+  if (gemm_tc_supported(A, B, C, M, N, K)) return RK_GEMM_TC_1SM;
+  return RK_GEMM_SIMT;
+}
+
+int rk_gemv_select_variant(const void* x, const void* W, const void* out, int64_t M, int64_t N,
+                           int64_t K, rk_dtype dt) {
+  (void)dt;
+  return gemv_stream_supported(x, W, out, M, N, K) ? RK_GEMV_STREAM : RK_GEMV_SCALAR;
+}
+
+rk_status rk_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                  rk_dtype dt, int variant, rk_stream_t stream) {
+  if (M < 0 || N < 0 || K < 0 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
+  if (variant < 0 || variant >= RK_GEMM_VARIANT_COUNT) return RK_ERR_UNSUPPORTED;
+  if (M == 0 || N == 0) return RK_OK;
+  if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    // Empty inner dimension: C is the zero matrix (torch.mm semantics).
+    return cuda_status(cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, s));
+  }
+  if (variant == RK_GEMM_AUTO) variant = rk_gemm_select_variant(A, B, C, M, N, K, dt);
+  switch (variant) {
+    case RK_GEMM_SIMT: return gemm_simt_launch(A, B, C, M, N, K, dt, s);
+    case RK_GEMM_TC_1SM: return gemm_tc_1sm_launch(A, B, C, M, N, K, dt, s);
+    case RK_GEMM_TC_2SM: return gemm_tc_2sm_launch(A, B, C, M, N, K, dt, s);
+  }
+  return RK_ERR_UNSUPPORTED;
+}
+
+rk_status rk_gemv(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
+                  rk_dtype dt, int variant, rk_stream_t stream) {
+  if (M < 1 || M > 32 || N < 1 || K < 1 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
+  if (x == nullptr || W == nullptr || out == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  if (variant < 0 || variant >= RK_GEMV_VARIANT_COUNT) return RK_ERR_UNSUPPORTED;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (variant == RK_GEMV_AUTO) variant = rk_gemv_select_variant(x, W, out, M, N, K, dt);
+  switch (variant) {
+    case RK_GEMV_SCALAR: return gemv_scalar_launch(x, W, out, M, N, K, dt, s);
+    case RK_GEMV_STREAM: return gemv_stream_launch(x, W, out, M, N, K, dt, s);
+  }
+  return RK_ERR_UNSUPPORTED;
+}
+
+rk_status rk_gather_column_blocks(const void* blocks, void* out, int64_t G, int64_t M, int64_t N,
+                                  rk_dtype dt, rk_stream_t stream) {
+  if (G < 1 || M < 0 || N < 0 || N % G != 0 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
+  if (M == 0 || N == 0) return RK_OK;
+  if (blocks == nullptr || out == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return gather_column_blocks_launch(blocks, out, G, M, N, dt,
+                                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+rk_status rk_device_status(rk_stream_t stream) {
+  DeviceInfo* d = current_device_info();
+  if (d == nullptr) return RK_ERR_NO_DEVICE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint32_t word = 0;
+  cudaError_t e = cudaMemcpyAsync(&word, d->status, sizeof(word), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (word != 0) {
+    e = cudaMemsetAsync(d->status, 0, sizeof(uint32_t), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_status(e);
+    return RK_ERR_TIMEOUT;
+  }
+  return RK_OK;
+}
+
+}  // extern "C"
+
+namespace rk {
+// The two-SM tensor-core variant is provided by gemm_tcgen05_2sm.cu when built;
+// this weak default reports it as unavailable.
+__attribute__((weak)) rk_status gemm_tc_2sm_launch(const void*, const void*, void*, int64_t,
+                                                   int64_t, int64_t, rk_dtype, cudaStream_t) {
+  return RK_ERR_UNSUPPORTED;
+}
+}  // namespace rk

@@ -1,0 +1,51 @@
+// rk_internal.h -- host-side declarations shared by the translation units of
+// librk_kernels.so.  Not part of the public ABI (see include/rk_kernels.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "rk_kernels.h"
+
+namespace rk {
+
+struct LaunchCtl {
+  uint32_t* status;     // device address of this device's status word
+  uint64_t timeout_ns;  // per-wait limit handed to the kernels
+  int inject_stall;     // test hook, see rk_debug_inject_stall()
+};
+
+// Fills `ctl` for the current device (status word address, limits).
+rk_status launch_ctl(LaunchCtl* ctl);
+// Cached per-device properties.
+int device_sm_count();
+int device_cc_major();
+// Counts one kernel launch (rk_launch_count()).
+void note_launch();
+// Maps a CUDA error to a status code (and remembers the message).
+rk_status cuda_status(cudaError_t e);
+
+// Kernel families.  All validate what they need and return RK_ERR_UNSUPPORTED
+// when the variant cannot run the request.
+rk_status gemm_simt_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                           rk_dtype dt, cudaStream_t s);
+rk_status gemm_tc_1sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                             int64_t K, rk_dtype dt, cudaStream_t s);
+rk_status gemm_tc_2sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                             int64_t K, rk_dtype dt, cudaStream_t s);
+bool gemm_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                       int64_t K);
+
+rk_status gemv_scalar_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,
+                             int64_t K, rk_dtype dt, cudaStream_t s);
+rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,
+                             int64_t K, rk_dtype dt, cudaStream_t s);
+bool gemv_stream_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,
+                           int64_t K);
+
+rk_status gather_column_blocks_launch(const void* blocks, void* out, int64_t G, int64_t M,
+                                      int64_t N, rk_dtype dt, cudaStream_t s);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace rk

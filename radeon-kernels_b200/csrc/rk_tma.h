@@ -1,0 +1,55 @@
+// rk_tma.h -- host-side construction of 2-D TMA tensor maps (CUtensorMap)
+// for row-major 16-bit matrices, with the 128-byte swizzle the UMMA
+// shared-memory descriptors expect.  cuTensorMapEncodeTiled is fetched from
+// the driver at run time, so the library does not link libcuda directly.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "rk_internal.h"
+
+namespace rk {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Tensor map over a row-major [outer, inner] matrix of 16-bit elements, read
+// in boxes of [box_outer, box_inner] with the 128-byte swizzle
+// (box_inner * 2 must be <= 128).  Out-of-range elements read as zero.
+inline rk_status make_tmap_2d(CUtensorMap* map, const void* base, rk_dtype dt, int64_t inner,
+                              int64_t outer, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr) return RK_ERR_CUDA;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * 2};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estride[2] = {1, 1};
+  const CUtensorMapDataType t =
+      dt == RK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(map, t, 2, const_cast<void*>(base), dims, strides, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? RK_OK : RK_ERR_UNSUPPORTED;
+}
+
+}  // namespace rk

@@ -1,0 +1,148 @@
+// torch_ext.cpp -- thin PyTorch binding over the C ABI (include/rk_kernels.h).
+//
+// Built twice from this one source:
+//   _rk_ext    the built-in "cuda" provider of radeon_kernels (links
+//              librk_kernels.so);
+//   rk_sm100a  the python_extension artifact of the sm_100a kernel pack
+//              (kernels linked in statically, so the SHA-256 in the pack
+//              manifest covers them).
+// It unwraps tensors into pointers and sizes, launches on the caller's
+// current CUDA stream, and turns a non-OK rk_status into RuntimeError.
+//
+// Entry points mirror the reference's pybind modules:
+//   gemm_out(a, b, out, variant) -> out   (wmma_gemm.hip:294-316, :326-329)
+//   gemm(a, b, variant) -> new tensor
+//   gemv_*(input, weight) -> new tensor   (native_gemv.hip:343-391)
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/extension.h>
+
+#include "rk_kernels.h"
+
+namespace {
+
+rk_dtype dtype_of(const at::Tensor& t, const char* name) {
+  if (t.scalar_type() == at::kHalf) return RK_DTYPE_FP16;
+  if (t.scalar_type() == at::kBFloat16) return RK_DTYPE_BF16;
+  TORCH_CHECK(false, name, " must use torch.float16 or torch.bfloat16");
+}
+
+void check_matrix(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.dim() == 2, name, " must be rank 2");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  dtype_of(t, name);
+}
+
+void check_status(rk_status st, const char* what) {
+  TORCH_CHECK(st == RK_OK, what, " failed: ", rk_status_string(st),
+              (st == RK_ERR_CUDA ? std::string(" (") + rk_last_error() + ")" : std::string()));
+}
+
+rk_stream_t current_stream(const at::Tensor& t) {
+  return reinterpret_cast<rk_stream_t>(c10::cuda::getCurrentCUDAStream(t.get_device()).stream());
+}
+
+at::Tensor gemm_out(const at::Tensor& a, const at::Tensor& b, at::Tensor out, int64_t variant) {
+  check_matrix(a, "a");
+  check_matrix(b, "b");
+  check_matrix(out, "out");
+  TORCH_CHECK(a.device() == b.device() && out.device() == a.device(),
+              "a, b and out must be on the same device");
+  TORCH_CHECK(a.scalar_type() == b.scalar_type() && out.scalar_type() == a.scalar_type(),
+              "a, b and out must have the same dtype");
+  TORCH_CHECK(a.size(1) == b.size(0), "incompatible GEMM dimensions");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == b.size(1), "out has the wrong shape");
+  c10::cuda::CUDAGuard guard(a.device());
+  check_status(rk_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.size(0), b.size(1),
+                       a.size(1), dtype_of(a, "a"), static_cast<int>(variant), current_stream(a)),
+               "rk_gemm");
+  return out;
+}
+
+at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, int64_t variant) {
+  check_matrix(a, "a");
+  check_matrix(b, "b");
+  TORCH_CHECK(a.size(1) == b.size(0), "incompatible GEMM dimensions");
+  auto out = at::empty({a.size(0), b.size(1)}, a.options());
+  return gemm_out(a, b, out, variant);
+}
+
+at::Tensor gemv_out(const at::Tensor& x, const at::Tensor& weight, at::Tensor out,
+                    int64_t variant) {
+  check_matrix(x, "input");
+  check_matrix(weight, "weight");
+  check_matrix(out, "out");
+  TORCH_CHECK(x.device() == weight.device() && out.device() == x.device(),
+              "input, weight and out must use the same device");
+  TORCH_CHECK(x.scalar_type() == weight.scalar_type() && out.scalar_type() == x.scalar_type(),
+              "input, weight and out must use the same dtype");
+  TORCH_CHECK(x.size(0) > 0 && x.size(0) <= 32, "input M must be in [1, 32]");
+  TORCH_CHECK(x.size(1) > 0 && weight.size(0) > 0, "N and K must be positive");
+  TORCH_CHECK(x.size(1) == weight.size(1), "input and weight must share K");
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == weight.size(0), "out has the wrong shape");
+  c10::cuda::CUDAGuard guard(x.device());
+  check_status(rk_gemv(x.data_ptr(), weight.data_ptr(), out.data_ptr(), x.size(0),
+                       weight.size(0), x.size(1), dtype_of(x, "input"),
+                       static_cast<int>(variant), current_stream(x)),
+               "rk_gemv");
+  return out;
+}
+
+at::Tensor gemv(const at::Tensor& x, const at::Tensor& weight, int64_t variant) {
+  check_matrix(x, "input");
+  check_matrix(weight, "weight");
+  auto out = at::empty({x.size(0), weight.size(0)}, x.options());
+  return gemv_out(x, weight, out, variant);
+}
+
+at::Tensor gemv_stream(const at::Tensor& x, const at::Tensor& weight) {
+  return gemv(x, weight, RK_GEMV_STREAM);
+}
+
+at::Tensor gemv_scalar(const at::Tensor& x, const at::Tensor& weight) {
+  return gemv(x, weight, RK_GEMV_SCALAR);
+}
+
+at::Tensor gather_column_blocks(const at::Tensor& blocks, at::Tensor out) {
+  TORCH_CHECK(blocks.is_cuda() && blocks.dim() == 3 && blocks.is_contiguous(),
+              "blocks must be a contiguous CUDA tensor [G, M, N/G]");
+  check_matrix(out, "out");
+  TORCH_CHECK(out.scalar_type() == blocks.scalar_type(), "dtype mismatch");
+  TORCH_CHECK(out.size(0) == blocks.size(1) && out.size(1) == blocks.size(0) * blocks.size(2),
+              "out must be [M, G * N/G]");
+  c10::cuda::CUDAGuard guard(out.device());
+  check_status(rk_gather_column_blocks(blocks.data_ptr(), out.data_ptr(), blocks.size(0),
+                                       out.size(0), out.size(1), dtype_of(out, "out"),
+                                       current_stream(out)),
+               "rk_gather_column_blocks");
+  return out;
+}
+
+int64_t device_status() {
+  return static_cast<int64_t>(rk_device_status(
+      reinterpret_cast<rk_stream_t>(c10::cuda::getCurrentCUDAStream().stream())));
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "B200 (sm_100a) GEMM/GEMV kernels behind the rk_kernels C ABI";
+  m.def("gemm_out", &gemm_out, "C = A @ B into the caller's output", py::arg("a"), py::arg("b"),
+        py::arg("out"), py::arg("variant") = 0);
+  m.def("gemm", &gemm, "C = A @ B", py::arg("a"), py::arg("b"), py::arg("variant") = 0);
+  m.def("gemv", &gemv, "out = x @ weight.T", py::arg("input"), py::arg("weight"),
+        py::arg("variant") = 0);
+  m.def("gemv_out", &gemv_out, "out = x @ weight.T into the caller's output", py::arg("input"),
+        py::arg("weight"), py::arg("out"), py::arg("variant") = 0);
+  m.def("gemv_stream", &gemv_stream, "128-bit weight-streaming GEMV (K % 8 == 0, 16B aligned)");
+  m.def("gemv_scalar", &gemv_scalar, "generic GEMV (any K, any alignment)");
+  m.def("gather_column_blocks", &gather_column_blocks, "[G,M,N/G] blocks -> row-major [M,N]");
+  m.def("device_status", &device_status, "read and clear the device status word");
+  m.def("set_wait_timeout_ns", [](uint64_t ns) { rk_set_wait_timeout_ns(ns); });
+  m.def("debug_inject_stall", [](bool on) { rk_debug_inject_stall(on ? 1 : 0); });
+  m.def("gemv_set_tuning", [](int rows, int ks) { rk_gemv_set_tuning(rows, ks); });
+  m.def("launch_count", []() { return rk_launch_count(); });
+  m.def("variant_name", [](int op, int v) { return std::string(rk_variant_name(op, v)); });
+  m.def("abi_version", []() { return rk_abi_version(); });
+}

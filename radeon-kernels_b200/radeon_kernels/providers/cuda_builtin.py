@@ -1,0 +1,104 @@
+"""The built-in ``cuda`` provider: the always-available fallback of every manifest.
+
+Where the reference falls back to ``torch.mm`` (src/radeon_kernels/providers/torch_fallback.py:6-9,
+src/radeon_kernels/ops/gemv/reference.py:12-15), this build falls back to its own CUDA
+kernels through the compiled binding, with the ``auto`` variant: the tcgen05 GEMM or the
+streaming GEMV when shape and alignment allow, the generic predicated kernels otherwise.
+So every call on a GPU, matched by a dispatch entry or not, runs a kernel of this
+library; nothing falls back to a vendor library or to the CPU.
+
+Inputs that are not contiguous are packed first (a device copy).  Inputs that require
+gradients go through :class:`_GemmFunction` / :class:`_GemvFunction`, whose backward passes
+are again this library's kernels on transposed copies.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+from radeon_kernels import _native
+
+SELECTED_GEMM = "cuda/gemm"
+SELECTED_GEMV = "cuda/gemv"
+
+
+def _contiguous(tensor: Any) -> Any:
+    return tensor if tensor.is_contiguous() else tensor.contiguous()
+
+
+def _gemm_raw(a: Any, b: Any, output: Any | None) -> Any:
+    ext = _native.extension()
+    a, b = _contiguous(a), _contiguous(b)
+    if output is None:
+        return ext.gemm(a, b, 0)
+    if output.is_contiguous():
+        return ext.gemm_out(a, b, output, 0)
+    output.copy_(ext.gemm(a, b, 0))
+    return output
+
+
+def _gemv_raw(x: Any, weight: Any) -> Any:
+    return _native.extension().gemv(_contiguous(x), _contiguous(weight), 0)
+
+
+def _autograd_functions() -> tuple[Any, Any]:
+    import torch
+
+    class _GemmFunction(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx: Any, a: Any, b: Any) -> Any:
+            ctx.save_for_backward(a, b)
+            return _gemm_raw(a.detach(), b.detach(), None)
+
+        @staticmethod
+        def backward(ctx: Any, grad: Any) -> Any:
+            a, b = ctx.saved_tensors
+            grad = _contiguous(grad)
+            grad_a = _gemm_raw(grad, b.detach().t(), None) if ctx.needs_input_grad[0] else None
+            grad_b = _gemm_raw(a.detach().t(), grad, None) if ctx.needs_input_grad[1] else None
+            return grad_a, grad_b
+
+    class _GemvFunction(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx: Any, x: Any, weight: Any) -> Any:
+            ctx.save_for_backward(x, weight)
+            return _gemv_raw(x.detach(), weight.detach())
+
+        @staticmethod
+        def backward(ctx: Any, grad: Any) -> Any:
+            x, weight = ctx.saved_tensors
+            grad = _contiguous(grad)
+            # out = x @ W^T:  dx = grad @ W,  dW = grad^T @ x
+            grad_x = _gemm_raw(grad, weight.detach(), None) if ctx.needs_input_grad[0] else None
+            grad_w = _gemm_raw(grad.t(), x.detach(), None) if ctx.needs_input_grad[1] else None
+            return grad_x, grad_w
+
+    return _GemmFunction, _GemvFunction
+
+
+_FUNCTIONS: tuple[Any, Any] | None = None
+
+
+def _functions() -> tuple[Any, Any]:
+    global _FUNCTIONS
+    if _FUNCTIONS is None:
+        _FUNCTIONS = _autograd_functions()
+    return _FUNCTIONS
+
+
+def _needs_grad(torch_module: Any, *tensors: Any) -> bool:
+    return torch_module.is_grad_enabled() and any(bool(t.requires_grad) for t in tensors)
+
+
+def gemm(torch_module: Any, a: Any, b: Any, output: Any | None = None) -> Any:
+    if _needs_grad(torch_module, a, b):
+        if output is not None:
+            raise RuntimeError("gemm(): an out= tensor does not support automatic differentiation")
+        return _functions()[0].apply(a, b)
+    return _gemm_raw(a, b, output)
+
+
+def gemv(torch_module: Any, x: Any, weight: Any) -> Any:
+    if _needs_grad(torch_module, x, weight):
+        return _functions()[1].apply(x, weight)
+    return _gemv_raw(x, weight)

@@ -1,0 +1,116 @@
+"""Generate the golden parity fixtures from the reference's own functions.
+
+Run in a container where the reference source tree is available (it is not on the GPU
+boxes; the fixtures it writes are committed):
+
+    python tests/golden/make_golden.py --reference-src <path to reference>/src
+
+For every case the inputs are drawn exactly as BASELINE.json describes (fp32 from a
+seeded ``torch.Generator``, then cast to the 16-bit dtype) and the outputs are produced
+by calling the reference package itself:
+
+* GEMM:  ``radeon_kernels.providers.torch_fallback.gemm(torch, a, b)``  (torch_fallback.py:6-9)
+* GEMV:  ``radeon_kernels.ops.gemv.reference.gemv_fallback`` and ``gemv_reference``
+  (ops/gemv/reference.py:6-15)
+
+plus the fp32 product before rounding.  16-bit arrays are stored as uint16 bit patterns.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+# name, dtype, M, N, K, seed, distribution
+GEMM_CASES = [
+    ("gemm_bf16_64x96x128_uniform", "bf16", 64, 96, 128, 0, "uniform"),
+    ("gemm_fp16_64x96x128_normal64", "fp16", 64, 96, 128, 3, "normal64"),
+    ("gemm_bf16_7x13x5_ragged", "bf16", 7, 13, 5, 10, "uniform"),
+    ("gemm_fp16_130x264x72_ragged_tiles", "fp16", 130, 264, 72, 11, "normal64"),
+    ("gemm_bf16_200x520x136_ragged_tiles", "bf16", 200, 520, 136, 12, "uniform16"),
+    ("gemm_bf16_1x8x8_tiny", "bf16", 1, 8, 8, 13, "uniform"),
+    ("gemm_fp16_3x5x0_empty_k", "fp16", 3, 5, 0, 14, "uniform"),
+    ("gemm_bf16_64x128x1024_k_deep", "bf16", 64, 128, 1024, 0, "uniform"),
+]
+# name, dtype, M, N, K, seed
+GEMV_CASES = [
+    ("gemv_bf16_m1_n256_k512", "bf16", 1, 256, 512, 1),
+    ("gemv_fp16_m4_n96_k1024", "fp16", 4, 96, 1024, 2),
+    ("gemv_bf16_m16_n64_k2048", "bf16", 16, 64, 2048, 1),
+    ("gemv_fp16_m3_n37_k13_ragged", "fp16", 3, 37, 13, 2),
+    ("gemv_bf16_m32_n40_k264", "bf16", 32, 40, 264, 1),
+    ("gemv_fp16_m4_n8_k14336_ffn_down", "fp16", 4, 8, 14336, 2),
+]
+
+
+def _bits(tensor):
+    import torch
+
+    return tensor.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def _draw(torch, shape, seed, dist, generator=None):
+    gen = generator or torch.Generator().manual_seed(seed)
+    if dist == "uniform":
+        return torch.rand(shape, generator=gen) * 2 - 1
+    if dist == "uniform16":
+        return (torch.rand(shape, generator=gen) * 2 - 1) / 16
+    if dist == "normal64":
+        return torch.randn(shape, generator=gen) / 64
+    raise ValueError(dist)
+
+
+def main(argv: list[str] | None = None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--reference-src", required=True, type=Path)
+    args = parser.parse_args(argv)
+    sys.path.insert(0, str(args.reference_src.resolve()))
+    import torch
+
+    import radeon_kernels  # the reference package
+    from radeon_kernels.ops.gemv.reference import gemv_fallback, gemv_reference
+    from radeon_kernels.providers import torch_fallback
+
+    origin = Path(radeon_kernels.__file__).resolve()
+    if not origin.is_relative_to(args.reference_src.resolve()):
+        raise SystemExit(f"imported radeon_kernels from {origin}, not from the reference")
+    dtypes = {"bf16": torch.bfloat16, "fp16": torch.float16}
+
+    for name, dt, m, n, k, seed, dist in GEMM_CASES:
+        gen = torch.Generator().manual_seed(seed)
+        a = _draw(torch, (m, k), seed, dist, gen).to(dtypes[dt])
+        b = _draw(torch, (k, n), seed, dist, gen).to(dtypes[dt])
+        c = torch_fallback.gemm(torch, a, b)
+        c32 = torch.mm(a.float(), b.float())
+        np.savez_compressed(
+            HERE / f"{name}.npz", dtype=dt, a=_bits(a), b=_bits(b), c_ref=_bits(c), c_fp32=c32.numpy()
+        )
+        print(name, tuple(c.shape))
+
+    for name, dt, m, n, k, seed in GEMV_CASES:
+        gen = torch.Generator().manual_seed(seed)
+        x = torch.randn((m, k), generator=gen).to(dtypes[dt])
+        w = (torch.randn((n, k), generator=gen) / k**0.5).to(dtypes[dt])
+        out = gemv_fallback(torch, x, w)
+        out_ref = gemv_reference(torch, x, w)
+        out32 = torch.mm(x.float(), w.float().t())
+        np.savez_compressed(
+            HERE / f"{name}.npz",
+            dtype=dt,
+            x=_bits(x),
+            w=_bits(w),
+            out_fallback=_bits(out),
+            out_reference=_bits(out_ref),
+            out_fp32=out32.numpy(),
+        )
+        print(name, tuple(out.shape))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,81 @@
+"""The CPU oracle, pinned against fixtures produced by the reference's own functions."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import golden_cases
+from oracle import oracle
+
+
+def _load(path):
+    data = np.load(path)
+    return {key: data[key] for key in data.files}
+
+
+@pytest.mark.parametrize("path", golden_cases("gemm"), ids=lambda p: p.stem)
+def test_oracle_gemm_matches_reference_fixtures(path):
+    case = _load(path)
+    dtype = str(case["dtype"])
+    c, acc = oracle.gemm(case["a"], case["b"], dtype)
+    # fp32 sums agree with the reference's fp32 product up to accumulation order.
+    np.testing.assert_allclose(acc, case["c_fp32"], rtol=0, atol=2e-5 * max(1.0, np.abs(case["c_fp32"]).max()))
+    # Rounded outputs: the reference's torch.mm result, to at most one representable step
+    # on every element not dominated by cancellation, and within the parity gate.
+    oracle.assert_parity(c, case["c_ref"], case["c_fp32"], dtype)
+
+
+@pytest.mark.parametrize("path", golden_cases("gemv"), ids=lambda p: p.stem)
+def test_oracle_gemv_matches_reference_fixtures(path):
+    case = _load(path)
+    dtype = str(case["dtype"])
+    out, acc = oracle.gemv(case["x"], case["w"], dtype)
+    np.testing.assert_allclose(acc, case["out_fp32"], rtol=0, atol=2e-5 * max(1.0, np.abs(case["out_fp32"]).max()))
+    oracle.assert_parity(out, case["out_reference"], case["out_fp32"], dtype)
+    oracle.assert_parity(out, case["out_fallback"], case["out_fp32"], dtype)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_conversions_round_trip_every_finite_pattern(dtype):
+    bits = np.arange(1 << 16, dtype=np.uint32).astype(np.uint16)
+    wide = oracle.widen(bits, dtype)
+    back = oracle.round_to(wide, dtype)
+    finite = np.isfinite(wide)
+    assert np.array_equal(back[finite], bits[finite])
+    assert np.all(np.isnan(oracle.widen(back[np.isnan(wide)], dtype)))
+
+
+def test_rounding_is_nearest_even_against_numpy_fp16():
+    rng = np.random.default_rng(7)
+    values = np.concatenate(
+        [
+            rng.standard_normal(200_000).astype(np.float32) * 1000,
+            rng.standard_normal(50_000).astype(np.float32) * 1e-5,  # subnormal range of fp16
+            np.array([65504.0, 65520.0, 65519.996, 6e-8, 3e-8, 2.98e-8, -0.0, 1e9], np.float32),
+        ]
+    )
+    ours = oracle.round_to(values, "fp16")
+    with np.errstate(over="ignore"):
+        expected = values.astype(np.float16).view(np.uint16)
+    assert np.array_equal(ours, expected)
+
+
+def test_parity_check_detects_a_planted_error():
+    # The mistake is planted in the oracle's own inputs on the CPU: one flipped mantissa
+    # bit of one A element must push the metric past the tolerance against the fixture.
+    case = _load(golden_cases("gemm_bf16_64x96x128")[0])
+    a = case["a"].copy()
+    a[5, 7] ^= np.uint16(0x0040)
+    c, _ = oracle.gemm(a, case["b"], "bf16")
+    assert oracle.ulp_distance(c, case["c_ref"]).max() > 1
+    a = case["a"].copy()
+    a[5] = 0x3F80  # a whole row set to 1.0
+    c, _ = oracle.gemm(a, case["b"], "bf16")
+    assert oracle.parity_error(oracle.widen(c, "bf16"), case["c_fp32"]) > oracle.TOLERANCE["bf16"]
+
+
+def test_parity_metric_definition():
+    ref = np.array([[1.0, -4.0], [2.0, 0.5]])
+    assert oracle.parity_error(ref, ref) == 0.0
+    assert oracle.parity_error(ref + 0.04, ref) == pytest.approx(0.01)
