@@ -21,7 +21,11 @@
 // stride K one element at a time (native_gemv.hip:49-58).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "rk_device.cuh"
 #include "rk_internal.h"
@@ -59,89 +63,123 @@ __device__ __forceinline__ void fma_vec(float (&acc)[MB][ROWS], const uint4 (&w)
   }
 }
 
+// Reduce V = MB*ROWS per-lane partial sums across the warp with a transposed
+// butterfly (V-1 + 5-log2(V) shuffles instead of 5*V): afterwards lane L holds
+// the full sum of value index (L >> (5 - log2 V)).
+template <int V>
+__device__ __forceinline__ float warp_reduce_scatter(float (&vals)[V], int lane) {
+  static_assert((V & (V - 1)) == 0 && V >= 1 && V <= 32, "V must be a power of two <= 32");
+  int count = V;
+#pragma unroll
+  for (int offset = 16; offset >= 1; offset >>= 1) {
+    if (count > 1) {
+      const bool upper = (lane & offset) != 0;
+      const int half = count / 2;
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) {
+        if (i < half) {
+          const float send = upper ? vals[i] : vals[i + half];
+          const float keep = upper ? vals[i + half] : vals[i];
+          vals[i] = keep + __shfl_xor_sync(0xffffffffu, send, offset);
+        }
+      }
+      count = half;
+    } else {
+      vals[0] += __shfl_xor_sync(0xffffffffu, vals[0], offset);
+    }
+  }
+  return vals[0];
+}
+
+template <int V>
+struct Log2 {
+  static constexpr int value = V <= 1 ? 0 : 1 + Log2<V / 2>::value;
+};
+template <>
+struct Log2<1> {
+  static constexpr int value = 0;
+};
+
+// Balanced streaming GEMV.  CTA c owns a contiguous block of rows (the grid is
+// sized to the GPU's resident-CTA capacity and rows are dealt out so no CTA has
+// more than one row more than another: no second-wave tail).  Inside the CTA
+// the 8 warps form (8/KS) row groups x KS K-slices; a warp streams ROWS rows of
+// its K-slice at a time with UNROLL 16-byte loads per row per lane in flight
+// (out-of-range vectors are predicated off, never loaded).  Per-warp partial
+// sums go to shared memory [KS][rows][MB] and are added in ks order.
 template <typename T, int MB, int ROWS, int KS>
 __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_stream_kernel(const T* __restrict__ x, const T* __restrict__ W, T* __restrict__ out,
-                       int M, int N, int K) {
+                       int M, int N, int K, int rows_base, int rows_rem, int rows_max) {
   constexpr int RG = GEMV_WARPS / KS;
-  constexpr int UNROLL = (ROWS >= 4) ? 2 : 4;
-  __shared__ float red[KS > 1 ? KS * RG * ROWS * MB : 1];
+  constexpr int UNROLL = ROWS >= 4 ? 2 : 4;
+  constexpr int V = MB * ROWS;
+  constexpr int LOGV = Log2<V>::value;
+  extern __shared__ float red[];  // [KS][rows_max][MB]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
-  const int row0 = (blockIdx.x * RG + rg) * ROWS;
+  const int cta = blockIdx.x;
+  const int row_begin = cta * rows_base + min(cta, rows_rem);
+  const int rows = rows_base + (cta < rows_rem ? 1 : 0);
   const int KV = K >> 3;  // 16-byte vectors per row
   const int v0 = static_cast<int>(static_cast<int64_t>(KV) * ks / KS);
   const int v1 = static_cast<int>(static_cast<int64_t>(KV) * (ks + 1) / KS);
-
-  const uint4* wrow[ROWS];
-#pragma unroll
-  for (int r = 0; r < ROWS; ++r) {
-    const int row = min(row0 + r, N - 1);  // rows past N re-read the last row; never stored
-    wrow[r] = reinterpret_cast<const uint4*>(W + static_cast<size_t>(row) * K);
-  }
   const uint4* xrow = reinterpret_cast<const uint4*>(x);
 
-  float acc[MB][ROWS];
+  // Row chunks of ROWS rows are dealt to the RG row groups round-robin.
+  for (int i0 = rg * ROWS; i0 < rows; i0 += RG * ROWS) {
+    const uint4* wrow[ROWS];
 #pragma unroll
-  for (int m = 0; m < MB; ++m)
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) acc[m][r] = 0.f;
-
-  int v = v0 + lane;
-  for (; v + 32 * (UNROLL - 1) < v1; v += 32 * UNROLL) {
-    uint4 w[UNROLL][ROWS];
-#pragma unroll
-    for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) w[u][r] = ld_stream_v4(wrow[r] + v + 32 * u);
-#pragma unroll
-    for (int u = 0; u < UNROLL; ++u)
-#pragma unroll
-      for (int m = 0; m < MB; ++m)
-        if (m < M) fma_vec<T, MB, ROWS>(acc, w[u], __ldg(xrow + static_cast<size_t>(m) * KV + v + 32 * u), m);
-  }
-  for (; v < v1; v += 32) {
-    uint4 w[ROWS];
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) w[r] = ld_stream_v4(wrow[r] + v);
+    for (int r = 0; r < ROWS; ++r) {
+      const int row = row_begin + min(i0 + r, rows - 1);  // duplicates are never stored
+      wrow[r] = reinterpret_cast<const uint4*>(W + static_cast<size_t>(row) * K);
+    }
+    float acc[MB][ROWS];
 #pragma unroll
     for (int m = 0; m < MB; ++m)
-      if (m < M) fma_vec<T, MB, ROWS>(acc, w, __ldg(xrow + static_cast<size_t>(m) * KV + v), m);
-  }
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) acc[m][r] = 0.f;
 
+    for (int v = v0 + lane; v < v1; v += 32 * UNROLL) {
+      uint4 w[UNROLL][ROWS];
 #pragma unroll
-  for (int m = 0; m < MB; ++m)
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) acc[m][r] = warp_sum(acc[m][r]);
-
-  if constexpr (KS == 1) {
-    if (lane == 0) {
-#pragma unroll
-      for (int m = 0; m < MB; ++m)
+      for (int u = 0; u < UNROLL; ++u) {
+        const bool in = v + 32 * u < v1;
 #pragma unroll
         for (int r = 0; r < ROWS; ++r)
-          if (m < M && row0 + r < N)
-            out[static_cast<size_t>(m) * N + row0 + r] = from_f32<T>(acc[m][r]);
-    }
-  } else {
-    if (lane == 0) {
+          w[u][r] = in ? ld_stream_v4(wrow[r] + v + 32 * u) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-      for (int m = 0; m < MB; ++m)
+      for (int u = 0; u < UNROLL; ++u) {
+        if (v + 32 * u < v1) {
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) red[((ks * RG + rg) * ROWS + r) * MB + m] = acc[m][r];
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < RG * ROWS * MB; i += GEMV_THREADS) {
-      const int m = i % MB, rr = i / MB;  // rr = rg * ROWS + r
-      const int row = blockIdx.x * RG * ROWS + rr;
-      if (m < M && row < N) {
-        float s = 0.f;
-#pragma unroll
-        for (int k = 0; k < KS; ++k) s += red[(k * RG * ROWS + rr) * MB + m];
-        out[static_cast<size_t>(m) * N + row] = from_f32<T>(s);
+          for (int m = 0; m < MB; ++m)
+            if (m < M)
+              fma_vec<T, MB, ROWS>(acc, w[u], __ldg(xrow + static_cast<size_t>(m) * KV + v + 32 * u), m);
+        }
       }
     }
+
+    float vals[V];
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) vals[m * ROWS + r] = acc[m][r];
+    const float sum = warp_reduce_scatter<V>(vals, lane);
+    const int idx = lane >> (5 - LOGV);  // value index this lane now holds
+    if ((lane & ((1 << (5 - LOGV)) - 1)) == 0) {
+      const int m = idx / ROWS, r = idx % ROWS;
+      if (i0 + r < rows) red[(ks * rows_max + i0 + r) * MB + m] = sum;
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {
+    const int i = t / M, m = t % M;
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < KS; ++k) s += red[(k * rows_max + i) * MB + m];
+    out[static_cast<size_t>(m) * N + row_begin + i] = from_f32<T>(s);
   }
 }
 
@@ -170,27 +208,38 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-using GemvFn = void (*)(const void*, const void*, void*, int, int, int, int, cudaStream_t);
+struct StreamLaunch {
+  const void* kernel;
+  void (*launch)(const void*, const void*, void*, int, int, int, int, int, int, int, size_t,
+                 cudaStream_t);
+};
 
 template <typename T, int MB, int ROWS, int KS>
 void launch_stream(const void* x, const void* W, void* out, int M, int N, int K, int grid,
-                   cudaStream_t s) {
-  gemv_stream_kernel<T, MB, ROWS, KS><<<grid, GEMV_THREADS, 0, s>>>(
-      static_cast<const T*>(x), static_cast<const T*>(W), static_cast<T*>(out), M, N, K);
+                   int rows_base, int rows_rem, int rows_max, size_t smem, cudaStream_t s) {
+  gemv_stream_kernel<T, MB, ROWS, KS><<<grid, GEMV_THREADS, smem, s>>>(
+      static_cast<const T*>(x), static_cast<const T*>(W), static_cast<T*>(out), M, N, K,
+      rows_base, rows_rem, rows_max);
+}
+
+template <typename T, int MB, int ROWS, int KS>
+StreamLaunch make_stream() {
+  return {reinterpret_cast<const void*>(&gemv_stream_kernel<T, MB, ROWS, KS>),
+          &launch_stream<T, MB, ROWS, KS>};
 }
 
 template <typename T, int MB, int ROWS>
-GemvFn pick_ks(int ks) {
+StreamLaunch pick_ks(int ks) {
   switch (ks) {
-    case 1: return &launch_stream<T, MB, ROWS, 1>;
-    case 2: return &launch_stream<T, MB, ROWS, 2>;
-    case 4: return &launch_stream<T, MB, ROWS, 4>;
-    default: return &launch_stream<T, MB, ROWS, 8>;
+    case 1: return make_stream<T, MB, ROWS, 1>();
+    case 2: return make_stream<T, MB, ROWS, 2>();
+    case 4: return make_stream<T, MB, ROWS, 4>();
+    default: return make_stream<T, MB, ROWS, 8>();
   }
 }
 
 template <typename T, int MB>
-GemvFn pick_rows(int rows, int ks) {
+StreamLaunch pick_rows(int rows, int ks) {
   if constexpr (MB <= 4) {
     if (rows >= 4) return pick_ks<T, MB, 4>(ks);
   }
@@ -201,7 +250,7 @@ GemvFn pick_rows(int rows, int ks) {
 }
 
 template <typename T>
-GemvFn pick(int mb, int rows, int ks) {
+StreamLaunch pick(int mb, int rows, int ks) {
   switch (mb) {
     case 1: return pick_rows<T, 1>(rows, ks);
     case 2: return pick_rows<T, 2>(rows, ks);
@@ -226,6 +275,24 @@ int clamp_rows(int mb, int rows) {
   return r;
 }
 
+// Resident CTAs per SM for a kernel (cached per device and kernel).
+int resident_ctas(const void* kernel, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, size_t>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, kernel, smem);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, GEMV_THREADS, smem) != cudaSuccess ||
+      n < 1)
+    n = 1;
+  cache.emplace(key, n);
+  return n;
+}
+
 }  // namespace
 
 bool gemv_stream_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,
@@ -243,23 +310,34 @@ rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M,
   if (!gemv_stream_supported(x, W, out, M, N, K)) return RK_ERR_UNSUPPORTED;
   const int mb = bucket_m(M);
   int rows = g_gemv_rows_override.load();
-  if (rows <= 0) rows = mb <= 16 ? 2 : 1;
+  if (rows <= 0) rows = mb <= 2 ? 2 : (mb <= 4 ? 4 : (mb <= 16 ? 2 : 1));
   rows = clamp_rows(mb, rows);
+  const int64_t kv = K / 8;
   int ks = g_gemv_ks_override.load();
   if (ks <= 0) {
-    // Enough CTAs that every SM holds several: split K inside the CTA when N is small.
-    const int64_t target = 4ll * device_sm_count();
-    ks = 1;
-    while (ks < 8 && (N + (GEMV_WARPS / ks) * rows - 1) / ((GEMV_WARPS / ks) * rows) < target) ks *= 2;
-    // Each K slice should still stream at least a few KB per row.
-    while (ks > 1 && (K / 8) / ks < 64) ks /= 2;
+    // Split K across the CTA's warps while each slice keeps >= 2 vectors per lane.
+    ks = 8;
+    while (ks > 1 && kv / ks < 64) ks /= 2;
   }
   ks = ks >= 8 ? 8 : (ks >= 4 ? 4 : (ks >= 2 ? 2 : 1));
-  const int rows_per_cta = (GEMV_WARPS / ks) * rows;
-  const int64_t grid = (N + rows_per_cta - 1) / rows_per_cta;
-  GemvFn fn = dt == RK_DTYPE_BF16 ? pick<__nv_bfloat16>(mb, rows, ks) : pick<__half>(mb, rows, ks);
-  fn(x, W, out, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
-     static_cast<int>(grid), s);
+  StreamLaunch L = dt == RK_DTYPE_BF16 ? pick<__nv_bfloat16>(mb, rows, ks) : pick<__half>(mb, rows, ks);
+  // Grid: every resident CTA slot of the GPU, rows dealt out evenly; more CTAs only
+  // when the per-CTA partial-sum buffer would exceed 32 KiB.
+  const int rows_per_group = (GEMV_WARPS / ks) * rows;
+  int64_t grid = static_cast<int64_t>(device_sm_count()) *
+                 resident_ctas(L.kernel, static_cast<size_t>(ks) * 64 * mb * sizeof(float));
+  const int64_t cap_rows = 32768 / (static_cast<int64_t>(ks) * mb * sizeof(float));
+  if ((N + grid - 1) / grid > cap_rows) grid = (N + cap_rows - 1) / cap_rows;
+  if (grid > N) grid = N;
+  // Keep at least one row chunk per row group where N allows it.
+  if (grid > 1 && N / grid < rows_per_group && N >= rows_per_group)
+    grid = std::max<int64_t>(1, N / rows_per_group);
+  const int rows_base = static_cast<int>(N / grid);
+  const int rows_rem = static_cast<int>(N % grid);
+  const int rows_max = rows_base + (rows_rem ? 1 : 0);
+  const size_t smem = static_cast<size_t>(ks) * rows_max * mb * sizeof(float);
+  L.launch(x, W, out, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+           static_cast<int>(grid), rows_base, rows_rem, rows_max, smem, s);
   note_launch();
   return cuda_status(cudaGetLastError());
 }

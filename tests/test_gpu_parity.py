@@ -55,7 +55,7 @@ def test_gemm_matches_reference_fixtures(path, variant):
     buf, c = _guarded(torch, m, n, dtype)
     a_before, b_before = to_bits(a), to_bits(b)
     status = abi_gemm(a, b, c, GEMM[variant], dtype)
-    if variant == "tc_1sm" and not _tc_ok(m, n, k) and m * n > 0:
+    if variant == "tc_1sm" and not _tc_ok(m, n, k) and m * n * k > 0:
         assert status == _native.RK_ERR_UNSUPPORTED
         return
     assert status == _native.RK_OK, _native.status_text(status)
