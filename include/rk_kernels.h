@@ -117,6 +117,10 @@ RK_API const char* rk_last_error(void);
  * K split (1, 2, 4, 8); 0 restores the built-in heuristic.  Process-wide. */
 RK_API void rk_gemv_set_tuning(int rows_per_warp, int ksplit);
 
+/* Tuning hook for the tensor-core GEMM variants: output tile width (64, 128,
+ * 256); 0 restores the built-in choice (fewest weighted waves).  Process-wide. */
+RK_API void rk_gemm_set_tile_n(int tile_n);
+
 /*
  * Reads and clears the device-side status word of the current device after
  * synchronising `stream`.  Returns RK_OK, or RK_ERR_TIMEOUT when a kernel

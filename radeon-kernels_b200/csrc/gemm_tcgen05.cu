@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -37,18 +38,25 @@ namespace rk {
 namespace tc1 {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 64;  // 64 x 16-bit = 128 bytes = one swizzle row
-constexpr int STAGES = 4;
 constexpr int UMMA_K = 16;
-constexpr int A_STAGE = BM * BK * 2;          // 16 KiB
-constexpr int B_BOX = 64 * BK * 2;            // 8 KiB: 64 N-columns x 64 K-rows
-constexpr int B_STAGE = BK * BN * 2;          // 32 KiB
-constexpr int STAGE_BYTES = A_STAGE + B_STAGE;  // 48 KiB
+constexpr int A_STAGE = BM * BK * 2;  // 16 KiB
+constexpr int B_BOX = 64 * BK * 2;    // 8 KiB: 64 N-columns x 64 K-rows
 constexpr int THREADS = 192;
-constexpr int TMEM_COLS = 2 * BN;  // two fp32 accumulators of 128 lanes x 256 columns
 constexpr int GROUP_M = 8;
+constexpr int RING_BYTES = 192 * 1024;  // shared-memory ring shared by all tile widths
 
+// Per tile width BN (64, 128 or 256): ring depth and TMEM footprint.
+template <int BN>
+struct Tile {
+  static constexpr int B_STAGE = BK * BN * 2;
+  static constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+  static constexpr int STAGES = RING_BYTES / STAGE_BYTES;  // 4, 6 or 8
+  static constexpr int TMEM_COLS = 2 * BN;                 // two fp32 accumulators
+  static_assert(BN == 64 || BN == 128 || BN == 256, "tile width");
+};
+
+template <int STAGES>
 struct __align__(8) Barriers {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -60,7 +68,11 @@ struct __align__(8) Barriers {
   int abort;
 };
 
-constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + STAGES * STAGE_BYTES + int(sizeof(Barriers));
+template <int BN>
+constexpr int smem_bytes() {
+  return 1024 /*alignment slack*/ + Tile<BN>::STAGES * Tile<BN>::STAGE_BYTES +
+         int(sizeof(Barriers<Tile<BN>::STAGES>));
+}
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
@@ -72,17 +84,21 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   nb = in_group / gsize;
 }
 
-template <typename T>
+template <typename T, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc1_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M, int N,
                     int K, KernelCtl ctl) {
+  constexpr int STAGES = Tile<BN>::STAGES;
+  constexpr int B_STAGE = Tile<BN>::B_STAGE;
+  constexpr int STAGE_BYTES = Tile<BN>::STAGE_BYTES;
+  constexpr int TMEM_COLS = Tile<BN>::TMEM_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + STAGES * A_STAGE;
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + STAGES * STAGE_BYTES);
+  auto* bars = reinterpret_cast<Barriers<STAGES>*>(smem + STAGES * STAGE_BYTES);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -274,7 +290,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 }  // namespace tc1
 
 namespace {
-template <typename T>
+template <typename T, int BN>
 rk_status launch_tc1(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                      rk_dtype dt, cudaStream_t s) {
   CUtensorMap ta, tb;
@@ -287,25 +303,61 @@ rk_status launch_tc1(const void* A, const void* B, void* C, int64_t M, int64_t N
   if ((st = launch_ctl(&lc)) != RK_OK) return st;
   KernelCtl ctl{lc.status, lc.timeout_ns, lc.inject_stall};
 
+  constexpr int smem = tc1::smem_bytes<BN>();
   static std::once_flag attr_once[64];
+  static cudaError_t attr_err[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  cudaError_t e = cudaSuccess;
   std::call_once(attr_once[dev & 63], [&] {
-    e = cudaFuncSetAttribute(tc1::gemm_tc1_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             tc1::SMEM_BYTES);
+    attr_err[dev & 63] = cudaFuncSetAttribute(
+        tc1::gemm_tc1_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   });
-  if (e != cudaSuccess) return cuda_status(e);
+  if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
 
-  const int num_tiles = static_cast<int>(((M + tc1::BM - 1) / tc1::BM) * ((N + tc1::BN - 1) / tc1::BN));
-  const int grid = num_tiles < device_sm_count() ? num_tiles : device_sm_count();
-  tc1::gemm_tc1_kernel<T><<<grid, tc1::THREADS, tc1::SMEM_BYTES, s>>>(
+  const int64_t num_tiles = ((M + tc1::BM - 1) / tc1::BM) * ((N + BN - 1) / BN);
+  const int grid = static_cast<int>(num_tiles < device_sm_count() ? num_tiles : device_sm_count());
+  tc1::gemm_tc1_kernel<T, BN><<<grid, tc1::THREADS, smem, s>>>(
       ta, tb, reinterpret_cast<T*>(C), static_cast<int>(M), static_cast<int>(N),
       static_cast<int>(K), ctl);
   note_launch();
   return cuda_status(cudaGetLastError());
 }
+
+// Tile width for a problem: fewest "waves" of persistent tiles weighted by the
+// per-tile cost (narrower tiles re-read A more often per flop).
+int pick_tile_n(int64_t M, int64_t N) {
+  const int64_t sms = device_sm_count();
+  const int widths[3] = {256, 128, 64};
+  const double cost[3] = {256.0, 128.0 * 1.05, 64.0 * 1.25};
+  int best = 256;
+  double best_cost = 1e300;
+  for (int i = 0; i < 3; ++i) {
+    const int64_t tiles = ((M + tc1::BM - 1) / tc1::BM) * ((N + widths[i] - 1) / widths[i]);
+    const int64_t waves = (tiles + sms - 1) / sms;
+    const double c = static_cast<double>(waves) * cost[i];
+    if (c < best_cost * 0.999) {
+      best_cost = c;
+      best = widths[i];
+    }
+  }
+  return best;
+}
+
+template <typename T>
+rk_status launch_tc1_auto(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                          rk_dtype dt, cudaStream_t s, int bn) {
+  if (bn <= 0) bn = pick_tile_n(M, N);
+  switch (bn) {
+    case 64: return launch_tc1<T, 64>(A, B, C, M, N, K, dt, s);
+    case 128: return launch_tc1<T, 128>(A, B, C, M, N, K, dt, s);
+    default: return launch_tc1<T, 256>(A, B, C, M, N, K, dt, s);
+  }
+}
 }  // namespace
+
+static std::atomic<int> g_tile_n_override{0};
+
+void gemm_set_tile_n(int bn) { g_tile_n_override.store(bn); }
 
 bool gemm_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
                        int64_t K) {
@@ -322,8 +374,9 @@ bool gemm_tc_supported(const void* A, const void* B, const void* C, int64_t M, i
 rk_status gemm_tc_1sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
                              int64_t K, rk_dtype dt, cudaStream_t s) {
   if (!gemm_tc_supported(A, B, C, M, N, K)) return RK_ERR_UNSUPPORTED;
-  if (dt == RK_DTYPE_BF16) return launch_tc1<__nv_bfloat16>(A, B, C, M, N, K, dt, s);
-  return launch_tc1<__half>(A, B, C, M, N, K, dt, s);
+  const int bn = g_tile_n_override.load();
+  if (dt == RK_DTYPE_BF16) return launch_tc1_auto<__nv_bfloat16>(A, B, C, M, N, K, dt, s, bn);
+  return launch_tc1_auto<__half>(A, B, C, M, N, K, dt, s, bn);
 }
 
 }  // namespace rk

@@ -13,6 +13,7 @@
 
 namespace rk {
 void gemv_set_tuning(int rows, int ks);
+void gemm_set_tile_n(int bn);
 }
 
 // One status word per device: kernels atomicOr RK_DEV_ERR_* bits into it when
@@ -123,6 +124,8 @@ void rk_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 10000000
 void rk_debug_inject_stall(int enable) { g_inject_stall.store(enable ? 1 : 0); }
 
 void rk_gemv_set_tuning(int rows, int ksplit) { rk::gemv_set_tuning(rows, ksplit); }
+
+void rk_gemm_set_tile_n(int tile_n) { rk::gemm_set_tile_n(tile_n); }
 
 const char* rk_variant_name(int op, int variant) {
   if (op == 0) {

@@ -142,6 +142,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_wait_timeout_ns", [](uint64_t ns) { rk_set_wait_timeout_ns(ns); });
   m.def("debug_inject_stall", [](bool on) { rk_debug_inject_stall(on ? 1 : 0); });
   m.def("gemv_set_tuning", [](int rows, int ks) { rk_gemv_set_tuning(rows, ks); });
+  m.def("gemm_set_tile_n", [](int bn) { rk_gemm_set_tile_n(bn); });
   m.def("launch_count", []() { return rk_launch_count(); });
   m.def("variant_name", [](int op, int v) { return std::string(rk_variant_name(op, v)); });
   m.def("abi_version", []() { return rk_abi_version(); });

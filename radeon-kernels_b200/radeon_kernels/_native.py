@@ -89,6 +89,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_debug_inject_stall.restype = None
     lib.rk_gemv_set_tuning.argtypes = [cint, cint]
     lib.rk_gemv_set_tuning.restype = None
+    lib.rk_gemm_set_tile_n.argtypes = [cint]
+    lib.rk_gemm_set_tile_n.restype = None
     lib.rk_variant_name.argtypes = [cint, cint]
     lib.rk_variant_name.restype = ctypes.c_char_p
     lib.rk_gemm_select_variant.argtypes = [vp, vp, vp, i64, i64, i64, cint]

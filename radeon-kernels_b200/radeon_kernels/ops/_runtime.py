@@ -20,7 +20,7 @@ from typing import Any, Callable, Iterable, Mapping
 from radeon_kernels.errors import RadeonKernelsError
 from radeon_kernels.providers import native
 from radeon_kernels.runtime.dispatcher import DispatchDecision, DispatchRequest, Dispatcher
-from radeon_kernels.runtime.explain import record_dispatch
+from radeon_kernels.runtime.explain import record_dispatch, record_dispatch_shared
 from radeon_kernels.runtime.fingerprint import EnvironmentFingerprint
 from radeon_kernels.runtime.loader import ArtifactError, PrecompiledArtifactLoader
 from radeon_kernels.runtime.packs import (
@@ -79,6 +79,12 @@ class DispatchingRuntime:
         self._loaders: dict[Path, PrecompiledArtifactLoader] = {}
         self._fingerprints: dict[int, EnvironmentFingerprint] = {}
         self._lock = Lock()
+        # (operator, device, signature items) -> (entrypoint, launch, shared record).
+        # Filled after a winner ran successfully; the reference re-selects, re-resolves
+        # and re-hashes on every call (ops/_runtime.py:87-121), which costs far more
+        # than a decode GEMV's kernel time.  Manifests and packs are immutable for the
+        # lifetime of a runtime, so the decision cannot change; reset_*runtime() drops it.
+        self._fast: dict[tuple, tuple[Any, Any, dict[str, Any]]] = {}
 
     @property
     def pack_registry(self) -> KernelPackRegistry:
@@ -96,6 +102,25 @@ class DispatchingRuntime:
             if root not in self._loaders:
                 self._loaders[root] = self._loader_factory(root)
             return self._loaders[root]
+
+    @staticmethod
+    def fast_key(operator: str, device_index: int, signature: Mapping[str, Any]) -> tuple:
+        return (operator, device_index, tuple(sorted(signature.items())))
+
+    def fast_lookup(self, key: tuple) -> tuple[Any, Any, dict[str, Any]] | None:
+        return self._fast.get(key)
+
+    def fast_store(self, key: tuple, entry: Any, launch: Any, decision: DispatchDecision, reason: str) -> None:
+        record = decision.to_dict()
+        record.update(
+            {
+                "selected": f"{decision.winner.provider}/{decision.winner.entrypoint}",
+                "artifact": decision.winner.artifact,
+                "evidence_id": decision.evidence_id,
+                "reason": reason,
+            }
+        )
+        self._fast[key] = (entry, launch, record)
 
     def decide(self, operator: str, version: str, signature: Mapping[str, Any], fingerprint: EnvironmentFingerprint):
         return self._dispatcher.select(DispatchRequest(operator, version, signature), fingerprint)
@@ -162,20 +187,33 @@ class OperatorRuntime(DispatchingRuntime):
         fallback: Callable[[], Any],
         fallback_selected: str,
     ) -> Any:
+        key = self.fast_key(operator, device_index, signature)
+        cached = self.fast_lookup(key)
+        if cached is not None:
+            entry, launch, record = cached
+            result = entry(*native_arguments, **launch)
+            if result is None:
+                raise native.NativeProviderError("native entrypoint returned no output")
+            record_dispatch_shared(record)
+            return result
         fingerprint = self.fingerprint(torch_module, device_index)
         decision = self.decide(operator, semantic_version, signature, fingerprint)
         failure: str | None = None
         if decision.matched:
             try:
                 resolved = self.resolve(decision, fingerprint)
-                result = native.execute(self.loader(resolved.pack.root), decision.winner, decision.launch, *native_arguments)
+                loader = self.loader(resolved.pack.root)
+                result = native.execute(loader, decision.winner, decision.launch, *native_arguments)
+                reason = f"{decision.reason}; loaded pack {resolved.pack.pack_id} {resolved.pack.pack_version}"
                 record_execution(
                     decision,
                     selected=f"{decision.winner.provider}/{decision.winner.entrypoint}",
                     artifact=decision.winner.artifact,
                     evidence_id=decision.evidence_id,
-                    reason=f"{decision.reason}; loaded pack {resolved.pack.pack_id} {resolved.pack.pack_version}",
+                    reason=reason,
                 )
+                entry = getattr(loader, "load_entrypoint")(decision.winner).callable
+                self.fast_store(key, entry, dict(decision.launch), decision, reason)
                 return result
             except WINNER_FAILURES as error:
                 failure = str(error)

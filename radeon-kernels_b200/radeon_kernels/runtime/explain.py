@@ -21,6 +21,16 @@ def record_dispatch(value: Mapping[str, Any]) -> None:
     _LAST.set(deepcopy(dict(value)))
 
 
+def record_dispatch_shared(value: dict[str, Any]) -> None:
+    """Record a dispatch dict that the caller promises never to mutate (no copy).
+
+    Used by the operator runtimes' decision cache: a cached record is created once per
+    (operator, signature, device) and shared; readers only ever get deep copies.
+    """
+
+    _LAST.set(value)
+
+
 def get_last_dispatch() -> dict[str, Any] | None:
     value = _LAST.get()
     return None if value is None else deepcopy(value)

@@ -243,3 +243,20 @@ def test_invalid_packs_are_ignored_but_reported(tmp_path):
     registry = KernelPackRegistry.discover((tmp_path,), require_signatures=False)
     assert registry.packs == ()
     assert len(registry.rejected) == 1
+
+
+def test_repeated_calls_use_the_cached_decision(env, tmp_path):
+    torch, cuda, make = env
+    write_pack(tmp_path, digest_of(ARTIFACT), ARTIFACT)
+    runtime = make()
+    for _ in range(3):
+        runtime.execute(FakeTensor((2, 3)), FakeTensor((3, 4)), torch_module=torch)
+    assert FakeLoader.variants == [2, 2, 2]
+    record = get_last_dispatch()
+    assert record["selected"] == "native/gemm_out" and "loaded pack" in record["reason"]
+    record["selected"] = "mutated"  # readers get copies; the cached record is untouched
+    runtime.execute(FakeTensor((2, 3)), FakeTensor((3, 4)), torch_module=torch)
+    assert get_last_dispatch()["selected"] == "native/gemm_out"
+    # a different signature is decided afresh
+    runtime.execute(FakeTensor((1, 3)), FakeTensor((3, 4)), torch_module=torch)
+    assert get_last_dispatch()["selected"] == "cuda/gemm"
