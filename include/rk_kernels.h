@@ -68,7 +68,9 @@ enum {
   RK_GEMV_AUTO = 0,        /* pick from M, N, K and alignment */
   RK_GEMV_SCALAR = 1,      /* generic kernel: any K, any alignment */
   RK_GEMV_STREAM = 2,      /* 128-bit weight streaming, in-CTA split-K, needs K%8==0 + 16B alignment */
-  RK_GEMV_VARIANT_COUNT = 3
+  RK_GEMV_TC = 3,          /* tcgen05 skinny GEMM (W as the 128-row operand, x as N=16/32), TMA ring,
+                              cluster split-K reduced through distributed shared memory */
+  RK_GEMV_VARIANT_COUNT = 4
 };
 
 /*
@@ -120,6 +122,10 @@ RK_API void rk_gemv_set_tuning(int rows_per_warp, int ksplit);
 /* Tuning hook for the tensor-core GEMM variants: output tile width (64, 128,
  * 256); 0 restores the built-in choice (fewest weighted waves).  Process-wide. */
 RK_API void rk_gemm_set_tile_n(int tile_n);
+
+/* Tuning hook for RK_GEMV_TC: thread-block cluster size (K split), 1..8;
+ * 0 restores the built-in choice.  Process-wide. */
+RK_API void rk_gemv_tc_set_cluster(int cluster_size);
 
 /*
  * Reads and clears the device-side status word of the current device after

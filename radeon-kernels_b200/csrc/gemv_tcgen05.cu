@@ -1,0 +1,428 @@
+// gemv_tcgen05.cu -- skinny GEMM / multi-row decode GEMV on the 5th-generation tensor
+// cores: out[M,N] = x[M,K] @ W[N,K]^T for 1 <= M <= 32.
+//
+// Why tensor cores here: with CUDA cores every weight element costs M fused
+// multiply-adds plus an x operand fetch, so at M >= 4 a CUDA-core kernel is bound by
+// FMA issue and L1 traffic long before HBM (measured: 3.8 TB/s at M=4, 0.6 TB/s at
+// M=16).  The tensor core does the M-fold reuse for free, leaving the kernel what it
+// should be -- a pure HBM stream of W.
+//
+// Formulation (operands swapped so the tiny M becomes the UMMA N dimension):
+//   D[128 rows of W, MN] += W_tile[128, 64] (A, K-major) * x_tile[MN, 64]^T (B, K-major)
+// with MN = M rounded up to 16 or 32; x rows >= M are zero-filled by TMA.
+//   * warp 0: TMA producer -- a 5-stage ring of {W 128x64 (16 KiB), x MNx64} boxes,
+//     128-byte swizzle, completion on mbarriers;
+//   * warp 1: TMEM allocation (32 columns) and one thread issuing tcgen05.mma
+//     (M=128, N=MN, K=16), tcgen05.commit releases ring slots;
+//   * warps 2..5: epilogue, tcgen05.ld of the 128 x MN fp32 accumulator.
+// Split-K over a thread-block cluster of C CTAs (C = 1..8, one cluster per 128-row
+// tile, CTA rank r owns K blocks [r*KB/C, (r+1)*KB/C)): non-leader CTAs park their
+// partial accumulator in their own (now idle) ring memory and signal the leader's
+// mbarrier remotely; the leader reads the partials through distributed shared memory
+// (ld.shared::cluster) in rank order, adds them to its own, rounds once, and stores.
+// Deterministic, no global workspace.  Every wait is bounded; the only unbounded
+// waits are the two cluster barriers every thread reaches unconditionally (after
+// barrier initialisation and before exit, so no CTA leaves while its shared memory
+// may still be read).
+//
+// Role of the reference: the skinny-GEMM half of gemv_wave/packed/lds kernels
+// (benchmarks/gemv/native_gemv.hip:30-203), which accept M <= 32 rows of x.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <mutex>
+#include <type_traits>
+
+#include "rk_device.cuh"
+#include "rk_internal.h"
+#include "rk_tma.h"
+
+namespace rk {
+namespace gtc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int UMMA_K = 16;
+constexpr int W_STAGE = BM * BK * 2;  // 16 KiB
+constexpr int THREADS = 192;
+constexpr int STAGES = 5;
+constexpr int TMEM_COLS = 32;
+constexpr int MAX_CLUSTER = 8;
+
+template <int MN>
+struct Cfg {
+  static constexpr int X_STAGE = MN * BK * 2;
+  static constexpr int STAGE = W_STAGE + X_STAGE;  // multiple of 1024
+  static constexpr int RING = STAGES * STAGE;
+  static constexpr int SLOT = BM * MN * 4;  // one fp32 partial tile
+  static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
+  static_assert(SLOT <= RING, "the partial tile is parked in the idle ring");
+};
+
+struct __align__(8) Bars {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full;
+  uint64_t drain;
+  uint64_t partials;  // leader: one remote arrival per non-leader CTA
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int MN>
+constexpr int smem_bytes() {
+  return 1024 + Cfg<MN>::RING + int(sizeof(Bars));
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ bool try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void epilogue_bar_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+template <int MN>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[MN]);
+
+template <>
+__device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld_cols<32>(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_ld_32x32b_x32(taddr, r);
+}
+
+template <typename T, int MN>
+__global__ void __launch_bounds__(THREADS, 2)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                   const __grid_constant__ CUtensorMap tmap_x, T* __restrict__ out, int M, int N,
+                   int K, int csize, KernelCtl ctl) {
+  using C = Cfg<MN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(ring + C::RING);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int tile = blockIdx.x / csize;
+  const int num_kb = (K + BK - 1) / BK;
+  const int kb0 = static_cast<int>(static_cast<int64_t>(num_kb) * rank / csize);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(num_kb) * (rank + 1) / csize);
+  volatile int* abort_flag = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bars->full[s]), 1);
+      mbar_init(smem_u32(&bars->empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bars->tmem_full), 1);
+    mbar_init(smem_u32(&bars->drain), 1);
+    mbar_init(smem_u32(&bars->partials), csize > 1 ? csize - 1 : 1);
+    bars->abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // Every CTA's barriers are initialised before any remote arrival can target them.
+  cluster_sync_all();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(smem_u32(&bars->empty[stage]), phase ^ 1, ctl.timeout_ns,
+                               abort_flag)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = smem_u32(&bars->full[stage]);
+        uint8_t* base = ring + stage * C::STAGE;
+        mbar_arrive_expect_tx(full, C::STAGE);
+        tma_load_2d(smem_u32(base), &tmap_w, full, kb * BK, tile * BM);
+        tma_load_2d(smem_u32(base + W_STAGE), &tmap_x, full, kb * BK, 0);
+        issued |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_PRODUCER);
+      }
+      int never = 0;
+      for (int s = 0; s < STAGES; ++s)
+        if ((issued >> s) & 1u)
+          if (!mbar_wait_bounded(smem_u32(&bars->full[s]), (issued_parity >> s) & 1u,
+                                 ctl.timeout_ns, &never))
+            atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc =
+          umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, MN, false, false);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(smem_u32(&bars->full[stage]), phase, ctl.timeout_ns, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t w0 = smem_u32(ring + stage * C::STAGE);
+        const uint32_t x0 = w0 + W_STAGE;
+#pragma unroll
+        for (int k = 0; k < BK / UMMA_K; ++k) {
+          // Both operands K-major with the 128-byte swizzle: 8-row core groups
+          // 1024 B apart; K advances 32 B inside the swizzle row.
+          const uint64_t adesc = umma_desc_sw128(w0 + k * UMMA_K * 2, 16, 1024);
+          const uint64_t bdesc = umma_desc_sw128(x0 + k * UMMA_K * 2, 16, 1024);
+          tc_mma_f16(tmem_base, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&bars->empty[stage]));
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (ok) tc_commit(smem_u32(&bars->tmem_full));
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_MMA);
+      }
+      tc_commit(smem_u32(&bars->drain));
+      int never = 0;
+      if (!mbar_wait_bounded(smem_u32(&bars->drain), 0, ctl.timeout_ns, &never))
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int row_local = quarter * 32 + lane;
+    const bool got = mbar_wait_bounded(smem_u32(&bars->tmem_full), 0, ctl.timeout_ns, abort_flag);
+    const bool ok = __all_sync(0xffffffffu, got);
+    float acc[MN];
+    if (ok) {
+      tc_fence_after();
+      uint32_t r[MN];
+      tmem_ld_cols<MN>(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < MN; ++j) acc[j] = __uint_as_float(r[j]);
+    } else {
+      *abort_flag = 1;
+      if (lane == 0) atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_EPILOGUE);
+#pragma unroll
+      for (int j = 0; j < MN; ++j) acc[j] = 0.f;
+    }
+    float* slot = reinterpret_cast<float*>(ring);  // the ring is idle once tmem_full fired
+    if (rank != 0) {
+      if (ok) {
+        // The async proxy (TMA, MMA) is done with the ring; order our generic writes after it.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < MN; j += 4)
+          *reinterpret_cast<float4*>(slot + row_local * MN + j) =
+              make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      }
+      epilogue_bar_sync();
+      if (warp == 2 && lane == 0) {
+        asm volatile("fence.acq_rel.cluster;" ::: "memory");
+        remote_arrive(map_to_rank(smem_u32(&bars->partials), 0));
+      }
+    } else {
+      if (csize > 1) {
+        bool ready = false;
+        if (ok) {
+          const uint64_t t0 = globaltimer_ns();
+          for (uint32_t it = 0;; ++it) {
+            if (try_wait_cluster(smem_u32(&bars->partials), 0)) {
+              ready = true;
+              break;
+            }
+            if ((it & 63u) == 63u && globaltimer_ns() - t0 > ctl.timeout_ns) break;
+          }
+        }
+        ready = __all_sync(0xffffffffu, ready);
+        if (ready) {
+          const uint32_t mine = smem_u32(slot + row_local * MN);
+          for (int c = 1; c < csize; ++c) {
+            const uint32_t remote = map_to_rank(mine, static_cast<uint32_t>(c));
+#pragma unroll
+            for (int j = 0; j < MN; j += 4) {
+              const float4 v = ld_cluster_v4(remote + j * 4);
+              acc[j] += v.x;
+              acc[j + 1] += v.y;
+              acc[j + 2] += v.z;
+              acc[j + 3] += v.w;
+            }
+          }
+        } else if (lane == 0) {
+          atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_EPILOGUE);
+        }
+      }
+      const int row = tile * BM + row_local;
+      if (ok && row < N) {
+#pragma unroll
+        for (int m = 0; m < MN; ++m)
+          if (m < M) out[static_cast<size_t>(m) * N + row] = from_f32<T>(acc[m]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // No CTA leaves while the leader may still read its parked partial.
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gtc
+
+namespace {
+
+template <typename T, int MN>
+rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
+                         rk_dtype dt, cudaStream_t s, int csize_override) {
+  CUtensorMap tw, tx;
+  rk_status st = make_tmap_2d(&tw, W, dt, K, N, 64, gtc::BM);
+  if (st != RK_OK) return st;
+  st = make_tmap_2d(&tx, x, dt, K, M, 64, MN);
+  if (st != RK_OK) return st;
+  LaunchCtl lc;
+  if ((st = launch_ctl(&lc)) != RK_OK) return st;
+  KernelCtl ctl{lc.status, lc.timeout_ns, 0};
+
+  constexpr int smem = gtc::smem_bytes<MN>();
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(gtc::gemv_tc_kernel<T, MN>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
+
+  const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
+  const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
+  int csize = csize_override;
+  if (csize <= 0) {
+    // Enough CTAs to keep every SM streaming (two resident per SM), K split at most 8 ways.
+    const int64_t target = 2ll * device_sm_count();
+    csize = 1;
+    while (csize < gtc::MAX_CLUSTER && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
+  }
+  if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
+  while (csize > 1 && csize > num_kb) csize /= 2;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * csize));
+  cfg.blockDim = dim3(gtc::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gtc::gemv_tc_kernel<T, MN>, tw, tx,
+                                           static_cast<T*>(out), static_cast<int>(M),
+                                           static_cast<int>(N), static_cast<int>(K), csize, ctl);
+  note_launch();
+  return cuda_status(e);
+}
+
+}  // namespace
+
+static std::atomic<int> g_gemv_tc_cluster{0};
+
+void gemv_tc_set_cluster(int c) { g_gemv_tc_cluster.store(c); }
+
+bool gemv_tc_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,
+                       int64_t K) {
+  (void)out;
+  if (device_cc_major() != 10) return false;
+  if (M < 1 || M > 32 || N < 1 || K < 8 || K % 8 != 0) return false;
+  if (!aligned16(x) || !aligned16(W)) return false;
+  if (N > (1ll << 31) - 256 || K > (1ll << 31) - 64) return false;
+  return true;
+}
+
+rk_status gemv_tc_launch(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
+                         rk_dtype dt, cudaStream_t s) {
+  if (!gemv_tc_supported(x, W, out, M, N, K)) return RK_ERR_UNSUPPORTED;
+  const int c = g_gemv_tc_cluster.load();
+  if (M <= 16) {
+    if (dt == RK_DTYPE_BF16) return launch_gemv_tc<__nv_bfloat16, 16>(x, W, out, M, N, K, dt, s, c);
+    return launch_gemv_tc<__half, 16>(x, W, out, M, N, K, dt, s, c);
+  }
+  if (dt == RK_DTYPE_BF16) return launch_gemv_tc<__nv_bfloat16, 32>(x, W, out, M, N, K, dt, s, c);
+  return launch_gemv_tc<__half, 32>(x, W, out, M, N, K, dt, s, c);
+}
+
+}  // namespace rk

@@ -14,6 +14,7 @@
 namespace rk {
 void gemv_set_tuning(int rows, int ks);
 void gemm_set_tile_n(int bn);
+void gemv_tc_set_cluster(int c);
 }
 
 // One status word per device: kernels atomicOr RK_DEV_ERR_* bits into it when
@@ -127,6 +128,8 @@ void rk_gemv_set_tuning(int rows, int ksplit) { rk::gemv_set_tuning(rows, ksplit
 
 void rk_gemm_set_tile_n(int tile_n) { rk::gemm_set_tile_n(tile_n); }
 
+void rk_gemv_tc_set_cluster(int cluster_size) { rk::gemv_tc_set_cluster(cluster_size); }
+
 const char* rk_variant_name(int op, int variant) {
   if (op == 0) {
     switch (variant) {
@@ -140,6 +143,7 @@ const char* rk_variant_name(int op, int variant) {
       case RK_GEMV_AUTO: return "gemv:auto";
       case RK_GEMV_SCALAR: return "gemv:scalar";
       case RK_GEMV_STREAM: return "gemv:stream";
+      case RK_GEMV_TC: return "gemv:tc";
     }
   }
   return "unknown";
@@ -155,6 +159,9 @@ int rk_gemm_select_variant(const void* A, const void* B, const void* C, int64_t 
 int rk_gemv_select_variant(const void* x, const void* W, const void* out, int64_t M, int64_t N,
                            int64_t K, rk_dtype dt) {
   (void)dt;
+  // M = 1 streams on CUDA cores; from M = 2 the tensor-core kernel keeps the weight
+  // stream at HBM speed where CUDA cores become FMA/L1 bound.
+  if (M >= 2 && gemv_tc_supported(x, W, out, M, N, K)) return RK_GEMV_TC;
   return gemv_stream_supported(x, W, out, M, N, K) ? RK_GEMV_STREAM : RK_GEMV_SCALAR;
 }
 
@@ -190,6 +197,7 @@ rk_status rk_gemv(const void* x, const void* W, void* out, int64_t M, int64_t N,
   switch (variant) {
     case RK_GEMV_SCALAR: return gemv_scalar_launch(x, W, out, M, N, K, dt, s);
     case RK_GEMV_STREAM: return gemv_stream_launch(x, W, out, M, N, K, dt, s);
+    case RK_GEMV_TC: return gemv_tc_launch(x, W, out, M, N, K, dt, s);
   }
   return RK_ERR_UNSUPPORTED;
 }

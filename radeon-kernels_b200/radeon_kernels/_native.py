@@ -41,7 +41,7 @@ RK_DTYPE_FP16 = 0
 RK_DTYPE_BF16 = 1
 # variants
 GEMM_VARIANTS = {"auto": 0, "simt": 1, "tc_1sm": 2, "tc_2sm": 3}
-GEMV_VARIANTS = {"auto": 0, "scalar": 1, "stream": 2}
+GEMV_VARIANTS = {"auto": 0, "scalar": 1, "stream": 2, "tc": 3}
 
 _lock = threading.Lock()
 _extension: ModuleType | None = None
@@ -91,6 +91,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_gemv_set_tuning.restype = None
     lib.rk_gemm_set_tile_n.argtypes = [cint]
     lib.rk_gemm_set_tile_n.restype = None
+    lib.rk_gemv_tc_set_cluster.argtypes = [cint]
+    lib.rk_gemv_tc_set_cluster.restype = None
     lib.rk_variant_name.argtypes = [cint, cint]
     lib.rk_variant_name.restype = ctypes.c_char_p
     lib.rk_gemm_select_variant.argtypes = [vp, vp, vp, i64, i64, i64, cint]

@@ -66,7 +66,7 @@ def test_gemm_matches_reference_fixtures(path, variant):
     oracle.assert_parity(to_bits(c), case["c_ref"], case["c_fp32"], dtype)
 
 
-@pytest.mark.parametrize("variant", ["auto", "scalar", "stream"])
+@pytest.mark.parametrize("variant", ["auto", "scalar", "stream", "tc"])
 @pytest.mark.parametrize("path", golden_cases("gemv"), ids=lambda p: p.stem)
 def test_gemv_matches_reference_fixtures(path, variant):
     import torch
@@ -78,7 +78,7 @@ def test_gemv_matches_reference_fixtures(path, variant):
     n = w.shape[0]
     buf, out = _guarded(torch, m, n, dtype)
     status = abi_gemv(x, w, out, GEMV[variant], dtype)
-    if variant == "stream" and k % 8 != 0:
+    if variant in ("stream", "tc") and k % 8 != 0:
         assert status == _native.RK_ERR_UNSUPPORTED
         return
     assert status == _native.RK_OK, _native.status_text(status)
@@ -284,6 +284,28 @@ def test_gemv_tunings_agree(rows, ks):
     finally:
         lib.rk_gemv_set_tuning(0, 0)
     oracle.assert_parity(to_bits(out), o_bits, o32, "bf16")
+
+
+@pytest.mark.parametrize("cluster", [1, 2, 4, 8])
+@pytest.mark.parametrize("m", [1, 5, 16, 17, 32])
+def test_gemv_tensor_core_cluster_split_k(cluster, m):
+    import torch
+
+    gen = torch.Generator().manual_seed(11 + m)
+    x = seeded((m, 4096 + 8), 11, "normal", "fp16", gen)  # K not a multiple of the 64-wide K block
+    w = seeded((1000, 4096 + 8), 11, "normal/4104", "fp16", gen)  # N not a multiple of 128
+    o_bits, o32 = oracle.gemv(to_bits(x), to_bits(w), "fp16")
+    lib = _native.library()
+    lib.rk_gemv_tc_set_cluster(cluster)
+    try:
+        buf, out = _guarded(torch, m, 1000, "fp16")
+        assert abi_gemv(x.cuda(), w.cuda(), out, GEMV["tc"], "fp16") == _native.RK_OK
+        torch.cuda.synchronize()
+        assert device_status() == _native.RK_OK
+    finally:
+        lib.rk_gemv_tc_set_cluster(0)
+    assert _guards_intact(buf)
+    oracle.assert_parity(to_bits(out), o_bits, o32, "fp16")
 
 
 def test_gather_column_blocks_matches_permute():
