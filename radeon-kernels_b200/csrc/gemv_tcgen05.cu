@@ -46,7 +46,7 @@ constexpr int BK = 64;
 constexpr int UMMA_K = 16;
 constexpr int W_STAGE = BM * BK * 2;  // 16 KiB
 constexpr int THREADS = 192;
-constexpr int STAGES = 5;
+constexpr int STAGES = 6;
 constexpr int TMEM_COLS = 32;
 constexpr int MAX_CLUSTER = 8;
 
@@ -84,6 +84,14 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
                    : "memory");
+}
+
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
@@ -179,8 +187,10 @@ __global__ void __launch_bounds__(THREADS, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // Every CTA's barriers are initialised before any remote arrival can target them.
-  cluster_sync_all();
+  // Announce "barriers initialised" to the cluster without waiting: the matching wait
+  // comes right before the first remote access (the partial-sum exchange), so the
+  // weight stream starts without a cluster-wide handshake on its critical path.
+  cluster_arrive();
   const uint32_t tmem_base = bars->tmem_base;
 
   if (warp == 0) {
@@ -275,6 +285,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       for (int j = 0; j < MN; ++j) acc[j] = 0.f;
     }
     float* slot = reinterpret_cast<float*>(ring);  // the ring is idle once tmem_full fired
+    cluster_wait();  // every CTA of the cluster has initialised its barriers
     if (rank != 0) {
       if (ok) {
         // The async proxy (TMA, MMA) is done with the ring; order our generic writes after it.
@@ -329,6 +340,10 @@ __global__ void __launch_bounds__(THREADS, 2)
     }
   }
 
+  if (warp < 2) {
+    __syncwarp();
+    cluster_wait();  // pairs with the arrive after initialisation (epilogue warps waited above)
+  }
   tc_fence_before();
   __syncthreads();
   // No CTA leaves while the leader may still read its parked partial.

@@ -159,9 +159,9 @@ int rk_gemm_select_variant(const void* A, const void* B, const void* C, int64_t 
 int rk_gemv_select_variant(const void* x, const void* W, const void* out, int64_t M, int64_t N,
                            int64_t K, rk_dtype dt) {
   (void)dt;
-  // M = 1 streams on CUDA cores; from M = 2 the tensor-core kernel keeps the weight
+  // M <= 2 streams on CUDA cores; from M = 3 the tensor-core kernel keeps the weight
   // stream at HBM speed where CUDA cores become FMA/L1 bound.
-  if (M >= 2 && gemv_tc_supported(x, W, out, M, N, K)) return RK_GEMV_TC;
+  if (M >= 3 && gemv_tc_supported(x, W, out, M, N, K)) return RK_GEMV_TC;
   return gemv_stream_supported(x, W, out, M, N, K) ? RK_GEMV_STREAM : RK_GEMV_SCALAR;
 }
 
