@@ -499,8 +499,48 @@ def run_reference(args) -> int:
     return 0
 
 
+PROFILE_CASES = {
+    # name: (kind, m, n, k, dtype, distribution)
+    "gemv_decode": ("gemv", 1, 8192, 8192, "bf16", "normal/8192"),
+    "gemv_decode_m16": ("gemv", 16, 8192, 8192, "bf16", "normal/8192"),
+    "gemv_ffn_down_m4": ("gemv", 4, 4096, 14336, "fp16", "normal/14336"),
+    "gemm_1024": ("gemm", 1024, 1024, 1024, "bf16", "uniform"),
+    "gemm_ffn_up": ("gemm", 4096, 14336, 4096, "fp16", "normal64"),
+    "gemm_8192": ("gemm", 8192, 8192, 8192, "bf16", "uniform16"),
+}
+
+
+def run_profile(args) -> int:
+    """A few launches of one kernel and nothing else of ours: the workload ncu captures."""
+
+    import torch
+
+    from radeon_kernels import _native
+
+    kind, m, n, k, dtype, dist_name = PROFILE_CASES[args.profile]
+    ext = _native.extension()
+    torch.cuda.set_device(0)
+    if kind == "gemv":
+        w = seeded((n, k), 1, dist_name, dtype)
+        x = seeded((m, k), 2, "normal", dtype)
+        out = torch.empty(m, n, dtype=x.dtype, device="cuda")
+        launch = lambda: ext.gemv_out(x, w, out, 0)  # noqa: E731
+    else:
+        a = seeded((m, k), 1, dist_name, dtype)
+        b = seeded((k, n), 2, dist_name, dtype)
+        out = torch.empty(m, n, dtype=a.dtype, device="cuda")
+        launch = lambda: ext.gemm_out(a, b, out, 0)  # noqa: E731
+    for _ in range(args.steps):
+        launch()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": args.profile, "launches": args.steps, "status": int(ext.device_status())}))
+    return 0
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description="B200 GEMM/GEMV hot-path benchmark")
+    parser.add_argument("--profile", choices=sorted(PROFILE_CASES), default=None,
+                        help="run --steps launches of one kernel only (the case ncu captures)")
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=40000)
     parser.add_argument("--warmup", type=int, default=20)
@@ -513,6 +553,8 @@ def main(argv=None) -> int:
 
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile:
+        return run_profile(args)
 
     import torch
 
