@@ -571,7 +571,7 @@ def main(argv=None) -> int:
         head = headline(args, dist, ext, peaks, peak_kind)
         end_to_end = e2e(args, dist)
         extra = {} if args.no_suite else suite(args, dist, ext, peaks)
-    traffic = load_traffic().get("gemv_decode_bf16_m1_n8192_k8192")
+    traffic = load_traffic().get("gemv_decode_bf16_m1_n8192_k8192")  # bytes per launch (ncu)
     head["roofline"]["traffic"] = traffic
     cpu = cpu_baseline(args.cpu_seconds) if dist.rank == 0 and dist.world == 1 else None
     dist.close()
