@@ -292,23 +292,16 @@ def e2e(args, dist: Dist):
     x_host = seeded((m, k), 1, "normal", "bf16", device="cpu").pin_memory()
     out_host = torch.empty((m, n * dist.world), dtype=torch.bfloat16).pin_memory()
     x_dev = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
-    gathered = torch.empty((dist.world, m, n), dtype=torch.bfloat16, device="cuda") if dist.world > 1 else None
     full = torch.empty((m, n * dist.world), dtype=torch.bfloat16, device="cuda") if dist.world > 1 else None
-    ext = None
-    if dist.world > 1:
-        from radeon_kernels import _native
+    from radeon_kernels.distributed import all_gather_columns
 
-        ext = _native.extension()
-        import torch.distributed as tdist
     stream = torch.cuda.current_stream()
 
     def step(i):
         x_dev.copy_(x_host, non_blocking=True)
         y = rk.gemv(x_dev, weights[i % ROTATE])
         if dist.world > 1:
-            tdist.all_gather_into_tensor(gathered, y)
-            ext.gather_column_blocks(gathered, full)
-            out_host.copy_(full, non_blocking=True)
+            out_host.copy_(all_gather_columns(y, out=full), non_blocking=True)
         else:
             out_host.copy_(y, non_blocking=True)
 
