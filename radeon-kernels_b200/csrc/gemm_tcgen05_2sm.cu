@@ -1,0 +1,328 @@
+// gemm_tcgen05_2sm.cu -- tcgen05 GEMM on SM pairs (cta_group::2), 256 x 256 tiles.
+//
+//   C[M,N] = A[M,K] @ B[K,N], fp16/bf16 in, fp32 accumulation, RN output.
+//
+// A cluster of 2 CTAs on one TPC computes a 256 x 256 output tile with single
+// tcgen05.mma.cta_group::2 instructions (M = 256, N = 256, K = 16) issued by the even
+// CTA.  Each CTA stages only its half of the operands -- A rows [128*rank, +128) and
+// B columns [128*rank, +128) -- so per SM the shared-memory operand traffic per FLOP is
+// 2/3 of the 1-SM 128 x 256 tile (32 KiB instead of 48 KiB per 64-deep K block), and
+// each CTA's TMEM receives its 128 rows of the 256-column accumulator.
+//   * warp 0 (both CTAs): TMA producer, 6-stage ring of {A 128x64, B 64x128};
+//     both CTAs' bulk copies complete on the even CTA's full barrier, which the even
+//     CTA arms with the bytes of both halves (no multicast anywhere);
+//   * warp 1: TMEM allocation for the pair (512 columns each: two accumulators);
+//     on the even CTA one thread issues the MMAs and commits with CTA mask 0b11 so
+//     ring slots and accumulators are released/published in both CTAs;
+//   * warps 2..5 (both CTAs): epilogue from each CTA's own TMEM; each warp reports
+//     "accumulator drained" to the even CTA's barrier (remote arrive for the odd CTA).
+// Persistent: clusters walk 256x256 tiles in the grouped order; edges handled by TMA
+// zero fill + predicated stores, as in the 1-SM kernel.  Every wait is bounded; the
+// two cluster barriers (after initialisation and before exit) are reached by every
+// thread unconditionally.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <mutex>
+#include <type_traits>
+
+#include "rk_device.cuh"
+#include "rk_internal.h"
+#include "rk_tma.h"
+
+namespace rk {
+namespace tc2 {
+
+constexpr int BM = 256;       // tile rows per pair (128 per CTA)
+constexpr int BN = 256;       // tile columns per pair (128 of B per CTA)
+constexpr int HALF = 128;
+constexpr int BK = 64;
+constexpr int UMMA_K = 16;
+constexpr int A_STAGE = HALF * BK * 2;  // 16 KiB
+constexpr int B_BOX = 64 * BK * 2;      // 8 KiB
+constexpr int B_STAGE = BK * HALF * 2;  // 16 KiB
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int STAGES = 6;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int GROUP_M = 8;  // in 256-row blocks
+
+struct __align__(8) Bars {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + int(sizeof(Bars));
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = GROUP_M * num_n;
+  const int group = t / per_group;
+  const int first_m = group * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int in_group = t - group * per_group;
+  mb = first_m + in_group % gsize;
+  nb = in_group / gsize;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M, int N,
+                    int K, KernelCtl ctl) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * A_STAGE;
+  Bars* bars = reinterpret_cast<Bars*>(smem + STAGES * STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = even CTA (issues the MMAs), 1 = odd
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+  volatile int* abort_flag = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bars->full[s]), 1);
+      mbar_init(smem_u32(&bars->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&bars->tmem_full[a]), 1);
+      mbar_init(smem_u32(&bars->tmem_empty[a]), 2 * 4);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(&bars->tmem_base), TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  cluster_sync_all();  // both CTAs' barriers exist before either signals the other
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------- producer
+      uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&bars->empty[stage]), phase ^ 1, ctl.timeout_ns,
+                                 abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_local = smem_u32(&bars->full[stage]);
+          const uint32_t full_even = map_to_rank(full_local, 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_local, 2 * STAGE_BYTES);
+          tma_load_2d_pair(smem_u32(smem_a + stage * A_STAGE), &tmap_a, full_even, kb * BK,
+                           mb * BM + static_cast<int>(rank) * HALF);
+#pragma unroll
+          for (int j = 0; j < HALF / 64; ++j)
+            tma_load_2d_pair(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b, full_even,
+                             nb * BN + static_cast<int>(rank) * HALF + j * 64, kb * BK);
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_PRODUCER);
+      }
+      if (rank == 0) {
+        // The even CTA's full barriers count both CTAs' copies: wait for the last phase
+        // armed on each stage so no copy into either CTA is left in flight.
+        int never = 0;
+        for (int s = 0; s < STAGES; ++s)
+          if ((issued >> s) & 1u)
+            if (!mbar_wait_bounded(smem_u32(&bars->full[s]), (issued_parity >> s) & 1u,
+                                   ctl.timeout_ns, &never))
+              atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------ MMA issuer (even CTA only)
+      const uint32_t idesc =
+          umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, BN, false, true);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int i = 0;
+      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++i) {
+        const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+        if (!mbar_wait_cluster_bounded(smem_u32(&bars->tmem_empty[acc]), acc_phase ^ 1,
+                                       ctl.timeout_ns, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(smem_u32(&bars->full[stage]), phase, ctl.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem_a + stage * A_STAGE);
+          const uint32_t b0 = smem_u32(smem_b + stage * B_STAGE);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            const uint64_t adesc = umma_desc_sw128(a0 + k * UMMA_K * 2, 16, 1024);
+            const uint64_t bdesc = umma_desc_sw128(b0 + k * UMMA_K * 128, B_BOX, 1024);
+            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair(smem_u32(&bars->empty[stage]), 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(smem_u32(&bars->tmem_full[acc]), 0x3);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_MMA);
+      }
+      tc_commit_pair(smem_u32(&bars->drain), 0x1);
+      int never = 0;
+      if (!mbar_wait_bounded(smem_u32(&bars->drain), 0, ctl.timeout_ns, &never))
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    }
+  } else {
+    // --------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    int i = 0;
+    for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
+      const bool got = mbar_wait_bounded(smem_u32(&bars->tmem_full[acc]), acc_phase,
+                                         ctl.timeout_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {
+        *abort_flag = 1;
+        if (lane == 0) atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_EPILOGUE);
+        break;
+      }
+      tc_fence_after();
+      const int row = mb * BM + static_cast<int>(rank) * HALF + quarter * 32 + lane;
+      T* crow = C + static_cast<size_t>(row) * N;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, r);
+        tmem_ld_wait();
+        const int n0 = nb * BN + c * 32;
+        if (row < M) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (n0 + 8 * q + 8 <= N) {
+              uint4 v;
+              v.x = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+              v.y = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+              v.z = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+              v.w = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+              *reinterpret_cast<uint4*>(crow + n0 + 8 * q) = v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&bars->tmem_empty[acc]), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the even CTA's MMAs read the odd CTA's shared memory until here
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace tc2
+
+namespace {
+template <typename T>
+rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                     rk_dtype dt, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  rk_status st = make_tmap_2d(&ta, A, dt, K, M, 64, tc2::HALF);
+  if (st != RK_OK) return st;
+  st = make_tmap_2d(&tb, B, dt, N, K, 64, tc2::BK);
+  if (st != RK_OK) return st;
+  LaunchCtl lc;
+  if ((st = launch_ctl(&lc)) != RK_OK) return st;
+  KernelCtl ctl{lc.status, lc.timeout_ns, 0};
+
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(tc2::gemm_tc2_kernel<T>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              tc2::SMEM_BYTES);
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
+
+  const int64_t tiles = ((M + tc2::BM - 1) / tc2::BM) * ((N + tc2::BN - 1) / tc2::BN);
+  const int64_t pairs_max = device_sm_count() / 2;
+  const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(tc2::THREADS);
+  cfg.dynamicSmemBytes = tc2::SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, tc2::gemm_tc2_kernel<T>, ta, tb,
+                                           reinterpret_cast<T*>(C), static_cast<int>(M),
+                                           static_cast<int>(N), static_cast<int>(K), ctl);
+  note_launch();
+  return cuda_status(e);
+}
+}  // namespace
+
+rk_status gemm_tc_2sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                             int64_t K, rk_dtype dt, cudaStream_t s) {
+  if (!gemm_tc_supported(A, B, C, M, N, K)) return RK_ERR_UNSUPPORTED;
+  if (device_sm_count() < 2) return RK_ERR_UNSUPPORTED;
+  if (dt == RK_DTYPE_BF16) return launch_tc2<__nv_bfloat16>(A, B, C, M, N, K, dt, s);
+  return launch_tc2<__half>(A, B, C, M, N, K, dt, s);
+}
+
+}  // namespace rk

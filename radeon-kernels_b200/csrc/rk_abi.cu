@@ -230,12 +230,3 @@ rk_status rk_device_status(rk_stream_t stream) {
 }
 
 }  // extern "C"
-
-namespace rk {
-// The two-SM tensor-core variant is provided by gemm_tcgen05_2sm.cu when built;
-// this weak default reports it as unavailable.
-__attribute__((weak)) rk_status gemm_tc_2sm_launch(const void*, const void*, void*, int64_t,
-                                                   int64_t, int64_t, rk_dtype, cudaStream_t) {
-  return RK_ERR_UNSUPPORTED;
-}
-}  // namespace rk

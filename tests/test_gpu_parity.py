@@ -42,7 +42,7 @@ def _tc_ok(m, n, k):
     return n % 8 == 0 and k % 8 == 0 and k > 0 and m > 0
 
 
-@pytest.mark.parametrize("variant", ["auto", "simt", "tc_1sm"])
+@pytest.mark.parametrize("variant", ["auto", "simt", "tc_1sm", "tc_2sm"])
 @pytest.mark.parametrize("path", golden_cases("gemm"), ids=lambda p: p.stem)
 def test_gemm_matches_reference_fixtures(path, variant):
     import torch
@@ -55,7 +55,7 @@ def test_gemm_matches_reference_fixtures(path, variant):
     buf, c = _guarded(torch, m, n, dtype)
     a_before, b_before = to_bits(a), to_bits(b)
     status = abi_gemm(a, b, c, GEMM[variant], dtype)
-    if variant == "tc_1sm" and not _tc_ok(m, n, k) and m * n * k > 0:
+    if variant in ("tc_1sm", "tc_2sm") and not _tc_ok(m, n, k) and m * n * k > 0:
         assert status == _native.RK_ERR_UNSUPPORTED
         return
     assert status == _native.RK_OK, _native.status_text(status)
@@ -112,11 +112,11 @@ def test_gemm_edge_shapes_against_oracle(shape, dtype):
     a_cpu = seeded((m, k), 0, "uniform", dtype, gen)
     b_cpu = seeded((k, n), 0, "uniform", dtype, gen)
     c_bits, c32 = oracle.gemm(to_bits(a_cpu), to_bits(b_cpu), dtype)
-    for variant in ("auto", "tc_1sm", "simt"):
+    for variant in ("auto", "tc_1sm", "tc_2sm", "simt"):
         a, b = a_cpu.cuda(), b_cpu.cuda()
         buf, c = _guarded(torch, m, n, dtype)
         status = abi_gemm(a, b, c, GEMM[variant], dtype)
-        if variant == "tc_1sm" and not _tc_ok(m, n, k):
+        if variant in ("tc_1sm", "tc_2sm") and not _tc_ok(m, n, k):
             assert status == _native.RK_ERR_UNSUPPORTED
             continue
         assert status == _native.RK_OK
@@ -180,7 +180,7 @@ def _fp32_reference(a, b):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-def _check_full_gemm(a, b, dtype, rows):
+def _check_full_gemm(a, b, dtype, rows, variant="auto"):
     """Full-size check against an fp32 product plus the C oracle on sampled rows."""
 
     import torch
@@ -188,7 +188,7 @@ def _check_full_gemm(a, b, dtype, rows):
     m, k = a.shape
     n = b.shape[1]
     c = torch.empty(m, n, dtype=a.dtype, device="cuda")
-    assert abi_gemm(a, b, c, GEMM["auto"], dtype) == _native.RK_OK
+    assert abi_gemm(a, b, c, GEMM[variant], dtype) == _native.RK_OK
     torch.cuda.synchronize()
     assert device_status() == _native.RK_OK
     ref32 = _fp32_reference(a, b)
@@ -201,7 +201,7 @@ def _check_full_gemm(a, b, dtype, rows):
     oracle.assert_parity(to_bits(c[rows]), o_bits, o32, dtype)
     # determinism: a second launch is bit-identical
     c2 = torch.empty_like(c)
-    assert abi_gemm(a, b, c2, GEMM["auto"], dtype) == _native.RK_OK
+    assert abi_gemm(a, b, c2, GEMM[variant], dtype) == _native.RK_OK
     assert torch.equal(c.view(torch.int16), c2.view(torch.int16))
     return err
 
@@ -213,11 +213,12 @@ def test_config1_gemm_1024_bf16():
     _check_full_gemm(a, b, "bf16", [0, 1, 511, 1023])
 
 
-def test_config4_gemm_ffn_up_fp16():
+@pytest.mark.parametrize("variant", ["auto", "tc_1sm", "tc_2sm"])
+def test_config4_gemm_ffn_up_fp16(variant):
     gen = __import__("torch").Generator().manual_seed(3)
     a = seeded((4096, 4096), 3, "normal64", "fp16", gen).cuda()
     b = seeded((4096, 14336), 3, "normal64", "fp16", gen).cuda()
-    _check_full_gemm(a, b, "fp16", [0, 4095])
+    _check_full_gemm(a, b, "fp16", [0, 4095], variant)
 
 
 @pytest.mark.parametrize("shards", [1, 8])
