@@ -152,8 +152,12 @@ const char* rk_variant_name(int op, int variant) {
 int rk_gemm_select_variant(const void* A, const void* B, const void* C, int64_t M, int64_t N,
                            int64_t K, rk_dtype dt) {
   (void)dt;
-  if (gemm_tc_supported(A, B, C, M, N, K)) return RK_GEMM_TC_1SM;
-  return RK_GEMM_SIMT;
+  if (!gemm_tc_supported(A, B, C, M, N, K)) return RK_GEMM_SIMT;
+  // SM pairs with 256x256 tiles once there is at least one tile per pair (they halve the
+  // per-SM operand traffic); smaller problems keep more, narrower 1-SM tiles in flight.
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  if (pair_tiles >= device_sm_count() / 2) return RK_GEMM_TC_2SM;
+  return RK_GEMM_TC_1SM;
 }
 
 int rk_gemv_select_variant(const void* x, const void* W, const void* out, int64_t M, int64_t N,
