@@ -36,8 +36,8 @@ inline EncodeTiledFn encode_tiled_fn() {
 // Tensor map over a row-major [outer, inner] matrix of 16-bit elements, read
 // in boxes of [box_outer, box_inner] with the 128-byte swizzle
 // (box_inner * 2 must be <= 128).  Out-of-range elements read as zero.
-inline rk_status make_tmap_2d(CUtensorMap* map, const void* base, rk_dtype dt, int64_t inner,
-                              int64_t outer, uint32_t box_inner, uint32_t box_outer) {
+inline rk_status encode_tmap_2d(CUtensorMap* map, const void* base, rk_dtype dt, int64_t inner,
+                                int64_t outer, uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (fn == nullptr) return RK_ERR_CUDA;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
@@ -50,6 +50,48 @@ inline rk_status make_tmap_2d(CUtensorMap* map, const void* base, rk_dtype dt, i
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? RK_OK : RK_ERR_UNSUPPORTED;
+}
+
+// Encoding a tensor map costs about a microsecond of host time per call; decode loops
+// call the same GEMV on the same weight and activation buffers every step, so recently
+// encoded maps are kept in a small process-wide cache keyed by every encoded field.
+struct TmapKey {
+  const void* base;
+  int64_t inner, outer;
+  uint32_t box_inner, box_outer;
+  int dt;
+  bool operator==(const TmapKey& o) const {
+    return base == o.base && inner == o.inner && outer == o.outer && box_inner == o.box_inner &&
+           box_outer == o.box_outer && dt == o.dt;
+  }
+};
+
+inline rk_status make_tmap_2d(CUtensorMap* map, const void* base, rk_dtype dt, int64_t inner,
+                              int64_t outer, uint32_t box_inner, uint32_t box_outer) {
+  constexpr int kSlots = 64;
+  struct Slot {
+    TmapKey key;
+    CUtensorMap map;
+    bool used;
+  };
+  static Slot slots[kSlots];
+  static int next = 0;
+  static std::mutex mu;
+  const TmapKey key{base, inner, outer, box_inner, box_outer, static_cast<int>(dt)};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < kSlots; ++i)
+      if (slots[i].used && slots[i].key == key) {
+        *map = slots[i].map;
+        return RK_OK;
+      }
+  }
+  const rk_status st = encode_tmap_2d(map, base, dt, inner, outer, box_inner, box_outer);
+  if (st != RK_OK) return st;
+  std::lock_guard<std::mutex> lock(mu);
+  slots[next] = Slot{key, *map, true};
+  next = (next + 1) % kSlots;
+  return RK_OK;
 }
 
 }  // namespace rk
