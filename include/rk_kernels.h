@@ -100,6 +100,23 @@ RK_API rk_status rk_gemv(const void* x, const void* weight, void* out, int64_t M
                   rk_stream_t stream);
 
 /*
+ * rk_gemv with a caller-owned workspace.  The tensor-core variant then splits K
+ * over independent CTAs that meet in the workspace (fp32 partial tiles plus one
+ * ticket counter per 128-row tile; the last CTA of a tile adds the partials in a
+ * fixed order), instead of over thread-block clusters.  `workspace` must be zero-
+ * filled before its first use; every call leaves it zeroed again.  Calls that share
+ * a workspace must be ordered (same stream).  NULL / too small: same as rk_gemv.
+ * No counterpart in the reference (its GEMV kernels do not split K).
+ */
+RK_API rk_status rk_gemv_ex(const void* x, const void* weight, void* out, int64_t M,
+                            int64_t N, int64_t K, rk_dtype dt, int variant,
+                            void* workspace, size_t workspace_bytes, rk_stream_t stream);
+
+/* Workspace bytes rk_gemv_ex can use for this problem (0: none needed). */
+RK_API rk_status rk_gemv_workspace_size(int64_t M, int64_t N, int64_t K, rk_dtype dt,
+                                        int variant, size_t* bytes);
+
+/*
  * Column-block gather for N-sharded GEMM/GEMV results.  `blocks` holds G
  * contiguous blocks [G][M][N/G] (the layout an NCCL all-gather of per-rank
  * C blocks produces); `out` receives the row-major [M, N] matrix.  N % G == 0.

@@ -68,6 +68,7 @@ struct __align__(8) Bars {
   uint64_t partials;  // leader: one remote arrival per non-leader CTA
   uint32_t tmem_base;
   int abort;
+  int last;  // workspace split-K: this CTA is the last of its tile to finish
 };
 
 template <int MN>
@@ -127,7 +128,8 @@ template <typename T, int MN>
 __global__ void __launch_bounds__(THREADS, 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x, T* __restrict__ out, int M, int N,
-                   int K, int csize, KernelCtl ctl) {
+                   int K, int csize, float* __restrict__ ws_part, int* __restrict__ ws_count,
+                   int ksplit, KernelCtl ctl) {
   using C = Cfg<MN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -135,10 +137,15 @@ __global__ void __launch_bounds__(THREADS, 2)
   Bars* bars = reinterpret_cast<Bars*>(ring + C::RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
-  const int tile = blockIdx.x / csize;
+  // K split: across the CTAs of a cluster (csize > 1), or across independent CTAs that
+  // meet in a global workspace (ws_part != nullptr, csize == 1).
+  const bool ws_mode = ws_part != nullptr && ksplit > 1;
+  const int parts = ws_mode ? ksplit : csize;
+  const int part = ws_mode ? static_cast<int>(blockIdx.x % ksplit) : static_cast<int>(rank);
+  const int tile = blockIdx.x / parts;
   const int num_kb = (K + BK - 1) / BK;
-  const int kb0 = static_cast<int>(static_cast<int64_t>(num_kb) * rank / csize);
-  const int kb1 = static_cast<int>(static_cast<int64_t>(num_kb) * (rank + 1) / csize);
+  const int kb0 = static_cast<int>(static_cast<int64_t>(num_kb) * part / parts);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(num_kb) * (part + 1) / parts);
   volatile int* abort_flag = &bars->abort;
 
   if (threadIdx.x == 0) {
@@ -306,7 +313,41 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
       }
       const int row = tile * BM + row_local;
-      if (ok && row < N) {
+      bool store = ok;
+      if (ws_mode) {
+        // Publish this CTA's partial tile; the last CTA of the tile (atomic ticket) adds
+        // all partials in part order -- the result does not depend on arrival order --
+        // and re-zeroes the ticket for the next call.  Nobody waits on anybody.
+        float* mine = ws_part + (static_cast<size_t>(tile) * parts + part) * BM * MN +
+                      static_cast<size_t>(row_local) * MN;
+#pragma unroll
+        for (int j = 0; j < MN; j += 4)
+          *reinterpret_cast<float4*>(mine + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        __threadfence();
+        epilogue_bar_sync();
+        if (warp == 2 && lane == 0) bars->last = atomicAdd(ws_count + tile, 1) == parts - 1;
+        epilogue_bar_sync();
+        store = bars->last != 0;
+        if (store) {
+          __threadfence();
+#pragma unroll
+          for (int j = 0; j < MN; ++j) acc[j] = 0.f;
+          for (int q = 0; q < parts; ++q) {
+            const float* src = ws_part + (static_cast<size_t>(tile) * parts + q) * BM * MN +
+                               static_cast<size_t>(row_local) * MN;
+#pragma unroll
+            for (int j = 0; j < MN; j += 4) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(src + j));
+              acc[j] += v.x;
+              acc[j + 1] += v.y;
+              acc[j + 2] += v.z;
+              acc[j + 3] += v.w;
+            }
+          }
+          if (warp == 2 && lane == 0) ws_count[tile] = 0;
+        }
+      }
+      if (store && row < N) {
 #pragma unroll
         for (int m = 0; m < MN; ++m)
           if (m < M) out[static_cast<size_t>(m) * N + row] = from_f32<T>(acc[m]);
@@ -332,9 +373,30 @@ __global__ void __launch_bounds__(THREADS, 2)
 
 namespace {
 
+// Workspace split-K: CTAs per 128-row tile so that the whole grid is resident
+// (two CTAs per SM), at most 8 and at most one per 64-deep K block.
+int workspace_parts(int64_t N, int64_t K) {
+  const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
+  const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
+  int64_t parts = (2ll * device_sm_count()) / (tiles > 0 ? tiles : 1);
+  if (parts > gtc::MAX_CLUSTER) parts = gtc::MAX_CLUSTER;
+  if (parts > num_kb) parts = num_kb;
+  return parts < 1 ? 1 : static_cast<int>(parts);
+}
+
+size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
+  const int parts = workspace_parts(N, K);
+  if (parts <= 1) return 0;
+  const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
+  const int mn = M <= 16 ? 16 : 32;
+  const size_t counters = ((static_cast<size_t>(tiles) * sizeof(int) + 255) / 256) * 256;
+  return counters + static_cast<size_t>(tiles) * parts * gtc::BM * mn * sizeof(float);
+}
+
 template <typename T, int MN>
 rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
-                         rk_dtype dt, cudaStream_t s, int csize_override) {
+                         rk_dtype dt, cudaStream_t s, int csize_override, void* workspace,
+                         size_t workspace_bytes) {
   CUtensorMap tw, tx;
   rk_status st = make_tmap_2d(&tw, W, dt, K, N, 64, gtc::BM);
   if (st != RK_OK) return st;
@@ -357,18 +419,30 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
 
   const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
   const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
-  int csize = csize_override;
-  if (csize <= 0) {
-    // Enough CTAs to keep every SM streaming (two resident per SM), K split at most 8 ways.
-    const int64_t target = 2ll * device_sm_count();
-    csize = 1;
-    while (csize < gtc::MAX_CLUSTER && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
+  float* ws_part = nullptr;
+  int* ws_count = nullptr;
+  int ksplit = 1;
+  int csize = 1;
+  const size_t need = workspace_bytes_for(M, N, K);
+  if (csize_override <= 0 && workspace != nullptr && need > 0 && workspace_bytes >= need) {
+    ksplit = workspace_parts(N, K);
+    ws_count = static_cast<int*>(workspace);
+    ws_part = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                       ((static_cast<size_t>(tiles) * sizeof(int) + 255) / 256) * 256);
+  } else {
+    csize = csize_override;
+    if (csize <= 0) {
+      // No workspace: split K over a thread-block cluster, reduced through DSMEM.
+      const int64_t target = 2ll * device_sm_count();
+      csize = 1;
+      while (csize < gtc::MAX_CLUSTER && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
+    }
+    if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
+    while (csize > 1 && csize > num_kb) csize /= 2;
   }
-  if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
-  while (csize > 1 && csize > num_kb) csize /= 2;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles * csize));
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * (ws_part ? ksplit : csize)));
   cfg.blockDim = dim3(gtc::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -381,12 +455,15 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, gtc::gemv_tc_kernel<T, MN>, tw, tx,
                                            static_cast<T*>(out), static_cast<int>(M),
-                                           static_cast<int>(N), static_cast<int>(K), csize, ctl);
+                                           static_cast<int>(N), static_cast<int>(K), csize, ws_part,
+                                           ws_count, ksplit, ctl);
   note_launch();
   return cuda_status(e);
 }
 
 }  // namespace
+
+size_t gemv_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) { return workspace_bytes_for(M, N, K); }
 
 static std::atomic<int> g_gemv_tc_cluster{0};
 
@@ -403,15 +480,17 @@ bool gemv_tc_supported(const void* x, const void* W, const void* out, int64_t M,
 }
 
 rk_status gemv_tc_launch(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
-                         rk_dtype dt, cudaStream_t s) {
+                         rk_dtype dt, cudaStream_t s, void* workspace, size_t workspace_bytes) {
   if (!gemv_tc_supported(x, W, out, M, N, K)) return RK_ERR_UNSUPPORTED;
   const int c = g_gemv_tc_cluster.load();
   if (M <= 16) {
-    if (dt == RK_DTYPE_BF16) return launch_gemv_tc<__nv_bfloat16, 16>(x, W, out, M, N, K, dt, s, c);
-    return launch_gemv_tc<__half, 16>(x, W, out, M, N, K, dt, s, c);
+    if (dt == RK_DTYPE_BF16)
+      return launch_gemv_tc<__nv_bfloat16, 16>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes);
+    return launch_gemv_tc<__half, 16>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes);
   }
-  if (dt == RK_DTYPE_BF16) return launch_gemv_tc<__nv_bfloat16, 32>(x, W, out, M, N, K, dt, s, c);
-  return launch_gemv_tc<__half, 32>(x, W, out, M, N, K, dt, s, c);
+  if (dt == RK_DTYPE_BF16)
+    return launch_gemv_tc<__nv_bfloat16, 32>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes);
+  return launch_gemv_tc<__half, 32>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes);
 }
 
 }  // namespace rk

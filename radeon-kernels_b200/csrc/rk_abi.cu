@@ -190,8 +190,9 @@ rk_status rk_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N, i
   return RK_ERR_UNSUPPORTED;
 }
 
-rk_status rk_gemv(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
-                  rk_dtype dt, int variant, rk_stream_t stream) {
+rk_status rk_gemv_ex(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
+                     rk_dtype dt, int variant, void* workspace, size_t workspace_bytes,
+                     rk_stream_t stream) {
   if (M < 1 || M > 32 || N < 1 || K < 1 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
   if (x == nullptr || W == nullptr || out == nullptr) return RK_ERR_INVALID_ARGUMENT;
   if (variant < 0 || variant >= RK_GEMV_VARIANT_COUNT) return RK_ERR_UNSUPPORTED;
@@ -201,9 +202,28 @@ rk_status rk_gemv(const void* x, const void* W, void* out, int64_t M, int64_t N,
   switch (variant) {
     case RK_GEMV_SCALAR: return gemv_scalar_launch(x, W, out, M, N, K, dt, s);
     case RK_GEMV_STREAM: return gemv_stream_launch(x, W, out, M, N, K, dt, s);
-    case RK_GEMV_TC: return gemv_tc_launch(x, W, out, M, N, K, dt, s);
+    case RK_GEMV_TC: return gemv_tc_launch(x, W, out, M, N, K, dt, s, workspace, workspace_bytes);
   }
   return RK_ERR_UNSUPPORTED;
+}
+
+rk_status rk_gemv(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
+                  rk_dtype dt, int variant, rk_stream_t stream) {
+  return rk_gemv_ex(x, W, out, M, N, K, dt, variant, nullptr, 0, stream);
+}
+
+rk_status rk_gemv_workspace_size(int64_t M, int64_t N, int64_t K, rk_dtype dt, int variant,
+                                 size_t* bytes) {
+  if (bytes == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  *bytes = 0;
+  if (M < 1 || M > 32 || N < 1 || K < 1 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
+  if (variant < 0 || variant >= RK_GEMV_VARIANT_COUNT) return RK_ERR_UNSUPPORTED;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  // Only the tensor-core variant splits K through a workspace; AUTO picks it for M >= 3.
+  if (variant == RK_GEMV_TC || (variant == RK_GEMV_AUTO && M >= 3 && device_cc_major() == 10 &&
+                                K % 8 == 0))
+    *bytes = gemv_tc_workspace_bytes(M, N, K);
+  return RK_OK;
 }
 
 rk_status rk_gather_column_blocks(const void* blocks, void* out, int64_t G, int64_t M, int64_t N,

@@ -17,9 +17,31 @@
 #include <c10/cuda/CUDAStream.h>
 #include <torch/extension.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "rk_kernels.h"
 
 namespace {
+
+// Split-K workspaces for rk_gemv_ex, one per (device, stream): calls on one stream are
+// ordered, so they can share it; the kernels leave it zeroed after every call.  Grown
+// (never shrunk) through the PyTorch caching allocator and zero-filled when created.
+void* gemv_workspace(const at::Tensor& like, size_t bytes, rk_stream_t stream) {
+  if (bytes == 0) return nullptr;
+  static std::mutex mu;
+  static std::map<std::pair<int, rk_stream_t>, at::Tensor> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(static_cast<int>(like.get_device()), stream);
+  auto it = cache.find(key);
+  if (it == cache.end() || static_cast<size_t>(it->second.numel()) < bytes) {
+    at::Tensor ws = at::zeros({static_cast<int64_t>(bytes)}, like.options().dtype(at::kByte));
+    cache[key] = ws;
+    return ws.data_ptr();
+  }
+  return it->second.data_ptr();
+}
 
 rk_dtype dtype_of(const at::Tensor& t, const char* name) {
   if (t.scalar_type() == at::kHalf) return RK_DTYPE_FP16;
@@ -82,9 +104,16 @@ at::Tensor gemv_out(const at::Tensor& x, const at::Tensor& weight, at::Tensor ou
   TORCH_CHECK(x.size(1) == weight.size(1), "input and weight must share K");
   TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == weight.size(0), "out has the wrong shape");
   c10::cuda::CUDAGuard guard(x.device());
-  check_status(rk_gemv(x.data_ptr(), weight.data_ptr(), out.data_ptr(), x.size(0),
-                       weight.size(0), x.size(1), dtype_of(x, "input"),
-                       static_cast<int>(variant), current_stream(x)),
+  const rk_dtype dt = dtype_of(x, "input");
+  const rk_stream_t stream = current_stream(x);
+  size_t ws_bytes = 0;
+  check_status(rk_gemv_workspace_size(x.size(0), weight.size(0), x.size(1), dt,
+                                      static_cast<int>(variant), &ws_bytes),
+               "rk_gemv_workspace_size");
+  void* ws = gemv_workspace(x, ws_bytes, stream);
+  check_status(rk_gemv_ex(x.data_ptr(), weight.data_ptr(), out.data_ptr(), x.size(0),
+                          weight.size(0), x.size(1), dt, static_cast<int>(variant), ws, ws_bytes,
+                          stream),
                "rk_gemv");
   return out;
 }

@@ -75,6 +75,11 @@ def test_arguments_are_validated_before_any_device_work():
     assert lib.rk_gemv(null, null, null, 0, 4, 4, 0, 0, null) == _native.RK_ERR_INVALID_ARGUMENT
     assert lib.rk_gemv(null, null, null, 1, 4, 4, 0, 0, null) == _native.RK_ERR_INVALID_ARGUMENT  # null pointers
     assert lib.rk_gather_column_blocks(null, null, 3, 2, 8, 0, null) == _native.RK_ERR_INVALID_ARGUMENT  # 8 % 3
+    assert lib.rk_gemv_workspace_size(1, 8, 8, 0, 0, None) == _native.RK_ERR_INVALID_ARGUMENT
+    size = ctypes.c_size_t(7)
+    assert lib.rk_gemv_workspace_size(40, 8, 8, 0, 0, ctypes.byref(size)) == _native.RK_ERR_INVALID_ARGUMENT
+    assert size.value == 0
+    assert lib.rk_gemv_ex(null, null, null, 1, 4, 4, 0, 0, null, 0, null) == _native.RK_ERR_INVALID_ARGUMENT
 
 
 def test_missing_binary_fails_loudly(monkeypatch, tmp_path):

@@ -309,6 +309,44 @@ def test_gemv_tensor_core_cluster_split_k(cluster, m):
     oracle.assert_parity(to_bits(out), o_bits, o32, "fp16")
 
 
+@pytest.mark.parametrize("m", [3, 5, 16, 17, 32])
+@pytest.mark.parametrize("n, k", [(1000, 4104), (8192, 8192), (4096, 14336)])
+def test_gemv_tensor_core_workspace_split_k(m, n, k):
+    """rk_gemv_ex: K split over independent CTAs meeting in a caller-owned workspace."""
+
+    import ctypes
+
+    import torch
+
+    gen = torch.Generator().manual_seed(m + n)
+    x = seeded((m, k), 13, "normal", "bf16", gen)
+    w = seeded((n, k), 13, f"normal/{k}", "bf16", gen)
+    o_bits, o32 = oracle.gemv(to_bits(x), to_bits(w), "bf16")
+    lib = _native.library()
+    need = ctypes.c_size_t(0)
+    assert lib.rk_gemv_workspace_size(m, n, k, 1, GEMV["tc"], ctypes.byref(need)) == _native.RK_OK
+    assert need.value > 0  # these shapes split K
+    ws = torch.zeros(need.value + 4096, dtype=torch.uint8, device="cuda")
+    xd, wd = x.cuda(), w.cuda()
+    outs = []
+    for _ in range(2):  # the second call relies on the first leaving the tickets zeroed
+        buf, out = _guarded(torch, m, n, "bf16")
+        st = lib.rk_gemv_ex(
+            ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(wd.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+            m, n, k, 1, GEMV["tc"], ctypes.c_void_p(ws.data_ptr()), need.value,
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+        )
+        assert st == _native.RK_OK, _native.status_text(st)
+        torch.cuda.synchronize()
+        assert _guards_intact(buf)
+        outs.append(out.clone())
+    assert device_status() == _native.RK_OK
+    tiles = (n + 127) // 128
+    assert int(ws[: 4 * tiles].view(torch.int32).abs().sum().item()) == 0  # tickets re-zeroed
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    oracle.assert_parity(to_bits(outs[0]), o_bits, o32, "bf16")
+
+
 def test_gather_column_blocks_matches_permute():
     import ctypes
 
