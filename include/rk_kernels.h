@@ -116,6 +116,32 @@ RK_API rk_status rk_gemv_ex(const void* x, const void* weight, void* out, int64_
 RK_API rk_status rk_gemv_workspace_size(int64_t M, int64_t N, int64_t K, rk_dtype dt,
                                         int variant, size_t* bytes);
 
+/* Capacity of the scratch array behind rk_gemv_fixed_scratch (8 MiB per device). */
+#define RK_GEMV_FIXED_SCRATCH_BYTES (8u << 20)
+
+/*
+ * The tensor-core GEMV (RK_GEMV_TC) for callers that cannot allocate device memory:
+ * it allocates nothing and takes no workspace.  No counterpart in the reference.
+ *
+ * Who needs it: plugins hosted by an engine that owns all device allocations and
+ * gives a custom op only its input and output buffers, and latency-critical serving
+ * loops that must not call cudaMalloc on the hot path (it can synchronise the device
+ * and fail under memory pressure).  The caller still passes x, weight and out.
+ *
+ * The split-K scratch is a fixed array of RK_GEMV_FIXED_SCRATCH_BYTES compiled into
+ * the library; every GPU that loads the library holds it until the process exits.
+ * The first call on a device looks up its device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.  All calls
+ * on a device share the one array and each call re-zeroes the part that must start
+ * at zero, so calls that may overlap on the GPU (different streams without ordering)
+ * race and must not be issued.  Problems needing more scratch than the capacity are
+ * rejected with RK_ERR_TOO_LARGE; shapes the tensor-core GEMV cannot run (K % 8 != 0,
+ * unaligned pointers, non-sm_100 device) with RK_ERR_UNSUPPORTED.
+ */
+RK_API rk_status rk_gemv_fixed_scratch(const void* x, const void* weight, void* out,
+                                       int64_t M, int64_t N, int64_t K, rk_dtype dt,
+                                       rk_stream_t stream);
+
 /*
  * Column-block gather for N-sharded GEMM/GEMV results.  `blocks` holds G
  * contiguous blocks [G][M][N/G] (the layout an NCCL all-gather of per-rank

@@ -494,3 +494,57 @@ rk_status gemv_tc_launch(const void* x, const void* W, void* out, int64_t M, int
 }
 
 }  // namespace rk
+
+// ---------------------------------------------------------------------------
+// rk_gemv_fixed_scratch: the tensor-core GEMV with its split-K scratch taken from
+// a fixed array compiled into this library instead of from the caller.
+//
+// Some callers cannot hand the library device memory for scratch: plugins hosted
+// by an engine that owns every device allocation and passes a custom op only its
+// input and output buffers, and latency-critical serving loops that must not call
+// cudaMalloc on the hot path (it can synchronise the device and can fail under
+// memory pressure).  For them this entry point uses RK_GEMV_FIXED_SCRATCH_BYTES of
+// device memory that every GPU loading the library holds until the process exits.
+//
+// Host code must not pass `g_gemv_fixed_scratch` itself to a kernel: in host code
+// that name is a host-side stand-in, not a device address.  The device address is
+// looked up once per device with cudaGetSymbolAddress while that device is current
+// (the first call on a device does this), and that address is what the kernel gets.
+namespace {
+
+static __device__ __align__(256) unsigned char g_gemv_fixed_scratch[RK_GEMV_FIXED_SCRATCH_BYTES];
+
+struct FixedScratch {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  void* ptr = nullptr;
+};
+FixedScratch g_fixed_scratch[64];
+
+}  // namespace
+
+extern "C" rk_status rk_gemv_fixed_scratch(const void* x, const void* weight, void* out,
+                                           int64_t M, int64_t N, int64_t K, rk_dtype dt,
+                                           rk_stream_t stream) {
+  using namespace rk;
+  if (M < 1 || M > 32 || N < 1 || K < 1 || (dt != RK_DTYPE_FP16 && dt != RK_DTYPE_BF16))
+    return RK_ERR_INVALID_ARGUMENT;
+  if (x == nullptr || weight == nullptr || out == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RK_ERR_NO_DEVICE;
+  if (!gemv_tc_supported(x, weight, out, M, N, K)) return RK_ERR_UNSUPPORTED;
+  FixedScratch& fs = g_fixed_scratch[dev];
+  std::call_once(fs.once, [&fs] { fs.err = cudaGetSymbolAddress(&fs.ptr, g_gemv_fixed_scratch); });
+  if (fs.err != cudaSuccess || fs.ptr == nullptr) return cuda_status(fs.err);
+  const size_t need = gemv_tc_workspace_bytes(M, N, K);
+  if (need > RK_GEMV_FIXED_SCRATCH_BYTES) return RK_ERR_TOO_LARGE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (need > 0) {
+    // The array keeps whatever the previous call left; the split-K tickets at its
+    // start must be zero when the kernel begins.
+    const size_t tickets = ((static_cast<size_t>((N + gtc::BM - 1) / gtc::BM) * sizeof(int) + 255) / 256) * 256;
+    const rk_status st = cuda_status(cudaMemsetAsync(fs.ptr, 0, tickets, s));
+    if (st != RK_OK) return st;
+  }
+  return gemv_tc_launch(x, weight, out, M, N, K, dt, s, need > 0 ? fs.ptr : nullptr, need);
+}
