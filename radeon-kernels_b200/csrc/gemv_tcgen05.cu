@@ -128,8 +128,7 @@ template <typename T, int MN>
 __global__ void __launch_bounds__(THREADS, 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x, T* __restrict__ out, int M, int N,
-                   int K, int csize, float* __restrict__ ws_part, int* __restrict__ ws_count,
-                   int ksplit, KernelCtl ctl) {
+                   int K, int csize, KernelCtl ctl) {
   using C = Cfg<MN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -137,15 +136,10 @@ __global__ void __launch_bounds__(THREADS, 2)
   Bars* bars = reinterpret_cast<Bars*>(ring + C::RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
-  // K split: across the CTAs of a cluster (csize > 1), or across independent CTAs that
-  // meet in a global workspace (ws_part != nullptr, csize == 1).
-  const bool ws_mode = ws_part != nullptr && ksplit > 1;
-  const int parts = ws_mode ? ksplit : csize;
-  const int part = ws_mode ? static_cast<int>(blockIdx.x % ksplit) : static_cast<int>(rank);
-  const int tile = blockIdx.x / parts;
+  const int tile = blockIdx.x / csize;
   const int num_kb = (K + BK - 1) / BK;
-  const int kb0 = static_cast<int>(static_cast<int64_t>(num_kb) * part / parts);
-  const int kb1 = static_cast<int>(static_cast<int64_t>(num_kb) * (part + 1) / parts);
+  const int kb0 = static_cast<int>(static_cast<int64_t>(num_kb) * rank / csize);
+  const int kb1 = static_cast<int>(static_cast<int64_t>(num_kb) * (rank + 1) / csize);
   volatile int* abort_flag = &bars->abort;
 
   if (threadIdx.x == 0) {
@@ -313,40 +307,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
       }
       const int row = tile * BM + row_local;
-      bool store = ok;
-      if (ws_mode) {
-        // Publish this CTA's partial tile; the last CTA of the tile (atomic ticket) adds
-        // all partials in part order -- the result does not depend on arrival order --
-        // and re-zeroes the ticket for the next call.  Nobody waits on anybody.
-        float* mine = ws_part + (static_cast<size_t>(tile) * parts + part) * BM * MN +
-                      static_cast<size_t>(row_local) * MN;
-#pragma unroll
-        for (int j = 0; j < MN; j += 4)
-          *reinterpret_cast<float4*>(mine + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-        __threadfence();
-        epilogue_bar_sync();
-        if (warp == 2 && lane == 0) bars->last = atomicAdd(ws_count + tile, 1) == parts - 1;
-        epilogue_bar_sync();
-        store = bars->last != 0;
-        if (store) {
-          __threadfence();
-#pragma unroll
-          for (int j = 0; j < MN; ++j) acc[j] = 0.f;
-          for (int q = 0; q < parts; ++q) {
-            const float* src = ws_part + (static_cast<size_t>(tile) * parts + q) * BM * MN +
-                               static_cast<size_t>(row_local) * MN;
-#pragma unroll
-            for (int j = 0; j < MN; j += 4) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(src + j));
-              acc[j] += v.x;
-              acc[j + 1] += v.y;
-              acc[j + 2] += v.z;
-              acc[j + 3] += v.w;
-            }
-          }
-          if (warp == 2 && lane == 0) ws_count[tile] = 0;
-        }
-      }
+      const bool store = ok;
       if (store && row < N) {
 #pragma unroll
         for (int m = 0; m < MN; ++m)
@@ -369,28 +330,278 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Stream-K variant (used when the caller provides a workspace).  One persistent CTA
+// per SM; the (128-row tile, 64-deep K block) work units are dealt out as equal
+// contiguous ranges, so every SM streams the same number of weight bytes -- the
+// kernel runs at the per-SM streaming rate on every SM for the whole call.  A range
+// covers whole tiles (stored directly) plus at most a partial tile at each end; a
+// shared tile's partials go to the workspace and the last CTA to finish it (atomic
+// ticket) adds them in CTA order and re-zeroes the ticket.  Accumulators are double
+// buffered in TMEM so the epilogue of one segment overlaps the MMAs of the next.
+template <int MN>
+struct Sk {
+  static constexpr int X_STAGE = MN * BK * 2;
+  static constexpr int STAGE = W_STAGE + X_STAGE;
+  static constexpr int STAGES = (180 * 1024) / STAGE;  // 10 for MN = 16, 9 for MN = 32
+  static constexpr int RING = STAGES * STAGE;
+  static constexpr int TMEM = 64;                        // two accumulators of <= 32 columns
+  static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
+};
+
+template <int STAGES_>
+struct __align__(8) SkBars {
+  uint64_t full[STAGES_];
+  uint64_t empty[STAGES_];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int last;
+};
+
+template <int MN>
+constexpr int sk_smem_bytes() {
+  return 1024 + Sk<MN>::RING + int(sizeof(SkBars<Sk<MN>::STAGES>));
+}
+
+__device__ __forceinline__ int64_t sk_unit_start(int cta, int64_t units, int grid) {
+  return static_cast<int64_t>(cta) * units / grid;
+}
+// CTA whose range contains unit u: the largest c with floor(c*U/G) <= u.
+__device__ __forceinline__ int sk_cta_of(int64_t u, int64_t units, int grid) {
+  return static_cast<int>(((u + 1) * grid - 1) / units);
+}
+
+template <typename T, int MN>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemv_tc_sk_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                      const __grid_constant__ CUtensorMap tmap_x, T* __restrict__ out, int M, int N,
+                      int K, float* __restrict__ part, int* __restrict__ ticket, KernelCtl ctl) {
+  using C = Sk<MN>;
+  constexpr int STAGES_ = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  auto* bars = reinterpret_cast<SkBars<STAGES_>*>(ring + C::RING);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grid = gridDim.x, cta = blockIdx.x;
+  const int num_kb = (K + BK - 1) / BK;
+  const int tiles = (N + BM - 1) / BM;
+  const int64_t units = static_cast<int64_t>(tiles) * num_kb;
+  const int64_t u0 = sk_unit_start(cta, units, grid);
+  const int64_t u1 = sk_unit_start(cta + 1, units, grid);
+  volatile int* abort_flag = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES_; ++s) {
+      mbar_init(smem_u32(&bars->full[s]), 1);
+      mbar_init(smem_u32(&bars->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&bars->tmem_full[a]), 1);
+      mbar_init(smem_u32(&bars->tmem_empty[a]), 4);  // one arrival per epilogue warp
+    }
+    mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), C::TMEM);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
+      bool ok = true;
+      for (int64_t u = u0; u < u1; ++u) {
+        if (!mbar_wait_bounded(smem_u32(&bars->empty[stage]), phase ^ 1, ctl.timeout_ns,
+                               abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int tile = static_cast<int>(u / num_kb), kb = static_cast<int>(u % num_kb);
+        const uint32_t full = smem_u32(&bars->full[stage]);
+        uint8_t* base = ring + stage * C::STAGE;
+        mbar_arrive_expect_tx(full, C::STAGE);
+        tma_load_2d(smem_u32(base), &tmap_w, full, kb * BK, tile * BM);
+        tma_load_2d(smem_u32(base + W_STAGE), &tmap_x, full, kb * BK, 0);
+        issued |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES_) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_PRODUCER);
+      }
+      int never = 0;
+      for (int s = 0; s < STAGES_; ++s)
+        if ((issued >> s) & 1u)
+          if (!mbar_wait_bounded(smem_u32(&bars->full[s]), (issued_parity >> s) & 1u,
+                                 ctl.timeout_ns, &never))
+            atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc =
+          umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, MN, false, false);
+      uint32_t stage = 0, phase = 0, seg = 0, acc = 0;
+      bool ok = true;
+      for (int64_t u = u0; u < u1 && ok; ++u) {
+        const bool first = (u == u0) || (u % num_kb == 0);
+        const bool last = (u + 1 == u1) || ((u + 1) % num_kb == 0);
+        if (first) {
+          acc = seg & 1;
+          if (!mbar_wait_bounded(smem_u32(&bars->tmem_empty[acc]), ((seg >> 1) & 1) ^ 1,
+                                 ctl.timeout_ns, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        if (!mbar_wait_bounded(smem_u32(&bars->full[stage]), phase, ctl.timeout_ns, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t w0 = smem_u32(ring + stage * C::STAGE);
+        const uint32_t x0 = w0 + W_STAGE;
+#pragma unroll
+        for (int k = 0; k < BK / UMMA_K; ++k) {
+          const uint64_t adesc = umma_desc_sw128(w0 + k * UMMA_K * 2, 16, 1024);
+          const uint64_t bdesc = umma_desc_sw128(x0 + k * UMMA_K * 2, 16, 1024);
+          tc_mma_f16(tmem_base + acc * 32, adesc, bdesc, idesc, (!first || k > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&bars->empty[stage]));
+        if (++stage == STAGES_) {
+          stage = 0;
+          phase ^= 1;
+        }
+        if (last) {
+          tc_commit(smem_u32(&bars->tmem_full[acc]));
+          ++seg;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_MMA);
+      }
+      tc_commit(smem_u32(&bars->drain));
+      int never = 0;
+      if (!mbar_wait_bounded(smem_u32(&bars->drain), 0, ctl.timeout_ns, &never))
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_local = quarter * 32 + lane;
+    uint32_t seg = 0;
+    for (int64_t u = u0; u < u1; ++seg) {
+      const int tile = static_cast<int>(u / num_kb);
+      const int64_t seg_end = min(u1, static_cast<int64_t>(tile + 1) * num_kb);
+      const uint32_t acc = seg & 1;
+      const bool got = mbar_wait_bounded(smem_u32(&bars->tmem_full[acc]), (seg >> 1) & 1,
+                                         ctl.timeout_ns, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) {
+        *abort_flag = 1;
+        if (lane == 0) atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_EPILOGUE);
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[MN];
+      tmem_ld_cols<MN>(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * 32, r);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[acc]));
+      float a[MN];
+#pragma unroll
+      for (int j = 0; j < MN; ++j) a[j] = __uint_as_float(r[j]);
+
+      const int c_first = sk_cta_of(static_cast<int64_t>(tile) * num_kb, units, grid);
+      const int c_last = sk_cta_of(static_cast<int64_t>(tile + 1) * num_kb - 1, units, grid);
+      bool store = true;
+      if (c_first != c_last) {
+        float* mine = part + (static_cast<size_t>(cta) * 2 + (u == u0 ? 0 : 1)) * BM * MN +
+                      static_cast<size_t>(row_local) * MN;
+#pragma unroll
+        for (int j = 0; j < MN; j += 4)
+          *reinterpret_cast<float4*>(mine + j) = make_float4(a[j], a[j + 1], a[j + 2], a[j + 3]);
+        __threadfence();
+        epilogue_bar_sync();
+        if (warp == 2 && lane == 0) bars->last = atomicAdd(ticket + tile, 1) == c_last - c_first;
+        epilogue_bar_sync();
+        store = bars->last != 0;
+        if (store) {
+          __threadfence();
+#pragma unroll
+          for (int j = 0; j < MN; ++j) a[j] = 0.f;
+          for (int c = c_first; c <= c_last; ++c) {
+            const int first_tile_of_c = static_cast<int>(sk_unit_start(c, units, grid) / num_kb);
+            const float* src = part + (static_cast<size_t>(c) * 2 + (first_tile_of_c == tile ? 0 : 1)) * BM * MN +
+                               static_cast<size_t>(row_local) * MN;
+#pragma unroll
+            for (int j = 0; j < MN; j += 4) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(src + j));
+              a[j] += v.x;
+              a[j + 1] += v.y;
+              a[j + 2] += v.z;
+              a[j + 3] += v.w;
+            }
+          }
+          if (warp == 2 && lane == 0) ticket[tile] = 0;
+        }
+      }
+      const int row = tile * BM + row_local;
+      if (store && row < N) {
+#pragma unroll
+        for (int m = 0; m < MN; ++m)
+          if (m < M) out[static_cast<size_t>(m) * N + row] = from_f32<T>(a[m]);
+      }
+      u = seg_end;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM);
+  }
+}
+
 }  // namespace gtc
 
 namespace {
 
-// Workspace split-K: CTAs per 128-row tile so that the whole grid is resident
-// (two CTAs per SM), at most 8 and at most one per 64-deep K block.
-int workspace_parts(int64_t N, int64_t K) {
-  const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
-  const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
-  int64_t parts = (2ll * device_sm_count()) / (tiles > 0 ? tiles : 1);
-  if (parts > gtc::MAX_CLUSTER) parts = gtc::MAX_CLUSTER;
-  if (parts > num_kb) parts = num_kb;
-  return parts < 1 ? 1 : static_cast<int>(parts);
+// Stream-K grid: one CTA per SM (at most one per work unit, at most 240 so the
+// partial slots of the largest case fit the fixed scratch of rk_gemv_fixed_scratch).
+int sk_grid(int64_t N, int64_t K) {
+  const int64_t units = ((N + gtc::BM - 1) / gtc::BM) * ((K + gtc::BK - 1) / gtc::BK);
+  int64_t g = device_sm_count();
+  if (g > 240) g = 240;
+  if (g > units) g = units;
+  return g < 1 ? 1 : static_cast<int>(g);
+}
+
+size_t sk_ticket_bytes(int64_t N) {
+  return ((static_cast<size_t>((N + gtc::BM - 1) / gtc::BM) * sizeof(int) + 255) / 256) * 256;
 }
 
 size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
-  const int parts = workspace_parts(N, K);
-  if (parts <= 1) return 0;
-  const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
   const int mn = M <= 16 ? 16 : 32;
-  const size_t counters = ((static_cast<size_t>(tiles) * sizeof(int) + 255) / 256) * 256;
-  return counters + static_cast<size_t>(tiles) * parts * gtc::BM * mn * sizeof(float);
+  return sk_ticket_bytes(N) + static_cast<size_t>(sk_grid(N, K)) * 2 * gtc::BM * mn * sizeof(float);
 }
 
 template <typename T, int MN>
@@ -419,30 +630,37 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
 
   const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
   const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
-  float* ws_part = nullptr;
-  int* ws_count = nullptr;
-  int ksplit = 1;
-  int csize = 1;
   const size_t need = workspace_bytes_for(M, N, K);
-  if (csize_override <= 0 && workspace != nullptr && need > 0 && workspace_bytes >= need) {
-    ksplit = workspace_parts(N, K);
-    ws_count = static_cast<int*>(workspace);
-    ws_part = reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                       ((static_cast<size_t>(tiles) * sizeof(int) + 255) / 256) * 256);
-  } else {
-    csize = csize_override;
-    if (csize <= 0) {
-      // No workspace: split K over a thread-block cluster, reduced through DSMEM.
-      const int64_t target = 2ll * device_sm_count();
-      csize = 1;
-      while (csize < gtc::MAX_CLUSTER && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
-    }
-    if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
-    while (csize > 1 && csize > num_kb) csize /= 2;
+  if (csize_override <= 0 && workspace != nullptr && workspace_bytes >= need) {
+    // Stream-K over all SMs, shared tiles meet in the caller's workspace.
+    constexpr int sk_smem = gtc::sk_smem_bytes<MN>();
+    static std::once_flag sk_once[64];
+    static cudaError_t sk_err[64];
+    std::call_once(sk_once[dev & 63], [&] {
+      sk_err[dev & 63] = cudaFuncSetAttribute(gtc::gemv_tc_sk_kernel<T, MN>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, sk_smem);
+    });
+    if (sk_err[dev & 63] != cudaSuccess) return cuda_status(sk_err[dev & 63]);
+    int* ticket = static_cast<int*>(workspace);
+    float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + sk_ticket_bytes(N));
+    gtc::gemv_tc_sk_kernel<T, MN><<<sk_grid(N, K), gtc::THREADS, sk_smem, s>>>(
+        tw, tx, static_cast<T*>(out), static_cast<int>(M), static_cast<int>(N),
+        static_cast<int>(K), part, ticket, ctl);
+    note_launch();
+    return cuda_status(cudaGetLastError());
   }
+  // No workspace: split K over a thread-block cluster, reduced through DSMEM.
+  int csize = csize_override;
+  if (csize <= 0) {
+    const int64_t target = 2ll * device_sm_count();
+    csize = 1;
+    while (csize < gtc::MAX_CLUSTER && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
+  }
+  if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
+  while (csize > 1 && csize > num_kb) csize /= 2;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles * (ws_part ? ksplit : csize)));
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * csize));
   cfg.blockDim = dim3(gtc::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -455,8 +673,7 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   cfg.numAttrs = 1;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, gtc::gemv_tc_kernel<T, MN>, tw, tx,
                                            static_cast<T*>(out), static_cast<int>(M),
-                                           static_cast<int>(N), static_cast<int>(K), csize, ws_part,
-                                           ws_count, ksplit, ctl);
+                                           static_cast<int>(N), static_cast<int>(K), csize, ctl);
   note_launch();
   return cuda_status(e);
 }
@@ -542,8 +759,7 @@ extern "C" rk_status rk_gemv_fixed_scratch(const void* x, const void* weight, vo
   if (need > 0) {
     // The array keeps whatever the previous call left; the split-K tickets at its
     // start must be zero when the kernel begins.
-    const size_t tickets = ((static_cast<size_t>((N + gtc::BM - 1) / gtc::BM) * sizeof(int) + 255) / 256) * 256;
-    const rk_status st = cuda_status(cudaMemsetAsync(fs.ptr, 0, tickets, s));
+    const rk_status st = cuda_status(cudaMemsetAsync(fs.ptr, 0, sk_ticket_bytes(N), s));
     if (st != RK_OK) return st;
   }
   return gemv_tc_launch(x, weight, out, M, N, K, dt, s, need > 0 ? fs.ptr : nullptr, need);
