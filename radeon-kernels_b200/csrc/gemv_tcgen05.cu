@@ -346,8 +346,14 @@ struct Sk {
   static constexpr int STAGE = W_STAGE + X_STAGE;
   static constexpr int STAGES = (180 * 1024) / STAGE;  // 10 for MN = 16, 9 for MN = 32
   static constexpr int RING = STAGES * STAGE;
-  static constexpr int TMEM = 64;                        // two accumulators of <= 32 columns
+  // NACC interleaved accumulators per segment: consecutive K=16 MMAs go to different
+  // accumulators, so the dependent-accumulate chain is NACC times shorter (a 128x16x16
+  // MMA is latency-, not throughput-bound); the epilogue adds them in a fixed order.
+  static constexpr int NACC = 8;
+  static constexpr int SET = NACC * MN;           // TMEM columns of one accumulator set
+  static constexpr int TMEM = 2 * SET;            // double-buffered sets: 256 or 512 columns
   static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
+  static_assert(TMEM <= 512, "TMEM has 512 columns");
 };
 
 template <int STAGES_>
@@ -457,10 +463,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       const uint32_t idesc =
           umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, MN, false, false);
-      uint32_t stage = 0, phase = 0, seg = 0, acc = 0;
+      uint32_t stage = 0, phase = 0, seg = 0, acc = 0, kk = 0;
       bool ok = true;
       for (int64_t u = u0; u < u1 && ok; ++u) {
         const bool first = (u == u0) || (u % num_kb == 0);
+        if (first) kk = 0;
         const bool last = (u + 1 == u1) || ((u + 1) % num_kb == 0);
         if (first) {
           acc = seg & 1;
@@ -479,10 +486,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t w0 = smem_u32(ring + stage * C::STAGE);
         const uint32_t x0 = w0 + W_STAGE;
 #pragma unroll
-        for (int k = 0; k < BK / UMMA_K; ++k) {
+        for (int k = 0; k < BK / UMMA_K; ++k, ++kk) {
           const uint64_t adesc = umma_desc_sw128(w0 + k * UMMA_K * 2, 16, 1024);
           const uint64_t bdesc = umma_desc_sw128(x0 + k * UMMA_K * 2, 16, 1024);
-          tc_mma_f16(tmem_base + acc * 32, adesc, bdesc, idesc, (!first || k > 0) ? 1u : 0u);
+          const uint32_t j = kk % C::NACC;  // the first NACC MMAs of a segment initialise
+          tc_mma_f16(tmem_base + acc * C::SET + j * MN, adesc, bdesc, idesc, kk >= C::NACC ? 1u : 0u);
         }
         tc_commit(smem_u32(&bars->empty[stage]));
         if (++stage == STAGES_) {
@@ -519,15 +527,22 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      uint32_t r[MN];
-      tmem_ld_cols<MN>(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * 32, r);
-      tmem_ld_wait();
+      float a[MN];
+#pragma unroll
+      for (int j = 0; j < MN; ++j) a[j] = 0.f;
+      // Accumulators written in this segment: min(NACC, MMAs issued) -- the rest hold stale data.
+      const int64_t mmas = (seg_end - u) * (BK / UMMA_K);
+      const int used = mmas < C::NACC ? static_cast<int>(mmas) : C::NACC;
+      for (int q = 0; q < used; ++q) {
+        uint32_t r[MN];
+        tmem_ld_cols<MN>(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * C::SET + q * MN, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < MN; ++j) a[j] += __uint_as_float(r[j]);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars->tmem_empty[acc]));
-      float a[MN];
-#pragma unroll
-      for (int j = 0; j < MN; ++j) a[j] = __uint_as_float(r[j]);
 
       const int c_first = sk_cta_of(static_cast<int64_t>(tile) * num_kb, units, grid);
       const int c_last = sk_cta_of(static_cast<int64_t>(tile + 1) * num_kb - 1, units, grid);
