@@ -332,10 +332,11 @@ __global__ void __launch_bounds__(THREADS, 2)
 
 
 // ---------------------------------------------------------------------------
-// Stream-K variant (used when the caller provides a workspace).  One persistent CTA
-// per SM; the (128-row tile, 64-deep K block) work units are dealt out as equal
-// contiguous ranges, so every SM streams the same number of weight bytes -- the
-// kernel runs at the per-SM streaming rate on every SM for the whole call.  A range
+// Stream-K variant (used when the caller provides a workspace).  Two persistent CTAs
+// per SM (one CTA's TMA stream tops out near 25 GB/s, two reach the ~45 GB/s an SM
+// can pull); the (128-row tile, 64-deep K block) work units are dealt out as equal
+// contiguous ranges, so every SM streams the same number of weight bytes for the
+// whole call.  A range
 // covers whole tiles (stored directly) plus at most a partial tile at each end; a
 // shared tile's partials go to the workspace and the last CTA to finish it (atomic
 // ticket) adds them in CTA order and re-zeroes the ticket.  Accumulators are double
@@ -344,14 +345,14 @@ template <int MN>
 struct Sk {
   static constexpr int X_STAGE = MN * BK * 2;
   static constexpr int STAGE = W_STAGE + X_STAGE;
-  static constexpr int STAGES = (180 * 1024) / STAGE;  // 10 for MN = 16, 9 for MN = 32
+  static constexpr int STAGES = (108 * 1024) / STAGE;  // 6 for MN = 16, 5 for MN = 32
   static constexpr int RING = STAGES * STAGE;
   // NACC interleaved accumulators per segment: consecutive K=16 MMAs go to different
-  // accumulators, so the dependent-accumulate chain is NACC times shorter (a 128x16x16
-  // MMA is latency-, not throughput-bound); the epilogue adds them in a fixed order.
-  static constexpr int NACC = 8;
+  // accumulators, so the chain of dependent accumulates is NACC times shorter; the
+  // epilogue adds them in a fixed order.
+  static constexpr int NACC = 4;
   static constexpr int SET = NACC * MN;           // TMEM columns of one accumulator set
-  static constexpr int TMEM = 2 * SET;            // double-buffered sets: 256 or 512 columns
+  static constexpr int TMEM = 2 * SET;            // double-buffered sets: 128 or 256 columns
   static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
   static_assert(TMEM <= 512, "TMEM has 512 columns");
 };
@@ -382,7 +383,7 @@ __device__ __forceinline__ int sk_cta_of(int64_t u, int64_t units, int grid) {
 }
 
 template <typename T, int MN>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, 2)
     gemv_tc_sk_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_x, T* __restrict__ out, int M, int N,
                       int K, float* __restrict__ part, int* __restrict__ ticket, KernelCtl ctl) {
@@ -600,12 +601,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 namespace {
 
-// Stream-K grid: one CTA per SM (at most one per work unit, at most 240 so the
-// partial slots of the largest case fit the fixed scratch of rk_gemv_fixed_scratch).
-int sk_grid(int64_t N, int64_t K) {
+// Stream-K grid: two CTAs per SM, at most one per work unit, and at most 240 CTAs for
+// 32-wide accumulators so the partial slots of the largest case fit the 8 MiB fixed
+// scratch of rk_gemv_fixed_scratch.
+int sk_grid(int64_t M, int64_t N, int64_t K) {
   const int64_t units = ((N + gtc::BM - 1) / gtc::BM) * ((K + gtc::BK - 1) / gtc::BK);
-  int64_t g = device_sm_count();
-  if (g > 240) g = 240;
+  int64_t g = 2ll * device_sm_count();
+  if (M > 16 && g > 240) g = 240;
+  if (g > 480) g = 480;
   if (g > units) g = units;
   return g < 1 ? 1 : static_cast<int>(g);
 }
@@ -616,7 +619,7 @@ size_t sk_ticket_bytes(int64_t N) {
 
 size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
   const int mn = M <= 16 ? 16 : 32;
-  return sk_ticket_bytes(N) + static_cast<size_t>(sk_grid(N, K)) * 2 * gtc::BM * mn * sizeof(float);
+  return sk_ticket_bytes(N) + static_cast<size_t>(sk_grid(M, N, K)) * 2 * gtc::BM * mn * sizeof(float);
 }
 
 template <typename T, int MN>
@@ -658,7 +661,7 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
     if (sk_err[dev & 63] != cudaSuccess) return cuda_status(sk_err[dev & 63]);
     int* ticket = static_cast<int*>(workspace);
     float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + sk_ticket_bytes(N));
-    gtc::gemv_tc_sk_kernel<T, MN><<<sk_grid(N, K), gtc::THREADS, sk_smem, s>>>(
+    gtc::gemv_tc_sk_kernel<T, MN><<<sk_grid(M, N, K), gtc::THREADS, sk_smem, s>>>(
         tw, tx, static_cast<T*>(out), static_cast<int>(M), static_cast<int>(N),
         static_cast<int>(K), part, ticket, ctl);
     note_launch();
