@@ -617,7 +617,16 @@ size_t sk_ticket_bytes(int64_t N) {
   return ((static_cast<size_t>((N + gtc::BM - 1) / gtc::BM) * sizeof(int) + 255) / 256) * 256;
 }
 
+// Stream-K pays a workspace fix-up per shared tile, which costs more than it gains
+// while cluster split-K (<= 4 CTAs per tile) still puts a CTA on most SMs; it is used
+// only for weights too short for that (fewer than SMs/8 row tiles).
+bool sk_preferred(int64_t N) {
+  const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
+  return tiles * 8 < device_sm_count();
+}
+
 size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
+  if (!sk_preferred(N)) return 0;
   const int mn = M <= 16 ? 16 : 32;
   return sk_ticket_bytes(N) + static_cast<size_t>(sk_grid(M, N, K)) * 2 * gtc::BM * mn * sizeof(float);
 }
@@ -649,7 +658,7 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
   const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
   const size_t need = workspace_bytes_for(M, N, K);
-  if (csize_override <= 0 && workspace != nullptr && workspace_bytes >= need) {
+  if (csize_override <= 0 && need > 0 && workspace != nullptr && workspace_bytes >= need) {
     // Stream-K over all SMs, shared tiles meet in the caller's workspace.
     constexpr int sk_smem = gtc::sk_smem_bytes<MN>();
     static std::once_flag sk_once[64];
@@ -667,12 +676,13 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
     note_launch();
     return cuda_status(cudaGetLastError());
   }
-  // No workspace: split K over a thread-block cluster, reduced through DSMEM.
+  // Split K over a thread-block cluster, reduced through DSMEM: the largest cluster of
+  // at most 4 CTAs (8-CTA clusters measured slower) keeping the grid within two CTAs per SM.
   int csize = csize_override;
   if (csize <= 0) {
     const int64_t target = 2ll * device_sm_count();
     csize = 1;
-    while (csize < gtc::MAX_CLUSTER && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
+    while (csize < 4 && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
   }
   if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
   while (csize > 1 && csize > num_kb) csize /= 2;

@@ -31,7 +31,7 @@ def _stream():
 
 @pytest.mark.parametrize(
     "dtype, m, n, k",
-    [("bf16", 5, 8192, 8192), ("fp16", 16, 4096, 14336), ("bf16", 32, 1000, 4104), ("fp16", 3, 40000, 512)],
+    [("bf16", 5, 2048, 8192), ("fp16", 16, 640, 14336), ("bf16", 32, 1000, 4104), ("fp16", 3, 40000, 512)],
 )
 def test_fixed_scratch_matches_the_workspace_entry_point(dtype, m, n, k):
     import torch
