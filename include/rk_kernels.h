@@ -166,8 +166,9 @@ RK_API void rk_gemv_set_tuning(int rows_per_warp, int ksplit);
  * 256); 0 restores the built-in choice (fewest weighted waves).  Process-wide. */
 RK_API void rk_gemm_set_tile_n(int tile_n);
 
-/* Tuning hook for RK_GEMV_TC: thread-block cluster size (K split), 1..8;
- * 0 restores the built-in choice.  Process-wide. */
+/* Tuning hook for RK_GEMV_TC: thread-block cluster size (K split), 1..8; -1 selects
+ * stream-K through the rk_gemv_ex workspace; 0 restores the built-in choice.
+ * Process-wide. */
 RK_API void rk_gemv_tc_set_cluster(int cluster_size);
 
 /*

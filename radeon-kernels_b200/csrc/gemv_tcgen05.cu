@@ -39,6 +39,11 @@
 #include "rk_tma.h"
 
 namespace rk {
+
+// Tuning override of the split-K strategy: 0 = automatic, 1/2/4/8 = cluster size,
+// -1 = stream-K through the workspace whenever one is supplied.
+static std::atomic<int> g_gemv_tc_cluster{0};
+
 namespace gtc {
 
 constexpr int BM = 128;
@@ -430,13 +435,13 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
       bool ok = true;
-      for (int64_t u = u0; u < u1; ++u) {
+      int tile = static_cast<int>(u0 / num_kb), kb = static_cast<int>(u0 % num_kb);
+      for (int64_t u = u0; u < u1; ++u, kb = (kb + 1 == num_kb) ? 0 : kb + 1, tile += (kb == 0)) {
         if (!mbar_wait_bounded(smem_u32(&bars->empty[stage]), phase ^ 1, ctl.timeout_ns,
                                abort_flag)) {
           ok = false;
           break;
         }
-        const int tile = static_cast<int>(u / num_kb), kb = static_cast<int>(u % num_kb);
         const uint32_t full = smem_u32(&bars->full[stage]);
         uint8_t* base = ring + stage * C::STAGE;
         mbar_arrive_expect_tx(full, C::STAGE);
@@ -466,10 +471,11 @@ __global__ void __launch_bounds__(THREADS, 2)
           umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, MN, false, false);
       uint32_t stage = 0, phase = 0, seg = 0, acc = 0, kk = 0;
       bool ok = true;
-      for (int64_t u = u0; u < u1 && ok; ++u) {
-        const bool first = (u == u0) || (u % num_kb == 0);
+      int kb = static_cast<int>(u0 % num_kb);
+      for (int64_t u = u0; u < u1 && ok; ++u, kb = (kb + 1 == num_kb) ? 0 : kb + 1) {
+        const bool first = (u == u0) || kb == 0;
         if (first) kk = 0;
-        const bool last = (u + 1 == u1) || ((u + 1) % num_kb == 0);
+        const bool last = (u + 1 == u1) || kb + 1 == num_kb;
         if (first) {
           acc = seg & 1;
           if (!mbar_wait_bounded(smem_u32(&bars->tmem_empty[acc]), ((seg >> 1) & 1) ^ 1,
@@ -626,7 +632,7 @@ bool sk_preferred(int64_t N) {
 }
 
 size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
-  if (!sk_preferred(N)) return 0;
+  if (!sk_preferred(N) && g_gemv_tc_cluster.load() != -1) return 0;
   const int mn = M <= 16 ? 16 : 32;
   return sk_ticket_bytes(N) + static_cast<size_t>(sk_grid(M, N, K)) * 2 * gtc::BM * mn * sizeof(float);
 }
@@ -658,7 +664,8 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
   const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
   const size_t need = workspace_bytes_for(M, N, K);
-  if (csize_override <= 0 && need > 0 && workspace != nullptr && workspace_bytes >= need) {
+  if ((csize_override == 0 || csize_override == -1) && need > 0 && workspace != nullptr &&
+      workspace_bytes >= need) {
     // Stream-K over all SMs, shared tiles meet in the caller's workspace.
     constexpr int sk_smem = gtc::sk_smem_bytes<MN>();
     static std::once_flag sk_once[64];
@@ -680,9 +687,12 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   // at most 4 CTAs (8-CTA clusters measured slower) keeping the grid within two CTAs per SM.
   int csize = csize_override;
   if (csize <= 0) {
+    // Measured on B200: 8-CTA clusters only pay off for very short weights (<= 12 row
+    // tiles); otherwise the largest of 1/2/4 keeping the grid within two CTAs per SM.
     const int64_t target = 2ll * device_sm_count();
+    const int cap = tiles <= 12 ? 8 : 4;
     csize = 1;
-    while (csize < 4 && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
+    while (csize < cap && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
   }
   if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
   while (csize > 1 && csize > num_kb) csize /= 2;
@@ -709,8 +719,6 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
 }  // namespace
 
 size_t gemv_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) { return workspace_bytes_for(M, N, K); }
-
-static std::atomic<int> g_gemv_tc_cluster{0};
 
 void gemv_tc_set_cluster(int c) { g_gemv_tc_cluster.store(c); }
 
