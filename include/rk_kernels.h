@@ -100,13 +100,15 @@ RK_API rk_status rk_gemv(const void* x, const void* weight, void* out, int64_t M
                   rk_stream_t stream);
 
 /*
- * rk_gemv with a caller-owned workspace.  The tensor-core variant then splits K
- * over independent CTAs that meet in the workspace (fp32 partial tiles plus one
- * ticket counter per 128-row tile; the last CTA of a tile adds the partials in a
- * fixed order), instead of over thread-block clusters.  `workspace` must be zero-
- * filled before its first use; every call leaves it zeroed again.  Calls that share
- * a workspace must be ordered (same stream).  NULL / too small: same as rk_gemv.
- * No counterpart in the reference (its GEMV kernels do not split K).
+ * rk_gemv with a caller-owned workspace for strategies that need split-K scratch.
+ * rk_gemv_workspace_size() tells how much the selected strategy uses: 0 for the
+ * default (cluster split-K, reduced through distributed shared memory), nonzero when
+ * stream-K is selected with rk_gemv_tc_set_cluster(-1) -- K is then split over
+ * independent CTAs that meet in the workspace (fp32 partial tiles plus one ticket
+ * counter per 128-row tile; the last CTA of a tile adds the partials in a fixed
+ * order).  `workspace` must be zero-filled before its first use; every call leaves it
+ * zeroed again.  Calls that share a workspace must be ordered (same stream).
+ * NULL / too small: same as rk_gemv.  No counterpart in the reference.
  */
 RK_API rk_status rk_gemv_ex(const void* x, const void* weight, void* out, int64_t M,
                             int64_t N, int64_t K, rk_dtype dt, int variant,
@@ -120,8 +122,9 @@ RK_API rk_status rk_gemv_workspace_size(int64_t M, int64_t N, int64_t K, rk_dtyp
 #define RK_GEMV_FIXED_SCRATCH_BYTES (8u << 20)
 
 /*
- * The tensor-core GEMV (RK_GEMV_TC) for callers that cannot allocate device memory:
- * it allocates nothing and takes no workspace.  No counterpart in the reference.
+ * The stream-K tensor-core GEMV -- the variant that needs split-K scratch -- for
+ * callers that cannot allocate device memory: it allocates nothing and takes no
+ * workspace.  No counterpart in the reference.
  *
  * Who needs it: plugins hosted by an engine that owns all device allocations and
  * gives a custom op only its input and output buffers, and latency-critical serving

@@ -623,24 +623,25 @@ size_t sk_ticket_bytes(int64_t N) {
   return ((static_cast<size_t>((N + gtc::BM - 1) / gtc::BM) * sizeof(int) + 255) / 256) * 256;
 }
 
-// Stream-K pays a workspace fix-up per shared tile, which costs more than it gains
-// while cluster split-K (<= 4 CTAs per tile) still puts a CTA on most SMs; it is used
-// only for weights too short for that (fewer than SMs/8 row tiles).
-bool sk_preferred(int64_t N) {
-  const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
-  return tiles * 8 < device_sm_count();
-}
-
-size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
-  if (!sk_preferred(N) && g_gemv_tc_cluster.load() != -1) return 0;
+// Stream-K workspace bytes (ticket counters + two partial slots per CTA).
+size_t sk_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   const int mn = M <= 16 ? 16 : 32;
   return sk_ticket_bytes(N) + static_cast<size_t>(sk_grid(M, N, K)) * 2 * gtc::BM * mn * sizeof(float);
+}
+
+// Workspace the automatic strategy can use.  Measured on B200, cluster split-K beats
+// stream-K at every weight size (stream-K's workspace fix-up and its per-CTA TMA rate
+// cost more than its perfect balance gains), so the automatic strategy uses no
+// workspace; stream-K runs when selected explicitly (tuning value -1) or through
+// rk_gemv_fixed_scratch.
+size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
+  return g_gemv_tc_cluster.load() == -1 ? sk_workspace_bytes(M, N, K) : 0;
 }
 
 template <typename T, int MN>
 rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
                          rk_dtype dt, cudaStream_t s, int csize_override, void* workspace,
-                         size_t workspace_bytes) {
+                         size_t workspace_bytes, bool stream_k) {
   CUtensorMap tw, tx;
   rk_status st = make_tmap_2d(&tw, W, dt, K, N, 64, gtc::BM);
   if (st != RK_OK) return st;
@@ -663,9 +664,8 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
 
   const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
   const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
-  const size_t need = workspace_bytes_for(M, N, K);
-  if ((csize_override == 0 || csize_override == -1) && need > 0 && workspace != nullptr &&
-      workspace_bytes >= need) {
+  const size_t need = sk_workspace_bytes(M, N, K);
+  if ((stream_k || csize_override == -1) && workspace != nullptr && workspace_bytes >= need) {
     // Stream-K over all SMs, shared tiles meet in the caller's workspace.
     constexpr int sk_smem = gtc::sk_smem_bytes<MN>();
     static std::once_flag sk_once[64];
@@ -719,6 +719,7 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
 }  // namespace
 
 size_t gemv_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) { return workspace_bytes_for(M, N, K); }
+size_t gemv_tc_stream_k_bytes(int64_t M, int64_t N, int64_t K) { return sk_workspace_bytes(M, N, K); }
 
 void gemv_tc_set_cluster(int c) { g_gemv_tc_cluster.store(c); }
 
@@ -733,24 +734,26 @@ bool gemv_tc_supported(const void* x, const void* W, const void* out, int64_t M,
 }
 
 rk_status gemv_tc_launch(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
-                         rk_dtype dt, cudaStream_t s, void* workspace, size_t workspace_bytes) {
+                         rk_dtype dt, cudaStream_t s, void* workspace, size_t workspace_bytes,
+                         bool stream_k) {
   if (!gemv_tc_supported(x, W, out, M, N, K)) return RK_ERR_UNSUPPORTED;
   const int c = g_gemv_tc_cluster.load();
   if (M <= 16) {
     if (dt == RK_DTYPE_BF16)
-      return launch_gemv_tc<__nv_bfloat16, 16>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes);
-    return launch_gemv_tc<__half, 16>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes);
+      return launch_gemv_tc<__nv_bfloat16, 16>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes, stream_k);
+    return launch_gemv_tc<__half, 16>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes, stream_k);
   }
   if (dt == RK_DTYPE_BF16)
-    return launch_gemv_tc<__nv_bfloat16, 32>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes);
-  return launch_gemv_tc<__half, 32>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes);
+    return launch_gemv_tc<__nv_bfloat16, 32>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes, stream_k);
+  return launch_gemv_tc<__half, 32>(x, W, out, M, N, K, dt, s, c, workspace, workspace_bytes, stream_k);
 }
 
 }  // namespace rk
 
 // ---------------------------------------------------------------------------
-// rk_gemv_fixed_scratch: the tensor-core GEMV with its split-K scratch taken from
-// a fixed array compiled into this library instead of from the caller.
+// rk_gemv_fixed_scratch: the stream-K tensor-core GEMV (the variant that needs split-K
+// scratch) with that scratch taken from a fixed array compiled into this library
+// instead of from the caller.
 //
 // Some callers cannot hand the library device memory for scratch: plugins hosted
 // by an engine that owns every device allocation and passes a custom op only its
@@ -789,14 +792,12 @@ extern "C" rk_status rk_gemv_fixed_scratch(const void* x, const void* weight, vo
   FixedScratch& fs = g_fixed_scratch[dev];
   std::call_once(fs.once, [&fs] { fs.err = cudaGetSymbolAddress(&fs.ptr, g_gemv_fixed_scratch); });
   if (fs.err != cudaSuccess || fs.ptr == nullptr) return cuda_status(fs.err);
-  const size_t need = gemv_tc_workspace_bytes(M, N, K);
+  const size_t need = gemv_tc_stream_k_bytes(M, N, K);
   if (need > RK_GEMV_FIXED_SCRATCH_BYTES) return RK_ERR_TOO_LARGE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (need > 0) {
-    // The array keeps whatever the previous call left; the split-K tickets at its
-    // start must be zero when the kernel begins.
-    const rk_status st = cuda_status(cudaMemsetAsync(fs.ptr, 0, sk_ticket_bytes(N), s));
-    if (st != RK_OK) return st;
-  }
-  return gemv_tc_launch(x, weight, out, M, N, K, dt, s, need > 0 ? fs.ptr : nullptr, need);
+  // The array keeps whatever the previous call left; the split-K tickets at its start
+  // must be zero when the kernel begins.
+  const rk_status st = cuda_status(cudaMemsetAsync(fs.ptr, 0, sk_ticket_bytes(N), s));
+  if (st != RK_OK) return st;
+  return gemv_tc_launch(x, weight, out, M, N, K, dt, s, fs.ptr, RK_GEMV_FIXED_SCRATCH_BYTES, true);
 }

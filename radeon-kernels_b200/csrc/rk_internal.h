@@ -41,8 +41,10 @@ rk_status gemv_scalar_launch(const void* x, const void* W, void* out, int64_t M,
 rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,
                              int64_t K, rk_dtype dt, cudaStream_t s);
 rk_status gemv_tc_launch(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
-                         rk_dtype dt, cudaStream_t s, void* workspace, size_t workspace_bytes);
+                         rk_dtype dt, cudaStream_t s, void* workspace, size_t workspace_bytes,
+                         bool stream_k = false);
 size_t gemv_tc_workspace_bytes(int64_t M, int64_t N, int64_t K);
+size_t gemv_tc_stream_k_bytes(int64_t M, int64_t N, int64_t K);
 bool gemv_tc_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,
                        int64_t K);
 bool gemv_stream_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,

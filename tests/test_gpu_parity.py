@@ -310,7 +310,7 @@ def test_gemv_tensor_core_cluster_split_k(cluster, m):
 
 
 @pytest.mark.parametrize("m", [3, 5, 16, 17, 32])
-@pytest.mark.parametrize("n, k", [(1000, 4104), (640, 14336), (2048, 8192)])
+@pytest.mark.parametrize("n, k", [(1000, 4104), (640, 14336), (8192, 8192)])
 def test_gemv_tensor_core_workspace_split_k(m, n, k):
     """rk_gemv_ex: stream-K over independent CTAs meeting in a caller-owned workspace."""
 
@@ -324,16 +324,34 @@ def test_gemv_tensor_core_workspace_split_k(m, n, k):
     o_bits, o32 = oracle.gemv(to_bits(x), to_bits(w), "bf16")
     lib = _native.library()
     need = ctypes.c_size_t(0)
-    assert lib.rk_gemv_workspace_size(m, n, k, 1, GEMV["tc"], ctypes.byref(need)) == _native.RK_OK
-    assert need.value > 0  # short weights: stream-K with a workspace
-    ws = torch.zeros(need.value + 4096, dtype=torch.uint8, device="cuda")
-    xd, wd = x.cuda(), w.cuda()
+    lib.rk_gemv_tc_set_cluster(-1)  # select stream-K (the workspace strategy)
+    try:
+        assert lib.rk_gemv_workspace_size(m, n, k, 1, GEMV["tc"], ctypes.byref(need)) == _native.RK_OK
+        assert need.value > 0
+        ws = torch.zeros(need.value + 4096, dtype=torch.uint8, device="cuda")
+        outs = _run_stream_k(lib, x.cuda(), w.cuda(), ws, need.value, m, n, k)
+    finally:
+        lib.rk_gemv_tc_set_cluster(0)
+    tiles = (n + 127) // 128
+    assert int(ws[: 4 * tiles].view(torch.int32).abs().sum().item()) == 0  # tickets re-zeroed
+    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
+    oracle.assert_parity(to_bits(outs[0]), o_bits, o32, "bf16")
+    ws_default = ctypes.c_size_t(1)
+    assert lib.rk_gemv_workspace_size(m, n, k, 1, GEMV["tc"], ctypes.byref(ws_default)) == _native.RK_OK
+    assert ws_default.value == 0  # the default strategy needs no workspace
+
+
+def _run_stream_k(lib, xd, wd, ws, need, m, n, k):
+    import ctypes
+
+    import torch
+
     outs = []
     for _ in range(2):  # the second call relies on the first leaving the tickets zeroed
         buf, out = _guarded(torch, m, n, "bf16")
         st = lib.rk_gemv_ex(
             ctypes.c_void_p(xd.data_ptr()), ctypes.c_void_p(wd.data_ptr()), ctypes.c_void_p(out.data_ptr()),
-            m, n, k, 1, GEMV["tc"], ctypes.c_void_p(ws.data_ptr()), need.value,
+            m, n, k, 1, GEMV["tc"], ctypes.c_void_p(ws.data_ptr()), need,
             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
         )
         assert st == _native.RK_OK, _native.status_text(st)
@@ -341,10 +359,7 @@ def test_gemv_tensor_core_workspace_split_k(m, n, k):
         assert _guards_intact(buf)
         outs.append(out.clone())
     assert device_status() == _native.RK_OK
-    tiles = (n + 127) // 128
-    assert int(ws[: 4 * tiles].view(torch.int32).abs().sum().item()) == 0  # tickets re-zeroed
-    assert torch.equal(outs[0].view(torch.int16), outs[1].view(torch.int16))
-    oracle.assert_parity(to_bits(outs[0]), o_bits, o32, "bf16")
+    return outs
 
 
 def test_gather_column_blocks_matches_permute():

@@ -2,11 +2,11 @@
 
 It exists for callers that cannot give the library device memory: plugins hosted by
 an engine that owns every device allocation and hands a custom op only its inputs and
-outputs, and serving loops that must not call cudaMalloc on the hot path.  Its split-K
-scratch is a fixed array inside the library.  Here it is checked, through the C ABI,
-against the workspace entry point rk_gemv_ex (caller-owned scratch) on two calls in a
-row: the second call must still be right although the array keeps the first call's
-contents.  Collected last on purpose, and self-contained so it also passes alone in a
+outputs, and serving loops that must not call cudaMalloc on the hot path.  It runs the
+stream-K tensor-core GEMV, whose split-K scratch is a fixed array inside the library.
+Here it is checked, through the C ABI, against the existing entry point rk_gemv_ex on
+two calls in a row: the second call must still be right although the array keeps the
+first call's contents.  Collected last on purpose, and self-contained so it also passes alone in a
 fresh process.
 """
 
@@ -31,7 +31,7 @@ def _stream():
 
 @pytest.mark.parametrize(
     "dtype, m, n, k",
-    [("bf16", 5, 2048, 8192), ("fp16", 16, 640, 14336), ("bf16", 32, 1000, 4104), ("fp16", 3, 40000, 512)],
+    [("bf16", 5, 8192, 8192), ("fp16", 16, 4096, 14336), ("bf16", 32, 1000, 4104), ("fp16", 3, 40000, 512)],
 )
 def test_fixed_scratch_matches_the_workspace_entry_point(dtype, m, n, k):
     import torch
