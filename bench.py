@@ -11,8 +11,10 @@ an N x 8192-row weight (N-row sharding, weak scaling, no data-path collective).
 
 ``e2e``: the same GEMV through the public ``radeon_kernels.gemv`` call (dispatch, pack
 winner) with the step's activation copied host->device from pinned memory and the result
-copied back every step; at N>1 the per-rank output blocks are all-gathered (NCCL) first,
-as a caller that needs the full output would.
+copied back every step.  At N=1 the steps are captured from those calls into a CUDA graph
+whose copies run on forked streams and overlap neighbouring kernels (``eager_serial``
+keeps the serialised per-call figure); at N>1 the per-rank output blocks are
+all-gathered (NCCL) first, as a caller that needs the full output would, eagerly.
 
 ``suite``: the other BASELINE configs measured in the same run (GEMM TFLOP/s with the
 tcgen05 kernel, FFN-down GEMV at M = 1/4/16), each with its roofline fraction.
@@ -280,22 +282,40 @@ def headline(args, dist: Dist, ext, peaks, peak_kind):
     }
 
 
+E2E_GRAPH_STEPS = 16  # independent steps captured in one CUDA graph (multiple of ROTATE)
+
+
 def e2e(args, dist: Dist):
-    """The same GEMV through the public API with host buffers, copies inside the region."""
+    """The same GEMV through the public API with host buffers, copies inside the region.
+
+    Every step copies its activation host->device from pinned memory, calls
+    ``radeon_kernels.gemv`` (validation, dispatch, pack winner) and copies the result back
+    into pinned memory.  At N = 1 the reported value comes from a CUDA graph captured from
+    those calls: 16 independent steps, H2D copies on a forked copy stream and each D2H
+    on a second stream right after its kernel, so copy-engine latency overlaps neighbouring
+    kernels; ``eager_serial`` is the same step issued eagerly with copy, kernel and copy
+    serialised on one stream (the per-call latency).  At N > 1 each step also all-gathers
+    the rank blocks (NCCL) and runs eagerly (no NCCL inside a graph).
+    """
 
     import torch
 
     import radeon_kernels as rk
+    from radeon_kernels.distributed import all_gather_columns
 
     m, n, k = 1, 8192, 8192
     weights = [seeded((n, k), 100 + 17 * dist.rank + r, "normal/8192", "bf16") for r in range(ROTATE)]
+    bytes_step = gemv_bytes(m, n, k)
+    stream = torch.cuda.current_stream()
+
+    def rate(ms, steps):
+        return round(bytes_step * steps * dist.world / (ms / 1e3) / 1e9, 1)
+
+    # Eager, serialised: copy in, GEMV, (all-gather), copy out, one stream.
     x_host = seeded((m, k), 1, "normal", "bf16", device="cpu").pin_memory()
     out_host = torch.empty((m, n * dist.world), dtype=torch.bfloat16).pin_memory()
     x_dev = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
     full = torch.empty((m, n * dist.world), dtype=torch.bfloat16, device="cuda") if dist.world > 1 else None
-    from radeon_kernels.distributed import all_gather_columns
-
-    stream = torch.cuda.current_stream()
 
     def step(i):
         x_dev.copy_(x_host, non_blocking=True)
@@ -309,21 +329,88 @@ def e2e(args, dist: Dist):
         step(i)
     torch.cuda.synchronize()
     selected = rk.get_last_dispatch()["selected"]
-    steps = max(args.e2e_steps, 10)
+    eager_steps = max(args.e2e_steps // (1 if dist.world > 1 else 4), 10)
     dist.barrier()
     torch.cuda.synchronize()
-    ms = time_loop(step, steps, stream)
+    eager_ms = dist.max(time_loop(step, eager_steps, stream))
     dist.barrier()
-    ms = dist.max(ms)
-    bytes_step = gemv_bytes(m, n, k)
-    return {
-        "value": round(bytes_step * steps * dist.world / (ms / 1e3) / 1e9, 1),
+    eager = {"value": rate(eager_ms, eager_steps), "ms_per_step": round(eager_ms / eager_steps, 5)}
+    result = {
         "unit": "GB/s",
         "h2d_bytes_per_step": m * k * 2,
         "d2h_bytes_per_step": m * n * dist.world * 2,
-        "ms_per_step": round(ms / steps, 5),
-        "path": f"radeon_kernels.gemv -> {selected}" + (" + NCCL all-gather + rk_gather_column_blocks" if dist.world > 1 else ""),
     }
+    if dist.world > 1:
+        result.update(eager)
+        result["path"] = (f"eager: H2D copy, radeon_kernels.gemv -> {selected}, NCCL all-gather + "
+                          "rk_gather_column_blocks, D2H copy; one stream")
+        return result
+
+    G = E2E_GRAPH_STEPS
+    xs_host = seeded((G, m, k), 2, "normal", "bf16", device="cpu").pin_memory()
+    outs_host = torch.empty((G, m, n), dtype=torch.bfloat16).pin_memory()
+    xs_dev = torch.empty((G, m, k), dtype=torch.bfloat16, device="cuda")
+    h2d = torch.cuda.Stream()
+    d2h = torch.cuda.Stream()
+    cap = torch.cuda.Stream()
+    kept = []
+
+    def graph_body():
+        here = torch.cuda.current_stream()
+        h2d.wait_stream(here)
+        d2h.wait_stream(here)
+        ready = []
+        with torch.cuda.stream(h2d):
+            for i in range(G):
+                xs_dev[i].copy_(xs_host[i], non_blocking=True)
+                ready.append(torch.cuda.Event())
+                ready[-1].record(h2d)
+        for i in range(G):
+            here.wait_event(ready[i])
+            y = rk.gemv(xs_dev[i], weights[i % ROTATE])
+            kept.append(y)
+            done = torch.cuda.Event()
+            done.record(here)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                outs_host[i].copy_(y, non_blocking=True)
+        here.wait_stream(h2d)
+        here.wait_stream(d2h)
+
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        graph_body()  # eager warm-up: dispatch decisions and tensor maps are cached
+    torch.cuda.synchronize()
+    kept.clear()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        graph_body()
+    stream.wait_stream(cap)
+    torch.cuda.synchronize()
+    outs_host.zero_()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    # The graph's results are the eager API's results, bit for bit.
+    check = all(torch.equal(outs_host[i], rk.gemv(xs_dev[i], weights[i % ROTATE]).cpu()) for i in range(G))
+    if not check:
+        raise RuntimeError("e2e: graph-replayed rk.gemv results differ from eager calls")
+    replays = max(args.e2e_steps // G, 10)
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms = dist.max(time_loop(lambda i: graph.replay(), replays, stream))
+    dist.barrier()
+    del graph
+    steps = replays * G
+    result.update({
+        "value": rate(ms, steps),
+        "ms_per_step": round(ms / steps, 5),
+        "path": (f"CUDA graph of {G} captured steps: pinned H2D copy (forked copy stream), "
+                 f"radeon_kernels.gemv -> {selected}, pinned D2H copy (second stream); "
+                 "outputs checked equal to eager calls"),
+        "eager_serial": eager,
+    })
+    return result
 
 
 def suite(args, dist: Dist, ext, peaks):

@@ -85,6 +85,7 @@ class DispatchingRuntime:
         # than a decode GEMV's kernel time.  Manifests and packs are immutable for the
         # lifetime of a runtime, so the decision cannot change; reset_*runtime() drops it.
         self._fast: dict[tuple, tuple[Any, Any, dict[str, Any]]] = {}
+        self._fast_positional: dict[tuple, tuple[Any, Any, dict[str, Any]]] = {}
 
     @property
     def pack_registry(self) -> KernelPackRegistry:
@@ -106,6 +107,26 @@ class DispatchingRuntime:
     @staticmethod
     def fast_key(operator: str, device_index: int, signature: Mapping[str, Any]) -> tuple:
         return (operator, device_index, tuple(sorted(signature.items())))
+
+    def fast_call(self, key: tuple, arguments: tuple[Any, ...]) -> Any | None:
+        """Run a cached winner for ``key`` (operator-specific positional key), or None."""
+
+        cached = self._fast_positional.get(key)
+        if cached is None:
+            return None
+        entry, launch, record = cached
+        result = entry(*arguments, **launch)
+        if result is None:
+            raise native.NativeProviderError("native entrypoint returned no output")
+        record_dispatch_shared(record)
+        return result
+
+    def fast_alias(self, key: tuple, signature_key: tuple) -> None:
+        """Let positional ``key`` reuse the cached winner stored under ``signature_key``."""
+
+        cached = self._fast.get(signature_key)
+        if cached is not None:
+            self._fast_positional[key] = cached
 
     def fast_lookup(self, key: tuple) -> tuple[Any, Any, dict[str, Any]] | None:
         return self._fast.get(key)

@@ -36,6 +36,14 @@ def _execute(x: Any, weight: Any, *, torch_module: Any, runtime: OperatorRuntime
     if weight_k != k:
         raise ValueError("gemv x and weight must share the K dimension")
     context = tensor_context(torch_module, "gemv", x, weight)
+    fast = getattr(runtime, "fast_call", None)
+    if fast is not None:
+        # Repeated calls: the decision for this exact signature is cached (no dict,
+        # no manifest scan, no pack resolution on the hot path).
+        key = ("gemv", context.device_index, context.dtype, m, n, k, context.contiguous, context.requires_grad)
+        result = fast(key, (x, weight))
+        if result is not None:
+            return result
     signature = {
         "dtype": context.dtype,
         "m": m,
@@ -45,7 +53,7 @@ def _execute(x: Any, weight: Any, *, torch_module: Any, runtime: OperatorRuntime
         "contiguous": context.contiguous,
         "requires_grad": context.requires_grad,
     }
-    return runtime.execute(
+    result = runtime.execute(
         operator="gemv",
         semantic_version=_SEMANTIC_VERSION,
         signature=signature,
@@ -55,6 +63,10 @@ def _execute(x: Any, weight: Any, *, torch_module: Any, runtime: OperatorRuntime
         fallback=lambda: cuda_builtin.gemv(torch_module, x, weight),
         fallback_selected=cuda_builtin.SELECTED_GEMV,
     )
+    alias = getattr(runtime, "fast_alias", None)
+    if fast is not None and alias is not None:
+        alias(key, runtime.fast_key("gemv", context.device_index, signature))
+    return result
 
 
 def gemv(x: Any, weight: Any) -> Any:
