@@ -174,6 +174,17 @@ RK_API void rk_gemm_set_tile_n(int tile_n);
  * Process-wide. */
 RK_API void rk_gemv_tc_set_cluster(int cluster_size);
 
+/* Programmatic dependent launch (on by default; no counterpart in the reference,
+ * whose kernels launch one after another).  When enabled every kernel of this
+ * library is launched with programmatic stream serialisation: it may be scheduled
+ * while the previous kernel in the stream is still finishing, runs its set-up
+ * (barrier initialisation, tensor-memory allocation, descriptor prefetch), then waits
+ * in griddepcontrol.wait until every earlier kernel of the stream has completed and
+ * its writes are visible, before it reads or writes global memory.  Results are
+ * identical either way; 0 disables it (kernels then start only after the previous
+ * kernel completes).  Returns the previous setting.  Process-wide. */
+RK_API int rk_set_programmatic_launch(int enable);
+
 /*
  * Reads and clears the device-side status word of the current device after
  * synchronising `stream`.  Returns RK_OK, or RK_ERR_TIMEOUT when a kernel

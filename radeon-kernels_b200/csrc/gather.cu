@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(256)
     gather_blocks_kernel(const V* __restrict__ blocks, V* __restrict__ out, int64_t G, int64_t M,
                          int64_t nb /* block row length in V units */) {
   const int64_t total = G * M * nb;
+  pdl_begin();
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total;
        i += int64_t(gridDim.x) * blockDim.x) {
     // i enumerates the destination: row m, block g, offset j.
@@ -40,15 +41,18 @@ rk_status gather_column_blocks_launch(const void* blocks, void* out, int64_t G, 
   if (nb % 8 == 0 && aligned16(blocks) && aligned16(out)) {
     const int64_t units = total / 8;
     const int grid = static_cast<int>(units / 256 + 1 < grid_cap ? units / 256 + 1 : grid_cap);
-    gather_blocks_kernel<uint4><<<grid, 256, 0, s>>>(static_cast<const uint4*>(blocks),
-                                                     static_cast<uint4*>(out), G, M, nb / 8);
-  } else {
-    const int grid = static_cast<int>(total / 256 + 1 < grid_cap ? total / 256 + 1 : grid_cap);
-    gather_blocks_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(blocks),
-                                                        static_cast<uint16_t*>(out), G, M, nb);
+    const cudaError_t e = launch_kernel(gather_blocks_kernel<uint4>, dim3(grid), dim3(256), 0, s, 0,
+                                        static_cast<const uint4*>(blocks), static_cast<uint4*>(out),
+                                        G, M, nb / 8);
+    note_launch();
+    return cuda_status(e);
   }
+  const int grid = static_cast<int>(total / 256 + 1 < grid_cap ? total / 256 + 1 : grid_cap);
+  const cudaError_t e = launch_kernel(gather_blocks_kernel<uint16_t>, dim3(grid), dim3(256), 0, s, 0,
+                                      static_cast<const uint16_t*>(blocks),
+                                      static_cast<uint16_t*>(out), G, M, nb);
   note_launch();
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
 }  // namespace rk

@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(256)
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * TM;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * TN;
   float acc[4][4] = {};
+  pdl_begin();
   for (int64_t k0 = 0; k0 < K; k0 += TK) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -71,16 +72,17 @@ rk_status gemm_simt_launch(const void* A, const void* B, void* C, int64_t M, int
   const int64_t gx = (N + TN - 1) / TN, gy = (M + TM - 1) / TM;
   if (gx > 0x7fffffffll || gy > 65535) return RK_ERR_UNSUPPORTED;
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+  cudaError_t e;
   if (dt == RK_DTYPE_BF16)
-    gemm_simt_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(B),
-        static_cast<__nv_bfloat16*>(C), M, N, K);
+    e = launch_kernel(gemm_simt_kernel<__nv_bfloat16>, grid, dim3(256), 0, s, 0,
+                      static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(B),
+                      static_cast<__nv_bfloat16*>(C), M, N, K);
   else
-    gemm_simt_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(A),
-                                                   static_cast<const __half*>(B),
-                                                   static_cast<__half*>(C), M, N, K);
+    e = launch_kernel(gemm_simt_kernel<__half>, grid, dim3(256), 0, s, 0,
+                      static_cast<const __half*>(A), static_cast<const __half*>(B),
+                      static_cast<__half*>(C), M, N, K);
   note_launch();
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
 }  // namespace rk

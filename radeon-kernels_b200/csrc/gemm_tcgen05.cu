@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  pdl_begin();  // global memory is touched only after this
 
   if (warp == 0) {
     if (lane == 0) {
@@ -316,11 +317,12 @@ rk_status launch_tc1(const void* A, const void* B, void* C, int64_t M, int64_t N
 
   const int64_t num_tiles = ((M + tc1::BM - 1) / tc1::BM) * ((N + BN - 1) / BN);
   const int grid = static_cast<int>(num_tiles < device_sm_count() ? num_tiles : device_sm_count());
-  tc1::gemm_tc1_kernel<T, BN><<<grid, tc1::THREADS, smem, s>>>(
-      ta, tb, reinterpret_cast<T*>(C), static_cast<int>(M), static_cast<int>(N),
-      static_cast<int>(K), ctl);
+  const cudaError_t e = launch_kernel(tc1::gemm_tc1_kernel<T, BN>, dim3(grid), dim3(tc1::THREADS),
+                                      smem, s, 0, ta, tb, reinterpret_cast<T*>(C),
+                                      static_cast<int>(M), static_cast<int>(N),
+                                      static_cast<int>(K), ctl);
   note_launch();
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
 // Tile width for a problem: fewest "waves" of persistent tiles weighted by the

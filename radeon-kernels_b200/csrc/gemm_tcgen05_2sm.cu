@@ -117,6 +117,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   cluster_sync_all();  // both CTAs' barriers exist before either signals the other
   const uint32_t tmem_base = bars->tmem_base;
+  pdl_begin();  // global memory is touched only after this
 
   if (warp == 0) {
     if (lane == 0) {
@@ -297,21 +298,10 @@ rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N
   const int64_t pairs_max = device_sm_count() / 2;
   const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
-  cfg.blockDim = dim3(tc2::THREADS);
-  cfg.dynamicSmemBytes = tc2::SMEM_BYTES;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, tc2::gemm_tc2_kernel<T>, ta, tb,
-                                           reinterpret_cast<T*>(C), static_cast<int>(M),
-                                           static_cast<int>(N), static_cast<int>(K), ctl);
+  const cudaError_t e = launch_kernel(tc2::gemm_tc2_kernel<T>, dim3(static_cast<unsigned>(2 * pairs)),
+                                      dim3(tc2::THREADS), tc2::SMEM_BYTES, s, 2, ta, tb,
+                                      reinterpret_cast<T*>(C), static_cast<int>(M),
+                                      static_cast<int>(N), static_cast<int>(K), ctl);
   note_launch();
   return cuda_status(e);
 }

@@ -117,6 +117,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   constexpr int LOGV = Log2<V>::value;
   extern __shared__ float red[];  // [KS][rows_max][MB]
 
+  pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int cta = blockIdx.x;
@@ -188,6 +189,7 @@ template <typename T, int MB>
 __global__ void __launch_bounds__(256)
     gemv_scalar_kernel(const T* __restrict__ x, const T* __restrict__ W, T* __restrict__ out,
                        int M, int N, int K) {
+  pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= N) return;
@@ -217,9 +219,10 @@ struct StreamLaunch {
 template <typename T, int MB, int ROWS, int KS>
 void launch_stream(const void* x, const void* W, void* out, int M, int N, int K, int grid,
                    int rows_base, int rows_rem, int rows_max, size_t smem, cudaStream_t s) {
-  gemv_stream_kernel<T, MB, ROWS, KS><<<grid, GEMV_THREADS, smem, s>>>(
-      static_cast<const T*>(x), static_cast<const T*>(W), static_cast<T*>(out), M, N, K,
-      rows_base, rows_rem, rows_max);
+  // Launch errors are left for the caller's cudaGetLastError().
+  (void)launch_kernel(gemv_stream_kernel<T, MB, ROWS, KS>, dim3(grid), dim3(GEMV_THREADS), smem, s, 0,
+                      static_cast<const T*>(x), static_cast<const T*>(W), static_cast<T*>(out), M, N,
+                      K, rows_base, rows_rem, rows_max);
 }
 
 template <typename T, int MB, int ROWS, int KS>
@@ -351,14 +354,14 @@ rk_status gemv_scalar_launch(const void* x, const void* W, void* out, int64_t M,
 #define RK_SCALAR_CASE(MBV)                                                                       \
   case MBV:                                                                                       \
     if (dt == RK_DTYPE_BF16)                                                                      \
-      gemv_scalar_kernel<__nv_bfloat16, MBV><<<grid, 256, 0, s>>>(                                \
-          static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(W),             \
-          static_cast<__nv_bfloat16*>(out), int(M), int(N), int(K));                              \
+      (void)launch_kernel(gemv_scalar_kernel<__nv_bfloat16, MBV>, dim3(grid), dim3(256), 0, s, 0, \
+                          static_cast<const __nv_bfloat16*>(x),                                   \
+                          static_cast<const __nv_bfloat16*>(W),                                   \
+                          static_cast<__nv_bfloat16*>(out), int(M), int(N), int(K));              \
     else                                                                                          \
-      gemv_scalar_kernel<__half, MBV><<<grid, 256, 0, s>>>(static_cast<const __half*>(x),        \
-                                                           static_cast<const __half*>(W),        \
-                                                           static_cast<__half*>(out), int(M),    \
-                                                           int(N), int(K));                      \
+      (void)launch_kernel(gemv_scalar_kernel<__half, MBV>, dim3(grid), dim3(256), 0, s, 0,        \
+                          static_cast<const __half*>(x), static_cast<const __half*>(W),           \
+                          static_cast<__half*>(out), int(M), int(N), int(K));                     \
     break;
   switch (mb) {
     RK_SCALAR_CASE(1)

@@ -115,13 +115,7 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[MN]);
 
 template <>
 __device__ __forceinline__ void tmem_ld_cols<16>(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+  tmem_ld_32x32b_x16(taddr, r);
 }
 
 template <>
@@ -172,6 +166,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   // weight stream starts without a cluster-wide handshake on its critical path.
   cluster_arrive();
   const uint32_t tmem_base = bars->tmem_base;
+  pdl_begin();  // global memory is touched only after this
 
   if (warp == 0) {
     if (lane == 0) {
@@ -430,6 +425,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  pdl_begin();  // global memory is touched only after this
 
   if (warp == 0) {
     if (lane == 0) {
@@ -569,17 +565,35 @@ __global__ void __launch_bounds__(THREADS, 2)
           __threadfence();
 #pragma unroll
           for (int j = 0; j < MN; ++j) a[j] = 0.f;
-          for (int c = c_first; c <= c_last; ++c) {
-            const int first_tile_of_c = static_cast<int>(sk_unit_start(c, units, grid) / num_kb);
-            const float* src = part + (static_cast<size_t>(c) * 2 + (first_tile_of_c == tile ? 0 : 1)) * BM * MN +
-                               static_cast<size_t>(row_local) * MN;
+          // Partials are loaded PF CTAs at a time (all loads in flight before the adds,
+          // so a tile shared by many CTAs costs a few L2 round trips, not one per CTA)
+          // and added in CTA order, which keeps the result deterministic.
+          constexpr int PF = MN <= 16 ? 4 : 2;
+          for (int c0 = c_first; c0 <= c_last; c0 += PF) {
+            float4 v[PF][MN / 4];
 #pragma unroll
-            for (int j = 0; j < MN; j += 4) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(src + j));
-              a[j] += v.x;
-              a[j + 1] += v.y;
-              a[j + 2] += v.z;
-              a[j + 3] += v.w;
+            for (int q = 0; q < PF; ++q) {
+              const int c = c0 + q;
+              if (c <= c_last) {
+                // Slot 0 holds a CTA's first segment; its tile is the one containing its first unit.
+                const bool first_seg = sk_unit_start(c, units, grid) >= static_cast<int64_t>(tile) * num_kb;
+                const float* src = part + (static_cast<size_t>(c) * 2 + (first_seg ? 0 : 1)) * BM * MN +
+                                   static_cast<size_t>(row_local) * MN;
+#pragma unroll
+                for (int j = 0; j < MN / 4; ++j) v[q][j] = __ldcg(reinterpret_cast<const float4*>(src) + j);
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < PF; ++q) {
+              if (c0 + q <= c_last) {
+#pragma unroll
+                for (int j = 0; j < MN / 4; ++j) {
+                  a[4 * j] += v[q][j].x;
+                  a[4 * j + 1] += v[q][j].y;
+                  a[4 * j + 2] += v[q][j].z;
+                  a[4 * j + 3] += v[q][j].w;
+                }
+              }
             }
           }
           if (warp == 2 && lane == 0) ticket[tile] = 0;
@@ -677,11 +691,12 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
     if (sk_err[dev & 63] != cudaSuccess) return cuda_status(sk_err[dev & 63]);
     int* ticket = static_cast<int*>(workspace);
     float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + sk_ticket_bytes(N));
-    gtc::gemv_tc_sk_kernel<T, MN><<<sk_grid(M, N, K), gtc::THREADS, sk_smem, s>>>(
-        tw, tx, static_cast<T*>(out), static_cast<int>(M), static_cast<int>(N),
-        static_cast<int>(K), part, ticket, ctl);
+    const cudaError_t e = launch_kernel(gtc::gemv_tc_sk_kernel<T, MN>, dim3(sk_grid(M, N, K)),
+                                        dim3(gtc::THREADS), sk_smem, s, 0, tw, tx,
+                                        static_cast<T*>(out), static_cast<int>(M),
+                                        static_cast<int>(N), static_cast<int>(K), part, ticket, ctl);
     note_launch();
-    return cuda_status(cudaGetLastError());
+    return cuda_status(e);
   }
   // Split K over a thread-block cluster, reduced through DSMEM: the largest cluster of
   // at most 4 CTAs (8-CTA clusters measured slower) keeping the grid within two CTAs per SM.
@@ -697,21 +712,10 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
   while (csize > 1 && csize > num_kb) csize /= 2;
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(tiles * csize));
-  cfg.blockDim = dim3(gtc::THREADS);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gtc::gemv_tc_kernel<T, MN>, tw, tx,
-                                           static_cast<T*>(out), static_cast<int>(M),
-                                           static_cast<int>(N), static_cast<int>(K), csize, ctl);
+  const cudaError_t e = launch_kernel(gtc::gemv_tc_kernel<T, MN>, dim3(static_cast<unsigned>(tiles * csize)),
+                                      dim3(gtc::THREADS), smem, s, csize, tw, tx,
+                                      static_cast<T*>(out), static_cast<int>(M),
+                                      static_cast<int>(N), static_cast<int>(K), csize, ctl);
   note_launch();
   return cuda_status(e);
 }

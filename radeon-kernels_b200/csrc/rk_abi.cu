@@ -73,6 +73,13 @@ rk_status cuda_status(cudaError_t e) {
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+namespace {
+std::atomic<bool> g_pdl{true};
+}  // namespace
+
+bool programmatic_launch() { return g_pdl.load(std::memory_order_relaxed); }
+bool set_programmatic_launch(bool enable) { return g_pdl.exchange(enable); }
+
 int device_sm_count() {
   DeviceInfo* d = current_device_info();
   return d ? d->sm_count : 1;
@@ -129,6 +136,8 @@ void rk_gemv_set_tuning(int rows, int ksplit) { rk::gemv_set_tuning(rows, ksplit
 void rk_gemm_set_tile_n(int tile_n) { rk::gemm_set_tile_n(tile_n); }
 
 void rk_gemv_tc_set_cluster(int cluster_size) { rk::gemv_tc_set_cluster(cluster_size); }
+
+int rk_set_programmatic_launch(int enable) { return rk::set_programmatic_launch(enable != 0) ? 1 : 0; }
 
 const char* rk_variant_name(int op, int variant) {
   if (op == 0) {

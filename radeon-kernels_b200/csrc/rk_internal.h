@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <utility>
 
 #include "rk_kernels.h"
 
@@ -22,6 +23,39 @@ int device_sm_count();
 int device_cc_major();
 // Counts one kernel launch (rk_launch_count()).
 void note_launch();
+// Programmatic dependent launch switch (rk_set_programmatic_launch()).
+bool programmatic_launch();
+bool set_programmatic_launch(bool enable);
+
+// Launches `kernel` with programmatic stream serialisation when it is enabled (the
+// kernel must call pdl_begin() before touching global memory) and, for cluster > 0,
+// with that thread-block cluster size along x.
+template <typename... Params, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t s, int cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (programmatic_launch()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 // Maps a CUDA error to a status code (and remembers the message).
 rk_status cuda_status(cudaError_t e);
 

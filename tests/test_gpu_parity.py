@@ -385,3 +385,70 @@ def test_gather_column_blocks_matches_permute():
     )
     assert st == _native.RK_OK
     assert torch.equal(out, blocks.permute(1, 0, 2).reshape(m, g * nb))
+
+
+@pytest.mark.parametrize(
+    "op, variant, m, n, k",
+    [
+        ("gemv", "stream", 1, 4096, 4096),
+        ("gemv", "tc", 16, 4096, 4096),
+        ("gemm", "tc_1sm", 512, 1024, 1024),
+        ("gemm", "tc_2sm", 512, 1024, 1024),
+    ],
+)
+def test_programmatic_launch_is_result_neutral(op, variant, m, n, k):
+    """Back-to-back launches with programmatic dependent launch on and off agree bit for bit.
+
+    Each launch reads the previous launch's output directly as its input (a chain with
+    N == K, no other kernel in between), so a kernel that touched global memory before its
+    predecessor finished would read a stale operand.
+    """
+
+    import torch
+
+    lib = _native.library()
+    gen = torch.Generator().manual_seed(23)
+    dtype = "bf16"
+    chain = 4
+    if op == "gemv":
+        w_cpu = seeded((n, k), 23, f"normal/{k}", dtype, gen)
+        x_cpu = seeded((m, k), 23, "normal", dtype, gen)
+        w = w_cpu.cuda()
+        results = {}
+        for pdl in (0, 1):
+            prev = lib.rk_set_programmatic_launch(pdl)
+            try:
+                xs = [x_cpu.cuda()]
+                for _ in range(chain):
+                    out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+                    assert abi_gemv(xs[-1], w, out, GEMV[variant], dtype) == _native.RK_OK
+                    xs.append(out)
+                torch.cuda.synchronize()
+                assert device_status() == _native.RK_OK
+            finally:
+                lib.rk_set_programmatic_launch(prev)
+            results[pdl] = [t.cpu() for t in xs[1:]]
+        first_bits, first32 = oracle.gemv(to_bits(x_cpu), to_bits(w_cpu), dtype)
+    else:
+        a_cpu = seeded((m, k), 23, "normal", dtype, gen)
+        b_cpu = seeded((k, n), 24, f"normal/{k}", dtype, gen)
+        b = b_cpu.cuda()
+        results = {}
+        for pdl in (0, 1):
+            prev = lib.rk_set_programmatic_launch(pdl)
+            try:
+                xs = [a_cpu.cuda()]
+                for _ in range(chain):
+                    c = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+                    assert abi_gemm(xs[-1], b, c, GEMM[variant], dtype) == _native.RK_OK
+                    xs.append(c)
+                torch.cuda.synchronize()
+                assert device_status() == _native.RK_OK
+            finally:
+                lib.rk_set_programmatic_launch(prev)
+            results[pdl] = [t.cpu() for t in xs[1:]]
+        first_bits, first32 = oracle.gemm(to_bits(a_cpu), to_bits(b_cpu), dtype)
+    for on, off in zip(results[1], results[0]):
+        assert torch.equal(on.view(torch.int16), off.view(torch.int16))
+    first = results[1][0]
+    oracle.assert_parity(to_bits(first), first_bits, first32, dtype)
