@@ -101,15 +101,16 @@ RK_API rk_status rk_gemv(const void* x, const void* weight, void* out, int64_t M
 
 /*
  * rk_gemv with a caller-owned workspace for strategies that need split-K scratch.
- * rk_gemv_workspace_size() tells how much the selected strategy uses: 0 for the
- * default (cluster split-K, reduced through distributed shared memory), nonzero when
- * stream-K is selected with rk_gemv_tc_set_cluster(-1) -- K is then split over
- * independent CTAs that meet in the workspace (fp32 partial tiles plus one ticket
- * counter per 128-row tile; the last CTA of a tile adds the partials in a fixed
- * order).  `workspace` must be zero-filled before its first use; every call leaves it
- * zeroed again.  Calls that share a workspace must be ordered (same stream).
- * NULL / too small: same as rk_gemv.  No counterpart in the reference.
+ * rk_gemv_workspace_size() tells how much the selected strategy uses (0: none).
+ * Strategies that use it split K over independent CTAs that meet in the workspace:
+ * fp32 partial tiles plus one ticket counter per shared tile; the last CTA of a tile
+ * adds the partials in a fixed order.  The first RK_GEMV_WORKSPACE_TICKET_BYTES of the
+ * workspace hold the ticket counters: they must be zero before the first use and every
+ * call leaves them zero; the rest is scratch.  A workspace can therefore be reused
+ * across problem sizes and strategies.  Calls that share a workspace must be ordered
+ * (same stream).  NULL / too small: same as rk_gemv.  No counterpart in the reference.
  */
+#define RK_GEMV_WORKSPACE_TICKET_BYTES (64u << 10)
 RK_API rk_status rk_gemv_ex(const void* x, const void* weight, void* out, int64_t M,
                             int64_t N, int64_t K, rk_dtype dt, int variant,
                             void* workspace, size_t workspace_bytes, rk_stream_t stream);
@@ -170,8 +171,8 @@ RK_API void rk_gemv_set_tuning(int rows_per_warp, int ksplit);
 RK_API void rk_gemm_set_tile_n(int tile_n);
 
 /* Tuning hook for RK_GEMV_TC: thread-block cluster size (K split), 1..8; -1 selects
- * stream-K through the rk_gemv_ex workspace; 0 restores the built-in choice.
- * Process-wide. */
+ * stream-K through the rk_gemv_ex workspace (without one it falls back to cluster
+ * split-K); 0 restores the built-in choice.  Process-wide. */
 RK_API void rk_gemv_tc_set_cluster(int cluster_size);
 
 /* Programmatic dependent launch (on by default; no counterpart in the reference,

@@ -633,8 +633,14 @@ int sk_grid(int64_t M, int64_t N, int64_t K) {
   return g < 1 ? 1 : static_cast<int>(g);
 }
 
+// Tickets live in the workspace's fixed ticket prefix (kept zero by every strategy).
 size_t sk_ticket_bytes(int64_t N) {
-  return ((static_cast<size_t>((N + gtc::BM - 1) / gtc::BM) * sizeof(int) + 255) / 256) * 256;
+  (void)N;
+  return RK_GEMV_WORKSPACE_TICKET_BYTES;
+}
+
+bool sk_fits(int64_t N) {
+  return (N + gtc::BM - 1) / gtc::BM <= static_cast<int64_t>(RK_GEMV_WORKSPACE_TICKET_BYTES / sizeof(int));
 }
 
 // Stream-K workspace bytes (ticket counters + two partial slots per CTA).
@@ -649,7 +655,7 @@ size_t sk_workspace_bytes(int64_t M, int64_t N, int64_t K) {
 // workspace; stream-K runs when selected explicitly (tuning value -1) or through
 // rk_gemv_fixed_scratch.
 size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
-  return g_gemv_tc_cluster.load() == -1 ? sk_workspace_bytes(M, N, K) : 0;
+  return g_gemv_tc_cluster.load() == -1 && sk_fits(N) ? sk_workspace_bytes(M, N, K) : 0;
 }
 
 template <typename T, int MN>
@@ -679,7 +685,8 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
   const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
   const size_t need = sk_workspace_bytes(M, N, K);
-  if ((stream_k || csize_override == -1) && workspace != nullptr && workspace_bytes >= need) {
+  if ((stream_k || csize_override == -1) && sk_fits(N) && workspace != nullptr &&
+      workspace_bytes >= need) {
     // Stream-K over all SMs, shared tiles meet in the caller's workspace.
     constexpr int sk_smem = gtc::sk_smem_bytes<MN>();
     static std::once_flag sk_once[64];
@@ -801,7 +808,11 @@ extern "C" rk_status rk_gemv_fixed_scratch(const void* x, const void* weight, vo
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // The array keeps whatever the previous call left; the split-K tickets at its start
   // must be zero when the kernel begins.
-  const rk_status st = cuda_status(cudaMemsetAsync(fs.ptr, 0, sk_ticket_bytes(N), s));
-  if (st != RK_OK) return st;
+  // (Weights taller than the ticket prefix covers run cluster split-K, which needs none.)
+  if (sk_fits(N)) {
+    const size_t used_tickets = ((N + gtc::BM - 1) / gtc::BM * sizeof(int) + 255) / 256 * 256;
+    const rk_status st = cuda_status(cudaMemsetAsync(fs.ptr, 0, used_tickets, s));
+    if (st != RK_OK) return st;
+  }
   return gemv_tc_launch(x, weight, out, M, N, K, dt, s, fs.ptr, RK_GEMV_FIXED_SCRATCH_BYTES, true);
 }
