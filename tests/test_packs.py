@@ -117,3 +117,39 @@ def test_builtin_pack_is_trusted_by_location_and_matches_dispatch():
         for entry in dispatch.get(operator, "1.0").entries:
             assert entry.winner == item.artifact, f"{entry.id} does not point at the built pack"
             assert entry.evidence_id == item.evidence_id
+
+
+def test_shipped_entries_pin_the_kernel_the_library_would_choose():
+    """A pinned variant agrees with the library's own rule for that shape range.
+
+    GEMV: the CUDA-core stream kernel (variant 2) only for M <= 2 -- from M = 3 it is
+    FMA/L1-bound -- and the tensor-core kernel (variant 3) only from M = 3.  GEMM: the
+    SM-pair kernel (variant 3) only with at least one 256 x 256 tile per SM pair of a
+    148-SM B200, the 1-SM kernel (variant 2) below that.
+    """
+
+    from radeon_kernels import _native
+
+    dispatch = builtin_dispatch_registry()
+    gemv_stream, gemv_tc = _native.GEMV_VARIANTS["stream"], _native.GEMV_VARIANTS["tc"]
+    for entry in dispatch.get("gemv", "1.0").entries:
+        variant = entry.launch["variant"]
+        m = entry.workload.values["m"]
+        lo, hi = m.value if m.kind == "range" else (min(m.values()), max(m.values()))
+        if variant == gemv_stream:
+            assert hi <= 2, f"{entry.id}: stream kernel pinned for M up to {hi}"
+        if variant == gemv_tc:
+            assert lo >= 3, f"{entry.id}: tensor-core kernel pinned for M from {lo}"
+    gemm_1sm, gemm_2sm = _native.GEMM_VARIANTS["tc_1sm"], _native.GEMM_VARIANTS["tc_2sm"]
+    for entry in dispatch.get("gemm", "1.0").entries:
+        variant = entry.launch["variant"]
+        if variant not in (gemm_1sm, gemm_2sm):
+            continue
+        if "n" not in entry.workload.values:
+            continue
+        m_values = entry.workload.values["m"].values()
+        n_values = entry.workload.values["n"].values()
+        for m_ in m_values:  # both ends of a range
+            for n_ in n_values:
+                pair_tiles = (-(-m_ // 256)) * (-(-n_ // 256))
+                assert (pair_tiles >= 74) == (variant == gemm_2sm), entry.id
