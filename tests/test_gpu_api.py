@@ -41,15 +41,23 @@ def test_gemm_dispatches_to_the_native_pack_winner():
     assert "selected: native/gemm_out" in rk.explain_last_dispatch()
 
 
-def test_gemv_dispatches_to_the_native_pack_winner():
-    import radeon_kernels as rk
+@pytest.mark.parametrize("m, entry", [(1, "m1-2"), (4, "m3-16"), (16, "m3-16")])
+def test_gemv_dispatches_to_the_native_pack_winner(m, entry):
+    """Config 3 through the public call: the stream kernel for M <= 2, tensor cores from M = 3."""
 
-    x = seeded((4, 14336), 2, "normal", "fp16").cuda()
+    import radeon_kernels as rk
+    from radeon_kernels import _native
+
+    x = seeded((m, 14336), 2, "normal", "fp16").cuda()
     w = seeded((4096, 14336), 2, "normal/14336", "fp16").cuda()
     out = rk.gemv(x, w)
     record = rk.get_last_dispatch()
     assert record["selected"] == "native/gemv", record["reason"]
-    assert record["entry_id"] == "gemv-sm100a-fp16-n4096-k14336"
+    assert record["entry_id"] == f"gemv-sm100a-fp16-n4096-k14336-{entry}"
+    from radeon_kernels.runtime.resources import builtin_dispatch_registry
+
+    pinned = {e.id: e.launch["variant"] for e in builtin_dispatch_registry().get("gemv", "1.0").entries}
+    assert pinned[record["entry_id"]] == _native.GEMV_VARIANTS["stream" if m <= 2 else "tc"]
     ref_bits, ref32 = oracle.gemv(to_bits(x), to_bits(w), "fp16")
     oracle.assert_parity(to_bits(out), ref_bits, ref32, "fp16")
 
