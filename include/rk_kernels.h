@@ -156,6 +156,40 @@ RK_API rk_status rk_gather_column_blocks(const void* blocks, void* out, int64_t 
                                   int64_t M, int64_t N, rk_dtype dt,
                                   rk_stream_t stream);
 
+/*
+ * out = silu(gate) * up elementwise, silu(g) = g / (1 + exp(-g)) evaluated as
+ * g * (1 / (1 + exp(-g))) in fp32, one rounding to `dt` per element.  gate, up,
+ * out: [tokens, hidden] row-major, same dtype; tokens, hidden >= 0.  Replaces the
+ * reference's pybind entry `silu_mul(gate, up)` (benchmarks/llm_ops/
+ * native_llm_ops.hip:397-416, kernel :125-133) behind rk.silu_mul (operator
+ * "swiglu", src/radeon_kernels/ops/swiglu/api.py:22-62); the output buffer is the
+ * caller's.
+ */
+RK_API rk_status rk_silu_mul(const void* gate, const void* up, void* out, int64_t tokens,
+                             int64_t hidden, rk_dtype dt, rk_stream_t stream);
+
+/*
+ * out = x * (1 / sqrt(mean(x^2) + eps)) * weight per row, fp32 arithmetic, one
+ * rounding per element.  x, out: [tokens, hidden]; weight: [hidden]; eps > 0.
+ * Replaces the reference's pybind entry `rms_norm(input, weight, eps)`
+ * (native_llm_ops.hip:306-325, kernel :51-67) behind rk.rms_norm
+ * (src/radeon_kernels/ops/rms_norm/api.py:22-61).
+ */
+RK_API rk_status rk_rms_norm(const void* x, const void* weight, void* out, int64_t tokens,
+                             int64_t hidden, float eps, rk_dtype dt, rk_stream_t stream);
+
+/*
+ * residual_out = x + residual (rounded to `dt`), out = rms_norm(residual_out, weight,
+ * eps).  x, residual, out, residual_out: [tokens, hidden]; weight: [hidden].
+ * Replaces the reference's pybind entry `add_rms_norm(input, residual, weight, eps)`
+ * (native_llm_ops.hip:327-353, kernel :69-94) behind rk.add_rms_norm
+ * (src/radeon_kernels/ops/add_rms_norm/api.py:22-79).
+ */
+RK_API rk_status rk_add_rms_norm(const void* x, const void* residual, const void* weight,
+                                 void* out, void* residual_out, int64_t tokens,
+                                 int64_t hidden, float eps, rk_dtype dt,
+                                 rk_stream_t stream);
+
 /* Static description of a status code; never NULL. */
 RK_API const char* rk_status_string(rk_status status);
 

@@ -49,6 +49,13 @@ def _library() -> ctypes.CDLL:
         lib.rk_oracle_round.restype = None
         lib.rk_oracle_widen.argtypes = [u16p, f32p, i64, cint]
         lib.rk_oracle_widen.restype = None
+        f32 = ctypes.c_float
+        lib.rk_oracle_silu_mul.argtypes = [u16p, u16p, u16p, f32p, i64, cint]
+        lib.rk_oracle_silu_mul.restype = None
+        lib.rk_oracle_rms_norm.argtypes = [u16p, u16p, u16p, f32p, f32p, i64, i64, f32, cint]
+        lib.rk_oracle_rms_norm.restype = None
+        lib.rk_oracle_add_rms_norm.argtypes = [u16p, u16p, u16p, u16p, u16p, f32p, f32p, i64, i64, f32, cint]
+        lib.rk_oracle_add_rms_norm.restype = None
         _lib = lib
     return _lib
 
@@ -89,6 +96,49 @@ def gemv(x_bits: np.ndarray, w_bits: np.ndarray, dtype: str) -> tuple[np.ndarray
     return out, acc
 
 
+def silu_mul(gate_bits: np.ndarray, up_bits: np.ndarray, dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """silu(gate) * up on 16-bit bit patterns [tokens, hidden]; returns (bits, fp32 before rounding)."""
+
+    g = np.ascontiguousarray(gate_bits, dtype=np.uint16)
+    u = np.ascontiguousarray(up_bits, dtype=np.uint16)
+    if g.shape != u.shape:
+        raise ValueError("gate and up shapes differ")
+    out = np.empty(g.shape, np.uint16)
+    exact = np.empty(g.shape, np.float32)
+    _library().rk_oracle_silu_mul(g.reshape(-1), u.reshape(-1), out.reshape(-1), exact.reshape(-1), g.size, _code(dtype))
+    return out, exact
+
+
+def rms_norm(x_bits: np.ndarray, w_bits: np.ndarray, eps: float, dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """Row RMS normalisation of x [tokens, hidden] by weight [hidden]; returns (bits, fp32)."""
+
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    tokens, hidden = x.shape
+    out = np.empty(x.shape, np.uint16)
+    exact = np.empty(x.shape, np.float32)
+    work = np.empty(hidden + 1, np.float32)
+    _library().rk_oracle_rms_norm(x, w, out, exact, work, tokens, hidden, eps, _code(dtype))
+    return out, exact
+
+
+def add_rms_norm(
+    x_bits: np.ndarray, r_bits: np.ndarray, w_bits: np.ndarray, eps: float, dtype: str
+) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """(rms_norm(x + residual), x + residual) on bit patterns; also the fp32 normalised values."""
+
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    r = np.ascontiguousarray(r_bits, dtype=np.uint16)
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    tokens, hidden = x.shape
+    out = np.empty(x.shape, np.uint16)
+    residual_out = np.empty(x.shape, np.uint16)
+    exact = np.empty(x.shape, np.float32)
+    work = np.empty(hidden + 1, np.float32)
+    _library().rk_oracle_add_rms_norm(x, r, w, out, residual_out, exact, work, tokens, hidden, eps, _code(dtype))
+    return out, residual_out, exact
+
+
 def widen(bits: np.ndarray, dtype: str) -> np.ndarray:
     src = np.ascontiguousarray(bits, dtype=np.uint16)
     dst = np.empty(src.shape, np.float32)
@@ -127,6 +177,43 @@ def ulp_distance(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
         return np.where(v & 0x8000, 0x8000 - (v & 0x7FFF), 0x8000 + (v & 0x7FFF))
 
     return np.abs(ordered(a_bits) - ordered(b_bits))
+
+
+def _is_nan(bits: np.ndarray, dtype: str) -> np.ndarray:
+    v = np.asarray(bits, np.uint16)
+    if dtype == "bf16":
+        return ((v & 0x7F80) == 0x7F80) & ((v & 0x007F) != 0)
+    return ((v & 0x7C00) == 0x7C00) & ((v & 0x03FF) != 0)
+
+
+# Elementwise and row-normalisation operators (silu_mul, rms_norm, add_rms_norm): every
+# output is a short fp32 expression of its inputs -- no long cancelling sum -- so the gate
+# is per element: NaN exactly where the reference has NaN (any sign or payload), and at
+# most one representable step from the reference's rounded value everywhere else.  One
+# step covers the last-bit differences between libm implementations of exp (sigmoid) and
+# between fp32 summation orders of the squares (RMS); it is below the reference
+# contracts' atol/rtol of 0.01 (contracts/swiglu-1.0.json, add_rms_norm-1.0.json).
+ELEMENTWISE_MAX_ULP = 1
+
+
+def assert_elementwise(result_bits: np.ndarray, ref_bits: np.ndarray, dtype: str, max_ulp: int = ELEMENTWISE_MAX_ULP) -> int:
+    """Raise AssertionError unless result matches ref per element (see above); returns the max step."""
+
+    result = np.asarray(result_bits, np.uint16)
+    ref = np.asarray(ref_bits, np.uint16)
+    if result.shape != ref.shape:
+        raise AssertionError(f"shape {result.shape} != {ref.shape}")
+    nan_r, nan_ref = _is_nan(result, dtype), _is_nan(ref, dtype)
+    if not np.array_equal(nan_r, nan_ref):
+        raise AssertionError(f"NaN positions differ at {np.argwhere(nan_r != nan_ref)[:5].tolist()}")
+    if result.size == 0 or nan_ref.all():
+        return 0
+    steps = ulp_distance(result[~nan_ref], ref[~nan_ref])
+    worst = int(steps.max())
+    if worst > max_ulp:
+        where = np.argwhere(~nan_ref)[int(np.argmax(steps))].tolist()
+        raise AssertionError(f"{worst} steps from the reference at {where} (max {max_ulp})")
+    return worst
 
 
 def compare(result_bits: np.ndarray, ref_bits: np.ndarray, ref_fp32: np.ndarray, dtype: str) -> dict[str, float]:

@@ -7,6 +7,9 @@ ops/gemm/api.py:62-63, so the baseline calls them directly):
 * ``gemm_fallback``  -- providers/torch_fallback.py:6-9
 * ``gemv_fallback``  -- ops/gemv/reference.py:12-15
 * ``gemv_reference`` -- ops/gemv/reference.py:6-9 (the gemv contract's declared oracle)
+* ``silu_mul_reference`` -- ops/swiglu/reference.py:6-9
+* ``rms_norm_reference`` -- ops/rms_norm/reference.py:6-10
+* ``add_rms_norm_reference`` -- ops/add_rms_norm/reference.py:8-12
 
 They are one-line calls of ``torch.mm``; torch is the reference's arithmetic engine (see
 ``rk_oracle.c`` for the version note).  ``bench.py --impl reference`` times them on the
@@ -34,3 +37,19 @@ def gemm_reference_fp32(torch_module: Any, a: Any, b: Any) -> Any:
     """fp32-accumulated product before the final rounding (parity metric denominator)."""
 
     return torch_module.mm(a.float(), b.float())
+
+
+def silu_mul_reference(torch_module: Any, gate: Any, up: Any) -> Any:
+    g = gate.float()
+    return (g * torch_module.sigmoid(g) * up.float()).to(dtype=gate.dtype)
+
+
+def rms_norm_reference(torch_module: Any, x: Any, weight: Any, eps: float) -> Any:
+    v = x.float()
+    scale = torch_module.rsqrt(v.square().mean(dim=-1, keepdim=True) + eps)
+    return (v * scale * weight.float()).to(dtype=x.dtype)
+
+
+def add_rms_norm_reference(torch_module: Any, x: Any, residual: Any, weight: Any, eps: float) -> tuple[Any, Any]:
+    residual_out = x + residual
+    return rms_norm_reference(torch_module, residual_out, weight, eps), residual_out

@@ -5,7 +5,8 @@
  * calls this file; only tests/, __graft_entry__.smoke() and bench.py's CPU baseline do,
  * as the checker.
  *
- * What is restated.  The reference computes both operators with PyTorch:
+ * What is restated (the decode neighbours silu_mul / rms_norm / add_rms_norm are at the
+ * end of the file).  The reference computes both operators with PyTorch:
  *   rk.gemm fallback:  torch.mm(a, b)                        providers/torch_fallback.py:6-9
  *   rk.gemv fallback:  torch.mm(x, weight.T)                 ops/gemv/reference.py:12-15
  *   rk.gemv oracle:    torch.mm(x.float(), weight.float().T).to(x.dtype)
@@ -23,6 +24,7 @@
  *
  * Conversions are written from the IEEE 754 binary16 / bfloat16 definitions.
  */
+#include <math.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -158,5 +160,69 @@ void rk_oracle_gemv(const uint16_t* x, const uint16_t* W, uint16_t* out, float* 
       acc[m * N + n] = s;
       out[m * N + n] = store16(s, dtype);
     }
+  }
+}
+
+/*
+ * Decode neighbours of the GEMV/GEMM path (the reference's fp32 definitions):
+ *   silu_mul_reference     ops/swiglu/reference.py:6-9
+ *       g = float(gate); out = (g * sigmoid(g)) * float(up), rounded once
+ *   rms_norm_reference     ops/rms_norm/reference.py:6-10
+ *       v = float(x); var = mean(v * v); out = (v * rsqrt(var + eps)) * float(weight)
+ *   add_rms_norm_reference ops/add_rms_norm/reference.py:8-12
+ *       s = x + residual in the 16-bit dtype (one rounding); out = rms_norm(s)
+ * sigmoid(g) = 1 / (1 + exp(-g)) with the C library's expf; rsqrt(v) = 1 / sqrtf(v).
+ * The squares are rounded to fp32 (as torch's square() stores them) and summed in double;
+ * PyTorch sums them in fp32 in a blocked order, so the two means agree to the last fp32
+ * bit or two.  `exact` receives every output before its final rounding.
+ */
+void rk_oracle_silu_mul(const uint16_t* gate, const uint16_t* up, uint16_t* out, float* exact,
+                        int64_t n, int dtype) {
+  for (int64_t i = 0; i < n; ++i) {
+    const float g = load16(gate, i, dtype);
+    const float s = 1.0f / (1.0f + expf(-g));
+    const float gs = g * s;
+    const float v = gs * load16(up, i, dtype);
+    exact[i] = v;
+    out[i] = store16(v, dtype);
+  }
+}
+
+static void rms_rows(const float* v, const uint16_t* weight, uint16_t* out, float* exact,
+                     int64_t hidden, float eps, int dtype) {
+  double sum = 0.0;
+  for (int64_t j = 0; j < hidden; ++j) {
+    const float sq = v[j] * v[j];
+    sum += (double)sq;
+  }
+  const float mean = (float)sum / (float)hidden;
+  const float r = 1.0f / sqrtf(mean + eps);
+  for (int64_t j = 0; j < hidden; ++j) {
+    const float normalized = v[j] * r;
+    const float y = normalized * load16(weight, j, dtype);
+    exact[j] = y;
+    out[j] = store16(y, dtype);
+  }
+}
+
+/* `work` must hold `hidden` floats. */
+void rk_oracle_rms_norm(const uint16_t* x, const uint16_t* weight, uint16_t* out, float* exact,
+                        float* work, int64_t tokens, int64_t hidden, float eps, int dtype) {
+  for (int64_t t = 0; t < tokens; ++t) {
+    rk_oracle_widen(x + t * hidden, work, hidden, dtype);
+    rms_rows(work, weight, out + t * hidden, exact + t * hidden, hidden, eps, dtype);
+  }
+}
+
+void rk_oracle_add_rms_norm(const uint16_t* x, const uint16_t* residual, const uint16_t* weight,
+                            uint16_t* out, uint16_t* residual_out, float* exact, float* work,
+                            int64_t tokens, int64_t hidden, float eps, int dtype) {
+  for (int64_t t = 0; t < tokens; ++t) {
+    for (int64_t j = 0; j < hidden; ++j) {
+      const int64_t i = t * hidden + j;
+      residual_out[i] = store16(load16(x, i, dtype) + load16(residual, i, dtype), dtype);
+      work[j] = load16(residual_out, i, dtype);
+    }
+    rms_rows(work, weight, out + t * hidden, exact + t * hidden, hidden, eps, dtype);
   }
 }

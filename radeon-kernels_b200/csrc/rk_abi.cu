@@ -216,6 +216,39 @@ rk_status rk_gemv_ex(const void* x, const void* W, void* out, int64_t M, int64_t
   return RK_ERR_UNSUPPORTED;
 }
 
+rk_status rk_silu_mul(const void* gate, const void* up, void* out, int64_t tokens,
+                      int64_t hidden, rk_dtype dt, rk_stream_t stream) {
+  if (tokens < 0 || hidden < 0 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
+  if (tokens > 0 && hidden > 0 && (gate == nullptr || up == nullptr || out == nullptr))
+    return RK_ERR_INVALID_ARGUMENT;
+  if (hidden > 0 && tokens > INT64_MAX / hidden) return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return silu_mul_launch(gate, up, out, tokens, hidden, dt, reinterpret_cast<cudaStream_t>(stream));
+}
+
+static bool valid_eps(float eps) { return eps > 0.0f && eps <= 3.4e38f; }  // positive, finite
+
+rk_status rk_rms_norm(const void* x, const void* weight, void* out, int64_t tokens,
+                      int64_t hidden, float eps, rk_dtype dt, rk_stream_t stream) {
+  if (tokens < 0 || hidden < 1 || !valid_dtype(dt) || !valid_eps(eps)) return RK_ERR_INVALID_ARGUMENT;
+  if (x == nullptr || weight == nullptr || out == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return rms_norm_launch(x, nullptr, weight, out, nullptr, tokens, hidden, eps, dt,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+rk_status rk_add_rms_norm(const void* x, const void* residual, const void* weight, void* out,
+                          void* residual_out, int64_t tokens, int64_t hidden, float eps,
+                          rk_dtype dt, rk_stream_t stream) {
+  if (tokens < 0 || hidden < 1 || !valid_dtype(dt) || !valid_eps(eps)) return RK_ERR_INVALID_ARGUMENT;
+  if (x == nullptr || residual == nullptr || weight == nullptr || out == nullptr ||
+      residual_out == nullptr)
+    return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return rms_norm_launch(x, residual, weight, out, residual_out, tokens, hidden, eps, dt,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
 rk_status rk_gemv(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
                   rk_dtype dt, int variant, rk_stream_t stream) {
   return rk_gemv_ex(x, W, out, M, N, K, dt, variant, nullptr, 0, stream);

@@ -84,6 +84,14 @@ bool gemv_tc_supported(const void* x, const void* W, const void* out, int64_t M,
 bool gemv_stream_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,
                            int64_t K);
 
+// Decode neighbours (llm_ops.cu).  rms_norm_launch: residual == nullptr -> rms_norm,
+// else add_rms_norm (residual_out receives x + residual).
+rk_status silu_mul_launch(const void* gate, const void* up, void* out, int64_t tokens,
+                          int64_t hidden, rk_dtype dt, cudaStream_t s);
+rk_status rms_norm_launch(const void* x, const void* residual, const void* weight, void* out,
+                          void* residual_out, int64_t tokens, int64_t hidden, float eps,
+                          rk_dtype dt, cudaStream_t s);
+
 rk_status gather_column_blocks_launch(const void* blocks, void* out, int64_t G, int64_t M,
                                       int64_t N, rk_dtype dt, cudaStream_t s);
 

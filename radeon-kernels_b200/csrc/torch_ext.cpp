@@ -18,6 +18,7 @@
 #include <torch/extension.h>
 
 #include <map>
+#include <vector>
 #include <mutex>
 #include <utility>
 
@@ -148,6 +149,67 @@ at::Tensor gather_column_blocks(const at::Tensor& blocks, at::Tensor out) {
   return out;
 }
 
+// Decode neighbours: the reference's pybind names and signatures
+// (benchmarks/llm_ops/native_llm_ops.hip:306-353, :397-416), outputs allocated here.
+void check_rows(const at::Tensor& t, const char* name, int64_t rank) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.dim() == rank, name, " must be rank ", rank);
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  dtype_of(t, name);
+}
+
+at::Tensor silu_mul(const at::Tensor& gate, const at::Tensor& up) {
+  check_rows(gate, "gate", 2);
+  check_rows(up, "up", 2);
+  TORCH_CHECK(gate.device() == up.device() && gate.scalar_type() == up.scalar_type(),
+              "gate and up must share device and dtype");
+  TORCH_CHECK(gate.sizes() == up.sizes(), "up shape must match gate");
+  c10::cuda::CUDAGuard guard(gate.device());
+  auto out = at::empty_like(gate);
+  check_status(rk_silu_mul(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.size(0),
+                           gate.size(1), dtype_of(gate, "gate"), current_stream(gate)),
+               "rk_silu_mul");
+  return out;
+}
+
+at::Tensor rms_norm(const at::Tensor& input, const at::Tensor& weight, double eps) {
+  check_rows(input, "input", 2);
+  check_rows(weight, "weight", 1);
+  TORCH_CHECK(input.device() == weight.device() && input.scalar_type() == weight.scalar_type(),
+              "input and weight must share device and dtype");
+  TORCH_CHECK(weight.numel() == input.size(1), "weight must match hidden size");
+  c10::cuda::CUDAGuard guard(input.device());
+  auto out = at::empty_like(input);
+  check_status(rk_rms_norm(input.data_ptr(), weight.data_ptr(), out.data_ptr(), input.size(0),
+                           input.size(1), static_cast<float>(eps), dtype_of(input, "input"),
+                           current_stream(input)),
+               "rk_rms_norm");
+  return out;
+}
+
+std::vector<at::Tensor> add_rms_norm(const at::Tensor& input, const at::Tensor& residual,
+                                     const at::Tensor& weight, double eps) {
+  check_rows(input, "input", 2);
+  check_rows(residual, "residual", 2);
+  check_rows(weight, "weight", 1);
+  TORCH_CHECK(input.device() == residual.device() && input.device() == weight.device(),
+              "input, residual and weight must share a device");
+  TORCH_CHECK(input.scalar_type() == residual.scalar_type() &&
+                  input.scalar_type() == weight.scalar_type(),
+              "input, residual and weight must share a dtype");
+  TORCH_CHECK(input.sizes() == residual.sizes(), "residual shape must match input");
+  TORCH_CHECK(weight.numel() == input.size(1), "weight must match hidden size");
+  c10::cuda::CUDAGuard guard(input.device());
+  auto out = at::empty_like(input);
+  auto residual_out = at::empty_like(input);
+  check_status(rk_add_rms_norm(input.data_ptr(), residual.data_ptr(), weight.data_ptr(),
+                               out.data_ptr(), residual_out.data_ptr(), input.size(0),
+                               input.size(1), static_cast<float>(eps), dtype_of(input, "input"),
+                               current_stream(input)),
+               "rk_add_rms_norm");
+  return {out, residual_out};
+}
+
 int64_t device_status() {
   return static_cast<int64_t>(rk_device_status(
       reinterpret_cast<rk_stream_t>(c10::cuda::getCurrentCUDAStream().stream())));
@@ -167,6 +229,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_stream", &gemv_stream, "128-bit weight-streaming GEMV (K % 8 == 0, 16B aligned)");
   m.def("gemv_scalar", &gemv_scalar, "generic GEMV (any K, any alignment)");
   m.def("gather_column_blocks", &gather_column_blocks, "[G,M,N/G] blocks -> row-major [M,N]");
+  m.def("silu_mul", &silu_mul, "silu(gate) * up", py::arg("gate"), py::arg("up"));
+  m.def("rms_norm", &rms_norm, "row RMS normalisation", py::arg("input"), py::arg("weight"),
+        py::arg("eps"));
+  m.def("add_rms_norm", &add_rms_norm, "residual add + row RMS normalisation -> [out, residual_out]",
+        py::arg("input"), py::arg("residual"), py::arg("weight"), py::arg("eps"));
   m.def("device_status", &device_status, "read and clear the device status word");
   m.def("set_wait_timeout_ns", [](uint64_t ns) { rk_set_wait_timeout_ns(ns); });
   m.def("debug_inject_stall", [](bool on) { rk_debug_inject_stall(on ? 1 : 0); });

@@ -7,6 +7,7 @@ so a bad call raises ``TypeError``/``ValueError`` and records no dispatch.
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 from typing import Any
 
@@ -50,6 +51,15 @@ def validate_same(operator: str, first: Any, second: Any, *, first_name: str, se
         raise ValueError(f"{operator} {first_name} and {second_name} must use the same device")
     if first.dtype != second.dtype:
         raise TypeError(f"{operator} {first_name} and {second_name} must use the same dtype")
+
+
+def validate_eps(eps: Any, operator: str) -> float:
+    if isinstance(eps, bool) or not isinstance(eps, (int, float)):
+        raise TypeError(f"{operator} eps must be a number")
+    normalized = float(eps)
+    if not math.isfinite(normalized) or normalized <= 0:
+        raise ValueError(f"{operator} eps must be positive and finite")
+    return normalized
 
 
 def device_index_of(torch_module: Any, tensor: Any) -> int:

@@ -20,6 +20,9 @@ from radeon_kernels import _native
 
 SELECTED_GEMM = "cuda/gemm"
 SELECTED_GEMV = "cuda/gemv"
+SELECTED_SILU_MUL = "cuda/silu_mul"
+SELECTED_RMS_NORM = "cuda/rms_norm"
+SELECTED_ADD_RMS_NORM = "cuda/add_rms_norm"
 
 
 def _contiguous(tensor: Any) -> Any:
@@ -102,3 +105,59 @@ def gemv(torch_module: Any, x: Any, weight: Any) -> Any:
     if _needs_grad(torch_module, x, weight):
         return _functions()[1].apply(x, weight)
     return _gemv_raw(x, weight)
+
+
+# --------------------------------------------------------------- decode neighbours
+# silu_mul / rms_norm / add_rms_norm (rk_silu_mul, rk_rms_norm, rk_add_rms_norm).  Their
+# backward passes are not built yet: an input that requires gradients gets an autograd node
+# whose backward raises, so a forward pass (e.g. evaluation with parameters that require
+# gradients) still runs on these kernels and a backward pass fails loudly instead of
+# silently computing with another library.
+
+_NEIGHBOUR_FUNCTION: Any = None
+
+
+def _no_backward_function() -> Any:
+    global _NEIGHBOUR_FUNCTION
+    if _NEIGHBOUR_FUNCTION is None:
+        import torch
+
+        class _ForwardOnly(torch.autograd.Function):
+            @staticmethod
+            def forward(ctx: Any, name: str, run: Any, *inputs: Any) -> Any:
+                ctx.name = name
+                return run(*[t.detach() for t in inputs])
+
+            @staticmethod
+            def backward(ctx: Any, *grads: Any) -> Any:
+                raise NotImplementedError(f"{ctx.name}: the backward pass is not implemented in this build")
+
+        _NEIGHBOUR_FUNCTION = _ForwardOnly
+    return _NEIGHBOUR_FUNCTION
+
+
+def _run(torch_module: Any, name: str, run: Any, *inputs: Any) -> Any:
+    inputs = tuple(_contiguous(t) for t in inputs)
+    if _needs_grad(torch_module, *inputs):
+        return _no_backward_function().apply(name, run, *inputs)
+    return run(*inputs)
+
+
+def silu_mul(torch_module: Any, gate: Any, up: Any) -> Any:
+    return _run(torch_module, "silu_mul", lambda g, u: _native.extension().silu_mul(g, u), gate, up)
+
+
+def rms_norm(torch_module: Any, x: Any, weight: Any, eps: float) -> Any:
+    return _run(torch_module, "rms_norm", lambda a, w: _native.extension().rms_norm(a, w, eps), x, weight)
+
+
+def add_rms_norm(torch_module: Any, x: Any, residual: Any, weight: Any, eps: float) -> tuple[Any, Any]:
+    out = _run(
+        torch_module,
+        "add_rms_norm",
+        lambda a, r, w: tuple(_native.extension().add_rms_norm(a, r, w, eps)),
+        x,
+        residual,
+        weight,
+    )
+    return out[0], out[1]

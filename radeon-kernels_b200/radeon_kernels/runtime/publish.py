@@ -27,6 +27,9 @@ ARTIFACT = "lib/rk_sm100a.so"
 ENTRYPOINTS = {
     ("gemm", "1.0"): ("gemm_out", "rk-sm100a-gemm"),
     ("gemv", "1.0"): ("gemv", "rk-sm100a-gemv"),
+    ("swiglu", "1.0"): ("silu_mul", "rk-sm100a-swiglu"),
+    ("rms_norm", "1.0"): ("rms_norm", "rk-sm100a-rms_norm"),
+    ("add_rms_norm", "1.0"): ("add_rms_norm", "rk-sm100a-add_rms_norm"),
 }
 
 

@@ -12,8 +12,13 @@ by calling the reference package itself:
 * GEMM:  ``radeon_kernels.providers.torch_fallback.gemm(torch, a, b)``  (torch_fallback.py:6-9)
 * GEMV:  ``radeon_kernels.ops.gemv.reference.gemv_fallback`` and ``gemv_reference``
   (ops/gemv/reference.py:6-15)
+* SwiGLU, RMSNorm, residual add + RMSNorm (the decode neighbours):
+  ``ops.swiglu.reference.silu_mul_reference`` (swiglu/reference.py:6-9),
+  ``ops.rms_norm.reference.rms_norm_reference`` (rms_norm/reference.py:6-10),
+  ``ops.add_rms_norm.reference.add_rms_norm_reference`` (add_rms_norm/reference.py:8-12)
 
-plus the fp32 product before rounding.  16-bit arrays are stored as uint16 bit patterns.
+plus the fp32 values before the final rounding.  16-bit arrays are stored as uint16 bit
+patterns.
 """
 
 from __future__ import annotations
@@ -48,6 +53,26 @@ GEMV_CASES = [
 ]
 
 
+# name, dtype, tokens, hidden, seed, gate scale (silu_mul cases)
+SILU_CASES = [
+    ("silu_bf16_t4_h264", "bf16", 4, 264, 20, 1.0),
+    ("silu_fp16_t1_h11008_decode", "fp16", 1, 11008, 21, 1.0),
+    ("silu_bf16_t3_h13_ragged", "bf16", 3, 13, 22, 1.0),
+    ("silu_fp16_t8_h96_wide_range", "fp16", 8, 96, 23, 12.0),
+]
+# name, operator, dtype, tokens, hidden, seed, eps
+NORM_CASES = [
+    ("rms_bf16_t4_h4096", "rms_norm", "bf16", 4, 4096, 30, 1e-6),
+    ("rms_fp16_t1_h8192_decode", "rms_norm", "fp16", 1, 8192, 31, 1e-6),
+    ("rms_bf16_t3_h13_ragged", "rms_norm", "bf16", 3, 13, 32, 1e-5),
+    ("rms_fp16_t2_h20000_long_row", "rms_norm", "fp16", 2, 20000, 33, 1e-6),
+    ("add_rms_bf16_t4_h4096", "add_rms_norm", "bf16", 4, 4096, 40, 1e-6),
+    ("add_rms_fp16_t1_h8192_decode", "add_rms_norm", "fp16", 1, 8192, 41, 1e-6),
+    ("add_rms_bf16_t5_h100_ragged", "add_rms_norm", "bf16", 5, 100, 42, 1e-5),
+    ("add_rms_bf16_t2_h16392_long_row", "add_rms_norm", "bf16", 2, 16392, 43, 1e-6),
+]
+
+
 def _bits(tensor):
     import torch
 
@@ -73,7 +98,10 @@ def main(argv: list[str] | None = None) -> int:
     import torch
 
     import radeon_kernels  # the reference package
+    from radeon_kernels.ops.add_rms_norm.reference import add_rms_norm_reference
     from radeon_kernels.ops.gemv.reference import gemv_fallback, gemv_reference
+    from radeon_kernels.ops.rms_norm.reference import rms_norm_reference
+    from radeon_kernels.ops.swiglu.reference import silu_mul_reference
     from radeon_kernels.providers import torch_fallback
 
     origin = Path(radeon_kernels.__file__).resolve()
@@ -109,6 +137,41 @@ def main(argv: list[str] | None = None) -> int:
             out_fp32=out32.numpy(),
         )
         print(name, tuple(out.shape))
+
+    for name, dt, tokens, hidden, seed, scale in SILU_CASES:
+        gen = torch.Generator().manual_seed(seed)
+        gate = (torch.randn((tokens, hidden), generator=gen) * scale).to(dtypes[dt])
+        up = torch.randn((tokens, hidden), generator=gen).to(dtypes[dt])
+        if name.endswith("wide_range"):
+            # saturated sigmoid at both ends, signed zeros, infinities and a NaN
+            specials = torch.tensor([60000.0, -60000.0, 0.0, -0.0, float("inf"), float("-inf"), float("nan"), 11.0])
+            gate[0, : specials.numel()] = specials.to(dtypes[dt])
+        out = silu_mul_reference(torch, gate, up)
+        g32 = gate.float()
+        exact = g32 * torch.sigmoid(g32) * up.float()
+        np.savez_compressed(
+            HERE / f"{name}.npz", dtype=dt, gate=_bits(gate), up=_bits(up), out_ref=_bits(out), out_fp32=exact.numpy()
+        )
+        print(name, tuple(out.shape))
+
+    for name, operator, dt, tokens, hidden, seed, eps in NORM_CASES:
+        gen = torch.Generator().manual_seed(seed)
+        x = torch.randn((tokens, hidden), generator=gen).to(dtypes[dt])
+        weight = (1.0 + 0.1 * torch.randn((hidden,), generator=gen)).to(dtypes[dt])
+        fields = {"dtype": dt, "eps": np.float64(eps), "x": _bits(x), "weight": _bits(weight)}
+        if operator == "rms_norm":
+            source = x
+            fields["out_ref"] = _bits(rms_norm_reference(torch, x, weight, eps))
+        else:
+            residual = torch.randn((tokens, hidden), generator=gen).to(dtypes[dt])
+            out, residual_out = add_rms_norm_reference(torch, x, residual, weight, eps)
+            fields.update(residual=_bits(residual), out_ref=_bits(out), residual_out_ref=_bits(residual_out))
+            source = residual_out
+        s32 = source.float()
+        exact = s32 * torch.rsqrt(s32.square().mean(dim=-1, keepdim=True) + eps) * weight.float()
+        fields["out_fp32"] = exact.numpy()
+        np.savez_compressed(HERE / f"{name}.npz", **fields)
+        print(name, (tokens, hidden))
     return 0
 
 

@@ -79,3 +79,47 @@ def test_parity_metric_definition():
     ref = np.array([[1.0, -4.0], [2.0, 0.5]])
     assert oracle.parity_error(ref, ref) == 0.0
     assert oracle.parity_error(ref + 0.04, ref) == pytest.approx(0.01)
+
+
+# ------------------------------------------------------------ decode neighbours
+
+
+@pytest.mark.parametrize("path", golden_cases("silu"), ids=lambda p: p.stem)
+def test_oracle_silu_mul_matches_reference_fixtures(path):
+    case = _load(path)
+    out, exact = oracle.silu_mul(case["gate"], case["up"], case["dtype"])
+    oracle.assert_elementwise(out, case["out_ref"], case["dtype"])
+    finite = np.isfinite(case["out_fp32"])
+    np.testing.assert_allclose(exact[finite], case["out_fp32"][finite], rtol=2e-6, atol=0)
+
+
+@pytest.mark.parametrize("path", golden_cases("rms"), ids=lambda p: p.stem)
+def test_oracle_rms_norm_matches_reference_fixtures(path):
+    case = _load(path)
+    out, exact = oracle.rms_norm(case["x"], case["weight"], float(case["eps"]), case["dtype"])
+    oracle.assert_elementwise(out, case["out_ref"], case["dtype"])
+    np.testing.assert_allclose(exact, case["out_fp32"], rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("path", golden_cases("add_rms"), ids=lambda p: p.stem)
+def test_oracle_add_rms_norm_matches_reference_fixtures(path):
+    case = _load(path)
+    out, residual_out, exact = oracle.add_rms_norm(
+        case["x"], case["residual"], case["weight"], float(case["eps"]), case["dtype"]
+    )
+    assert np.array_equal(residual_out, case["residual_out_ref"])  # one rounded add: bit-exact
+    oracle.assert_elementwise(out, case["out_ref"], case["dtype"])
+    np.testing.assert_allclose(exact, case["out_fp32"], rtol=2e-6, atol=1e-7)
+
+
+def test_elementwise_gate_detects_a_planted_error():
+    case = _load(golden_cases("rms_bf16_t4")[0])
+    out, _ = oracle.rms_norm(case["x"], case["weight"], float(case["eps"]), case["dtype"])
+    planted = out.copy()
+    planted[1, 7] += 2  # two representable steps
+    with pytest.raises(AssertionError):
+        oracle.assert_elementwise(planted, case["out_ref"], case["dtype"])
+    nan = out.copy()
+    nan[0, 0] = 0x7FC0  # a NaN where the reference is finite
+    with pytest.raises(AssertionError):
+        oracle.assert_elementwise(nan, case["out_ref"], case["dtype"])
