@@ -503,6 +503,60 @@ def suite(args, dist: Dist, ext, peaks):
         }
         del ws
 
+    def neighbour_case(name, op, tokens, hidden, dtype, seed):
+        """silu_mul / rms_norm / add_rms_norm: HBM streams (bytes each launch must move)."""
+
+        elems = tokens * hidden
+        per_set = {"silu_mul": 3, "rms_norm": 2, "add_rms_norm": 4}[op] * elems * 2 + (hidden * 2 if op != "silu_mul" else 0)
+        # Enough rotated input sets that a replay cycle touches > 2 x L2 (decode-sized cases
+        # stay L2-resident whatever: they are launch-latency bound and reported as such).
+        sets = max(2, min(64, -(-300_000_000 // per_set)))
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        tdt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
+        a = [torch.randn((tokens, hidden), generator=gen, device="cuda").to(tdt) for _ in range(sets)]
+        b = [torch.randn((tokens, hidden), generator=gen, device="cuda").to(tdt) for _ in range(sets)]
+        w = (1 + 0.1 * torch.randn((hidden,), generator=gen, device="cuda")).to(tdt)
+        if op == "silu_mul":
+            step = lambda i: ext.silu_mul(a[i % sets], b[i % sets])  # noqa: E731
+        elif op == "rms_norm":
+            step = lambda i: ext.rms_norm(a[i % sets], w, 1e-6)  # noqa: E731
+        else:
+            step = lambda i: ext.add_rms_norm(a[i % sets], b[i % sets], w, 1e-6)  # noqa: E731
+        for i in range(3):
+            step(i)
+        torch.cuda.synchronize()
+        launches = max(20, sets)
+        g = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(g, stream=cap):
+                for i in range(launches):
+                    step(i)
+        stream.wait_stream(cap)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        reps = 10
+        ms = time_loop(lambda i: g.replay(), reps, stream) / (reps * launches)
+        del g
+        dist.barrier()
+        ms = dist.max(ms)
+        gbs = per_set / (ms / 1e3) / 1e9
+        results[name] = {
+            "unit": "GB/s",
+            "value": round(gbs * dist.world, 1),
+            "per_gpu": round(gbs, 1),
+            "us": round(ms * 1e3, 2),
+            "roofline_frac": round(gbs / peaks["hbm_gbs"], 4),
+            "scaling": "replica",
+            "shape": [tokens, hidden],
+            "dtype": dtype,
+            "timing": f"CUDA graph of {launches} launches over {sets} input sets"
+            + (" (L2-resident: launch-latency bound)" if per_set * sets < 256_000_000 else ""),
+        }
+        del a, b
+
     def cool_down():
         # Let the power/clock state recover between long GEMM cases so one case's
         # power capping does not leak into the next measurement.
@@ -514,6 +568,14 @@ def suite(args, dist: Dist, ext, peaks):
         gemv_case(f"c2_gemv_decode_bf16_m{m}", m, 8192, 8192, "bf16", 1, 400)
     for m in (1, 4, 16):
         gemv_case(f"c3_gemv_ffn_down_fp16_m{m}", m, 4096, 14336, "fp16", 2, 400)
+    # Decode neighbours, the reference's workload cases (benchmarks/workloads/*.yaml).
+    neighbour_case("swiglu_decode_h11008_bf16", "silu_mul", 1, 11008, "bf16", 50)
+    neighbour_case("swiglu_prefill_t1024_h11008_bf16", "silu_mul", 1024, 11008, "bf16", 51)
+    neighbour_case("swiglu_prefill_t512_h28672_bf16", "silu_mul", 512, 28672, "bf16", 52)
+    neighbour_case("add_rms_norm_decode_h4096_bf16", "add_rms_norm", 1, 4096, "bf16", 53)
+    neighbour_case("add_rms_norm_prefill_t2048_h4096_bf16", "add_rms_norm", 2048, 4096, "bf16", 54)
+    neighbour_case("add_rms_norm_prefill_t1024_h8192_bf16", "add_rms_norm", 1024, 8192, "bf16", 55)
+    neighbour_case("rms_norm_prefill_t2048_h4096_bf16", "rms_norm", 2048, 4096, "bf16", 56)
     gemm_case("c1_gemm_1024_bf16", 1024, 1024, 1024, "bf16", "uniform", 0, 10, graph=True)
     cool_down()
     gemm_case("c4_gemm_ffn_up_fp16", 4096, 14336, 4096, "fp16", "normal64", 3, 10)
@@ -628,6 +690,8 @@ PROFILE_CASES = {
     "gemm_1024": ("gemm", 1024, 1024, 1024, "bf16", "uniform"),
     "gemm_ffn_up": ("gemm", 4096, 14336, 4096, "fp16", "normal64"),
     "gemm_8192": ("gemm", 8192, 8192, 8192, "bf16", "uniform16"),
+    "swiglu_prefill": ("silu_mul", 1024, 11008, 0, "bf16", "normal"),
+    "add_rms_norm_prefill": ("add_rms_norm", 2048, 4096, 0, "bf16", "normal"),
 }
 
 
@@ -646,6 +710,15 @@ def run_profile(args) -> int:
         x = seeded((m, k), 2, "normal", dtype)
         out = torch.empty(m, n, dtype=x.dtype, device="cuda")
         launch = lambda: ext.gemv_out(x, w, out, 0)  # noqa: E731
+    elif kind == "silu_mul":  # m = tokens, n = hidden
+        gate = seeded((m, n), 1, dist_name, dtype)
+        up = seeded((m, n), 2, dist_name, dtype)
+        launch = lambda: ext.silu_mul(gate, up)  # noqa: E731
+    elif kind == "add_rms_norm":
+        x = seeded((m, n), 1, dist_name, dtype)
+        r = seeded((m, n), 2, dist_name, dtype)
+        w = seeded((n,), 3, dist_name, dtype)
+        launch = lambda: ext.add_rms_norm(x, r, w, 1e-6)  # noqa: E731
     else:
         a = seeded((m, k), 1, dist_name, dtype)
         b = seeded((k, n), 2, dist_name, dtype)

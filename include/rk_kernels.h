@@ -204,6 +204,11 @@ RK_API void rk_gemv_set_tuning(int rows_per_warp, int ksplit);
  * 256); 0 restores the built-in choice (fewest weighted waves).  Process-wide. */
 RK_API void rk_gemm_set_tile_n(int tile_n);
 
+/* Tuning hook for rk_rms_norm / rk_add_rms_norm: threads per row (64, 128, 256); 0
+ * restores the built-in choice (256 for few rows, 128 from two rows per SM).
+ * Process-wide. */
+RK_API void rk_norm_set_threads(int threads_per_row);
+
 /* Tuning hook for RK_GEMV_TC: thread-block cluster size (K split), 1..8; -1 selects
  * stream-K through the rk_gemv_ex workspace (without one it falls back to cluster
  * split-K); 0 restores the built-in choice.  Process-wide. */

@@ -10,18 +10,24 @@
 //   * 16-byte vector loads/stores (8 elements) when the hidden size is a multiple of 8
 //     and every pointer is 16-byte aligned; a scalar path otherwise;
 //   * silu_mul: one grid-stride loop over the flat tensor, grid = resident CTAs x SMs;
-//   * (add_)rms_norm: one CTA of 256 threads per row (grid-stride over rows); rows of up
-//     to 8192 elements stay in registers between the sum of squares and the scaled
-//     store, longer rows are re-read from L2 for the second pass; the per-row sum is a
-//     warp-shuffle tree plus a fixed-order sum over the 8 warps (deterministic).
+//   * (add_)rms_norm: one CTA per row (grid-stride over rows), each thread holding up to
+//     4 16-byte vectors of the row in registers between the sum of squares and the scaled
+//     store (longer rows are re-read from L2 for the second pass); the per-row sum is a
+//     warp-shuffle tree plus a fixed-order sum over the warps (deterministic).  The CTA
+//     size per row is chosen from the shape: few rows (decode) get 256 threads, many rows
+//     (prefill) the fewest threads whose registers hold the row, so more rows are
+//     resident per SM and fewer waves are needed.
 // Arithmetic follows the reference's fp32 definitions (src/radeon_kernels/ops/swiglu/
 // reference.py:6-9, ops/rms_norm/reference.py:6-10, ops/add_rms_norm/reference.py:8-12):
-// silu(g) * u = (g * (1 / (1 + exp(-g)))) * u, rsqrt(v) = 1 / sqrt(v) with IEEE sqrt and
-// division, the mean as the fp32 sum divided by the hidden size.
+// silu(g) * u = (g * (1 / (1 + exp(-g)))) * u (exp and the reciprocal through the fast
+// intrinsics, see silu_mul_f32), rsqrt(v) = 1 / sqrt(v) with IEEE sqrt and division, the
+// mean as the fp32 sum divided by the hidden size.
 //
 // Role of the reference: silu_mul_kernel, rms_norm_kernel, add_rms_norm_kernel and their
 // bindings (benchmarks/llm_ops/native_llm_ops.hip:51-94, :125-133, :306-353, :397-416).
 #include <cuda_runtime.h>
+
+#include <atomic>
 
 #include "rk_device.cuh"
 #include "rk_internal.h"
@@ -29,11 +35,18 @@
 namespace rk {
 namespace {
 
-constexpr int ROW_THREADS = 256;
-constexpr int ROW_CACHE = 4;  // 16-byte vectors per thread kept in registers (8192 elements)
+constexpr int ROW_CACHE = 4;  // 16-byte vectors per thread kept in registers
 
+// Tuning override of the threads per row (64, 128, 256; 0 = built-in choice).
+std::atomic<int> g_norm_threads{0};
+
+// sigmoid through the hardware exp2 / reciprocal intrinsics (__expf, __fdividef): a few
+// instructions per element instead of the ~30 of IEEE expf plus a division, which would
+// make the kernel issue-bound below the HBM rate.  Their fp32 error (a few ulp) is far
+// below one step of the 16-bit output; the parity tests hold the result to one step of the
+// reference.  Saturation: g -> -inf gives exp -> inf, 1/inf -> 0; NaN propagates.
 __device__ __forceinline__ float silu_mul_f32(float g, float u) {
-  const float s = 1.0f / (1.0f + expf(-g));
+  const float s = __fdividef(1.0f, 1.0f + __expf(-g));
   return (g * s) * u;
 }
 
@@ -76,6 +89,7 @@ __global__ void __launch_bounds__(256)
 
 // Sum over the CTA in a fixed order: shuffle tree inside each warp, then warp 0 adds the
 // eight warp sums in warp order.  Every thread receives the total.
+template <int ROW_THREADS>
 __device__ __forceinline__ float row_sum(float v, float* scratch) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -107,7 +121,7 @@ __device__ __forceinline__ uint32_t scale_pack(uint32_t v2, uint32_t w2, float r
 
 // One CTA per row.  ADD: s = x + residual is formed, stored to residual_out and
 // normalised; otherwise x is normalised.  VEC: 16-byte vectors (hidden % 8 == 0, aligned).
-template <typename T, bool ADD, bool VEC>
+template <typename T, bool ADD, bool VEC, int ROW_THREADS>
 __global__ void __launch_bounds__(ROW_THREADS)
     rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ residual,
                     const T* __restrict__ weight, T* __restrict__ out, T* __restrict__ residual_out,
@@ -181,7 +195,7 @@ __global__ void __launch_bounds__(ROW_THREADS)
           }
         }
       }
-      const float total = row_sum(sq, scratch);
+      const float total = row_sum<ROW_THREADS>(sq, scratch);
       const float r = 1.0f / sqrtf(total / static_cast<float>(hidden) + eps);
 #pragma unroll
       for (int c = 0; c < ROW_CACHE; ++c) {
@@ -218,7 +232,7 @@ __global__ void __launch_bounds__(ROW_THREADS)
         }
         sq += v * v;
       }
-      const float total = row_sum(sq, scratch);
+      const float total = row_sum<ROW_THREADS>(sq, scratch);
       const float r = 1.0f / sqrtf(total / static_cast<float>(hidden) + eps);
       for (int i = threadIdx.x; i < hidden; i += ROW_THREADS) {
         const float v = to_f32(ADD ? residual_out[base + i] : x[base + i]);
@@ -234,8 +248,10 @@ int elementwise_grid(int64_t vectors) {
   return static_cast<int>(want < 1 ? 1 : (want < cap ? want : cap));
 }
 
-int row_grid(int64_t rows) {
-  const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
+// Enough CTAs to fill every SM's thread slots (2048 threads per SM); more rows are
+// walked grid-stride.
+int row_grid(int64_t rows, int threads) {
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * (2048 / threads);
   return static_cast<int>(rows < cap ? rows : cap);
 }
 
@@ -254,18 +270,44 @@ rk_status silu_mul_typed(const void* gate, const void* up, void* out, int64_t n,
   return cuda_status(e);
 }
 
+template <typename T, bool ADD, int THREADS>
+cudaError_t launch_rows(bool vec, int64_t rows, const void* x, const void* residual,
+                        const void* weight, void* out, void* residual_out, int64_t hidden,
+                        float eps, cudaStream_t s) {
+  const int grid = row_grid(rows, THREADS);
+  auto kernel = vec ? rms_norm_kernel<T, ADD, true, THREADS> : rms_norm_kernel<T, ADD, false, THREADS>;
+  return launch_kernel(kernel, dim3(grid), dim3(THREADS), 0, s, 0, static_cast<const T*>(x),
+                       static_cast<const T*>(residual), static_cast<const T*>(weight),
+                       static_cast<T*>(out), static_cast<T*>(residual_out), rows,
+                       static_cast<int>(hidden), eps);
+}
+
 template <typename T, bool ADD>
 rk_status rms_norm_typed(const void* x, const void* residual, const void* weight, void* out,
                          void* residual_out, int64_t rows, int64_t hidden, float eps,
                          cudaStream_t s) {
   bool vec = hidden % 8 == 0 && aligned16(x) && aligned16(weight) && aligned16(out);
   if (ADD) vec = vec && aligned16(residual) && aligned16(residual_out);
-  const int grid = row_grid(rows);
-  auto kernel = vec ? rms_norm_kernel<T, ADD, true> : rms_norm_kernel<T, ADD, false>;
-  const cudaError_t e = launch_kernel(
-      kernel, dim3(grid), dim3(ROW_THREADS), 0, s, 0, static_cast<const T*>(x),
-      static_cast<const T*>(residual), static_cast<const T*>(weight), static_cast<T*>(out),
-      static_cast<T*>(residual_out), rows, static_cast<int>(hidden), eps);
+  int threads = g_norm_threads.load();
+  if (threads != 64 && threads != 128 && threads != 256) {
+    // Few rows (decode): 256 threads per row, the shortest latency per row.  Many rows
+    // (prefill): the fewest threads whose register cache still holds the whole row, so
+    // more rows are resident per SM (measured on B200: 2048 x 4096 add_rms_norm 10.7 us
+    // with 128 threads vs 11.5 us with 256; 1024 x 8192 best with 256).
+    threads = 256;
+    if (rows >= 2ll * device_sm_count()) {
+      const int64_t per_thread = (hidden / 8 + ROW_CACHE - 1) / ROW_CACHE;
+      threads = 64;
+      while (threads < 256 && threads < per_thread) threads *= 2;
+    }
+  }
+  cudaError_t e;
+  if (threads == 64)
+    e = launch_rows<T, ADD, 64>(vec, rows, x, residual, weight, out, residual_out, hidden, eps, s);
+  else if (threads == 128)
+    e = launch_rows<T, ADD, 128>(vec, rows, x, residual, weight, out, residual_out, hidden, eps, s);
+  else
+    e = launch_rows<T, ADD, 256>(vec, rows, x, residual, weight, out, residual_out, hidden, eps, s);
   note_launch();
   return cuda_status(e);
 }
@@ -279,6 +321,8 @@ rk_status silu_mul_launch(const void* gate, const void* up, void* out, int64_t t
   return dt == RK_DTYPE_BF16 ? silu_mul_typed<__nv_bfloat16>(gate, up, out, n, s)
                              : silu_mul_typed<__half>(gate, up, out, n, s);
 }
+
+void norm_set_threads(int threads) { g_norm_threads.store(threads); }
 
 rk_status rms_norm_launch(const void* x, const void* residual, const void* weight, void* out,
                           void* residual_out, int64_t tokens, int64_t hidden, float eps,

@@ -137,6 +137,8 @@ void rk_gemm_set_tile_n(int tile_n) { rk::gemm_set_tile_n(tile_n); }
 
 void rk_gemv_tc_set_cluster(int cluster_size) { rk::gemv_tc_set_cluster(cluster_size); }
 
+void rk_norm_set_threads(int threads_per_row) { rk::norm_set_threads(threads_per_row); }
+
 int rk_set_programmatic_launch(int enable) { return rk::set_programmatic_launch(enable != 0) ? 1 : 0; }
 
 const char* rk_variant_name(int op, int variant) {

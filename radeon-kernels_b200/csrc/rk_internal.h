@@ -91,6 +91,7 @@ rk_status silu_mul_launch(const void* gate, const void* up, void* out, int64_t t
 rk_status rms_norm_launch(const void* x, const void* residual, const void* weight, void* out,
                           void* residual_out, int64_t tokens, int64_t hidden, float eps,
                           rk_dtype dt, cudaStream_t s);
+void norm_set_threads(int threads);
 
 rk_status gather_column_blocks_launch(const void* blocks, void* out, int64_t G, int64_t M,
                                       int64_t N, rk_dtype dt, cudaStream_t s);

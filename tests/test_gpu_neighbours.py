@@ -151,7 +151,11 @@ def test_add_rms_norm_workloads(tokens, hidden, dtype):
 
 
 @pytest.mark.parametrize("offset", [0, 1])  # 1: every pointer 2 bytes off 16-byte alignment -> scalar path
-@pytest.mark.parametrize("tokens, hidden", [(3, 4100), (2, 7), (5, 24), (1, 33000)])
+@pytest.mark.parametrize(
+    "tokens, hidden",
+    # few rows: a CTA per row; >= 2 x SMs rows (aligned): a warp per row
+    [(3, 4100), (2, 7), (5, 24), (1, 33000), (400, 16392), (300, 24), (1000, 4104)],
+)
 def test_ragged_and_unaligned_shapes(tokens, hidden, offset):
     import torch
 
