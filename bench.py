@@ -557,6 +557,36 @@ def suite(args, dist: Dist, ext, peaks):
         }
         del a, b
 
+    def ffn_swiglu_case(name, m, n, k, dtype, iters):
+        """Fused FFN-up + SwiGLU: both products (2 x 2MNK FLOP) and the epilogue, one kernel."""
+
+        gen = torch.Generator(device="cuda").manual_seed(3)
+        tdt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
+        a = (torch.randn((m, k), generator=gen, device="cuda") / 64).to(tdt)
+        b = (torch.randn((k, 2 * n), generator=gen, device="cuda") / 64).to(tdt)
+        for _ in range(2):
+            ext.gemm_swiglu(a, b, 0)
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(iters):
+            flush.zero_()  # L2 flush between timed launches
+            times.append(time_loop(lambda i: ext.gemm_swiglu(a, b, 0), 1, stream))
+        dist.barrier()
+        ms = dist.max(statistics.median(times))
+        achieved = 2.0 * m * (2 * n) * k / (ms / 1e3) / 1e12
+        results[name] = {
+            "unit": "TFLOP/s",
+            "value": round(achieved * dist.world, 1),
+            "per_gpu": round(achieved, 1),
+            "ms": round(ms, 4),
+            "roofline_frac": round(achieved / peaks["bf16_tflops"], 4),
+            "scaling": "replica",
+            "shape": [m, n, k],
+            "dtype": dtype,
+            "timing": "single launch, L2 flushed; FLOP of both gate and up products",
+        }
+        del a, b
+
     def cool_down():
         # Let the power/clock state recover between long GEMM cases so one case's
         # power capping does not leak into the next measurement.
@@ -579,6 +609,8 @@ def suite(args, dist: Dist, ext, peaks):
     gemm_case("c1_gemm_1024_bf16", 1024, 1024, 1024, "bf16", "uniform", 0, 10, graph=True)
     cool_down()
     gemm_case("c4_gemm_ffn_up_fp16", 4096, 14336, 4096, "fp16", "normal64", 3, 10)
+    cool_down()
+    ffn_swiglu_case("c4_ffn_up_swiglu_fused_fp16", 4096, 14336, 4096, "fp16", 10)
     cool_down()
     if not args.quick:
         gemm_case("gemm_8192_bf16", 8192, 8192, 8192, "bf16", "uniform16", 7, 5)

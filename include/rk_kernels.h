@@ -157,6 +157,21 @@ RK_API rk_status rk_gather_column_blocks(const void* blocks, void* out, int64_t 
                                   rk_stream_t stream);
 
 /*
+ * Fused FFN-up projection with SwiGLU: C = silu(A @ B[:, :N]) * (A @ B[:, N:]).
+ * A: [M,K] row-major; B: [K, 2N] row-major, the gate projection in columns [0, N) and the
+ * up projection in columns [N, 2N) (torch.cat([w_gate, w_up], dim=1)); C: [M,N].  Both
+ * products accumulate in fp32 in TMEM and the epilogue applies silu(g) * u to the fp32
+ * sums before the one rounding to `dt`, so neither the [M, 2N] intermediate nor a second
+ * kernel touches HBM.  variant: RK_GEMM_AUTO, RK_GEMM_TC_1SM or RK_GEMM_TC_2SM; needs
+ * N % 8 == 0, K % 8 == 0 and 16-byte-aligned pointers (RK_ERR_UNSUPPORTED otherwise --
+ * callers then run rk_gemm into a [M, 2N] buffer followed by rk_silu_mul).  No
+ * counterpart in the reference, whose FFN runs rk.gemm and rk.silu_mul
+ * (src/radeon_kernels/ops/swiglu/api.py) as separate operators.
+ */
+RK_API rk_status rk_gemm_swiglu(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                                int64_t K, rk_dtype dt, int variant, rk_stream_t stream);
+
+/*
  * out = silu(gate) * up elementwise, silu(g) = g / (1 + exp(-g)) evaluated as
  * g * (1 / (1 + exp(-g))) in fp32, one rounding to `dt` per element.  gate, up,
  * out: [tokens, hidden] row-major, same dtype; tokens, hidden >= 0.  Replaces the

@@ -96,6 +96,24 @@ def gemv(x_bits: np.ndarray, w_bits: np.ndarray, dtype: str) -> tuple[np.ndarray
     return out, acc
 
 
+def gemm_swiglu(a_bits: np.ndarray, b_bits: np.ndarray, dtype: str) -> tuple[np.ndarray, np.ndarray]:
+    """silu(A @ B[:, :N]) * (A @ B[:, N:]) from the fp32 sums (B [K, 2N]); returns (bits, fp32).
+
+    The fused operator has no counterpart in the reference; its definition is the
+    reference's two operators composed in fp32 -- the GEMM sums (as rk_oracle_gemm forms
+    them) fed to silu_mul_reference's arithmetic (ops/swiglu/reference.py:6-9) before any
+    rounding.
+    """
+
+    _, acc = gemm(a_bits, b_bits, dtype)
+    n = acc.shape[1] // 2
+    g, u = acc[:, :n], acc[:, n:]
+    with np.errstate(over="ignore", invalid="ignore"):
+        s = (np.float32(1) / (np.float32(1) + np.exp(-g))).astype(np.float32)
+        out32 = ((g * s).astype(np.float32) * u).astype(np.float32)
+    return round_to(out32, dtype), out32
+
+
 def silu_mul(gate_bits: np.ndarray, up_bits: np.ndarray, dtype: str) -> tuple[np.ndarray, np.ndarray]:
     """silu(gate) * up on 16-bit bit patterns [tokens, hidden]; returns (bits, fp32 before rounding)."""
 

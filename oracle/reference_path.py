@@ -10,6 +10,8 @@ ops/gemm/api.py:62-63, so the baseline calls them directly):
 * ``silu_mul_reference`` -- ops/swiglu/reference.py:6-9
 * ``rms_norm_reference`` -- ops/rms_norm/reference.py:6-10
 * ``add_rms_norm_reference`` -- ops/add_rms_norm/reference.py:8-12
+* ``gemm_swiglu_reference`` -- no single reference function: the fused FFN-up operator's
+  definition, the reference's GEMM and silu_mul composed in fp32
 
 They are one-line calls of ``torch.mm``; torch is the reference's arithmetic engine (see
 ``rk_oracle.c`` for the version note).  ``bench.py --impl reference`` times them on the
@@ -53,3 +55,10 @@ def rms_norm_reference(torch_module: Any, x: Any, weight: Any, eps: float) -> An
 def add_rms_norm_reference(torch_module: Any, x: Any, residual: Any, weight: Any, eps: float) -> tuple[Any, Any]:
     residual_out = x + residual
     return rms_norm_reference(torch_module, residual_out, weight, eps), residual_out
+
+
+def gemm_swiglu_reference(torch_module: Any, a: Any, b: Any) -> Any:
+    n = int(b.shape[1]) // 2
+    y = torch_module.mm(a.float(), b.float())
+    g, u = y[:, :n], y[:, n:]
+    return (g * torch_module.sigmoid(g) * u).to(dtype=a.dtype)

@@ -84,7 +84,10 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   nb = in_group / gsize;
 }
 
-template <typename T, int BN>
+// SWIGLU (BN = 256 only): B is [K, 2N] = [gate | up]; a tile has 128 output columns,
+// B chunks 0-1 come from the gate columns and 2-3 from the matching up columns, and the
+// epilogue stores silu(gate) * up (N is the output width).
+template <typename T, int BN, bool SWIGLU = false>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc1_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M, int N,
@@ -103,7 +106,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_m = (M + BM - 1) / BM;
-  const int num_n = (N + BN - 1) / BN;
+  static_assert(!SWIGLU || BN == 256, "the fused SwiGLU epilogue pairs 128 gate and 128 up columns");
+  const int num_n = SWIGLU ? (N + 127) / 128 : (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
   volatile int* abort_flag = &bars->abort;
@@ -153,9 +157,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           mbar_arrive_expect_tx(full, STAGE_BYTES);
           tma_load_2d(smem_u32(smem_a + stage * A_STAGE), &tmap_a, full, kb * BK, mb * BM);
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b, full,
-                        nb * BN + j * 64, kb * BK);
+          for (int j = 0; j < BN / 64; ++j) {
+            const int bcol = SWIGLU ? (j < 2 ? nb * 128 + j * 64 : N + nb * 128 + (j - 2) * 64)
+                                    : nb * BN + j * 64;
+            tma_load_2d(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b, full, bcol,
+                        kb * BK);
+          }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -256,11 +263,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       T* crow = C + static_cast<size_t>(row) * N;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < (SWIGLU ? 128 : BN) / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tbase + c * 32, r);
-        tmem_ld_wait();
-        const int n0 = nb * BN + c * 32;
+        if (SWIGLU) {
+          uint32_t u[32];
+          tmem_ld_32x32b_x32(tbase + 128 + c * 32, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            r[j] = __float_as_uint(swiglu_f32(__uint_as_float(r[j]), __uint_as_float(u[j])));
+        } else {
+          tmem_ld_wait();
+        }
+        const int n0 = (SWIGLU ? nb * 128 : nb * BN) + c * 32;
         if (row < M) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -291,14 +307,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 }  // namespace tc1
 
 namespace {
-template <typename T, int BN>
+template <typename T, int BN, bool SWIGLU = false>
 rk_status launch_tc1(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                      rk_dtype dt, cudaStream_t s) {
   CUtensorMap ta, tb;
   rk_status st = make_tmap_2d(&ta, A, dt, /*inner*/ K, /*outer*/ M, /*box_inner*/ 64,
                               /*box_outer*/ tc1::BM);
   if (st != RK_OK) return st;
-  st = make_tmap_2d(&tb, B, dt, N, K, 64, tc1::BK);
+  st = make_tmap_2d(&tb, B, dt, SWIGLU ? 2 * N : N, K, 64, tc1::BK);
   if (st != RK_OK) return st;
   LaunchCtl lc;
   if ((st = launch_ctl(&lc)) != RK_OK) return st;
@@ -311,13 +327,14 @@ rk_status launch_tc1(const void* A, const void* B, void* C, int64_t M, int64_t N
   cudaGetDevice(&dev);
   std::call_once(attr_once[dev & 63], [&] {
     attr_err[dev & 63] = cudaFuncSetAttribute(
-        tc1::gemm_tc1_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        tc1::gemm_tc1_kernel<T, BN, SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   });
   if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
 
-  const int64_t num_tiles = ((M + tc1::BM - 1) / tc1::BM) * ((N + BN - 1) / BN);
+  const int64_t tile_n = SWIGLU ? 128 : BN;
+  const int64_t num_tiles = ((M + tc1::BM - 1) / tc1::BM) * ((N + tile_n - 1) / tile_n);
   const int grid = static_cast<int>(num_tiles < device_sm_count() ? num_tiles : device_sm_count());
-  const cudaError_t e = launch_kernel(tc1::gemm_tc1_kernel<T, BN>, dim3(grid), dim3(tc1::THREADS),
+  const cudaError_t e = launch_kernel(tc1::gemm_tc1_kernel<T, BN, SWIGLU>, dim3(grid), dim3(tc1::THREADS),
                                       smem, s, 0, ta, tb, reinterpret_cast<T*>(C),
                                       static_cast<int>(M), static_cast<int>(N),
                                       static_cast<int>(K), ctl);
@@ -361,6 +378,13 @@ static std::atomic<int> g_tile_n_override{0};
 
 void gemm_set_tile_n(int bn) { g_tile_n_override.store(bn); }
 
+bool gemm_swiglu_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                           int64_t K) {
+  // B is [K, 2N]: the same rules as the plain GEMM with 2N columns, plus an output width
+  // that is a multiple of 8 (16-byte stores).
+  return N <= (1ll << 30) - 256 && gemm_tc_supported(A, B, C, M, 2 * N, K) && N % 8 == 0;
+}
+
 bool gemm_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
                        int64_t K) {
   if (device_cc_major() != 10) return false;
@@ -371,6 +395,13 @@ bool gemm_tc_supported(const void* A, const void* B, const void* C, int64_t M, i
   if (M > (1ll << 31) - 256 || N > (1ll << 31) - 256 || K > (1ll << 31) - 64) return false;
   if (M * N > (1ll << 62)) return false;
   return true;
+}
+
+rk_status gemm_swiglu_1sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                                 int64_t K, rk_dtype dt, cudaStream_t s) {
+  if (!gemm_swiglu_supported(A, B, C, M, N, K)) return RK_ERR_UNSUPPORTED;
+  if (dt == RK_DTYPE_BF16) return launch_tc1<__nv_bfloat16, 256, true>(A, B, C, M, N, K, dt, s);
+  return launch_tc1<__half, 256, true>(A, B, C, M, N, K, dt, s);
 }
 
 rk_status gemm_tc_1sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,

@@ -70,7 +70,11 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   nb = in_group / gsize;
 }
 
-template <typename T>
+// SWIGLU: B is [K, 2N] = [gate | up]; a tile has 128 output columns, the even CTA
+// stages the tile's 128 gate columns and the odd CTA the matching 128 up columns, so
+// accumulator columns 0-127 hold gate and 128-255 up for the CTA's rows, and the
+// epilogue stores silu(gate) * up (N is the output width).
+template <typename T, bool SWIGLU = false>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M, int N,
@@ -88,7 +92,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
   const int num_m = (M + BM - 1) / BM;
-  const int num_n = (N + BN - 1) / BN;
+  const int num_n = SWIGLU ? (N + HALF - 1) / HALF : (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + BK - 1) / BK;
   volatile int* abort_flag = &bars->abort;
@@ -138,10 +142,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (rank == 0) mbar_arrive_expect_tx(full_local, 2 * STAGE_BYTES);
           tma_load_2d_pair(smem_u32(smem_a + stage * A_STAGE), &tmap_a, full_even, kb * BK,
                            mb * BM + static_cast<int>(rank) * HALF);
+          const int bcol = SWIGLU ? (rank == 0 ? nb * HALF : N + nb * HALF)
+                                  : nb * BN + static_cast<int>(rank) * HALF;
 #pragma unroll
           for (int j = 0; j < HALF / 64; ++j)
             tma_load_2d_pair(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b, full_even,
-                             nb * BN + static_cast<int>(rank) * HALF + j * 64, kb * BK);
+                             bcol + j * 64, kb * BK);
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -234,11 +240,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       T* crow = C + static_cast<size_t>(row) * N;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < (SWIGLU ? HALF : BN) / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tbase + c * 32, r);
-        tmem_ld_wait();
-        const int n0 = nb * BN + c * 32;
+        if (SWIGLU) {
+          uint32_t u[32];
+          tmem_ld_32x32b_x32(tbase + HALF + c * 32, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            r[j] = __float_as_uint(swiglu_f32(__uint_as_float(r[j]), __uint_as_float(u[j])));
+        } else {
+          tmem_ld_wait();
+        }
+        const int n0 = (SWIGLU ? nb * HALF : nb * BN) + c * 32;
         if (row < M) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -271,13 +286,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 }  // namespace tc2
 
 namespace {
-template <typename T>
+template <typename T, bool SWIGLU = false>
 rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                      rk_dtype dt, cudaStream_t s) {
   CUtensorMap ta, tb;
   rk_status st = make_tmap_2d(&ta, A, dt, K, M, 64, tc2::HALF);
   if (st != RK_OK) return st;
-  st = make_tmap_2d(&tb, B, dt, N, K, 64, tc2::BK);
+  st = make_tmap_2d(&tb, B, dt, SWIGLU ? 2 * N : N, K, 64, tc2::BK);
   if (st != RK_OK) return st;
   LaunchCtl lc;
   if ((st = launch_ctl(&lc)) != RK_OK) return st;
@@ -288,17 +303,18 @@ rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [&] {
-    attr_err[dev & 63] = cudaFuncSetAttribute(tc2::gemm_tc2_kernel<T>,
+    attr_err[dev & 63] = cudaFuncSetAttribute(tc2::gemm_tc2_kernel<T, SWIGLU>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               tc2::SMEM_BYTES);
   });
   if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
 
-  const int64_t tiles = ((M + tc2::BM - 1) / tc2::BM) * ((N + tc2::BN - 1) / tc2::BN);
+  const int64_t tile_n = SWIGLU ? tc2::HALF : tc2::BN;
+  const int64_t tiles = ((M + tc2::BM - 1) / tc2::BM) * ((N + tile_n - 1) / tile_n);
   const int64_t pairs_max = device_sm_count() / 2;
   const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
 
-  const cudaError_t e = launch_kernel(tc2::gemm_tc2_kernel<T>, dim3(static_cast<unsigned>(2 * pairs)),
+  const cudaError_t e = launch_kernel(tc2::gemm_tc2_kernel<T, SWIGLU>, dim3(static_cast<unsigned>(2 * pairs)),
                                       dim3(tc2::THREADS), tc2::SMEM_BYTES, s, 2, ta, tb,
                                       reinterpret_cast<T*>(C), static_cast<int>(M),
                                       static_cast<int>(N), static_cast<int>(K), ctl);
@@ -313,6 +329,14 @@ rk_status gemm_tc_2sm_launch(const void* A, const void* B, void* C, int64_t M, i
   if (device_sm_count() < 2) return RK_ERR_UNSUPPORTED;
   if (dt == RK_DTYPE_BF16) return launch_tc2<__nv_bfloat16>(A, B, C, M, N, K, dt, s);
   return launch_tc2<__half>(A, B, C, M, N, K, dt, s);
+}
+
+rk_status gemm_swiglu_2sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                                 int64_t K, rk_dtype dt, cudaStream_t s) {
+  if (!gemm_swiglu_supported(A, B, C, M, N, K)) return RK_ERR_UNSUPPORTED;
+  if (device_sm_count() < 2) return RK_ERR_UNSUPPORTED;
+  if (dt == RK_DTYPE_BF16) return launch_tc2<__nv_bfloat16, true>(A, B, C, M, N, K, dt, s);
+  return launch_tc2<__half, true>(A, B, C, M, N, K, dt, s);
 }
 
 }  // namespace rk

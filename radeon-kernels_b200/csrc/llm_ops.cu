@@ -40,15 +40,8 @@ constexpr int ROW_CACHE = 4;  // 16-byte vectors per thread kept in registers
 // Tuning override of the threads per row (64, 128, 256; 0 = built-in choice).
 std::atomic<int> g_norm_threads{0};
 
-// sigmoid through the hardware exp2 / reciprocal intrinsics (__expf, __fdividef): a few
-// instructions per element instead of the ~30 of IEEE expf plus a division, which would
-// make the kernel issue-bound below the HBM rate.  Their fp32 error (a few ulp) is far
-// below one step of the 16-bit output; the parity tests hold the result to one step of the
-// reference.  Saturation: g -> -inf gives exp -> inf, 1/inf -> 0; NaN propagates.
-__device__ __forceinline__ float silu_mul_f32(float g, float u) {
-  const float s = __fdividef(1.0f, 1.0f + __expf(-g));
-  return (g * s) * u;
-}
+// silu(g) * u: swiglu_f32 (rk_device.cuh), shared with the fused GEMM epilogue.
+__device__ __forceinline__ float silu_mul_f32(float g, float u) { return swiglu_f32(g, u); }
 
 template <typename T>
 __device__ __forceinline__ uint32_t pack_silu(uint32_t g2, uint32_t u2) {

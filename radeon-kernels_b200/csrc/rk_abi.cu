@@ -218,6 +218,28 @@ rk_status rk_gemv_ex(const void* x, const void* W, void* out, int64_t M, int64_t
   return RK_ERR_UNSUPPORTED;
 }
 
+rk_status rk_gemm_swiglu(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                         rk_dtype dt, int variant, rk_stream_t stream) {
+  if (M < 0 || N < 0 || K < 0 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
+  if (M > 0 && N > 0 && (A == nullptr || B == nullptr || C == nullptr)) return RK_ERR_INVALID_ARGUMENT;
+  if (variant < 0 || variant >= RK_GEMM_VARIANT_COUNT) return RK_ERR_UNSUPPORTED;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  if (M == 0 || N == 0) return RK_OK;
+  if (!gemm_swiglu_supported(A, B, C, M, N, K)) return RK_ERR_UNSUPPORTED;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (variant == RK_GEMM_AUTO) {
+    // SM pairs once there is a 256 x 128 output tile per pair (the plain GEMM's rule with
+    // the fused tile's 128 output columns).
+    const int64_t pair_tiles = ((M + 255) / 256) * ((N + 127) / 128);
+    variant = pair_tiles >= device_sm_count() / 2 ? RK_GEMM_TC_2SM : RK_GEMM_TC_1SM;
+  }
+  switch (variant) {
+    case RK_GEMM_TC_1SM: return gemm_swiglu_1sm_launch(A, B, C, M, N, K, dt, s);
+    case RK_GEMM_TC_2SM: return gemm_swiglu_2sm_launch(A, B, C, M, N, K, dt, s);
+  }
+  return RK_ERR_UNSUPPORTED;
+}
+
 rk_status rk_silu_mul(const void* gate, const void* up, void* out, int64_t tokens,
                       int64_t hidden, rk_dtype dt, rk_stream_t stream) {
   if (tokens < 0 || hidden < 0 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;

@@ -69,6 +69,13 @@ rk_status gemm_tc_2sm_launch(const void* A, const void* B, void* C, int64_t M, i
                              int64_t K, rk_dtype dt, cudaStream_t s);
 bool gemm_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
                        int64_t K);
+// Fused FFN-up + SwiGLU: C[M,N] = silu(A @ B[:, :N]) * (A @ B[:, N:]), B [K, 2N].
+bool gemm_swiglu_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                           int64_t K);
+rk_status gemm_swiglu_1sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                                 int64_t K, rk_dtype dt, cudaStream_t s);
+rk_status gemm_swiglu_2sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                                 int64_t K, rk_dtype dt, cudaStream_t s);
 
 rk_status gemv_scalar_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,
                              int64_t K, rk_dtype dt, cudaStream_t s);

@@ -149,6 +149,24 @@ at::Tensor gather_column_blocks(const at::Tensor& blocks, at::Tensor out) {
   return out;
 }
 
+// Fused FFN-up + SwiGLU (rk_gemm_swiglu): b is [K, 2N] = [gate | up], returns [M, N].
+at::Tensor gemm_swiglu(const at::Tensor& a, const at::Tensor& b, int64_t variant) {
+  check_matrix(a, "a");
+  check_matrix(b, "b");
+  TORCH_CHECK(a.device() == b.device() && a.scalar_type() == b.scalar_type(),
+              "a and b must share device and dtype");
+  TORCH_CHECK(a.size(1) == b.size(0), "incompatible GEMM dimensions");
+  TORCH_CHECK(b.size(1) % 2 == 0, "b must hold the gate and up projections side by side");
+  c10::cuda::CUDAGuard guard(a.device());
+  const int64_t n = b.size(1) / 2;
+  auto out = at::empty({a.size(0), n}, a.options());
+  check_status(rk_gemm_swiglu(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.size(0), n,
+                              a.size(1), dtype_of(a, "a"), static_cast<int>(variant),
+                              current_stream(a)),
+               "rk_gemm_swiglu");
+  return out;
+}
+
 // Decode neighbours: the reference's pybind names and signatures
 // (benchmarks/llm_ops/native_llm_ops.hip:306-353, :397-416), outputs allocated here.
 void check_rows(const at::Tensor& t, const char* name, int64_t rank) {
@@ -229,6 +247,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_stream", &gemv_stream, "128-bit weight-streaming GEMV (K % 8 == 0, 16B aligned)");
   m.def("gemv_scalar", &gemv_scalar, "generic GEMV (any K, any alignment)");
   m.def("gather_column_blocks", &gather_column_blocks, "[G,M,N/G] blocks -> row-major [M,N]");
+  m.def("gemm_swiglu", &gemm_swiglu, "silu(a @ b[:, :N]) * (a @ b[:, N:])", py::arg("a"),
+        py::arg("b"), py::arg("variant") = 0);
   m.def("silu_mul", &silu_mul, "silu(gate) * up", py::arg("gate"), py::arg("up"));
   m.def("rms_norm", &rms_norm, "row RMS normalisation", py::arg("input"), py::arg("weight"),
         py::arg("eps"));

@@ -79,6 +79,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_gemv_ex.restype = cint
     lib.rk_gemv_workspace_size.argtypes = [i64, i64, i64, cint, cint, ctypes.POINTER(ctypes.c_size_t)]
     lib.rk_gemv_workspace_size.restype = cint
+    lib.rk_gemm_swiglu.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, vp]
+    lib.rk_gemm_swiglu.restype = cint
     lib.rk_silu_mul.argtypes = [vp, vp, vp, i64, i64, cint, vp]
     lib.rk_silu_mul.restype = cint
     lib.rk_rms_norm.argtypes = [vp, vp, vp, i64, i64, ctypes.c_float, cint, vp]

@@ -23,6 +23,7 @@ SELECTED_GEMV = "cuda/gemv"
 SELECTED_SILU_MUL = "cuda/silu_mul"
 SELECTED_RMS_NORM = "cuda/rms_norm"
 SELECTED_ADD_RMS_NORM = "cuda/add_rms_norm"
+SELECTED_GEMM_SWIGLU = "cuda/gemm_swiglu"
 
 
 def _contiguous(tensor: Any) -> Any:
@@ -161,3 +162,20 @@ def add_rms_norm(torch_module: Any, x: Any, residual: Any, weight: Any, eps: flo
         weight,
     )
     return out[0], out[1]
+
+
+def _gemm_swiglu_raw(a: Any, b: Any) -> Any:
+    ext = _native.extension()
+    n = int(b.shape[1]) // 2
+    try:
+        return ext.gemm_swiglu(a, b, 0)
+    except RuntimeError as error:
+        if "variant does not support" not in str(error):
+            raise
+    # Shapes the fused kernel cannot take: this library's GEMM, then its silu_mul.
+    y = ext.gemm(a, b, 0)
+    return ext.silu_mul(y[:, :n].contiguous(), y[:, n:].contiguous())
+
+
+def gemm_swiglu(torch_module: Any, a: Any, b: Any) -> Any:
+    return _run(torch_module, "gemm_swiglu", _gemm_swiglu_raw, a, b)

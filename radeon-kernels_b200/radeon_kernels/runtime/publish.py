@@ -30,6 +30,7 @@ ENTRYPOINTS = {
     ("swiglu", "1.0"): ("silu_mul", "rk-sm100a-swiglu"),
     ("rms_norm", "1.0"): ("rms_norm", "rk-sm100a-rms_norm"),
     ("add_rms_norm", "1.0"): ("add_rms_norm", "rk-sm100a-add_rms_norm"),
+    ("gemm_swiglu", "1.0"): ("gemm_swiglu", "rk-sm100a-gemm_swiglu"),
 }
 
 
