@@ -724,6 +724,7 @@ PROFILE_CASES = {
     "gemm_8192": ("gemm", 8192, 8192, 8192, "bf16", "uniform16"),
     "swiglu_prefill": ("silu_mul", 1024, 11008, 0, "bf16", "normal"),
     "add_rms_norm_prefill": ("add_rms_norm", 2048, 4096, 0, "bf16", "normal"),
+    "ffn_swiglu": ("gemm_swiglu", 4096, 14336, 4096, "fp16", "normal64"),
 }
 
 
@@ -746,6 +747,10 @@ def run_profile(args) -> int:
         gate = seeded((m, n), 1, dist_name, dtype)
         up = seeded((m, n), 2, dist_name, dtype)
         launch = lambda: ext.silu_mul(gate, up)  # noqa: E731
+    elif kind == "gemm_swiglu":  # b is [K, 2N]
+        a = seeded((m, k), 1, dist_name, dtype)
+        b = seeded((k, 2 * n), 2, dist_name, dtype)
+        launch = lambda: ext.gemm_swiglu(a, b, 0)  # noqa: E731
     elif kind == "add_rms_norm":
         x = seeded((m, n), 1, dist_name, dtype)
         r = seeded((m, n), 2, dist_name, dtype)
