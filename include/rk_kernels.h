@@ -172,6 +172,42 @@ RK_API rk_status rk_gemm_swiglu(const void* A, const void* B, void* C, int64_t M
                                 int64_t K, rk_dtype dt, int variant, rk_stream_t stream);
 
 /*
+ * Decode attention over a paged K/V cache, one query token per sequence:
+ *   out[b,h,:] = softmax_t(scale * query[b,h,:] . K[b,t,:]) @ V[b,t,:],  t < context_lengths[b]
+ * query, out: [batch, query_heads, head_dim]; key_cache, value_cache: [num_blocks,
+ * block_size, kv_heads, head_dim] ("block_slot_head_dim"); block_tables: [batch,
+ * max_blocks_per_sequence] and context_lengths: [batch], both int32 (index_bits 32) or
+ * int64 (index_bits 64) on the device.  Query head h reads KV head h / (query_heads /
+ * kv_heads).  head_dim 64, 128 or 256; query and caches 16-byte aligned.  fp32 scores,
+ * softmax and sum, one rounding of the output; a sequence with context length 0 gives NaN
+ * (as the reference's softmax of an all -inf row).  Context lengths above
+ * max_blocks_per_sequence * block_size are clamped to it.  Block-table entries outside
+ * [0, num_blocks) are not dereferenced: those positions are skipped and
+ * rk_device_status() reports RK_ERR_INVALID_ARGUMENT.  Long contexts are split over
+ * several CTAs per sequence whose partial results meet in `workspace`
+ * (rk_paged_attention_workspace_size(); no initialisation needed); NULL or too small when
+ * one is needed -> RK_ERR_INVALID_ARGUMENT.  Replaces the reference's pybind entries
+ * attention_wave1/4/8 (benchmarks/paged_attention/native_paged_attention.hip:192-283)
+ * behind rk.paged_attention_decode (src/radeon_kernels/ops/paged_attention/api.py:38-157).
+ */
+RK_API rk_status rk_paged_attention_decode(const void* query, const void* key_cache,
+                                           const void* value_cache, const void* block_tables,
+                                           const void* context_lengths, void* out,
+                                           int64_t batch, int64_t query_heads,
+                                           int64_t kv_heads, int64_t head_dim,
+                                           int64_t num_blocks, int64_t block_size,
+                                           int64_t max_blocks_per_sequence, float scale,
+                                           rk_dtype dt, int index_bits, void* workspace,
+                                           size_t workspace_bytes, rk_stream_t stream);
+
+/* Workspace bytes rk_paged_attention_decode needs for this shape (0: none). */
+RK_API rk_status rk_paged_attention_workspace_size(int64_t batch, int64_t query_heads,
+                                                   int64_t kv_heads, int64_t head_dim,
+                                                   int64_t block_size,
+                                                   int64_t max_blocks_per_sequence,
+                                                   size_t* bytes);
+
+/*
  * out = silu(gate) * up elementwise, silu(g) = g / (1 + exp(-g)) evaluated as
  * g * (1 / (1 + exp(-g))) in fp32, one rounding to `dt` per element.  gate, up,
  * out: [tokens, hidden] row-major, same dtype; tokens, hidden >= 0.  Replaces the
@@ -242,8 +278,10 @@ RK_API int rk_set_programmatic_launch(int enable);
 
 /*
  * Reads and clears the device-side status word of the current device after
- * synchronising `stream`.  Returns RK_OK, or RK_ERR_TIMEOUT when a kernel
- * launched since the previous call gave up on a bounded wait.
+ * synchronising `stream`.  Returns RK_OK, RK_ERR_TIMEOUT when a kernel launched
+ * since the previous call gave up on a bounded wait, or RK_ERR_INVALID_ARGUMENT
+ * when one met an out-of-range index in device memory (a paged-attention block
+ * table entry) and skipped it.
  */
 RK_API rk_status rk_device_status(rk_stream_t stream);
 

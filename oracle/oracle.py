@@ -157,6 +157,70 @@ def add_rms_norm(
     return out, residual_out, exact
 
 
+def paged_attention_decode(
+    q_bits: np.ndarray,
+    k_bits: np.ndarray,
+    v_bits: np.ndarray,
+    block_tables: np.ndarray,
+    context_lengths: np.ndarray,
+    scale: float,
+    dtype: str,
+) -> tuple[np.ndarray, np.ndarray]:
+    """Decode attention over a paged K/V cache; returns (bits, fp32 before rounding).
+
+    Restates paged_attention_decode_reference (src/radeon_kernels/ops/paged_attention/
+    reference.py:8-47) in numpy fp32: positions t < context_length map to cache slot
+    block_tables[b, t // block_size] * block_size + t % block_size; query head h reads KV head
+    h // (query_heads // kv_heads); scores q . k * scale, softmax with the maximum
+    subtracted, probabilities times V.  A sequence with no position gives NaN (the
+    reference's softmax of an all -inf row).
+    """
+
+    q = widen(q_bits, dtype)
+    k = widen(k_bits, dtype)
+    v = widen(v_bits, dtype)
+    batch, heads, head_dim = q.shape
+    _, block_size, kv_heads, _ = k.shape
+    group = heads // kv_heads
+    max_ctx = block_tables.shape[1] * block_size
+    out = np.empty((batch, heads, head_dim), np.float32)
+    sc = np.float32(scale)
+    for b in range(batch):
+        ctx = int(min(max(int(context_lengths[b]), 0), max_ctx))
+        if ctx == 0:
+            out[b] = np.nan
+            continue
+        t = np.arange(ctx)
+        blocks = np.asarray(block_tables[b], np.int64)[t // block_size]
+        keys = k[blocks, t % block_size]  # [ctx, kv_heads, head_dim]
+        values = v[blocks, t % block_size]
+        for h in range(heads):
+            kvh = h // group
+            scores = (keys[:, kvh, :] @ q[b, h]).astype(np.float32) * sc
+            e = np.exp(scores - scores.max()).astype(np.float32)
+            p = (e / e.sum(dtype=np.float32)).astype(np.float32)
+            out[b, h] = (p @ values[:, kvh, :]).astype(np.float32)
+    return round_to(out, dtype), out
+
+
+def assert_attention(result_bits: np.ndarray, ref_bits: np.ndarray, ref_fp32: np.ndarray, dtype: str) -> dict[str, float]:
+    """NaN exactly where the reference has NaN; the GEMM parity gate on the rest.
+
+    Attention outputs are fp32 sums over the context (q.k, then p.V) whose order differs
+    between implementations, like a GEMM's, so the finite part gets assert_parity.
+    """
+
+    result = np.asarray(result_bits, np.uint16)
+    ref = np.asarray(ref_bits, np.uint16)
+    nan_r, nan_ref = _is_nan(result, dtype), _is_nan(ref, dtype)
+    if not np.array_equal(nan_r, nan_ref):
+        raise AssertionError(f"NaN positions differ at {np.argwhere(nan_r != nan_ref)[:5].tolist()}")
+    keep = ~nan_ref
+    if not keep.any():
+        return {"parity_error": 0.0}
+    return assert_parity(result[keep], ref[keep], np.asarray(ref_fp32)[keep], dtype)
+
+
 def widen(bits: np.ndarray, dtype: str) -> np.ndarray:
     src = np.ascontiguousarray(bits, dtype=np.uint16)
     dst = np.empty(src.shape, np.float32)

@@ -10,6 +10,7 @@ ops/gemm/api.py:62-63, so the baseline calls them directly):
 * ``silu_mul_reference`` -- ops/swiglu/reference.py:6-9
 * ``rms_norm_reference`` -- ops/rms_norm/reference.py:6-10
 * ``add_rms_norm_reference`` -- ops/add_rms_norm/reference.py:8-12
+* ``paged_attention_decode_reference`` -- ops/paged_attention/reference.py:8-47
 * ``gemm_swiglu_reference`` -- no single reference function: the fused FFN-up operator's
   definition, the reference's GEMM and silu_mul composed in fp32
 
@@ -62,3 +63,23 @@ def gemm_swiglu_reference(torch_module: Any, a: Any, b: Any) -> Any:
     y = torch_module.mm(a.float(), b.float())
     g, u = y[:, :n], y[:, n:]
     return (g * torch_module.sigmoid(g) * u).to(dtype=a.dtype)
+
+
+def paged_attention_decode_reference(
+    torch_module: Any, query: Any, key_cache: Any, value_cache: Any, block_tables: Any, context_lengths: Any, scale: float
+) -> Any:
+    batch, heads, head_dim = (int(n) for n in query.shape)
+    block_size, kv_heads = int(key_cache.shape[1]), int(key_cache.shape[2])
+    max_ctx = int(block_tables.shape[1]) * block_size
+    positions = torch_module.arange(max_ctx, device=query.device)
+    slots = block_tables.long().index_select(1, positions // block_size) * block_size + (positions % block_size).unsqueeze(0)
+    keys = key_cache.view(-1, kv_heads, head_dim).index_select(0, slots.reshape(-1)).view(batch, max_ctx, kv_heads, head_dim)
+    values = value_cache.view(-1, kv_heads, head_dim).index_select(0, slots.reshape(-1)).view(batch, max_ctx, kv_heads, head_dim)
+    kv_index = torch_module.arange(heads, device=query.device) // (heads // kv_heads)
+    keys = keys.index_select(2, kv_index).float()
+    values = values.index_select(2, kv_index).float()
+    scores = torch_module.einsum("bhd,bthd->bht", query.float(), keys) * scale
+    valid = positions.unsqueeze(0) < context_lengths.long().unsqueeze(1)
+    scores = scores.masked_fill(~valid.unsqueeze(1), float("-inf"))
+    probabilities = torch_module.softmax(scores, dim=-1, dtype=torch_module.float32)
+    return torch_module.einsum("bht,bthd->bhd", probabilities, values).to(dtype=query.dtype)

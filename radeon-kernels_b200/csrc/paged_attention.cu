@@ -1,0 +1,357 @@
+// paged_attention.cu -- decode attention over a paged K/V cache (one query token per
+// sequence), the B200 counterpart of rk.paged_attention_decode:
+//
+//   out[b, h, :] = softmax_t(scale * q[b, h, :] . K[b, t, kvh, :]) @ V[b, t, kvh, :]
+//   t < context_lengths[b], kvh = h / (query_heads / kv_heads),
+//   K[b, t] = key_cache[block_tables[b, t / block_size], t % block_size]   (same for V)
+//
+// Arithmetic follows the reference's fp32 definition (src/radeon_kernels/ops/
+// paged_attention/reference.py:8-47): fp32 scores, fp32 softmax, fp32 weighted sum, one
+// rounding of the output.  A sequence with no valid position gives NaN, as torch's softmax
+// of an all -inf row does.
+//
+// Design (an HBM stream over the K/V bytes of every sequence, "flash decoding"):
+//   * grid (partition, kv head x head group, sequence): a CTA walks one contiguous range
+//     of positions of one sequence for one KV head and the G (1, 2, 4 or 8) query heads
+//     that share it (GQA), so every K/V vector is read from HBM once per group of up to
+//     8 query heads;
+//   * 128 threads; a position's 16-byte K and V vectors (8 elements) are spread over
+//     D/8 threads, so 128*8/D positions are processed side by side, 4 deep in flight per
+//     thread; the dot product of a position is a shuffle tree over its D/8 threads;
+//   * online softmax per head and position group in fp32 (running max, running sum,
+//     rescaled accumulator), merged across the groups of the CTA in shared memory in a
+//     fixed order;
+//   * several partitions per sequence: the partial (max, sum, accumulator) of each goes to
+//     the caller's workspace and a second kernel merges them in partition order; a
+//     single partition writes the output directly.
+// Block-table entries outside [0, num_blocks) are never dereferenced: the position is
+// skipped and RK_DEV_ERR_BAD_INDEX is set in the device status word.
+//
+// Role of the reference: attention_wave1/4/8 and paged_attention_impl
+// (benchmarks/paged_attention/native_paged_attention.hip:192-283).
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "rk_device.cuh"
+#include "rk_internal.h"
+
+namespace rk {
+namespace pa {
+
+constexpr int THREADS = 128;
+constexpr int GMAX = 8;    // query heads per CTA at most
+constexpr int UNROLL = 4;  // positions in flight per thread
+
+struct Params {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* tables;
+  const void* lens;
+  void* out;
+  float* part_acc;  // [batch, hq, partitions, D]
+  float* part_ml;   // [batch, hq, partitions, 2] (max, sum)
+  int batch, hq, hkv, group, head_groups;
+  int num_blocks, block_size, max_blocks;
+  int partitions, part_tokens;
+  float scale;
+};
+
+// G: query heads handled per CTA (the GQA group size rounded up to 1, 2, 4 or 8).
+template <typename T, typename Index, int D, int G>
+__global__ void __launch_bounds__(THREADS)
+    paged_partition_kernel(Params p, KernelCtl ctl) {
+  constexpr int TPT = D / 8;             // threads per position
+  constexpr int GROUPS = THREADS / TPT;  // positions side by side
+  __shared__ float s_m[GROUPS][G];
+  __shared__ float s_l[GROUPS][G];
+  __shared__ float s_acc[GROUPS][G][D];
+
+  pdl_begin();
+  const int part = blockIdx.x;
+  const int kvh = blockIdx.y / p.head_groups;
+  const int hg = blockIdx.y - kvh * p.head_groups;
+  const int b = blockIdx.z;
+  const int tg = threadIdx.x / TPT, ti = threadIdx.x - tg * TPT;
+  const int h0 = kvh * p.group + hg * G;
+  const int nh = min(G, p.group - hg * G);
+
+  const Index* tables = static_cast<const Index*>(p.tables) + static_cast<int64_t>(b) * p.max_blocks;
+  int64_t ctx = static_cast<int64_t>(static_cast<const Index*>(p.lens)[b]);
+  const int64_t max_ctx = static_cast<int64_t>(p.max_blocks) * p.block_size;
+  ctx = ctx < 0 ? 0 : (ctx > max_ctx ? max_ctx : ctx);
+  const int64_t t_begin = static_cast<int64_t>(part) * p.part_tokens;
+  const int64_t t_end = min(t_begin + p.part_tokens, ctx);
+
+  // This thread's 8 dims of each query head, in fp32.
+  float q[G][8];
+  const T* qb = static_cast<const T*>(p.q) + (static_cast<int64_t>(b) * p.hq + h0) * D + ti * 8;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (g < nh) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(qb + static_cast<int64_t>(g) * D);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = Pack2<T>::to_floats(w[j]);
+        q[g][2 * j] = f.x;
+        q[g][2 * j + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[g][j] = 0.f;
+    }
+  }
+  float m[G], l[G], acc[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[g][j] = 0.f;
+  }
+
+  const int64_t row_stride = static_cast<int64_t>(p.hkv) * D;  // elements between slots
+  const T* kbase = static_cast<const T*>(p.k) + static_cast<int64_t>(kvh) * D + ti * 8;
+  const T* vbase = static_cast<const T*>(p.v) + static_cast<int64_t>(kvh) * D + ti * 8;
+
+  // The trip count is the same for every thread of the CTA (the shuffles below are
+  // warp-wide); a thread's positions are tb + tg + u * GROUPS.
+  for (int64_t tb = t_begin; tb < t_end; tb += GROUPS * UNROLL) {
+    uint4 kv[UNROLL], vv[UNROLL];
+    bool use[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const int64_t t = tb + tg + static_cast<int64_t>(u) * GROUPS;
+      use[u] = false;
+      kv[u] = make_uint4(0, 0, 0, 0);
+      vv[u] = make_uint4(0, 0, 0, 0);
+      if (t < t_end) {
+        const int64_t blk = static_cast<int64_t>(tables[t / p.block_size]);
+        if (blk >= 0 && blk < p.num_blocks) {
+          const int64_t slot = blk * p.block_size + (t - (t / p.block_size) * p.block_size);
+          kv[u] = ld_stream_v4(kbase + slot * row_stride);
+          vv[u] = ld_stream_v4(vbase + slot * row_stride);
+          use[u] = true;
+        } else if (ti == 0) {
+          atomicOr(ctl.status, RK_DEV_ERR_BAD_INDEX);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      // Warp-wide shuffles run for every lane, used position or not (a warp holds
+      // several position groups that can reach the end of the range at different u);
+      // only the softmax update is skipped for unused positions.
+      float kf[8], vf[8];
+      const uint32_t kw[4] = {kv[u].x, kv[u].y, kv[u].z, kv[u].w};
+      const uint32_t vw[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = Pack2<T>::to_floats(use[u] ? kw[j] : 0u);
+        const float2 c = Pack2<T>::to_floats(use[u] ? vw[j] : 0u);
+        kf[2 * j] = a.x;
+        kf[2 * j + 1] = a.y;
+        vf[2 * j] = c.x;
+        vf[2 * j + 1] = c.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s = fmaf(q[g][j], kf[j], s);
+#pragma unroll
+        for (int o = TPT / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (use[u] && g < nh) {
+          s *= p.scale;
+          const float m_new = fmaxf(m[g], s);
+          const float alpha = __expf(m[g] - m_new);  // 0 when m was -inf
+          const float beta = __expf(s - m_new);
+          l[g] = l[g] * alpha + beta;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(beta, vf[j], acc[g][j] * alpha);
+          m[g] = m_new;
+        }
+      }
+    }
+  }
+
+  // Merge the position groups of this CTA in group order.
+  if (ti == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      s_m[tg][g] = m[g];
+      s_l[tg][g] = l[g];
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s_acc[tg][g][ti * 8 + j] = acc[g][j];
+  __syncthreads();
+
+  for (int idx = threadIdx.x; idx < nh * D; idx += THREADS) {
+    const int g = idx / D, d = idx - g * D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < GROUPS; ++j) mx = fmaxf(mx, s_m[j][g]);
+    float sum = 0.f, a = 0.f;
+    if (mx != -INFINITY) {
+#pragma unroll
+      for (int j = 0; j < GROUPS; ++j) {
+        if (s_m[j][g] != -INFINITY) {
+          const float w = __expf(s_m[j][g] - mx);
+          sum += s_l[j][g] * w;
+          a += s_acc[j][g][d] * w;
+        }
+      }
+    }
+    const int64_t head = static_cast<int64_t>(b) * p.hq + h0 + g;
+    if (p.partitions == 1) {
+      static_cast<T*>(p.out)[head * D + d] = from_f32<T>(a / sum);  // 0/0 = NaN for ctx 0
+    } else {
+      const int64_t slot = head * p.partitions + part;
+      p.part_acc[slot * D + d] = a;
+      if (d == 0) {
+        p.part_ml[2 * slot] = mx;
+        p.part_ml[2 * slot + 1] = sum;
+      }
+    }
+  }
+}
+
+// One CTA per (sequence, query head), one thread per output element: merges the
+// partitions in partition order.
+template <typename T, int D>
+__global__ void __launch_bounds__(D) paged_merge_kernel(Params p) {
+  pdl_begin();
+  const int64_t head = blockIdx.x;
+  const int d = threadIdx.x;
+  const float* ml = p.part_ml + head * p.partitions * 2;
+  const float* acc = p.part_acc + head * p.partitions * D + d;
+  float mx = -INFINITY;
+  for (int j = 0; j < p.partitions; ++j) mx = fmaxf(mx, ml[2 * j]);
+  float sum = 0.f, a = 0.f;
+  if (mx != -INFINITY) {
+    for (int j = 0; j < p.partitions; ++j) {
+      if (ml[2 * j] != -INFINITY) {
+        const float w = __expf(ml[2 * j] - mx);
+        sum += ml[2 * j + 1] * w;
+        a += acc[static_cast<int64_t>(j) * D] * w;
+      }
+    }
+  }
+  static_cast<T*>(p.out)[head * D + d] = from_f32<T>(a / sum);
+}
+
+struct Plan {
+  int g, head_groups, partitions, part_tokens;
+};
+
+Plan plan(int64_t batch, int64_t hq, int64_t hkv, int64_t max_ctx, int sms) {
+  Plan pl{};
+  const int64_t group = hq / hkv;
+  pl.g = 1;
+  while (pl.g < GMAX && pl.g < group) pl.g *= 2;
+  pl.head_groups = static_cast<int>((group + pl.g - 1) / pl.g);
+  const int64_t base = batch * hkv * pl.head_groups;
+  // Enough partitions for two CTAs per SM, each at least 64 positions long.
+  int64_t parts = (2ll * sms + base - 1) / base;
+  const int64_t cap = (max_ctx + 63) / 64;
+  if (parts > cap) parts = cap;
+  if (parts < 1) parts = 1;
+  pl.partitions = static_cast<int>(parts);
+  pl.part_tokens = static_cast<int>((max_ctx + parts - 1) / parts);
+  return pl;
+}
+
+template <typename T, typename Index, int D, int G>
+rk_status launch(Params prm, const Plan& pl, cudaStream_t s) {
+  LaunchCtl lc;
+  rk_status st = launch_ctl(&lc);
+  if (st != RK_OK) return st;
+  const KernelCtl ctl{lc.status, lc.timeout_ns, 0};
+  const dim3 grid(static_cast<unsigned>(pl.partitions),
+                  static_cast<unsigned>(prm.hkv * pl.head_groups), static_cast<unsigned>(prm.batch));
+  cudaError_t e = launch_kernel(paged_partition_kernel<T, Index, D, G>, grid, dim3(THREADS), 0, s, 0,
+                                prm, ctl);
+  note_launch();
+  if (e == cudaSuccess && pl.partitions > 1) {
+    e = launch_kernel(paged_merge_kernel<T, D>, dim3(static_cast<unsigned>(prm.batch * prm.hq)),
+                      dim3(D), 0, s, 0, prm);
+    note_launch();
+  }
+  return cuda_status(e);
+}
+
+template <typename T, typename Index, int D>
+rk_status launch_g(Params prm, const Plan& pl, cudaStream_t s) {
+  switch (pl.g) {
+    case 1: return launch<T, Index, D, 1>(prm, pl, s);
+    case 2: return launch<T, Index, D, 2>(prm, pl, s);
+    case 4: return launch<T, Index, D, 4>(prm, pl, s);
+    default: return launch<T, Index, D, 8>(prm, pl, s);
+  }
+}
+
+template <typename T, typename Index>
+rk_status launch_d(Params prm, const Plan& pl, int64_t head_dim, cudaStream_t s) {
+  switch (head_dim) {
+    case 64: return launch_g<T, Index, 64>(prm, pl, s);
+    case 128: return launch_g<T, Index, 128>(prm, pl, s);
+    case 256: return launch_g<T, Index, 256>(prm, pl, s);
+  }
+  return RK_ERR_UNSUPPORTED;
+}
+
+}  // namespace pa
+
+size_t paged_attention_workspace_bytes(int64_t batch, int64_t hq, int64_t hkv, int64_t head_dim,
+                                       int64_t max_blocks, int64_t block_size) {
+  if (batch <= 0 || hq <= 0 || hkv <= 0 || hq % hkv != 0 || max_blocks <= 0 || block_size <= 0)
+    return 0;
+  const pa::Plan pl = pa::plan(batch, hq, hkv, max_blocks * block_size, device_sm_count());
+  if (pl.partitions == 1) return 0;
+  return static_cast<size_t>(batch) * hq * pl.partitions * (head_dim + 2) * sizeof(float);
+}
+
+rk_status paged_attention_launch(const void* query, const void* key_cache, const void* value_cache,
+                                 const void* block_tables, const void* context_lengths, void* out,
+                                 int64_t batch, int64_t hq, int64_t hkv, int64_t head_dim,
+                                 int64_t num_blocks, int64_t block_size, int64_t max_blocks,
+                                 float scale, rk_dtype dt, int index_bits, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t s) {
+  const pa::Plan pl = pa::plan(batch, hq, hkv, max_blocks * block_size, device_sm_count());
+  const size_t need = paged_attention_workspace_bytes(batch, hq, hkv, head_dim, max_blocks, block_size);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return RK_ERR_INVALID_ARGUMENT;
+  if (batch > 65535 || hkv * pl.head_groups > 65535) return RK_ERR_UNSUPPORTED;
+  pa::Params prm{};
+  prm.q = query;
+  prm.k = key_cache;
+  prm.v = value_cache;
+  prm.tables = block_tables;
+  prm.lens = context_lengths;
+  prm.out = out;
+  prm.part_acc = static_cast<float*>(workspace);
+  prm.part_ml = need > 0 ? static_cast<float*>(workspace) + batch * hq * pl.partitions * head_dim : nullptr;
+  prm.batch = static_cast<int>(batch);
+  prm.hq = static_cast<int>(hq);
+  prm.hkv = static_cast<int>(hkv);
+  prm.group = static_cast<int>(hq / hkv);
+  prm.head_groups = pl.head_groups;
+  prm.num_blocks = static_cast<int>(num_blocks);
+  prm.block_size = static_cast<int>(block_size);
+  prm.max_blocks = static_cast<int>(max_blocks);
+  prm.partitions = pl.partitions;
+  prm.part_tokens = pl.part_tokens;
+  prm.scale = scale;
+  const bool bf16 = dt == RK_DTYPE_BF16;
+  if (index_bits == 32)
+    return bf16 ? pa::launch_d<__nv_bfloat16, int32_t>(prm, pl, head_dim, s)
+                : pa::launch_d<__half, int32_t>(prm, pl, head_dim, s);
+  return bf16 ? pa::launch_d<__nv_bfloat16, int64_t>(prm, pl, head_dim, s)
+              : pa::launch_d<__half, int64_t>(prm, pl, head_dim, s);
+}
+
+}  // namespace rk

@@ -218,6 +218,47 @@ rk_status rk_gemv_ex(const void* x, const void* W, void* out, int64_t M, int64_t
   return RK_ERR_UNSUPPORTED;
 }
 
+rk_status rk_paged_attention_workspace_size(int64_t batch, int64_t query_heads,
+                                           int64_t kv_heads, int64_t head_dim,
+                                           int64_t block_size, int64_t max_blocks,
+                                           size_t* bytes) {
+  if (bytes == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  *bytes = 0;
+  if (batch < 1 || query_heads < 1 || kv_heads < 1 || query_heads % kv_heads != 0 ||
+      block_size < 1 || max_blocks < 1 || (head_dim != 64 && head_dim != 128 && head_dim != 256))
+    return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  *bytes = paged_attention_workspace_bytes(batch, query_heads, kv_heads, head_dim, max_blocks,
+                                           block_size);
+  return RK_OK;
+}
+
+rk_status rk_paged_attention_decode(const void* query, const void* key_cache,
+                                    const void* value_cache, const void* block_tables,
+                                    const void* context_lengths, void* out, int64_t batch,
+                                    int64_t query_heads, int64_t kv_heads, int64_t head_dim,
+                                    int64_t num_blocks, int64_t block_size, int64_t max_blocks,
+                                    float scale, rk_dtype dt, int index_bits, void* workspace,
+                                    size_t workspace_bytes, rk_stream_t stream) {
+  if (batch < 1 || query_heads < 1 || kv_heads < 1 || query_heads % kv_heads != 0 ||
+      num_blocks < 1 || block_size < 1 || max_blocks < 1 || !valid_dtype(dt) ||
+      (index_bits != 32 && index_bits != 64) || !(scale > 0.0f && scale <= 3.4e38f))
+    return RK_ERR_INVALID_ARGUMENT;
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return RK_ERR_INVALID_ARGUMENT;
+  if (query == nullptr || key_cache == nullptr || value_cache == nullptr ||
+      block_tables == nullptr || context_lengths == nullptr || out == nullptr)
+    return RK_ERR_INVALID_ARGUMENT;
+  if (!aligned16(query) || !aligned16(key_cache) || !aligned16(value_cache)) return RK_ERR_UNSUPPORTED;
+  if (num_blocks > INT32_MAX || block_size > INT32_MAX || max_blocks > INT32_MAX ||
+      max_blocks * block_size > INT32_MAX || batch * query_heads > INT32_MAX)
+    return RK_ERR_UNSUPPORTED;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return paged_attention_launch(query, key_cache, value_cache, block_tables, context_lengths, out,
+                                batch, query_heads, kv_heads, head_dim, num_blocks, block_size,
+                                max_blocks, scale, dt, index_bits, workspace, workspace_bytes,
+                                reinterpret_cast<cudaStream_t>(stream));
+}
+
 rk_status rk_gemm_swiglu(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                          rk_dtype dt, int variant, rk_stream_t stream) {
   if (M < 0 || N < 0 || K < 0 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
@@ -314,7 +355,8 @@ rk_status rk_device_status(rk_stream_t stream) {
     e = cudaMemsetAsync(d->status, 0, sizeof(uint32_t), s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return cuda_status(e);
-    return RK_ERR_TIMEOUT;
+    return (word & ~static_cast<uint32_t>(RK_DEV_ERR_BAD_INDEX)) != 0 ? RK_ERR_TIMEOUT
+                                                                      : RK_ERR_INVALID_ARGUMENT;
   }
   return RK_OK;
 }

@@ -17,6 +17,7 @@ enum : uint32_t {
   RK_DEV_ERR_TIMEOUT_MMA = 1u << 1,
   RK_DEV_ERR_TIMEOUT_EPILOGUE = 1u << 2,
   RK_DEV_ERR_TIMEOUT_DRAIN = 1u << 3,
+  RK_DEV_ERR_BAD_INDEX = 1u << 4,  // an index read from device memory was out of range
 };
 
 struct KernelCtl {

@@ -91,6 +91,16 @@ bool gemv_tc_supported(const void* x, const void* W, const void* out, int64_t M,
 bool gemv_stream_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,
                            int64_t K);
 
+// Paged decode attention (paged_attention.cu).
+size_t paged_attention_workspace_bytes(int64_t batch, int64_t hq, int64_t hkv, int64_t head_dim,
+                                       int64_t max_blocks, int64_t block_size);
+rk_status paged_attention_launch(const void* query, const void* key_cache, const void* value_cache,
+                                 const void* block_tables, const void* context_lengths, void* out,
+                                 int64_t batch, int64_t hq, int64_t hkv, int64_t head_dim,
+                                 int64_t num_blocks, int64_t block_size, int64_t max_blocks,
+                                 float scale, rk_dtype dt, int index_bits, void* workspace,
+                                 size_t workspace_bytes, cudaStream_t s);
+
 // Decode neighbours (llm_ops.cu).  rms_norm_launch: residual == nullptr -> rms_norm,
 // else add_rms_norm (residual_out receives x + residual).
 rk_status silu_mul_launch(const void* gate, const void* up, void* out, int64_t tokens,

@@ -57,6 +57,13 @@ void check_matrix(const at::Tensor& t, const char* name) {
   dtype_of(t, name);
 }
 
+void check_rows(const at::Tensor& t, const char* name, int64_t rank) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.dim() == rank, name, " must be rank ", rank);
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  dtype_of(t, name);
+}
+
 void check_status(rk_status st, const char* what) {
   TORCH_CHECK(st == RK_OK, what, " failed: ", rk_status_string(st),
               (st == RK_ERR_CUDA ? std::string(" (") + rk_last_error() + ")" : std::string()));
@@ -149,6 +156,51 @@ at::Tensor gather_column_blocks(const at::Tensor& blocks, at::Tensor out) {
   return out;
 }
 
+// Paged decode attention: the reference's argument order
+// (query, key_cache, value_cache, block_tables, context_lengths, scale) -> new output.
+at::Tensor paged_attention_decode(const at::Tensor& query, const at::Tensor& key_cache,
+                                  const at::Tensor& value_cache, const at::Tensor& block_tables,
+                                  const at::Tensor& context_lengths, double scale) {
+  check_rows(query, "query", 3);
+  check_rows(key_cache, "key_cache", 4);
+  check_rows(value_cache, "value_cache", 4);
+  TORCH_CHECK(block_tables.is_cuda() && block_tables.dim() == 2 && block_tables.is_contiguous(),
+              "block_tables must be a contiguous CUDA tensor [batch, max_blocks]");
+  TORCH_CHECK(context_lengths.is_cuda() && context_lengths.dim() == 1 && context_lengths.is_contiguous(),
+              "context_lengths must be a contiguous CUDA tensor [batch]");
+  TORCH_CHECK(block_tables.scalar_type() == context_lengths.scalar_type() &&
+                  (block_tables.scalar_type() == at::kInt || block_tables.scalar_type() == at::kLong),
+              "index tensors must share int32 or int64");
+  TORCH_CHECK(query.scalar_type() == key_cache.scalar_type() &&
+                  key_cache.scalar_type() == value_cache.scalar_type(),
+              "query and caches must share a dtype");
+  TORCH_CHECK(key_cache.sizes() == value_cache.sizes(), "K/V cache shapes must match");
+  TORCH_CHECK(query.device() == key_cache.device() && query.device() == value_cache.device() &&
+                  query.device() == block_tables.device() && query.device() == context_lengths.device(),
+              "all inputs must use the query's device");
+  const int64_t batch = query.size(0), hq = query.size(1), d = query.size(2);
+  TORCH_CHECK(block_tables.size(0) == batch && context_lengths.size(0) == batch,
+              "index tensors must have one row per sequence");
+  TORCH_CHECK(key_cache.size(3) == d, "query and cache head dimensions must match");
+  c10::cuda::CUDAGuard guard(query.device());
+  auto out = at::empty_like(query);
+  size_t ws_bytes = 0;
+  check_status(rk_paged_attention_workspace_size(batch, hq, key_cache.size(2), d, key_cache.size(1),
+                                                 block_tables.size(1), &ws_bytes),
+               "rk_paged_attention_workspace_size");
+  at::Tensor ws;
+  if (ws_bytes > 0) ws = at::empty({static_cast<int64_t>(ws_bytes)}, query.options().dtype(at::kByte));
+  check_status(rk_paged_attention_decode(
+                   query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(),
+                   block_tables.data_ptr(), context_lengths.data_ptr(), out.data_ptr(), batch, hq,
+                   key_cache.size(2), d, key_cache.size(0), key_cache.size(1), block_tables.size(1),
+                   static_cast<float>(scale), dtype_of(query, "query"),
+                   block_tables.scalar_type() == at::kInt ? 32 : 64,
+                   ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, current_stream(query)),
+               "rk_paged_attention_decode");
+  return out;
+}
+
 // Fused FFN-up + SwiGLU (rk_gemm_swiglu): b is [K, 2N] = [gate | up], returns [M, N].
 at::Tensor gemm_swiglu(const at::Tensor& a, const at::Tensor& b, int64_t variant) {
   check_matrix(a, "a");
@@ -169,13 +221,6 @@ at::Tensor gemm_swiglu(const at::Tensor& a, const at::Tensor& b, int64_t variant
 
 // Decode neighbours: the reference's pybind names and signatures
 // (benchmarks/llm_ops/native_llm_ops.hip:306-353, :397-416), outputs allocated here.
-void check_rows(const at::Tensor& t, const char* name, int64_t rank) {
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
-  TORCH_CHECK(t.dim() == rank, name, " must be rank ", rank);
-  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
-  dtype_of(t, name);
-}
-
 at::Tensor silu_mul(const at::Tensor& gate, const at::Tensor& up) {
   check_rows(gate, "gate", 2);
   check_rows(up, "up", 2);
@@ -247,6 +292,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_stream", &gemv_stream, "128-bit weight-streaming GEMV (K % 8 == 0, 16B aligned)");
   m.def("gemv_scalar", &gemv_scalar, "generic GEMV (any K, any alignment)");
   m.def("gather_column_blocks", &gather_column_blocks, "[G,M,N/G] blocks -> row-major [M,N]");
+  m.def("paged_attention_decode", &paged_attention_decode, "decode attention over a paged K/V cache",
+        py::arg("query"), py::arg("key_cache"), py::arg("value_cache"), py::arg("block_tables"),
+        py::arg("context_lengths"), py::arg("scale"));
   m.def("gemm_swiglu", &gemm_swiglu, "silu(a @ b[:, :N]) * (a @ b[:, N:])", py::arg("a"),
         py::arg("b"), py::arg("variant") = 0);
   m.def("silu_mul", &silu_mul, "silu(gate) * up", py::arg("gate"), py::arg("up"));

@@ -79,6 +79,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_gemv_ex.restype = cint
     lib.rk_gemv_workspace_size.argtypes = [i64, i64, i64, cint, cint, ctypes.POINTER(ctypes.c_size_t)]
     lib.rk_gemv_workspace_size.restype = cint
+    lib.rk_paged_attention_decode.argtypes = [vp] * 6 + [i64] * 7 + [ctypes.c_float, cint, cint, vp, ctypes.c_size_t, vp]
+    lib.rk_paged_attention_decode.restype = cint
+    lib.rk_paged_attention_workspace_size.argtypes = [i64] * 6 + [ctypes.POINTER(ctypes.c_size_t)]
+    lib.rk_paged_attention_workspace_size.restype = cint
     lib.rk_gemm_swiglu.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, vp]
     lib.rk_gemm_swiglu.restype = cint
     lib.rk_silu_mul.argtypes = [vp, vp, vp, i64, i64, cint, vp]

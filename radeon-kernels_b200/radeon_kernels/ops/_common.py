@@ -46,6 +46,24 @@ def validate_tensor(torch_module: Any, tensor: Any, *, name: str, rank: int, ope
     dtype_name(torch_module, tensor.dtype, operator)
 
 
+def index_dtype_name(torch_module: Any, dtype: Any, operator: str) -> str:
+    if dtype == torch_module.int32:
+        return "int32"
+    if dtype == torch_module.int64:
+        return "int64"
+    raise TypeError(f"{operator} index tensors must use torch.int32 or torch.int64")
+
+
+def validate_index_tensor(torch_module: Any, tensor: Any, *, name: str, rank: int, operator: str) -> None:
+    if not isinstance(tensor, getattr(torch_module, "Tensor", ())):
+        raise TypeError(f"{operator} {name} must be a PyTorch tensor")
+    if tensor.dim() != rank:
+        raise ValueError(f"{operator} {name} must be rank {rank}")
+    if not tensor.is_cuda:
+        raise ValueError(f"{operator} {name} must be on a visible CUDA GPU")
+    index_dtype_name(torch_module, tensor.dtype, operator)
+
+
 def validate_same(operator: str, first: Any, second: Any, *, first_name: str, second_name: str) -> None:
     if first.device != second.device:
         raise ValueError(f"{operator} {first_name} and {second_name} must use the same device")

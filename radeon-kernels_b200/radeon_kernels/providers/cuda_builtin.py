@@ -24,6 +24,7 @@ SELECTED_SILU_MUL = "cuda/silu_mul"
 SELECTED_RMS_NORM = "cuda/rms_norm"
 SELECTED_ADD_RMS_NORM = "cuda/add_rms_norm"
 SELECTED_GEMM_SWIGLU = "cuda/gemm_swiglu"
+SELECTED_PAGED_ATTENTION = "cuda/paged_attention_decode"
 
 
 def _contiguous(tensor: Any) -> Any:
@@ -179,3 +180,11 @@ def _gemm_swiglu_raw(a: Any, b: Any) -> Any:
 
 def gemm_swiglu(torch_module: Any, a: Any, b: Any) -> Any:
     return _run(torch_module, "gemm_swiglu", _gemm_swiglu_raw, a, b)
+
+
+def paged_attention_decode(
+    torch_module: Any, query: Any, key_cache: Any, value_cache: Any, block_tables: Any, context_lengths: Any, scale: float
+) -> Any:
+    """rk_paged_attention_decode (inference only; the front-end rejects autograd inputs)."""
+
+    return _native.extension().paged_attention_decode(query, key_cache, value_cache, block_tables, context_lengths, scale)

@@ -12,6 +12,8 @@ by calling the reference package itself:
 * GEMM:  ``radeon_kernels.providers.torch_fallback.gemm(torch, a, b)``  (torch_fallback.py:6-9)
 * GEMV:  ``radeon_kernels.ops.gemv.reference.gemv_fallback`` and ``gemv_reference``
   (ops/gemv/reference.py:6-15)
+* paged decode attention: ``ops.paged_attention.reference.paged_attention_decode_reference``
+  (paged_attention/reference.py:8-47)
 * SwiGLU, RMSNorm, residual add + RMSNorm (the decode neighbours):
   ``ops.swiglu.reference.silu_mul_reference`` (swiglu/reference.py:6-9),
   ``ops.rms_norm.reference.rms_norm_reference`` (rms_norm/reference.py:6-10),
@@ -73,6 +75,16 @@ NORM_CASES = [
 ]
 
 
+# name, dtype, batch, query_heads, kv_heads, head_dim, block_size, num_blocks, max_blocks,
+# context lengths, index dtype, scale (None: 1/sqrt(head_dim)), seed
+PAGED_CASES = [
+    ("paged_bf16_b2_gqa4x2_d64_p16", "bf16", 2, 4, 2, 64, 16, 12, 5, [37, 64], "int32", None, 60),
+    ("paged_fp16_b1_mqa8x1_d128_p16", "fp16", 1, 8, 1, 128, 16, 9, 8, [113], "int64", None, 61),
+    ("paged_bf16_b3_mha4_d256_p32_zero_len", "bf16", 3, 4, 4, 256, 32, 6, 3, [1, 70, 0], "int32", 0.05, 62),
+    ("paged_fp16_b2_gqa32x8_d128_p16", "fp16", 2, 32, 8, 128, 16, 40, 16, [200, 256], "int32", None, 63),
+]
+
+
 def _bits(tensor):
     import torch
 
@@ -100,6 +112,7 @@ def main(argv: list[str] | None = None) -> int:
     import radeon_kernels  # the reference package
     from radeon_kernels.ops.add_rms_norm.reference import add_rms_norm_reference
     from radeon_kernels.ops.gemv.reference import gemv_fallback, gemv_reference
+    from radeon_kernels.ops.paged_attention.reference import paged_attention_decode_reference
     from radeon_kernels.ops.rms_norm.reference import rms_norm_reference
     from radeon_kernels.ops.swiglu.reference import silu_mul_reference
     from radeon_kernels.providers import torch_fallback
@@ -135,6 +148,24 @@ def main(argv: list[str] | None = None) -> int:
             out_fallback=_bits(out),
             out_reference=_bits(out_ref),
             out_fp32=out32.numpy(),
+        )
+        print(name, tuple(out.shape))
+
+    for name, dt, batch, hq, hkv, d, bs, nb, maxb, lens, idx, scale, seed in PAGED_CASES:
+        gen = torch.Generator().manual_seed(seed)
+        q = torch.randn((batch, hq, d), generator=gen).to(dtypes[dt])
+        k = torch.randn((nb, bs, hkv, d), generator=gen).to(dtypes[dt])
+        v = torch.randn((nb, bs, hkv, d), generator=gen).to(dtypes[dt])
+        # every sequence's logical blocks map to scattered physical blocks
+        tables = torch.stack([torch.randperm(nb, generator=gen)[:maxb] for _ in range(batch)])
+        itype = torch.int32 if idx == "int32" else torch.int64
+        tables = tables.to(itype)
+        lengths = torch.tensor(lens, dtype=itype)
+        eff_scale = scale if scale is not None else 1.0 / d**0.5
+        out = paged_attention_decode_reference(torch, q, k, v, tables, lengths, scale)
+        np.savez_compressed(
+            HERE / f"{name}.npz", dtype=dt, q=_bits(q), k=_bits(k), v=_bits(v), block_tables=tables.numpy(),
+            context_lengths=lengths.numpy(), scale=np.float64(eff_scale), out_ref=_bits(out),
         )
         print(name, tuple(out.shape))
 

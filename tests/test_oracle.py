@@ -123,3 +123,13 @@ def test_elementwise_gate_detects_a_planted_error():
     nan[0, 0] = 0x7FC0  # a NaN where the reference is finite
     with pytest.raises(AssertionError):
         oracle.assert_elementwise(nan, case["out_ref"], case["dtype"])
+
+
+@pytest.mark.parametrize("path", golden_cases("paged"), ids=lambda p: p.stem)
+def test_oracle_paged_attention_matches_reference_fixtures(path):
+    case = _load(path)
+    dtype = str(case["dtype"])
+    out, out32 = oracle.paged_attention_decode(
+        case["q"], case["k"], case["v"], case["block_tables"], case["context_lengths"], float(case["scale"]), dtype
+    )
+    oracle.assert_attention(out, case["out_ref"], out32, dtype)

@@ -111,7 +111,7 @@ def test_builtin_pack_is_trusted_by_location_and_matches_dispatch():
     pack = registry.packs[0]
     assert pack.environment.architecture == "sm_100a"
     dispatch = builtin_dispatch_registry()
-    for operator in ("gemm", "gemv", "swiglu", "rms_norm", "add_rms_norm", "gemm_swiglu"):
+    for operator in ("gemm", "gemv", "swiglu", "rms_norm", "add_rms_norm", "gemm_swiglu", "paged_attention_decode"):
         item = pack.get(operator, "1.0")
         assert sha256_of(pack.root / item.artifact.artifact) == item.artifact.sha256
         for entry in dispatch.get(operator, "1.0").entries:
