@@ -557,6 +557,61 @@ def suite(args, dist: Dist, ext, peaks):
         }
         del a, b
 
+    def paged_case(name, batch, hq, hkv, ctx, d, bs, dtype, seed):
+        """Paged decode attention: bytes = the K/V cache positions every sequence reads."""
+
+        tdt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
+        maxb = -(-ctx // bs)
+        kv_bytes = batch * ctx * hkv * d * 2 * 2
+        io_bytes = 2 * batch * hq * d * 2
+        sets = max(2, min(32, -(-300_000_000 // kv_bytes)))
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        cases = []
+        for _ in range(sets):
+            nb = batch * maxb
+            q = torch.randn((batch, hq, d), generator=gen, device="cuda").to(tdt)
+            k = torch.randn((nb, bs, hkv, d), generator=gen, device="cuda").to(tdt)
+            v = torch.randn((nb, bs, hkv, d), generator=gen, device="cuda").to(tdt)
+            tables = torch.randperm(nb, generator=gen, device="cuda").view(batch, maxb).to(torch.int32)
+            lens = torch.full((batch,), ctx, dtype=torch.int32, device="cuda")
+            cases.append((q, k, v, tables, lens))
+        scale = d ** -0.5
+        step = lambda i: ext.paged_attention_decode(*cases[i % sets], scale)  # noqa: E731
+        for i in range(3):
+            step(i)
+        torch.cuda.synchronize()
+        launches = max(20, sets)
+        g = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(g, stream=cap):
+                for i in range(launches):
+                    step(i)
+        stream.wait_stream(cap)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        reps = 10
+        ms = time_loop(lambda i: g.replay(), reps, stream) / (reps * launches)
+        del g
+        dist.barrier()
+        ms = dist.max(ms)
+        gbs = (kv_bytes + io_bytes) / (ms / 1e3) / 1e9
+        results[name] = {
+            "unit": "GB/s",
+            "value": round(gbs * dist.world, 1),
+            "per_gpu": round(gbs, 1),
+            "us": round(ms * 1e3, 2),
+            "roofline_frac": round(gbs / peaks["hbm_gbs"], 4),
+            "scaling": "replica",
+            "shape": {"batch": batch, "query_heads": hq, "kv_heads": hkv, "context": ctx, "head_dim": d, "block_size": bs},
+            "dtype": dtype,
+            "timing": f"CUDA graph of {launches} launches over {sets} caches"
+            + (" (L2-resident: latency bound)" if kv_bytes * sets < 256_000_000 else ""),
+        }
+        del cases
+
     def ffn_swiglu_case(name, m, n, k, dtype, iters):
         """Fused FFN-up + SwiGLU: both products (2 x 2MNK FLOP) and the epilogue, one kernel."""
 
@@ -606,6 +661,12 @@ def suite(args, dist: Dist, ext, peaks):
     neighbour_case("add_rms_norm_prefill_t2048_h4096_bf16", "add_rms_norm", 2048, 4096, "bf16", 54)
     neighbour_case("add_rms_norm_prefill_t1024_h8192_bf16", "add_rms_norm", 1024, 8192, "bf16", 55)
     neighbour_case("rms_norm_prefill_t2048_h4096_bf16", "rms_norm", 2048, 4096, "bf16", 56)
+    # Paged decode attention, the reference's workload cases (paged_attention_decode-1.0.yaml).
+    paged_case("paged_b1_gqa32x8_c4096_d128_bf16", 1, 32, 8, 4096, 128, 16, "bf16", 60)
+    paged_case("paged_b8_gqa32x8_c1024_d128_bf16", 8, 32, 8, 1024, 128, 16, "bf16", 61)
+    paged_case("paged_b16_gqa32x8_c2048_d128_bf16", 16, 32, 8, 2048, 128, 16, "bf16", 62)
+    paged_case("paged_b4_mha16_c2048_d64_bf16", 4, 16, 16, 2048, 64, 32, "bf16", 63)
+    paged_case("paged_b4_gqa32x8_c1024_d256_bf16", 4, 32, 8, 1024, 256, 16, "bf16", 64)
     gemm_case("c1_gemm_1024_bf16", 1024, 1024, 1024, "bf16", "uniform", 0, 10, graph=True)
     cool_down()
     gemm_case("c4_gemm_ffn_up_fp16", 4096, 14336, 4096, "fp16", "normal64", 3, 10)
@@ -725,6 +786,7 @@ PROFILE_CASES = {
     "swiglu_prefill": ("silu_mul", 1024, 11008, 0, "bf16", "normal"),
     "add_rms_norm_prefill": ("add_rms_norm", 2048, 4096, 0, "bf16", "normal"),
     "ffn_swiglu": ("gemm_swiglu", 4096, 14336, 4096, "fp16", "normal64"),
+    "paged_b16_c2048": ("paged", 16, 2048, 0, "bf16", "normal"),
 }
 
 
@@ -747,6 +809,14 @@ def run_profile(args) -> int:
         gate = seeded((m, n), 1, dist_name, dtype)
         up = seeded((m, n), 2, dist_name, dtype)
         launch = lambda: ext.silu_mul(gate, up)  # noqa: E731
+    elif kind == "paged":  # m = batch, n = context; GQA 32 x 8, head_dim 128, block 16
+        maxb = -(-n // 16)
+        q = seeded((m, 32, 128), 1, dist_name, dtype)
+        kc = seeded((m * maxb, 16, 8, 128), 2, dist_name, dtype)
+        vc = seeded((m * maxb, 16, 8, 128), 3, dist_name, dtype)
+        tables = torch.arange(m * maxb, device="cuda", dtype=torch.int32).view(m, maxb)
+        lens = torch.full((m,), n, dtype=torch.int32, device="cuda")
+        launch = lambda: ext.paged_attention_decode(q, kc, vc, tables, lens, 128 ** -0.5)  # noqa: E731
     elif kind == "gemm_swiglu":  # b is [K, 2N]
         a = seeded((m, k), 1, dist_name, dtype)
         b = seeded((k, 2 * n), 2, dist_name, dtype)

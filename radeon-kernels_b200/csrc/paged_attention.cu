@@ -54,6 +54,7 @@ struct Params {
   float* part_ml;   // [batch, hq, partitions, 2] (max, sum)
   int batch, hq, hkv, group, head_groups;
   int num_blocks, block_size, max_blocks;
+  int block_shift;  // log2(block_size) when it is a power of two, else -1
   int partitions, part_tokens;
   float scale;
 };
@@ -82,7 +83,7 @@ __global__ void __launch_bounds__(THREADS)
   const int64_t max_ctx = static_cast<int64_t>(p.max_blocks) * p.block_size;
   ctx = ctx < 0 ? 0 : (ctx > max_ctx ? max_ctx : ctx);
   const int64_t t_begin = static_cast<int64_t>(part) * p.part_tokens;
-  const int64_t t_end = min(t_begin + p.part_tokens, ctx);
+  const int t_end = static_cast<int>(min(t_begin + p.part_tokens, ctx));
 
   // This thread's 8 dims of each query head, in fp32.
   float q[G][8];
@@ -123,14 +124,17 @@ __global__ void __launch_bounds__(THREADS)
     bool use[UNROLL];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
-      const int64_t t = tb + tg + static_cast<int64_t>(u) * GROUPS;
+      // Positions fit in 32 bits (max_blocks * block_size < 2^31, checked by the host).
+      const int t = static_cast<int>(tb) + tg + u * GROUPS;
       use[u] = false;
       kv[u] = make_uint4(0, 0, 0, 0);
       vv[u] = make_uint4(0, 0, 0, 0);
       if (t < t_end) {
-        const int64_t blk = static_cast<int64_t>(tables[t / p.block_size]);
+        const int lb = p.block_shift >= 0 ? t >> p.block_shift : t / p.block_size;
+        const int off = p.block_shift >= 0 ? t & (p.block_size - 1) : t - lb * p.block_size;
+        const int64_t blk = static_cast<int64_t>(tables[lb]);
         if (blk >= 0 && blk < p.num_blocks) {
-          const int64_t slot = blk * p.block_size + (t - (t / p.block_size) * p.block_size);
+          const int64_t slot = blk * p.block_size + off;
           kv[u] = ld_stream_v4(kbase + slot * row_stride);
           vv[u] = ld_stream_v4(vbase + slot * row_stride);
           use[u] = true;
@@ -139,22 +143,19 @@ __global__ void __launch_bounds__(THREADS)
         }
       }
     }
+    // Scores of the UNROLL positions first (warp-wide shuffles run for every lane, used
+    // position or not: a warp holds several position groups that can reach the end of the
+    // range at different u), then one online-softmax step per head for the whole chunk.
+    float sc[G][UNROLL];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
-      // Warp-wide shuffles run for every lane, used position or not (a warp holds
-      // several position groups that can reach the end of the range at different u);
-      // only the softmax update is skipped for unused positions.
-      float kf[8], vf[8];
+      float kf[8];
       const uint32_t kw[4] = {kv[u].x, kv[u].y, kv[u].z, kv[u].w};
-      const uint32_t vw[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 a = Pack2<T>::to_floats(use[u] ? kw[j] : 0u);
-        const float2 c = Pack2<T>::to_floats(use[u] ? vw[j] : 0u);
+        const float2 a = Pack2<T>::to_floats(kw[j]);
         kf[2 * j] = a.x;
         kf[2 * j + 1] = a.y;
-        vf[2 * j] = c.x;
-        vf[2 * j + 1] = c.y;
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -163,16 +164,37 @@ __global__ void __launch_bounds__(THREADS)
         for (int j = 0; j < 8; ++j) s = fmaf(q[g][j], kf[j], s);
 #pragma unroll
         for (int o = TPT / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (use[u] && g < nh) {
-          s *= p.scale;
-          const float m_new = fmaxf(m[g], s);
-          const float alpha = __expf(m[g] - m_new);  // 0 when m was -inf
-          const float beta = __expf(s - m_new);
-          l[g] = l[g] * alpha + beta;
+        sc[g][u] = use[u] ? s * p.scale : -INFINITY;
+      }
+    }
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[g][j] = fmaf(beta, vf[j], acc[g][j] * alpha);
-          m[g] = m_new;
+    for (int g = 0; g < G; ++g) {
+      if (g < nh && use[0]) {  // use[0] is false only when the whole chunk is past the end
+        float cm = m[g];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) cm = fmaxf(cm, sc[g][u]);
+        const float alpha = __expf(m[g] - cm);  // 0 when m was -inf
+        float beta[UNROLL];
+        float bsum = 0.f;
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+          beta[u] = __expf(sc[g][u] - cm);  // 0 for unused positions (-inf)
+          bsum += beta[u];
         }
+        l[g] = l[g] * alpha + bsum;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[g][j] *= alpha;
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+          const uint32_t vw[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 c = Pack2<T>::to_floats(vw[j]);
+            acc[g][2 * j] = fmaf(beta[u], c.x, acc[g][2 * j]);
+            acc[g][2 * j + 1] = fmaf(beta[u], c.y, acc[g][2 * j + 1]);
+          }
+        }
+        m[g] = cm;
       }
     }
   }
@@ -222,23 +244,43 @@ __global__ void __launch_bounds__(THREADS)
 }
 
 // One CTA per (sequence, query head), one thread per output element: merges the
-// partitions in partition order.
+// partitions in partition order.  Loads are issued 8 partitions at a time so a long
+// partition list costs a few L2 round trips, not one per partition.
 template <typename T, int D>
 __global__ void __launch_bounds__(D) paged_merge_kernel(Params p) {
+  constexpr int B8 = 8;
   pdl_begin();
   const int64_t head = blockIdx.x;
   const int d = threadIdx.x;
   const float* ml = p.part_ml + head * p.partitions * 2;
   const float* acc = p.part_acc + head * p.partitions * D + d;
   float mx = -INFINITY;
-  for (int j = 0; j < p.partitions; ++j) mx = fmaxf(mx, ml[2 * j]);
+  for (int j0 = 0; j0 < p.partitions; j0 += B8) {
+    float v[B8];
+#pragma unroll
+    for (int i = 0; i < B8; ++i) v[i] = j0 + i < p.partitions ? ml[2 * (j0 + i)] : -INFINITY;
+#pragma unroll
+    for (int i = 0; i < B8; ++i) mx = fmaxf(mx, v[i]);
+  }
   float sum = 0.f, a = 0.f;
   if (mx != -INFINITY) {
-    for (int j = 0; j < p.partitions; ++j) {
-      if (ml[2 * j] != -INFINITY) {
-        const float w = __expf(ml[2 * j] - mx);
-        sum += ml[2 * j + 1] * w;
-        a += acc[static_cast<int64_t>(j) * D] * w;
+    for (int j0 = 0; j0 < p.partitions; j0 += B8) {
+      float pm[B8], pl[B8], pa[B8];
+#pragma unroll
+      for (int i = 0; i < B8; ++i) {
+        const int j = j0 + i;
+        const bool in = j < p.partitions;
+        pm[i] = in ? ml[2 * j] : -INFINITY;
+        pl[i] = in ? ml[2 * j + 1] : 0.f;
+        pa[i] = in ? acc[static_cast<int64_t>(j) * D] : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < B8; ++i) {
+        if (pm[i] != -INFINITY) {
+          const float w = __expf(pm[i] - mx);
+          sum += pl[i] * w;
+          a += pa[i] * w;
+        }
       }
     }
   }
@@ -256,9 +298,11 @@ Plan plan(int64_t batch, int64_t hq, int64_t hkv, int64_t max_ctx, int sms) {
   while (pl.g < GMAX && pl.g < group) pl.g *= 2;
   pl.head_groups = static_cast<int>((group + pl.g - 1) / pl.g);
   const int64_t base = batch * hkv * pl.head_groups;
-  // Enough partitions for two CTAs per SM, each at least 64 positions long.
-  int64_t parts = (2ll * sms + base - 1) / base;
-  const int64_t cap = (max_ctx + 63) / 64;
+  // Enough partitions for eight CTAs (32 warps) per SM, each at least 128 positions long
+  // (a CTA's positions are walked a few deep per thread, so latency is hidden by the
+  // number of CTAs in flight; shorter partitions only add merge work).
+  int64_t parts = (8ll * sms + base - 1) / base;
+  const int64_t cap = (max_ctx + 127) / 128;
   if (parts > cap) parts = cap;
   if (parts < 1) parts = 1;
   pl.partitions = static_cast<int>(parts);
@@ -343,6 +387,9 @@ rk_status paged_attention_launch(const void* query, const void* key_cache, const
   prm.num_blocks = static_cast<int>(num_blocks);
   prm.block_size = static_cast<int>(block_size);
   prm.max_blocks = static_cast<int>(max_blocks);
+  prm.block_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((int64_t{1} << sh) == block_size) prm.block_shift = sh;
   prm.partitions = pl.partitions;
   prm.part_tokens = pl.part_tokens;
   prm.scale = scale;
