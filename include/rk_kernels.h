@@ -63,6 +63,17 @@ enum {
   RK_GEMM_VARIANT_COUNT = 4
 };
 
+/* Operand storage for rk_gemm_layout, named as in the reference's Layout enum
+ * (src/radeon_kernels/ops/gemm/spec.py:12-15): the first letter describes A, the second
+ * B; "n" = stored as the operand ([M,K] for A, [K,N] for B), "t" = stored transposed
+ * ([K,M] for A, [N,K] for B), each row-major and dense.  TT is an extension. */
+typedef enum rk_layout {
+  RK_LAYOUT_NN = 0,
+  RK_LAYOUT_NT = 1,
+  RK_LAYOUT_TN = 2,
+  RK_LAYOUT_TT = 3
+} rk_layout;
+
 /* GEMV variants. */
 enum {
   RK_GEMV_AUTO = 0,        /* pick from M, N, K and alignment */
@@ -85,6 +96,23 @@ enum {
  */
 RK_API rk_status rk_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N,
                   int64_t K, rk_dtype dt, int variant, rk_stream_t stream);
+
+/*
+ * C = op(A) @ op(B) with either operand read in its stored orientation (rk_layout):
+ * RK_LAYOUT_NT takes B as [N,K] row-major (C = A @ B^T, the activation gradient
+ * dA = dC @ B^T of C = A @ B), RK_LAYOUT_TN takes A as [K,M] row-major (C = A^T @ B,
+ * the weight gradient dB = A^T @ dC).  No transpose copy is made: the tensor-core
+ * variants load the stored tiles with TMA in the matching major order.  These are the
+ * layouts the reference declares (src/radeon_kernels/ops/gemm/spec.py:12-15) but never
+ * runs natively -- its rk.gemm signs every call "nn" (ops/gemm/api.py:93) and transposed
+ * views reach torch.mm through the fallback.  Same variants and K == 0 rule as rk_gemm;
+ * RK_GEMM_AUTO uses tensor cores when N%8 == 0, K%8 == 0, pointers are 16-byte aligned
+ * and, for a transposed A, M%8 == 0.  rk_gemm(...) equals rk_gemm_layout(...,
+ * RK_LAYOUT_NN, ...).
+ */
+RK_API rk_status rk_gemm_layout(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                  int64_t K, rk_layout layout, rk_dtype dt, int variant,
+                  rk_stream_t stream);
 
 /*
  * out = x @ weight^T.  x: [M,K] row-major, weight: [N,K] row-major ("nk"),

@@ -20,6 +20,14 @@
 // Requirements: N % 8 == 0, K % 8 == 0, 16-byte aligned A, B, C (TMA row
 // strides are multiples of 16 bytes).
 //
+// Operand layouts (the reference's Layout enum, src/radeon_kernels/ops/gemm/spec.py:12-15):
+// A_MN = A stored transposed, [K, M] row-major ("tn"); B_K = B stored transposed,
+// [N, K] row-major ("nt").  Neither needs a transpose pass: an M-major A tile is two
+// 64 x 64 boxes laid out like the N-major B chunks (the UMMA descriptor's MN-major
+// form), and a K-major B tile is one 64 x BN box laid out like the K-major A tile;
+// the instruction descriptor's major bits tell the tensor core which is which.
+// A stored [K, M] adds M % 8 == 0 (its row stride is M elements).
+//
 // Role of the reference: replaces wmma_gemm_kernel
 // (src/radeon_kernels/ops/gemm/native/wmma_gemm.hip:20-193), which stages
 // A and a transposed B panel in LDS and runs rocWMMA 16x16x16 fragments.
@@ -87,7 +95,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 // SWIGLU (BN = 256 only): B is [K, 2N] = [gate | up]; a tile has 128 output columns,
 // B chunks 0-1 come from the gate columns and 2-3 from the matching up columns, and the
 // epilogue stores silu(gate) * up (N is the output width).
-template <typename T, int BN, bool SWIGLU = false>
+template <typename T, int BN, bool SWIGLU = false, bool A_MN = false, bool B_K = false>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc1_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M, int N,
@@ -155,13 +163,24 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           const uint32_t full = smem_u32(&bars->full[stage]);
           mbar_arrive_expect_tx(full, STAGE_BYTES);
-          tma_load_2d(smem_u32(smem_a + stage * A_STAGE), &tmap_a, full, kb * BK, mb * BM);
+          if constexpr (A_MN) {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) {
-            const int bcol = SWIGLU ? (j < 2 ? nb * 128 + j * 64 : N + nb * 128 + (j - 2) * 64)
-                                    : nb * BN + j * 64;
-            tma_load_2d(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b, full, bcol,
-                        kb * BK);
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(smem_u32(smem_a + stage * A_STAGE + j * B_BOX), &tmap_a, full,
+                          mb * BM + j * 64, kb * BK);
+          } else {
+            tma_load_2d(smem_u32(smem_a + stage * A_STAGE), &tmap_a, full, kb * BK, mb * BM);
+          }
+          if constexpr (B_K) {
+            tma_load_2d(smem_u32(smem_b + stage * B_STAGE), &tmap_b, full, kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              const int bcol = SWIGLU ? (j < 2 ? nb * 128 + j * 64 : N + nb * 128 + (j - 2) * 64)
+                                      : nb * BN + j * 64;
+              tma_load_2d(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b, full, bcol,
+                          kb * BK);
+            }
           }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -186,8 +205,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc_bf16 = umma_idesc_f16(true, BM, BN, false, true);
-      constexpr uint32_t idesc_f16 = umma_idesc_f16(false, BM, BN, false, true);
+      constexpr uint32_t idesc_bf16 = umma_idesc_f16(true, BM, BN, A_MN, !B_K);
+      constexpr uint32_t idesc_f16 = umma_idesc_f16(false, BM, BN, A_MN, !B_K);
       const uint32_t idesc = std::is_same<T, __nv_bfloat16>::value ? idesc_bf16 : idesc_f16;
       uint32_t stage = 0, phase = 0;
       bool ok = true;
@@ -215,12 +234,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b0 = smem_u32(smem_b + stage * B_STAGE);
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
-            // A: K-major SW128, 8-row core groups 1024 B apart; K advances 32 B
-            // inside the swizzle row.  B: MN-major SW128, 64-column chunks
-            // 8 KiB apart (LBO), 8-row K groups 1024 B apart (SBO); K advances
-            // by two groups (16 rows) per MMA.
-            const uint64_t adesc = umma_desc_sw128(a0 + k * UMMA_K * 2, 16, 1024);
-            const uint64_t bdesc = umma_desc_sw128(b0 + k * UMMA_K * 128, B_BOX, 1024);
+            // K-major SW128 (A, or B stored [N, K]): 8-row core groups 1024 B apart;
+            // K advances 32 B inside the swizzle row.  MN-major SW128 (B, or A stored
+            // [K, M]): 64-column chunks 8 KiB apart (LBO), 8-row K groups 1024 B
+            // apart (SBO); K advances by two groups (16 rows) per MMA.
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a0 + k * UMMA_K * 128, B_BOX, 1024)
+                                        : umma_desc_sw128(a0 + k * UMMA_K * 2, 16, 1024);
+            const uint64_t bdesc = B_K ? umma_desc_sw128(b0 + k * UMMA_K * 2, 16, 1024)
+                                       : umma_desc_sw128(b0 + k * UMMA_K * 128, B_BOX, 1024);
             tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           tc_commit(smem_u32(&bars->empty[stage]));
@@ -307,14 +328,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 }  // namespace tc1
 
 namespace {
-template <typename T, int BN, bool SWIGLU = false>
+template <typename T, int BN, bool SWIGLU = false, bool A_MN = false, bool B_K = false>
 rk_status launch_tc1(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                      rk_dtype dt, cudaStream_t s) {
+  static_assert(!(SWIGLU && (A_MN || B_K)), "the fused SwiGLU GEMM takes the nn layout");
   CUtensorMap ta, tb;
-  rk_status st = make_tmap_2d(&ta, A, dt, /*inner*/ K, /*outer*/ M, /*box_inner*/ 64,
-                              /*box_outer*/ tc1::BM);
+  rk_status st = A_MN ? make_tmap_2d(&ta, A, dt, /*inner*/ M, /*outer*/ K, 64, tc1::BK)
+                      : make_tmap_2d(&ta, A, dt, /*inner*/ K, /*outer*/ M, /*box_inner*/ 64,
+                                     /*box_outer*/ tc1::BM);
   if (st != RK_OK) return st;
-  st = make_tmap_2d(&tb, B, dt, SWIGLU ? 2 * N : N, K, 64, tc1::BK);
+  st = B_K ? make_tmap_2d(&tb, B, dt, K, N, 64, BN)
+           : make_tmap_2d(&tb, B, dt, SWIGLU ? 2 * N : N, K, 64, tc1::BK);
   if (st != RK_OK) return st;
   LaunchCtl lc;
   if ((st = launch_ctl(&lc)) != RK_OK) return st;
@@ -327,14 +351,16 @@ rk_status launch_tc1(const void* A, const void* B, void* C, int64_t M, int64_t N
   cudaGetDevice(&dev);
   std::call_once(attr_once[dev & 63], [&] {
     attr_err[dev & 63] = cudaFuncSetAttribute(
-        tc1::gemm_tc1_kernel<T, BN, SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        tc1::gemm_tc1_kernel<T, BN, SWIGLU, A_MN, B_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        smem);
   });
   if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
 
   const int64_t tile_n = SWIGLU ? 128 : BN;
   const int64_t num_tiles = ((M + tc1::BM - 1) / tc1::BM) * ((N + tile_n - 1) / tile_n);
   const int grid = static_cast<int>(num_tiles < device_sm_count() ? num_tiles : device_sm_count());
-  const cudaError_t e = launch_kernel(tc1::gemm_tc1_kernel<T, BN, SWIGLU>, dim3(grid), dim3(tc1::THREADS),
+  const cudaError_t e = launch_kernel(tc1::gemm_tc1_kernel<T, BN, SWIGLU, A_MN, B_K>, dim3(grid),
+                                      dim3(tc1::THREADS),
                                       smem, s, 0, ta, tb, reinterpret_cast<T*>(C),
                                       static_cast<int>(M), static_cast<int>(N),
                                       static_cast<int>(K), ctl);
@@ -362,15 +388,27 @@ int pick_tile_n(int64_t M, int64_t N) {
   return best;
 }
 
-template <typename T>
+template <typename T, bool A_MN, bool B_K>
 rk_status launch_tc1_auto(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                           rk_dtype dt, cudaStream_t s, int bn) {
   if (bn <= 0) bn = pick_tile_n(M, N);
   switch (bn) {
-    case 64: return launch_tc1<T, 64>(A, B, C, M, N, K, dt, s);
-    case 128: return launch_tc1<T, 128>(A, B, C, M, N, K, dt, s);
-    default: return launch_tc1<T, 256>(A, B, C, M, N, K, dt, s);
+    case 64: return launch_tc1<T, 64, false, A_MN, B_K>(A, B, C, M, N, K, dt, s);
+    case 128: return launch_tc1<T, 128, false, A_MN, B_K>(A, B, C, M, N, K, dt, s);
+    default: return launch_tc1<T, 256, false, A_MN, B_K>(A, B, C, M, N, K, dt, s);
   }
+}
+
+template <typename T>
+rk_status launch_tc1_layout(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                            int64_t K, rk_layout layout, rk_dtype dt, cudaStream_t s, int bn) {
+  switch (layout) {
+    case RK_LAYOUT_NN: return launch_tc1_auto<T, false, false>(A, B, C, M, N, K, dt, s, bn);
+    case RK_LAYOUT_NT: return launch_tc1_auto<T, false, true>(A, B, C, M, N, K, dt, s, bn);
+    case RK_LAYOUT_TN: return launch_tc1_auto<T, true, false>(A, B, C, M, N, K, dt, s, bn);
+    case RK_LAYOUT_TT: return launch_tc1_auto<T, true, true>(A, B, C, M, N, K, dt, s, bn);
+  }
+  return RK_ERR_INVALID_ARGUMENT;
 }
 }  // namespace
 
@@ -382,14 +420,17 @@ bool gemm_swiglu_supported(const void* A, const void* B, const void* C, int64_t 
                            int64_t K) {
   // B is [K, 2N]: the same rules as the plain GEMM with 2N columns, plus an output width
   // that is a multiple of 8 (16-byte stores).
-  return N <= (1ll << 30) - 256 && gemm_tc_supported(A, B, C, M, 2 * N, K) && N % 8 == 0;
+  return N <= (1ll << 30) - 256 && gemm_tc_supported(A, B, C, M, 2 * N, K, RK_LAYOUT_NN) &&
+         N % 8 == 0;
 }
 
 bool gemm_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
-                       int64_t K) {
+                       int64_t K, rk_layout layout) {
   if (device_cc_major() != 10) return false;
   if (M <= 0 || N <= 0 || K <= 0) return false;
   if (N % 8 != 0 || K % 8 != 0) return false;
+  // A stored [K, M] has a row stride of M elements; TMA strides are multiples of 16 bytes.
+  if ((layout == RK_LAYOUT_TN || layout == RK_LAYOUT_TT) && M % 8 != 0) return false;
   if (!aligned16(A) || !aligned16(B) || !aligned16(C)) return false;
   // TMA coordinates and the kernel's tile arithmetic are 32-bit.
   if (M > (1ll << 31) - 256 || N > (1ll << 31) - 256 || K > (1ll << 31) - 64) return false;
@@ -405,11 +446,12 @@ rk_status gemm_swiglu_1sm_launch(const void* A, const void* B, void* C, int64_t 
 }
 
 rk_status gemm_tc_1sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
-                             int64_t K, rk_dtype dt, cudaStream_t s) {
-  if (!gemm_tc_supported(A, B, C, M, N, K)) return RK_ERR_UNSUPPORTED;
+                             int64_t K, rk_layout layout, rk_dtype dt, cudaStream_t s) {
+  if (!gemm_tc_supported(A, B, C, M, N, K, layout)) return RK_ERR_UNSUPPORTED;
   const int bn = g_tile_n_override.load();
-  if (dt == RK_DTYPE_BF16) return launch_tc1_auto<__nv_bfloat16>(A, B, C, M, N, K, dt, s, bn);
-  return launch_tc1_auto<__half>(A, B, C, M, N, K, dt, s, bn);
+  if (dt == RK_DTYPE_BF16)
+    return launch_tc1_layout<__nv_bfloat16>(A, B, C, M, N, K, layout, dt, s, bn);
+  return launch_tc1_layout<__half>(A, B, C, M, N, K, layout, dt, s, bn);
 }
 
 }  // namespace rk

@@ -17,7 +17,9 @@
 //   * warps 2..5 (both CTAs): epilogue from each CTA's own TMEM; each warp reports
 //     "accumulator drained" to the even CTA's barrier (remote arrive for the odd CTA).
 // Persistent: clusters walk 256x256 tiles in the grouped order; edges handled by TMA
-// zero fill + predicated stores, as in the 1-SM kernel.  Every wait is bounded; the
+// zero fill + predicated stores, as in the 1-SM kernel.  Operand layouts as in the 1-SM
+// kernel: A_MN = A stored [K, M] (each CTA stages its 128 rows as two M-major 64 x 64
+// boxes), B_K = B stored [N, K] (each CTA stages its 128 columns as one K-major box).  Every wait is bounded; the
 // two cluster barriers (after initialisation and before exit) are reached by every
 // thread unconditionally.
 #include <cuda.h>
@@ -74,7 +76,7 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 // stages the tile's 128 gate columns and the odd CTA the matching 128 up columns, so
 // accumulator columns 0-127 hold gate and 128-255 up for the CTA's rows, and the
 // epilogue stores silu(gate) * up (N is the output width).
-template <typename T, bool SWIGLU = false>
+template <typename T, bool SWIGLU = false, bool A_MN = false, bool B_K = false>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M, int N,
@@ -140,14 +142,27 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t full_local = smem_u32(&bars->full[stage]);
           const uint32_t full_even = map_to_rank(full_local, 0);
           if (rank == 0) mbar_arrive_expect_tx(full_local, 2 * STAGE_BYTES);
-          tma_load_2d_pair(smem_u32(smem_a + stage * A_STAGE), &tmap_a, full_even, kb * BK,
-                           mb * BM + static_cast<int>(rank) * HALF);
+          const int arow = mb * BM + static_cast<int>(rank) * HALF;
+          if constexpr (A_MN) {
+#pragma unroll
+            for (int j = 0; j < HALF / 64; ++j)
+              tma_load_2d_pair(smem_u32(smem_a + stage * A_STAGE + j * B_BOX), &tmap_a,
+                               full_even, arow + j * 64, kb * BK);
+          } else {
+            tma_load_2d_pair(smem_u32(smem_a + stage * A_STAGE), &tmap_a, full_even, kb * BK,
+                             arow);
+          }
           const int bcol = SWIGLU ? (rank == 0 ? nb * HALF : N + nb * HALF)
                                   : nb * BN + static_cast<int>(rank) * HALF;
+          if constexpr (B_K) {
+            tma_load_2d_pair(smem_u32(smem_b + stage * B_STAGE), &tmap_b, full_even, kb * BK,
+                             bcol);
+          } else {
 #pragma unroll
-          for (int j = 0; j < HALF / 64; ++j)
-            tma_load_2d_pair(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b, full_even,
-                             bcol + j * 64, kb * BK);
+            for (int j = 0; j < HALF / 64; ++j)
+              tma_load_2d_pair(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b,
+                               full_even, bcol + j * 64, kb * BK);
+          }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -175,7 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0 && rank == 0) {
       // ------------------------------------------------ MMA issuer (even CTA only)
       const uint32_t idesc =
-          umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, BN, false, true);
+          umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, BN, A_MN, !B_K);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       int i = 0;
@@ -198,8 +213,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t b0 = smem_u32(smem_b + stage * B_STAGE);
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
-            const uint64_t adesc = umma_desc_sw128(a0 + k * UMMA_K * 2, 16, 1024);
-            const uint64_t bdesc = umma_desc_sw128(b0 + k * UMMA_K * 128, B_BOX, 1024);
+            const uint64_t adesc = A_MN ? umma_desc_sw128(a0 + k * UMMA_K * 128, B_BOX, 1024)
+                                        : umma_desc_sw128(a0 + k * UMMA_K * 2, 16, 1024);
+            const uint64_t bdesc = B_K ? umma_desc_sw128(b0 + k * UMMA_K * 2, 16, 1024)
+                                       : umma_desc_sw128(b0 + k * UMMA_K * 128, B_BOX, 1024);
             tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           tc_commit_pair(smem_u32(&bars->empty[stage]), 0x3);
@@ -286,13 +303,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 }  // namespace tc2
 
 namespace {
-template <typename T, bool SWIGLU = false>
+template <typename T, bool SWIGLU = false, bool A_MN = false, bool B_K = false>
 rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                      rk_dtype dt, cudaStream_t s) {
+  static_assert(!(SWIGLU && (A_MN || B_K)), "the fused SwiGLU GEMM takes the nn layout");
   CUtensorMap ta, tb;
-  rk_status st = make_tmap_2d(&ta, A, dt, K, M, 64, tc2::HALF);
+  rk_status st = A_MN ? make_tmap_2d(&ta, A, dt, M, K, 64, tc2::BK)
+                      : make_tmap_2d(&ta, A, dt, K, M, 64, tc2::HALF);
   if (st != RK_OK) return st;
-  st = make_tmap_2d(&tb, B, dt, SWIGLU ? 2 * N : N, K, 64, tc2::BK);
+  st = B_K ? make_tmap_2d(&tb, B, dt, K, N, 64, tc2::HALF)
+           : make_tmap_2d(&tb, B, dt, SWIGLU ? 2 * N : N, K, 64, tc2::BK);
   if (st != RK_OK) return st;
   LaunchCtl lc;
   if ((st = launch_ctl(&lc)) != RK_OK) return st;
@@ -303,7 +323,7 @@ rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [&] {
-    attr_err[dev & 63] = cudaFuncSetAttribute(tc2::gemm_tc2_kernel<T, SWIGLU>,
+    attr_err[dev & 63] = cudaFuncSetAttribute(tc2::gemm_tc2_kernel<T, SWIGLU, A_MN, B_K>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               tc2::SMEM_BYTES);
   });
@@ -314,7 +334,8 @@ rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N
   const int64_t pairs_max = device_sm_count() / 2;
   const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
 
-  const cudaError_t e = launch_kernel(tc2::gemm_tc2_kernel<T, SWIGLU>, dim3(static_cast<unsigned>(2 * pairs)),
+  const cudaError_t e = launch_kernel(tc2::gemm_tc2_kernel<T, SWIGLU, A_MN, B_K>,
+                                      dim3(static_cast<unsigned>(2 * pairs)),
                                       dim3(tc2::THREADS), tc2::SMEM_BYTES, s, 2, ta, tb,
                                       reinterpret_cast<T*>(C), static_cast<int>(M),
                                       static_cast<int>(N), static_cast<int>(K), ctl);
@@ -323,12 +344,24 @@ rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N
 }
 }  // namespace
 
+template <typename T>
+rk_status launch_tc2_layout(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                            int64_t K, rk_layout layout, rk_dtype dt, cudaStream_t s) {
+  switch (layout) {
+    case RK_LAYOUT_NN: return launch_tc2<T, false, false, false>(A, B, C, M, N, K, dt, s);
+    case RK_LAYOUT_NT: return launch_tc2<T, false, false, true>(A, B, C, M, N, K, dt, s);
+    case RK_LAYOUT_TN: return launch_tc2<T, false, true, false>(A, B, C, M, N, K, dt, s);
+    case RK_LAYOUT_TT: return launch_tc2<T, false, true, true>(A, B, C, M, N, K, dt, s);
+  }
+  return RK_ERR_INVALID_ARGUMENT;
+}
+
 rk_status gemm_tc_2sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
-                             int64_t K, rk_dtype dt, cudaStream_t s) {
-  if (!gemm_tc_supported(A, B, C, M, N, K)) return RK_ERR_UNSUPPORTED;
+                             int64_t K, rk_layout layout, rk_dtype dt, cudaStream_t s) {
+  if (!gemm_tc_supported(A, B, C, M, N, K, layout)) return RK_ERR_UNSUPPORTED;
   if (device_sm_count() < 2) return RK_ERR_UNSUPPORTED;
-  if (dt == RK_DTYPE_BF16) return launch_tc2<__nv_bfloat16>(A, B, C, M, N, K, dt, s);
-  return launch_tc2<__half>(A, B, C, M, N, K, dt, s);
+  if (dt == RK_DTYPE_BF16) return launch_tc2_layout<__nv_bfloat16>(A, B, C, M, N, K, layout, dt, s);
+  return launch_tc2_layout<__half>(A, B, C, M, N, K, layout, dt, s);
 }
 
 rk_status gemm_swiglu_2sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,

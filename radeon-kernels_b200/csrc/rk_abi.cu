@@ -99,12 +99,26 @@ rk_status launch_ctl(LaunchCtl* ctl) {
   return RK_OK;
 }
 
-rk_status gemm_tc_2sm_launch(const void*, const void*, void*, int64_t, int64_t, int64_t, rk_dtype,
-                             cudaStream_t);
-
 }  // namespace rk
 
 using namespace rk;
+
+namespace {
+int select_gemm_variant(const void* A, const void* B, const void* C, int64_t M, int64_t N,
+                        int64_t K, rk_layout layout) {
+  if (!gemm_tc_supported(A, B, C, M, N, K, layout)) return RK_GEMM_SIMT;
+  // SM pairs with 256x256 tiles once there is at least one tile per pair (they halve the
+  // per-SM operand traffic); smaller problems keep more, narrower 1-SM tiles in flight.
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  if (pair_tiles >= device_sm_count() / 2) return RK_GEMM_TC_2SM;
+  return RK_GEMM_TC_1SM;
+}
+
+bool valid_layout(rk_layout layout) {
+  return layout == RK_LAYOUT_NN || layout == RK_LAYOUT_NT || layout == RK_LAYOUT_TN ||
+         layout == RK_LAYOUT_TT;
+}
+}  // namespace
 
 extern "C" {
 
@@ -163,12 +177,7 @@ const char* rk_variant_name(int op, int variant) {
 int rk_gemm_select_variant(const void* A, const void* B, const void* C, int64_t M, int64_t N,
                            int64_t K, rk_dtype dt) {
   (void)dt;
-  if (!gemm_tc_supported(A, B, C, M, N, K)) return RK_GEMM_SIMT;
-  // SM pairs with 256x256 tiles once there is at least one tile per pair (they halve the
-  // per-SM operand traffic); smaller problems keep more, narrower 1-SM tiles in flight.
-  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
-  if (pair_tiles >= device_sm_count() / 2) return RK_GEMM_TC_2SM;
-  return RK_GEMM_TC_1SM;
+  return select_gemm_variant(A, B, C, M, N, K, RK_LAYOUT_NN);
 }
 
 int rk_gemv_select_variant(const void* x, const void* W, const void* out, int64_t M, int64_t N,
@@ -182,7 +191,13 @@ int rk_gemv_select_variant(const void* x, const void* W, const void* out, int64_
 
 rk_status rk_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                   rk_dtype dt, int variant, rk_stream_t stream) {
-  if (M < 0 || N < 0 || K < 0 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
+  return rk_gemm_layout(A, B, C, M, N, K, RK_LAYOUT_NN, dt, variant, stream);
+}
+
+rk_status rk_gemm_layout(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                         rk_layout layout, rk_dtype dt, int variant, rk_stream_t stream) {
+  if (M < 0 || N < 0 || K < 0 || !valid_dtype(dt) || !valid_layout(layout))
+    return RK_ERR_INVALID_ARGUMENT;
   if (variant < 0 || variant >= RK_GEMM_VARIANT_COUNT) return RK_ERR_UNSUPPORTED;
   if (M == 0 || N == 0) return RK_OK;
   if (C == nullptr || (K > 0 && (A == nullptr || B == nullptr))) return RK_ERR_INVALID_ARGUMENT;
@@ -192,11 +207,11 @@ rk_status rk_gemm(const void* A, const void* B, void* C, int64_t M, int64_t N, i
     // Empty inner dimension: C is the zero matrix (torch.mm semantics).
     return cuda_status(cudaMemsetAsync(C, 0, static_cast<size_t>(M) * N * 2, s));
   }
-  if (variant == RK_GEMM_AUTO) variant = rk_gemm_select_variant(A, B, C, M, N, K, dt);
+  if (variant == RK_GEMM_AUTO) variant = select_gemm_variant(A, B, C, M, N, K, layout);
   switch (variant) {
-    case RK_GEMM_SIMT: return gemm_simt_launch(A, B, C, M, N, K, dt, s);
-    case RK_GEMM_TC_1SM: return gemm_tc_1sm_launch(A, B, C, M, N, K, dt, s);
-    case RK_GEMM_TC_2SM: return gemm_tc_2sm_launch(A, B, C, M, N, K, dt, s);
+    case RK_GEMM_SIMT: return gemm_simt_launch(A, B, C, M, N, K, layout, dt, s);
+    case RK_GEMM_TC_1SM: return gemm_tc_1sm_launch(A, B, C, M, N, K, layout, dt, s);
+    case RK_GEMM_TC_2SM: return gemm_tc_2sm_launch(A, B, C, M, N, K, layout, dt, s);
   }
   return RK_ERR_UNSUPPORTED;
 }

@@ -62,13 +62,13 @@ rk_status cuda_status(cudaError_t e);
 // Kernel families.  All validate what they need and return RK_ERR_UNSUPPORTED
 // when the variant cannot run the request.
 rk_status gemm_simt_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
-                           rk_dtype dt, cudaStream_t s);
+                           rk_layout layout, rk_dtype dt, cudaStream_t s);
 rk_status gemm_tc_1sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
-                             int64_t K, rk_dtype dt, cudaStream_t s);
+                             int64_t K, rk_layout layout, rk_dtype dt, cudaStream_t s);
 rk_status gemm_tc_2sm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N,
-                             int64_t K, rk_dtype dt, cudaStream_t s);
+                             int64_t K, rk_layout layout, rk_dtype dt, cudaStream_t s);
 bool gemm_tc_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
-                       int64_t K);
+                       int64_t K, rk_layout layout);
 // Fused FFN-up + SwiGLU: C[M,N] = silu(A @ B[:, :N]) * (A @ B[:, N:]), B [K, 2N].
 bool gemm_swiglu_supported(const void* A, const void* B, const void* C, int64_t M, int64_t N,
                            int64_t K);

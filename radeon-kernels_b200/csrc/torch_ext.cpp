@@ -12,6 +12,7 @@
 // Entry points mirror the reference's pybind modules:
 //   gemm_out(a, b, out, variant) -> out   (wmma_gemm.hip:294-316, :326-329)
 //   gemm(a, b, variant) -> new tensor
+//   gemm_views(a, b, out=None, variant) -> C   (transposed views in place: rk_gemm_layout)
 //   gemv_*(input, weight) -> new tensor   (native_gemv.hip:343-391)
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -96,6 +97,43 @@ at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, int64_t variant) {
   TORCH_CHECK(a.size(1) == b.size(0), "incompatible GEMM dimensions");
   auto out = at::empty({a.size(0), b.size(1)}, a.options());
   return gemm_out(a, b, out, variant);
+}
+
+// Orientation of a 2-D view: 'n' when it is row-major dense, 't' when it is the transpose
+// of a row-major dense matrix (x.t() of a contiguous x), 0 otherwise.
+char orientation(const at::Tensor& t) {
+  if (t.is_contiguous()) return 'n';
+  if (t.t().is_contiguous()) return 't';
+  return 0;
+}
+
+// C = a @ b where a and b may be transposed views (rk_gemm_layout): a.t() or b.t() of a
+// contiguous matrix is read in place, with no transpose copy.  out (optional) must be
+// contiguous [M, N].
+at::Tensor gemm_views(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tensor> out_opt,
+                      int64_t variant) {
+  for (const auto* t : {&a, &b}) {
+    TORCH_CHECK(t->is_cuda(), "gemm operands must be CUDA tensors");
+    TORCH_CHECK(t->dim() == 2, "gemm operands must be rank 2");
+  }
+  const rk_dtype dt = dtype_of(a, "a");
+  TORCH_CHECK(a.scalar_type() == b.scalar_type(), "a and b must have the same dtype");
+  TORCH_CHECK(a.device() == b.device(), "a and b must be on the same device");
+  TORCH_CHECK(a.size(1) == b.size(0), "incompatible GEMM dimensions");
+  const char oa = orientation(a), ob = orientation(b);
+  TORCH_CHECK(oa != 0 && ob != 0, "gemm operands must be dense matrices or their transposes");
+  const rk_layout layout = oa == 'n' ? (ob == 'n' ? RK_LAYOUT_NN : RK_LAYOUT_NT)
+                                     : (ob == 'n' ? RK_LAYOUT_TN : RK_LAYOUT_TT);
+  at::Tensor out = out_opt.has_value() ? *out_opt : at::empty({a.size(0), b.size(1)}, a.options());
+  check_matrix(out, "out");
+  TORCH_CHECK(out.device() == a.device() && out.scalar_type() == a.scalar_type(),
+              "out must match the operands' device and dtype");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == b.size(1), "out has the wrong shape");
+  c10::cuda::CUDAGuard guard(a.device());
+  check_status(rk_gemm_layout(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.size(0), b.size(1),
+                              a.size(1), layout, dt, static_cast<int>(variant), current_stream(a)),
+               "rk_gemm_layout");
+  return out;
 }
 
 at::Tensor gemv_out(const at::Tensor& x, const at::Tensor& weight, at::Tensor out,
@@ -285,6 +323,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_out", &gemm_out, "C = A @ B into the caller's output", py::arg("a"), py::arg("b"),
         py::arg("out"), py::arg("variant") = 0);
   m.def("gemm", &gemm, "C = A @ B", py::arg("a"), py::arg("b"), py::arg("variant") = 0);
+  m.def("gemm_views", &gemm_views, "C = A @ B with A and/or B transposed views read in place",
+        py::arg("a"), py::arg("b"), py::arg("out") = py::none(), py::arg("variant") = 0);
   m.def("gemv", &gemv, "out = x @ weight.T", py::arg("input"), py::arg("weight"),
         py::arg("variant") = 0);
   m.def("gemv_out", &gemv_out, "out = x @ weight.T into the caller's output", py::arg("input"),

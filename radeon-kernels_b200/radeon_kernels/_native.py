@@ -73,6 +73,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     i64, vp, cint = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int
     lib.rk_gemm.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, vp]
     lib.rk_gemm.restype = cint
+    lib.rk_gemm_layout.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, cint, vp]
+    lib.rk_gemm_layout.restype = cint
     lib.rk_gemv.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, vp]
     lib.rk_gemv.restype = cint
     lib.rk_gemv_ex.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, vp, ctypes.c_size_t, vp]

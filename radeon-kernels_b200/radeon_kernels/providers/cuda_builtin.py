@@ -7,9 +7,10 @@ streaming GEMV when shape and alignment allow, the generic predicated kernels ot
 So every call on a GPU, matched by a dispatch entry or not, runs a kernel of this
 library; nothing falls back to a vendor library or to the CPU.
 
-Inputs that are not contiguous are packed first (a device copy).  Inputs that require
-gradients go through :class:`_GemmFunction` / :class:`_GemvFunction`, whose backward passes
-are again this library's kernels on transposed copies.
+GEMM operands that are transposed views of dense matrices (``x.t()``) are read in place
+through ``rk_gemm_layout`` (the "nt"/"tn" layouts); other non-contiguous inputs are packed
+first (a device copy).  Inputs that require gradients go through :class:`_GemmFunction` /
+:class:`_GemvFunction`, whose backward GEMMs read the saved operands transposed in place.
 """
 
 from __future__ import annotations
@@ -31,18 +32,29 @@ def _contiguous(tensor: Any) -> Any:
     return tensor if tensor.is_contiguous() else tensor.contiguous()
 
 
+def _in_place_operand(tensor: Any) -> Any:
+    """The operand as rk_gemm_layout reads it: dense, or the transpose of a dense matrix."""
+    if tensor.is_contiguous() or tensor.t().is_contiguous():
+        return tensor
+    return tensor.contiguous()
+
+
 def _gemm_raw(a: Any, b: Any, output: Any | None) -> Any:
     ext = _native.extension()
-    a, b = _contiguous(a), _contiguous(b)
+    a, b = _in_place_operand(a), _in_place_operand(b)
     if output is None:
-        return ext.gemm(a, b, 0)
+        return ext.gemm_views(a, b, None, 0)
     if output.is_contiguous():
-        return ext.gemm_out(a, b, output, 0)
-    output.copy_(ext.gemm(a, b, 0))
+        return ext.gemm_views(a, b, output, 0)
+    output.copy_(ext.gemm_views(a, b, None, 0))
     return output
 
 
 def _gemv_raw(x: Any, weight: Any) -> Any:
+    if not weight.is_contiguous() and weight.t().is_contiguous():
+        # weight is the transpose of a dense [K, N] matrix: x @ weight^T is the nn GEMM
+        # x @ weight.t() on the stored matrix.
+        return _native.extension().gemm_views(_contiguous(x), weight.t(), None, 0)
     return _native.extension().gemv(_contiguous(x), _contiguous(weight), 0)
 
 
@@ -59,6 +71,8 @@ def _autograd_functions() -> tuple[Any, Any]:
         def backward(ctx: Any, grad: Any) -> Any:
             a, b = ctx.saved_tensors
             grad = _contiguous(grad)
+            # dA = dC @ B^T ("nt"), dB = A^T @ dC ("tn"): the saved operands are read
+            # transposed in place.
             grad_a = _gemm_raw(grad, b.detach().t(), None) if ctx.needs_input_grad[0] else None
             grad_b = _gemm_raw(a.detach().t(), grad, None) if ctx.needs_input_grad[1] else None
             return grad_a, grad_b

@@ -53,6 +53,30 @@ def abi_gemm(a, b, c, variant: int, dtype: str) -> int:
     )
 
 
+LAYOUT_CODE = {"nn": 0, "nt": 1, "tn": 2, "tt": 3}
+
+
+def abi_gemm_layout(a_stored, b_stored, c, layout: str, variant: int, dtype: str) -> int:
+    """rk_gemm_layout on stored operands: A is [M,K] ("n") or [K,M] ("t"), B is [K,N] or [N,K]."""
+
+    lib = _native.library()
+    m = a_stored.shape[1] if layout[0] == "t" else a_stored.shape[0]
+    k = a_stored.shape[0] if layout[0] == "t" else a_stored.shape[1]
+    n = b_stored.shape[0] if layout[1] == "t" else b_stored.shape[1]
+    return lib.rk_gemm_layout(
+        ctypes.c_void_p(a_stored.data_ptr()),
+        ctypes.c_void_p(b_stored.data_ptr()),
+        ctypes.c_void_p(c.data_ptr()),
+        m,
+        n,
+        k,
+        LAYOUT_CODE[layout],
+        DTYPE_CODE[dtype],
+        variant,
+        stream_handle(),
+    )
+
+
 def abi_gemv(x, w, out, variant: int, dtype: str) -> int:
     lib = _native.library()
     m, k = x.shape

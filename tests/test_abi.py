@@ -71,6 +71,11 @@ def test_arguments_are_validated_before_any_device_work():
     assert lib.rk_gemm(null, null, null, 4, 4, 4, 0, 99, null) == _native.RK_ERR_UNSUPPORTED
     assert lib.rk_gemm(null, null, null, 4, 4, 4, 0, 0, null) == _native.RK_ERR_INVALID_ARGUMENT  # null C
     assert lib.rk_gemm(null, null, null, 0, 4, 4, 0, 0, null) == _native.RK_OK  # empty: nothing to do
+    # rk_gemm_layout: layouts 0-3 (nn, nt, tn, tt); anything else is rejected up front
+    assert lib.rk_gemm_layout(null, null, null, 4, 4, 4, 4, 0, 0, null) == _native.RK_ERR_INVALID_ARGUMENT
+    assert lib.rk_gemm_layout(null, null, null, 4, 4, 4, -1, 0, 0, null) == _native.RK_ERR_INVALID_ARGUMENT
+    assert lib.rk_gemm_layout(null, null, null, 0, 4, 4, 2, 0, 0, null) == _native.RK_OK
+    assert lib.rk_gemm_layout(null, null, null, 4, 4, 4, 1, 0, 99, null) == _native.RK_ERR_UNSUPPORTED
     assert lib.rk_gemv(null, null, null, 33, 4, 4, 0, 0, null) == _native.RK_ERR_INVALID_ARGUMENT
     assert lib.rk_gemv(null, null, null, 0, 4, 4, 0, 0, null) == _native.RK_ERR_INVALID_ARGUMENT
     assert lib.rk_gemv(null, null, null, 1, 4, 4, 0, 0, null) == _native.RK_ERR_INVALID_ARGUMENT  # null pointers
