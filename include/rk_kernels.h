@@ -269,6 +269,55 @@ RK_API rk_status rk_add_rms_norm(const void* x, const void* residual, const void
                                  int64_t hidden, float eps, rk_dtype dt,
                                  rk_stream_t stream);
 
+/*
+ * Backward passes of the three neighbours.  The reference runs inputs that require
+ * gradients through its torch fallbacks (ops/swiglu/api.py:49, ops/rms_norm/api.py:53,
+ * ops/add_rms_norm/api.py:57), so its gradients are the autograd of those fp32 graphs
+ * (swiglu/reference.py:6-9, rms_norm/reference.py:6-10, add_rms_norm/reference.py:8-12);
+ * these kernels evaluate the same chain-rule terms in fp32 and round once to the dtype.
+ * All tensors are contiguous [tokens, hidden] (weight and its gradient [hidden]) of
+ * dtype `dt`.
+ *
+ * rk_silu_mul_backward: grad_gate = dy * u * s * (1 + g * (1 - s)) (evaluated as
+ * t*s + ((t*g)*(1-s))*s with t = dy*u), grad_up = dy * (g * s), s = sigmoid(gate).
+ */
+RK_API rk_status rk_silu_mul_backward(const void* grad_out, const void* gate, const void* up,
+                                      void* grad_gate, void* grad_up, int64_t tokens,
+                                      int64_t hidden, rk_dtype dt, rk_stream_t stream);
+
+/*
+ * Workspace bytes rk_rms_norm_backward / rk_add_rms_norm_backward need on the current
+ * device when a weight gradient is requested (fp32 partial column sums, one row per CTA;
+ * 0 for tokens == 0).  Without a weight gradient no workspace is used.
+ */
+RK_API rk_status rk_rms_norm_backward_workspace_size(int64_t tokens, int64_t hidden,
+                                                     size_t* bytes);
+
+/*
+ * rms_norm backward: grad_input = (dy*w)*r + (((-0.5*c)*r^3)/H)*(2*x) with
+ * r = rsqrt(mean(x^2) + eps) and c = sum_j (dy_j*w_j)*x_j per row; grad_weight (nullable:
+ * not computed) = sum over rows of dy*(x*r), added in a fixed order (deterministic).
+ * hidden <= 49152 when grad_weight is requested (RK_ERR_UNSUPPORTED otherwise).
+ */
+RK_API rk_status rk_rms_norm_backward(const void* grad_out, const void* input,
+                                      const void* weight, void* grad_input, void* grad_weight,
+                                      int64_t tokens, int64_t hidden, float eps, rk_dtype dt,
+                                      void* workspace, size_t workspace_bytes,
+                                      rk_stream_t stream);
+
+/*
+ * add_rms_norm backward, from the saved residual_out s = x + residual: the rms_norm
+ * input gradient at s, rounded, plus grad_residual_out (nullable: no gradient flows into
+ * residual_out), rounded again, is stored to grad_input and (nullable) grad_residual --
+ * both inputs of the add receive it; grad_weight as in rk_rms_norm_backward.
+ */
+RK_API rk_status rk_add_rms_norm_backward(const void* grad_out, const void* grad_residual_out,
+                                          const void* residual_out, const void* weight,
+                                          void* grad_input, void* grad_residual,
+                                          void* grad_weight, int64_t tokens, int64_t hidden,
+                                          float eps, rk_dtype dt, void* workspace,
+                                          size_t workspace_bytes, rk_stream_t stream);
+
 /* Static description of a status code; never NULL. */
 RK_API const char* rk_status_string(rk_status status);
 
@@ -287,6 +336,11 @@ RK_API void rk_gemm_set_tile_n(int tile_n);
  * restores the built-in choice (256 for few rows, 128 from two rows per SM).
  * Process-wide. */
 RK_API void rk_norm_set_threads(int threads_per_row);
+
+/* Tuning hook for the rms_norm backward row kernel: CTAs per SM (1..32); 0 restores the
+ * built-in choice (1024 threads per SM with a weight gradient, 2048 without).
+ * Process-wide.  Changes the workspace size. */
+RK_API void rk_norm_backward_set_ctas_per_sm(int ctas_per_sm);
 
 /* Tuning hook for RK_GEMV_TC: thread-block cluster size (K split), 1..8; -1 selects
  * stream-K through the rk_gemv_ex workspace (without one it falls back to cluster

@@ -71,6 +71,8 @@ rk_status cuda_status(cudaError_t e) {
   return RK_ERR_CUDA;
 }
 
+void note_error(const std::string& message) { g_last_error = message; }
+
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 namespace {
@@ -327,6 +329,63 @@ rk_status rk_add_rms_norm(const void* x, const void* residual, const void* weigh
   if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
   return rms_norm_launch(x, residual, weight, out, residual_out, tokens, hidden, eps, dt,
                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+rk_status rk_silu_mul_backward(const void* grad_out, const void* gate, const void* up,
+                               void* grad_gate, void* grad_up, int64_t tokens, int64_t hidden,
+                               rk_dtype dt, rk_stream_t stream) {
+  if (tokens < 0 || hidden < 0 || !valid_dtype(dt)) return RK_ERR_INVALID_ARGUMENT;
+  if (tokens > 0 && hidden > 0 &&
+      (grad_out == nullptr || gate == nullptr || up == nullptr || grad_gate == nullptr ||
+       grad_up == nullptr))
+    return RK_ERR_INVALID_ARGUMENT;
+  if (hidden > 0 && tokens > INT64_MAX / hidden) return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return silu_mul_backward_launch(grad_out, gate, up, grad_gate, grad_up, tokens, hidden, dt,
+                                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+rk_status rk_rms_norm_backward_workspace_size(int64_t tokens, int64_t hidden, size_t* bytes) {
+  if (bytes == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  *bytes = 0;
+  if (tokens < 0 || hidden < 1) return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  *bytes = rms_norm_backward_workspace_bytes(tokens, hidden);
+  return RK_OK;
+}
+
+rk_status rk_rms_norm_backward(const void* grad_out, const void* input, const void* weight,
+                               void* grad_input, void* grad_weight, int64_t tokens,
+                               int64_t hidden, float eps, rk_dtype dt, void* workspace,
+                               size_t workspace_bytes, rk_stream_t stream) {
+  if (tokens < 0 || hidden < 1 || !valid_dtype(dt) || !valid_eps(eps)) return RK_ERR_INVALID_ARGUMENT;
+  if (tokens > 0 && (grad_out == nullptr || input == nullptr || grad_input == nullptr))
+    return RK_ERR_INVALID_ARGUMENT;
+  if (weight == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return rms_norm_backward_launch(grad_out, input, weight, false, nullptr, grad_input, nullptr,
+                                  grad_weight, tokens, hidden, eps, dt, workspace,
+                                  workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+rk_status rk_add_rms_norm_backward(const void* grad_out, const void* grad_residual_out,
+                                   const void* residual_out, const void* weight, void* grad_input,
+                                   void* grad_residual, void* grad_weight, int64_t tokens,
+                                   int64_t hidden, float eps, rk_dtype dt, void* workspace,
+                                   size_t workspace_bytes, rk_stream_t stream) {
+  if (tokens < 0 || hidden < 1 || !valid_dtype(dt) || !valid_eps(eps)) return RK_ERR_INVALID_ARGUMENT;
+  if (tokens > 0 && (grad_out == nullptr || residual_out == nullptr || grad_input == nullptr))
+    return RK_ERR_INVALID_ARGUMENT;
+  if (weight == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return rms_norm_backward_launch(grad_out, residual_out, weight, true, grad_residual_out,
+                                  grad_input, grad_residual, grad_weight, tokens, hidden, eps, dt,
+                                  workspace, workspace_bytes,
+                                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+void rk_norm_backward_set_ctas_per_sm(int ctas_per_sm) {
+  norm_backward_set_ctas_per_sm(ctas_per_sm >= 1 && ctas_per_sm <= 32 ? ctas_per_sm : 0);
 }
 
 rk_status rk_gemv(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,

@@ -3,6 +3,8 @@
 #pragma once
 
 #include <cuda_runtime.h>
+
+#include <string>
 #include <cstdint>
 #include <utility>
 
@@ -58,6 +60,8 @@ cudaError_t launch_kernel(void (*kernel)(Params...), dim3 grid, dim3 block, size
 }
 // Maps a CUDA error to a status code (and remembers the message).
 rk_status cuda_status(cudaError_t e);
+// Records a message for rk_last_error() (this thread) without changing any status.
+void note_error(const std::string& message);
 
 // Kernel families.  All validate what they need and return RK_ERR_UNSUPPORTED
 // when the variant cannot run the request.
@@ -109,6 +113,19 @@ rk_status rms_norm_launch(const void* x, const void* residual, const void* weigh
                           void* residual_out, int64_t tokens, int64_t hidden, float eps,
                           rk_dtype dt, cudaStream_t s);
 void norm_set_threads(int threads);
+// Backward passes (llm_ops_backward.cu).  rms_norm_backward_launch: add == false ->
+// rms_norm (x = input, dres/dres_out unused); add == true -> add_rms_norm (x =
+// residual_out, dres nullable = no residual_out gradient, dres_out nullable).  dw
+// nullable: no weight gradient (no workspace needed).
+rk_status silu_mul_backward_launch(const void* dy, const void* gate, const void* up, void* dgate,
+                                   void* dup, int64_t tokens, int64_t hidden, rk_dtype dt,
+                                   cudaStream_t s);
+rk_status rms_norm_backward_launch(const void* dy, const void* x, const void* w, bool add,
+                                   const void* dres, void* dx, void* dres_out, void* dw,
+                                   int64_t tokens, int64_t hidden, float eps, rk_dtype dt,
+                                   void* workspace, size_t workspace_bytes, cudaStream_t s);
+size_t rms_norm_backward_workspace_bytes(int64_t tokens, int64_t hidden);
+void norm_backward_set_ctas_per_sm(int ctas);
 
 rk_status gather_column_blocks_launch(const void* blocks, void* out, int64_t G, int64_t M,
                                       int64_t N, rk_dtype dt, cudaStream_t s);

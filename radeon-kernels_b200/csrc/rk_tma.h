@@ -9,6 +9,7 @@
 
 #include <cstdint>
 #include <mutex>
+#include <string>
 
 #include "rk_internal.h"
 
@@ -49,7 +50,12 @@ inline rk_status encode_tmap_2d(CUtensorMap* map, const void* base, rk_dtype dt,
   const CUresult r = fn(map, t, 2, const_cast<void*>(base), dims, strides, box, estride,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? RK_OK : RK_ERR_UNSUPPORTED;
+  if (r == CUDA_SUCCESS) return RK_OK;
+  note_error("cuTensorMapEncodeTiled failed (CUresult " + std::to_string(static_cast<int>(r)) +
+             ") for a [" + std::to_string(outer) + ", " + std::to_string(inner) + "] matrix at " +
+             std::to_string(reinterpret_cast<uintptr_t>(base)) + " with box [" +
+             std::to_string(box_outer) + ", " + std::to_string(box_inner) + "]");
+  return RK_ERR_UNSUPPORTED;
 }
 
 // Encoding a tensor map costs about a microsecond of host time per call; decode loops

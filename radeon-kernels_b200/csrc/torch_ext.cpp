@@ -66,8 +66,12 @@ void check_rows(const at::Tensor& t, const char* name, int64_t rank) {
 }
 
 void check_status(rk_status st, const char* what) {
-  TORCH_CHECK(st == RK_OK, what, " failed: ", rk_status_string(st),
-              (st == RK_ERR_CUDA ? std::string(" (") + rk_last_error() + ")" : std::string()));
+  if (st == RK_OK) return;
+  const std::string detail = rk_last_error();
+  TORCH_CHECK(false, what, " failed: ", rk_status_string(st),
+              (st == RK_ERR_CUDA || (st == RK_ERR_UNSUPPORTED && !detail.empty())
+                   ? std::string(" (") + detail + ")"
+                   : std::string()));
 }
 
 rk_stream_t current_stream(const at::Tensor& t) {
@@ -130,9 +134,12 @@ at::Tensor gemm_views(const at::Tensor& a, const at::Tensor& b, c10::optional<at
               "out must match the operands' device and dtype");
   TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == b.size(1), "out has the wrong shape");
   c10::cuda::CUDAGuard guard(a.device());
+  const std::string what = "rk_gemm_layout(layout " + std::to_string(static_cast<int>(layout)) +
+                           ", M " + std::to_string(a.size(0)) + ", N " + std::to_string(b.size(1)) +
+                           ", K " + std::to_string(a.size(1)) + ")";
   check_status(rk_gemm_layout(a.data_ptr(), b.data_ptr(), out.data_ptr(), a.size(0), b.size(1),
                               a.size(1), layout, dt, static_cast<int>(variant), current_stream(a)),
-               "rk_gemm_layout");
+               what.c_str());
   return out;
 }
 
@@ -311,6 +318,112 @@ std::vector<at::Tensor> add_rms_norm(const at::Tensor& input, const at::Tensor& 
   return {out, residual_out};
 }
 
+// ------------------------------------------------------------------ backward passes
+std::vector<at::Tensor> silu_mul_backward(const at::Tensor& grad, const at::Tensor& gate,
+                                          const at::Tensor& up) {
+  for (const auto& [t, name] : {std::pair<const at::Tensor*, const char*>{&grad, "grad"},
+                                {&gate, "gate"}, {&up, "up"}}) {
+    check_rows(*t, name, 2);
+    TORCH_CHECK(t->device() == gate.device() && t->scalar_type() == gate.scalar_type(),
+                "grad, gate and up must share device and dtype");
+    TORCH_CHECK(t->sizes() == gate.sizes(), "grad, gate and up must have one shape");
+  }
+  c10::cuda::CUDAGuard guard(gate.device());
+  auto grad_gate = at::empty_like(gate);
+  auto grad_up = at::empty_like(gate);
+  check_status(rk_silu_mul_backward(grad.data_ptr(), gate.data_ptr(), up.data_ptr(),
+                                    grad_gate.data_ptr(), grad_up.data_ptr(), gate.size(0),
+                                    gate.size(1), dtype_of(gate, "gate"), current_stream(gate)),
+               "rk_silu_mul_backward");
+  return {grad_gate, grad_up};
+}
+
+// Shared by rms_norm_backward / add_rms_norm_backward: the weight gradient (when wanted)
+// and its workspace.
+struct WeightGrad {
+  at::Tensor grad, workspace;
+};
+
+WeightGrad weight_grad_buffers(const at::Tensor& x, const at::Tensor& weight, bool want) {
+  WeightGrad w;
+  if (!want) return w;
+  w.grad = at::empty_like(weight);
+  size_t bytes = 0;
+  check_status(rk_rms_norm_backward_workspace_size(x.size(0), x.size(1), &bytes),
+               "rk_rms_norm_backward_workspace_size");
+  if (bytes > 0) w.workspace = at::empty({static_cast<int64_t>(bytes)}, x.options().dtype(at::kByte));
+  return w;
+}
+
+// Returns [grad_input, grad_weight]; grad_weight is undefined (None) when not wanted.
+std::vector<at::Tensor> rms_norm_backward(const at::Tensor& grad, const at::Tensor& input,
+                                          const at::Tensor& weight, double eps,
+                                          bool weight_grad) {
+  check_rows(grad, "grad", 2);
+  check_rows(input, "input", 2);
+  check_rows(weight, "weight", 1);
+  TORCH_CHECK(grad.sizes() == input.sizes(), "grad shape must match input");
+  TORCH_CHECK(grad.device() == input.device() && weight.device() == input.device() &&
+                  grad.scalar_type() == input.scalar_type() &&
+                  weight.scalar_type() == input.scalar_type(),
+              "grad, input and weight must share device and dtype");
+  TORCH_CHECK(weight.numel() == input.size(1), "weight must match hidden size");
+  c10::cuda::CUDAGuard guard(input.device());
+  auto grad_input = at::empty_like(input);
+  WeightGrad w = weight_grad_buffers(input, weight, weight_grad);
+  check_status(rk_rms_norm_backward(grad.data_ptr(), input.data_ptr(), weight.data_ptr(),
+                                    grad_input.data_ptr(),
+                                    w.grad.defined() ? w.grad.data_ptr() : nullptr, input.size(0),
+                                    input.size(1), static_cast<float>(eps),
+                                    dtype_of(input, "input"),
+                                    w.workspace.defined() ? w.workspace.data_ptr() : nullptr,
+                                    w.workspace.defined() ? w.workspace.numel() : 0,
+                                    current_stream(input)),
+               "rk_rms_norm_backward");
+  return {grad_input, w.grad};
+}
+
+// Returns [grad_input, grad_residual, grad_weight] (grad_weight undefined when not wanted);
+// grad_residual_out may be None (no gradient flows into residual_out).
+std::vector<at::Tensor> add_rms_norm_backward(const at::Tensor& grad,
+                                              c10::optional<at::Tensor> grad_residual_out,
+                                              const at::Tensor& residual_out,
+                                              const at::Tensor& weight, double eps,
+                                              bool weight_grad) {
+  check_rows(grad, "grad", 2);
+  check_rows(residual_out, "residual_out", 2);
+  check_rows(weight, "weight", 1);
+  TORCH_CHECK(grad.sizes() == residual_out.sizes(), "grad shape must match residual_out");
+  TORCH_CHECK(grad.device() == residual_out.device() && weight.device() == residual_out.device() &&
+                  grad.scalar_type() == residual_out.scalar_type() &&
+                  weight.scalar_type() == residual_out.scalar_type(),
+              "grad, residual_out and weight must share device and dtype");
+  TORCH_CHECK(weight.numel() == residual_out.size(1), "weight must match hidden size");
+  const void* dres = nullptr;
+  if (grad_residual_out.has_value() && grad_residual_out->defined()) {
+    check_rows(*grad_residual_out, "grad_residual_out", 2);
+    TORCH_CHECK(grad_residual_out->sizes() == residual_out.sizes() &&
+                    grad_residual_out->device() == residual_out.device() &&
+                    grad_residual_out->scalar_type() == residual_out.scalar_type(),
+                "grad_residual_out must match residual_out");
+    dres = grad_residual_out->data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(residual_out.device());
+  auto grad_input = at::empty_like(residual_out);
+  auto grad_residual = at::empty_like(residual_out);
+  WeightGrad w = weight_grad_buffers(residual_out, weight, weight_grad);
+  check_status(rk_add_rms_norm_backward(
+                   grad.data_ptr(), dres, residual_out.data_ptr(), weight.data_ptr(),
+                   grad_input.data_ptr(), grad_residual.data_ptr(),
+                   w.grad.defined() ? w.grad.data_ptr() : nullptr, residual_out.size(0),
+                   residual_out.size(1), static_cast<float>(eps),
+                   dtype_of(residual_out, "residual_out"),
+                   w.workspace.defined() ? w.workspace.data_ptr() : nullptr,
+                   w.workspace.defined() ? w.workspace.numel() : 0, current_stream(residual_out)),
+               "rk_add_rms_norm_backward");
+  return {grad_input, grad_residual, w.grad};
+}
+
 int64_t device_status() {
   return static_cast<int64_t>(rk_device_status(
       reinterpret_cast<rk_stream_t>(c10::cuda::getCurrentCUDAStream().stream())));
@@ -342,6 +455,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("eps"));
   m.def("add_rms_norm", &add_rms_norm, "residual add + row RMS normalisation -> [out, residual_out]",
         py::arg("input"), py::arg("residual"), py::arg("weight"), py::arg("eps"));
+  m.def("silu_mul_backward", &silu_mul_backward, "gradients of silu(gate) * up -> [grad_gate, grad_up]",
+        py::arg("grad"), py::arg("gate"), py::arg("up"));
+  m.def("rms_norm_backward", &rms_norm_backward, "rms_norm gradients -> [grad_input, grad_weight]",
+        py::arg("grad"), py::arg("input"), py::arg("weight"), py::arg("eps"),
+        py::arg("weight_grad") = true);
+  m.def("add_rms_norm_backward", &add_rms_norm_backward,
+        "add_rms_norm gradients -> [grad_input, grad_residual, grad_weight]", py::arg("grad"),
+        py::arg("grad_residual_out"), py::arg("residual_out"), py::arg("weight"), py::arg("eps"),
+        py::arg("weight_grad") = true);
+  m.def("norm_backward_set_ctas_per_sm", [](int c) { rk_norm_backward_set_ctas_per_sm(c); });
   m.def("device_status", &device_status, "read and clear the device status word");
   m.def("set_wait_timeout_ns", [](uint64_t ns) { rk_set_wait_timeout_ns(ns); });
   m.def("debug_inject_stall", [](bool on) { rk_debug_inject_stall(on ? 1 : 0); });

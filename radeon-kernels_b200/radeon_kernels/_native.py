@@ -75,6 +75,16 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_gemm.restype = cint
     lib.rk_gemm_layout.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, cint, vp]
     lib.rk_gemm_layout.restype = cint
+    lib.rk_silu_mul_backward.argtypes = [vp] * 5 + [i64, i64, cint, vp]
+    lib.rk_silu_mul_backward.restype = cint
+    lib.rk_rms_norm_backward_workspace_size.argtypes = [i64, i64, ctypes.POINTER(ctypes.c_size_t)]
+    lib.rk_rms_norm_backward_workspace_size.restype = cint
+    lib.rk_rms_norm_backward.argtypes = [vp] * 5 + [i64, i64, ctypes.c_float, cint, vp, ctypes.c_size_t, vp]
+    lib.rk_rms_norm_backward.restype = cint
+    lib.rk_add_rms_norm_backward.argtypes = [vp] * 7 + [i64, i64, ctypes.c_float, cint, vp, ctypes.c_size_t, vp]
+    lib.rk_add_rms_norm_backward.restype = cint
+    lib.rk_norm_backward_set_ctas_per_sm.argtypes = [cint]
+    lib.rk_norm_backward_set_ctas_per_sm.restype = None
     lib.rk_gemv.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, vp]
     lib.rk_gemv.restype = cint
     lib.rk_gemv_ex.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, vp, ctypes.c_size_t, vp]

@@ -124,59 +124,126 @@ def gemv(torch_module: Any, x: Any, weight: Any) -> Any:
 
 
 # --------------------------------------------------------------- decode neighbours
-# silu_mul / rms_norm / add_rms_norm (rk_silu_mul, rk_rms_norm, rk_add_rms_norm).  Their
-# backward passes are not built yet: an input that requires gradients gets an autograd node
-# whose backward raises, so a forward pass (e.g. evaluation with parameters that require
-# gradients) still runs on these kernels and a backward pass fails loudly instead of
-# silently computing with another library.
+# silu_mul / rms_norm / add_rms_norm (rk_silu_mul, rk_rms_norm, rk_add_rms_norm) and the
+# fused gemm_swiglu.  Inputs that require gradients run the same forward kernels under an
+# autograd node whose backward is this library's backward kernels (rk_silu_mul_backward,
+# rk_rms_norm_backward, rk_add_rms_norm_backward): the gradients of the reference's fp32
+# fallback graphs, which is what a reference user gets for such inputs.
 
-_NEIGHBOUR_FUNCTION: Any = None
-
-
-def _no_backward_function() -> Any:
-    global _NEIGHBOUR_FUNCTION
-    if _NEIGHBOUR_FUNCTION is None:
-        import torch
-
-        class _ForwardOnly(torch.autograd.Function):
-            @staticmethod
-            def forward(ctx: Any, name: str, run: Any, *inputs: Any) -> Any:
-                ctx.name = name
-                return run(*[t.detach() for t in inputs])
-
-            @staticmethod
-            def backward(ctx: Any, *grads: Any) -> Any:
-                raise NotImplementedError(f"{ctx.name}: the backward pass is not implemented in this build")
-
-        _NEIGHBOUR_FUNCTION = _ForwardOnly
-    return _NEIGHBOUR_FUNCTION
+_NEIGHBOUR_FUNCTIONS: dict[str, Any] | None = None
 
 
-def _run(torch_module: Any, name: str, run: Any, *inputs: Any) -> Any:
-    inputs = tuple(_contiguous(t) for t in inputs)
-    if _needs_grad(torch_module, *inputs):
-        return _no_backward_function().apply(name, run, *inputs)
-    return run(*inputs)
+def _neighbour_functions() -> dict[str, Any]:
+    global _NEIGHBOUR_FUNCTIONS
+    if _NEIGHBOUR_FUNCTIONS is not None:
+        return _NEIGHBOUR_FUNCTIONS
+    import torch
+
+    ext = _native.extension
+
+    class _SiluMulFunction(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx: Any, gate: Any, up: Any) -> Any:
+            ctx.save_for_backward(gate, up)
+            return ext().silu_mul(gate, up)
+
+        @staticmethod
+        def backward(ctx: Any, grad: Any) -> Any:
+            gate, up = ctx.saved_tensors
+            grad_gate, grad_up = ext().silu_mul_backward(_contiguous(grad), gate, up)
+            return grad_gate, grad_up
+
+    class _RmsNormFunction(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx: Any, x: Any, weight: Any, eps: float) -> Any:
+            ctx.save_for_backward(x, weight)
+            ctx.eps = eps
+            return ext().rms_norm(x, weight, eps)
+
+        @staticmethod
+        def backward(ctx: Any, grad: Any) -> Any:
+            x, weight = ctx.saved_tensors
+            grad_x, grad_w = ext().rms_norm_backward(_contiguous(grad), x, weight, ctx.eps, ctx.needs_input_grad[1])
+            return grad_x, grad_w, None
+
+    class _AddRmsNormFunction(torch.autograd.Function):
+        @staticmethod
+        def forward(ctx: Any, x: Any, residual: Any, weight: Any, eps: float) -> Any:
+            out, residual_out = ext().add_rms_norm(x, residual, weight, eps)
+            ctx.save_for_backward(residual_out, weight)
+            ctx.eps = eps
+            # An output that receives no gradient arrives as None, not as zeros: the
+            # reference's graph adds no term for it (a -0 gradient stays -0).
+            ctx.set_materialize_grads(False)
+            return out, residual_out
+
+        @staticmethod
+        def backward(ctx: Any, grad_out: Any, grad_residual_out: Any) -> Any:
+            residual_out, weight = ctx.saved_tensors
+            if grad_out is None:
+                # Only residual_out = x + residual carries a gradient: it passes to both.
+                if grad_residual_out is None:
+                    return None, None, None, None
+                return grad_residual_out, grad_residual_out.clone(), None, None
+            dres = None if grad_residual_out is None else _contiguous(grad_residual_out)
+            grad_x, grad_residual, grad_w = ext().add_rms_norm_backward(
+                _contiguous(grad_out), dres, residual_out, weight, ctx.eps, ctx.needs_input_grad[2]
+            )
+            return grad_x, grad_residual, grad_w, None
+
+    class _GemmSwigluFunction(torch.autograd.Function):
+        """Backward of the composition rk.gemm -> rk.silu_mul that the fused kernel replaces:
+        the [M, 2N] product is recomputed (rounded, as the composition stores it), then
+        silu_mul's backward and the two GEMM gradients (nt and tn layouts, read in place)."""
+
+        @staticmethod
+        def forward(ctx: Any, a: Any, b: Any) -> Any:
+            ctx.save_for_backward(a, b)
+            return _gemm_swiglu_raw(a, b)
+
+        @staticmethod
+        def backward(ctx: Any, grad: Any) -> Any:
+            a, b = ctx.saved_tensors
+            n = int(b.shape[1]) // 2
+            y = _gemm_raw(a, b, None)
+            grad_gate, grad_up = ext().silu_mul_backward(
+                _contiguous(grad), y[:, :n].contiguous(), y[:, n:].contiguous()
+            )
+            grad_y = torch.cat([grad_gate, grad_up], dim=1)
+            grad_a = _gemm_raw(grad_y, b.t(), None) if ctx.needs_input_grad[0] else None
+            grad_b = _gemm_raw(a.t(), grad_y, None) if ctx.needs_input_grad[1] else None
+            return grad_a, grad_b
+
+    _NEIGHBOUR_FUNCTIONS = {
+        "silu_mul": _SiluMulFunction,
+        "rms_norm": _RmsNormFunction,
+        "add_rms_norm": _AddRmsNormFunction,
+        "gemm_swiglu": _GemmSwigluFunction,
+    }
+    return _NEIGHBOUR_FUNCTIONS
 
 
 def silu_mul(torch_module: Any, gate: Any, up: Any) -> Any:
-    return _run(torch_module, "silu_mul", lambda g, u: _native.extension().silu_mul(g, u), gate, up)
+    gate, up = _contiguous(gate), _contiguous(up)
+    if _needs_grad(torch_module, gate, up):
+        return _neighbour_functions()["silu_mul"].apply(gate, up)
+    return _native.extension().silu_mul(gate, up)
 
 
 def rms_norm(torch_module: Any, x: Any, weight: Any, eps: float) -> Any:
-    return _run(torch_module, "rms_norm", lambda a, w: _native.extension().rms_norm(a, w, eps), x, weight)
+    x, weight = _contiguous(x), _contiguous(weight)
+    if _needs_grad(torch_module, x, weight):
+        return _neighbour_functions()["rms_norm"].apply(x, weight, eps)
+    return _native.extension().rms_norm(x, weight, eps)
 
 
 def add_rms_norm(torch_module: Any, x: Any, residual: Any, weight: Any, eps: float) -> tuple[Any, Any]:
-    out = _run(
-        torch_module,
-        "add_rms_norm",
-        lambda a, r, w: tuple(_native.extension().add_rms_norm(a, r, w, eps)),
-        x,
-        residual,
-        weight,
-    )
-    return out[0], out[1]
+    x, residual, weight = _contiguous(x), _contiguous(residual), _contiguous(weight)
+    if _needs_grad(torch_module, x, residual, weight):
+        out, residual_out = _neighbour_functions()["add_rms_norm"].apply(x, residual, weight, eps)
+    else:
+        out, residual_out = _native.extension().add_rms_norm(x, residual, weight, eps)
+    return out, residual_out
 
 
 def _gemm_swiglu_raw(a: Any, b: Any) -> Any:
@@ -193,7 +260,10 @@ def _gemm_swiglu_raw(a: Any, b: Any) -> Any:
 
 
 def gemm_swiglu(torch_module: Any, a: Any, b: Any) -> Any:
-    return _run(torch_module, "gemm_swiglu", _gemm_swiglu_raw, a, b)
+    a, b = _contiguous(a), _contiguous(b)
+    if _needs_grad(torch_module, a, b):
+        return _neighbour_functions()["gemm_swiglu"].apply(a, b)
+    return _gemm_swiglu_raw(a, b)
 
 
 def paged_attention_decode(
