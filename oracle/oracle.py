@@ -56,6 +56,13 @@ def _library() -> ctypes.CDLL:
         lib.rk_oracle_rms_norm.restype = None
         lib.rk_oracle_add_rms_norm.argtypes = [u16p, u16p, u16p, u16p, u16p, f32p, f32p, i64, i64, f32, cint]
         lib.rk_oracle_add_rms_norm.restype = None
+        f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
+        lib.rk_oracle_silu_mul_backward.argtypes = [u16p, u16p, u16p, u16p, u16p, f32p, f32p, f32p, i64, cint]
+        lib.rk_oracle_silu_mul_backward.restype = None
+        lib.rk_oracle_rms_norm_backward.argtypes = [
+            u16p, u16p, u16p, ctypes.c_void_p, u16p, f32p, f32p, u16p, f32p, f32p, f64p, i64, i64, f32, cint, cint,
+        ]
+        lib.rk_oracle_rms_norm_backward.restype = None
         _lib = lib
     return _lib
 
@@ -155,6 +162,106 @@ def add_rms_norm(
     work = np.empty(hidden + 1, np.float32)
     _library().rk_oracle_add_rms_norm(x, r, w, out, residual_out, exact, work, tokens, hidden, eps, _code(dtype))
     return out, residual_out, exact
+
+
+def silu_mul_backward(dy_bits: np.ndarray, gate_bits: np.ndarray, up_bits: np.ndarray, dtype: str) -> dict[str, np.ndarray]:
+    """Gradients of silu(gate) * up (reference autograd order); bits, fp32 values and term scales."""
+
+    dy, g, u = (np.ascontiguousarray(a, dtype=np.uint16) for a in (dy_bits, gate_bits, up_bits))
+    if not (dy.shape == g.shape == u.shape):
+        raise ValueError("dy, gate and up shapes differ")
+    out = {
+        "grad_gate": np.empty(g.shape, np.uint16),
+        "grad_up": np.empty(g.shape, np.uint16),
+        "grad_gate_fp32": np.empty(g.shape, np.float32),
+        "grad_up_fp32": np.empty(g.shape, np.float32),
+        "grad_gate_scale": np.empty(g.shape, np.float32),
+    }
+    _library().rk_oracle_silu_mul_backward(
+        dy.reshape(-1), g.reshape(-1), u.reshape(-1), out["grad_gate"].reshape(-1), out["grad_up"].reshape(-1),
+        out["grad_gate_fp32"].reshape(-1), out["grad_up_fp32"].reshape(-1), out["grad_gate_scale"].reshape(-1),
+        g.size, _code(dtype),
+    )
+    out["grad_up_scale"] = np.abs(out["grad_up_fp32"])
+    return out
+
+
+def _norm_backward(dy_bits, x_bits, w_bits, dres_bits, eps: float, add: bool, dtype: str) -> dict[str, np.ndarray]:
+    dy = np.ascontiguousarray(dy_bits, dtype=np.uint16)
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    tokens, hidden = x.shape
+    if dy.shape != x.shape or w.shape != (hidden,):
+        raise ValueError("shapes of dy, x and weight do not match")
+    dres = None if dres_bits is None else np.ascontiguousarray(dres_bits, dtype=np.uint16)
+    out = {
+        "grad_x": np.empty(x.shape, np.uint16),
+        "grad_x_fp32": np.empty(x.shape, np.float32),
+        "grad_x_scale": np.empty(x.shape, np.float32),
+        "grad_weight": np.empty(hidden, np.uint16),
+        "grad_weight_fp32": np.empty(hidden, np.float32),
+        "grad_weight_scale": np.empty(hidden, np.float32),
+    }
+    work = np.empty(2 * hidden, np.float64)
+    _library().rk_oracle_rms_norm_backward(
+        dy, x, w, None if dres is None else dres.ctypes.data_as(ctypes.c_void_p), out["grad_x"], out["grad_x_fp32"],
+        out["grad_x_scale"], out["grad_weight"], out["grad_weight_fp32"], out["grad_weight_scale"], work,
+        tokens, hidden, eps, 1 if add else 0, _code(dtype),
+    )
+    return out
+
+
+def rms_norm_backward(dy_bits, x_bits, w_bits, eps: float, dtype: str) -> dict[str, np.ndarray]:
+    """Gradients of rms_norm(x, weight) for the output gradient dy (reference autograd order)."""
+
+    return _norm_backward(dy_bits, x_bits, w_bits, None, eps, False, dtype)
+
+
+def add_rms_norm_backward(dy_bits, dres_bits, residual_out_bits, w_bits, eps: float, dtype: str) -> dict[str, np.ndarray]:
+    """Gradients of add_rms_norm from the saved residual_out: grad_x (= the residual's gradient)
+    and grad_weight; dres_bits is the residual_out gradient, or None when none flows."""
+
+    return _norm_backward(dy_bits, residual_out_bits, w_bits, dres_bits, eps, True, dtype)
+
+
+# Gradients: elementwise expressions whose terms can cancel (silu_mul's dgate at
+# g ~ -1.28, rms_norm's dx where its two terms meet) and fp32 sums over a row or over the
+# rows (rms_norm's c and dw) whose order differs between implementations.  The gate per
+# element: NaN exactly where the reference has NaN; otherwise at most one representable
+# step from the reference's rounded gradient, or -- where the value is much smaller than
+# the terms that formed it -- within GRADIENT_REL x (the sum of the terms' magnitudes)
+# plus one step of the value.  A wrong formula misses by a large fraction of the terms.
+GRADIENT_REL = 2.0**-14
+_STEP = {"bf16": 2.0**-7, "fp16": 2.0**-10}
+
+
+def assert_gradient(result_bits, ref_bits, ref_fp32, ref_scale, dtype: str, rel: float = GRADIENT_REL) -> dict[str, float]:
+    """Raise AssertionError unless a 16-bit gradient passes the gate above."""
+
+    result = np.asarray(result_bits, np.uint16)
+    ref = np.asarray(ref_bits, np.uint16)
+    if result.shape != ref.shape:
+        raise AssertionError(f"shape {result.shape} != {ref.shape}")
+    nan_r, nan_ref = _is_nan(result, dtype), _is_nan(ref, dtype)
+    if not np.array_equal(nan_r, nan_ref):
+        raise AssertionError(f"NaN positions differ at {np.argwhere(nan_r != nan_ref)[:5].tolist()}")
+    keep = ~nan_ref
+    steps = ulp_distance(result[keep], ref[keep])
+    value = widen(result[keep], dtype).astype(np.float64)
+    ref32 = np.asarray(ref_fp32, np.float64)[keep]
+    scale = np.asarray(ref_scale, np.float64)[keep]
+    with np.errstate(invalid="ignore"):
+        allowed = rel * scale + _STEP[dtype] * np.abs(ref32)
+        close = np.abs(value - ref32) <= allowed
+    ok = (steps <= 1) | close
+    if not ok.all():
+        i = int(np.argmin(ok))
+        where = np.argwhere(keep)[i].tolist()
+        raise AssertionError(
+            f"gradient at {where}: {value[i]!r} vs reference {ref32[i]!r} ({int(steps[i])} steps, "
+            f"terms of magnitude {scale[i]:.3e})"
+        )
+    return {"max_steps": float(steps.max(initial=0)), "within_one_step": float(np.mean(steps <= 1)) if steps.size else 1.0}
 
 
 def paged_attention_decode(

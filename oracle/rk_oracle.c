@@ -226,3 +226,91 @@ void rk_oracle_add_rms_norm(const uint16_t* x, const uint16_t* residual, const u
     rms_rows(work, weight, out + t * hidden, exact + t * hidden, hidden, eps, dtype);
   }
 }
+
+/*
+ * Backward passes: what autograd computes through the three reference graphs above (the
+ * reference sends inputs that require gradients to those fallbacks: ops/swiglu/api.py:49,
+ * ops/rms_norm/api.py:53, ops/add_rms_norm/api.py:57), term for term in fp32:
+ *   silu_mul:     s = sigmoid(g); du = dy*(g*s); t = dy*u; dg = t*s + ((t*g)*(1-s))*s
+ *                 (mul backward twice, then sigmoid backward grad*(1-s)*s)
+ *   rms_norm:     r as in the forward; c = sum_j (dy_j*w_j)*x_j (rsqrt's input gradient
+ *                 source); q = ((-0.5*c)*(r*r*r))/H (rsqrt backward, then mean backward);
+ *                 dx = (dy*w)*r + q*(2*x) (pow backward); dw = sum over rows of dy*(x*r)
+ *   add_rms_norm: x is the saved residual_out s; ds = round(round(dx) + dres) when the
+ *                 residual_out gradient dres is given (two 16-bit gradients of s added),
+ *                 round(dx) otherwise; both inputs of the add receive ds
+ * Row and column sums are taken in double (PyTorch sums in fp32 in its own order, so the
+ * two agree to the last fp32 bits).  Every output also gets `scale`, the sum of the
+ * magnitudes of the terms that form it, so a checker can tell cancellation (a result much
+ * smaller than its terms) from a wrong value.
+ */
+void rk_oracle_silu_mul_backward(const uint16_t* dy, const uint16_t* gate, const uint16_t* up,
+                                 uint16_t* dgate, uint16_t* dup, float* dgate32, float* dup32,
+                                 float* dgate_scale, int64_t n, int dtype) {
+  for (int64_t i = 0; i < n; ++i) {
+    const float d = load16(dy, i, dtype), g = load16(gate, i, dtype), u = load16(up, i, dtype);
+    const float s = 1.0f / (1.0f + expf(-g));
+    const float du = d * (g * s);
+    const float t = d * u;
+    const float direct = t * s;
+    const float through_sigmoid = ((t * g) * (1.0f - s)) * s;
+    const float dg = direct + through_sigmoid;
+    dgate32[i] = dg;
+    dup32[i] = du;
+    dgate_scale[i] = fabsf(direct) + fabsf(through_sigmoid);
+    dgate[i] = store16(dg, dtype);
+    dup[i] = store16(du, dtype);
+  }
+}
+
+/* `work` must hold 2 * hidden doubles; dres may be NULL; add != 0 selects add_rms_norm. */
+void rk_oracle_rms_norm_backward(const uint16_t* dy, const uint16_t* x, const uint16_t* weight,
+                                 const uint16_t* dres, uint16_t* dx, float* dx32, float* dx_scale,
+                                 uint16_t* dw, float* dw32, float* dw_scale, double* work,
+                                 int64_t tokens, int64_t hidden, float eps, int add, int dtype) {
+  double* dw_acc = work;
+  double* dw_abs = work + hidden;
+  for (int64_t j = 0; j < hidden; ++j) dw_acc[j] = dw_abs[j] = 0.0;
+  for (int64_t t = 0; t < tokens; ++t) {
+    const int64_t row = t * hidden;
+    double sum_sq = 0.0, c = 0.0, c_abs = 0.0;
+    for (int64_t j = 0; j < hidden; ++j) {
+      const float v = load16(x, row + j, dtype);
+      const float sq = v * v;
+      sum_sq += (double)sq;
+      const float term = (load16(dy, row + j, dtype) * load16(weight, j, dtype)) * v;
+      c += (double)term;
+      c_abs += fabs((double)term);
+    }
+    const float mean = (float)sum_sq / (float)hidden;
+    const float r = 1.0f / sqrtf(mean + eps);
+    const float q = ((-0.5f * (float)c) * (r * r * r)) / (float)hidden;
+    const float q_abs = ((0.5f * (float)c_abs) * (r * r * r)) / (float)hidden;
+    for (int64_t j = 0; j < hidden; ++j) {
+      const float d = load16(dy, row + j, dtype), v = load16(x, row + j, dtype);
+      const float w = load16(weight, j, dtype);
+      const float direct = (d * w) * r;
+      const float g = direct + q * (2.0f * v);
+      float scale = fabsf(direct) + q_abs * fabsf(2.0f * v);
+      uint16_t bits = store16(g, dtype);
+      float exact = g;
+      if (add && dres != NULL) {
+        const float e = load16(dres, row + j, dtype);
+        exact = load16(&bits, 0, dtype) + e;
+        bits = store16(exact, dtype);
+        scale += fabsf(e);
+      }
+      dx[row + j] = bits;
+      dx32[row + j] = exact;
+      dx_scale[row + j] = scale;
+      const float contribution = d * (v * r);
+      dw_acc[j] += (double)contribution;
+      dw_abs[j] += fabs((double)contribution);
+    }
+  }
+  for (int64_t j = 0; j < hidden; ++j) {
+    dw32[j] = (float)dw_acc[j];
+    dw_scale[j] = (float)dw_abs[j];
+    dw[j] = store16((float)dw_acc[j], dtype);
+  }
+}

@@ -18,6 +18,8 @@ by calling the reference package itself:
   ``ops.swiglu.reference.silu_mul_reference`` (swiglu/reference.py:6-9),
   ``ops.rms_norm.reference.rms_norm_reference`` (rms_norm/reference.py:6-10),
   ``ops.add_rms_norm.reference.add_rms_norm_reference`` (add_rms_norm/reference.py:8-12)
+* gradients of those three (``grad_*`` fixtures): torch autograd run through the same
+  reference functions, which is how the reference serves inputs that require gradients
 
 plus the fp32 values before the final rounding.  16-bit arrays are stored as uint16 bit
 patterns.
@@ -74,6 +76,20 @@ NORM_CASES = [
     ("add_rms_bf16_t2_h16392_long_row", "add_rms_norm", "bf16", 2, 16392, 43, 1e-6),
 ]
 
+# Gradients (autograd through the reference's own fallback functions; the reference runs
+# inputs that require gradients on exactly these graphs).
+# name, operator, dtype, tokens, hidden, seed, eps (norms) / gate scale (silu_mul), flags
+GRAD_CASES = [
+    ("grad_silu_bf16_t4_h264", "silu_mul", "bf16", 4, 264, 70, 1.0, ""),
+    ("grad_silu_fp16_t3_h13_ragged", "silu_mul", "fp16", 3, 13, 71, 1.0, ""),
+    ("grad_silu_bf16_t8_h96_wide_range", "silu_mul", "bf16", 8, 96, 72, 12.0, "specials"),
+    ("grad_rms_bf16_t4_h4096", "rms_norm", "bf16", 4, 4096, 73, 1e-6, ""),
+    ("grad_rms_fp16_t3_h13_ragged", "rms_norm", "fp16", 3, 13, 74, 1e-5, ""),
+    ("grad_rms_bf16_t2_h20000_long_row", "rms_norm", "bf16", 2, 20000, 75, 1e-6, ""),
+    ("grad_add_rms_bf16_t4_h4096", "add_rms_norm", "bf16", 4, 4096, 76, 1e-6, ""),
+    ("grad_add_rms_fp16_t5_h100_ragged_out_only", "add_rms_norm", "fp16", 5, 100, 77, 1e-5, "out_only"),
+    ("grad_add_rms_bf16_t2_h16392_long_row", "add_rms_norm", "bf16", 2, 16392, 78, 1e-6, ""),
+]
 
 # name, dtype, batch, query_heads, kv_heads, head_dim, block_size, num_blocks, max_blocks,
 # context lengths, index dtype, scale (None: 1/sqrt(head_dim)), seed
@@ -202,6 +218,44 @@ def main(argv: list[str] | None = None) -> int:
         exact = s32 * torch.rsqrt(s32.square().mean(dim=-1, keepdim=True) + eps) * weight.float()
         fields["out_fp32"] = exact.numpy()
         np.savez_compressed(HERE / f"{name}.npz", **fields)
+        print(name, (tokens, hidden))
+
+    for name, operator, dt, tokens, hidden, seed, param, flags in GRAD_CASES:
+        gen = torch.Generator().manual_seed(seed)
+        dy = torch.randn((tokens, hidden), generator=gen).to(dtypes[dt])
+        if operator == "silu_mul":
+            gate = (torch.randn((tokens, hidden), generator=gen) * param).to(dtypes[dt])
+            up = torch.randn((tokens, hidden), generator=gen).to(dtypes[dt])
+            if flags == "specials":
+                specials = torch.tensor([60000.0, -60000.0, 0.0, -0.0, float("inf"), float("-inf"), float("nan"), -1.28])
+                gate[0, : specials.numel()] = specials.to(dtypes[dt])
+            gate.requires_grad_(True)
+            up.requires_grad_(True)
+            silu_mul_reference(torch, gate, up).backward(dy)
+            np.savez_compressed(
+                HERE / f"{name}.npz", dtype=dt, dy=_bits(dy), gate=_bits(gate.detach()), up=_bits(up.detach()),
+                grad_gate_ref=_bits(gate.grad), grad_up_ref=_bits(up.grad),
+            )
+        else:
+            x = torch.randn((tokens, hidden), generator=gen).to(dtypes[dt]).requires_grad_(True)
+            weight = (1.0 + 0.1 * torch.randn((hidden,), generator=gen)).to(dtypes[dt]).requires_grad_(True)
+            fields = {"dtype": dt, "eps": np.float64(param), "dy": _bits(dy), "x": _bits(x.detach()),
+                      "weight": _bits(weight.detach())}
+            if operator == "rms_norm":
+                rms_norm_reference(torch, x, weight, param).backward(dy)
+            else:
+                residual = torch.randn((tokens, hidden), generator=gen).to(dtypes[dt]).requires_grad_(True)
+                dres = torch.randn((tokens, hidden), generator=gen).to(dtypes[dt])
+                out, residual_out = add_rms_norm_reference(torch, x, residual, weight, param)
+                if flags == "out_only":
+                    torch.autograd.backward([out], [dy])
+                else:
+                    torch.autograd.backward([out, residual_out], [dy, dres])
+                    fields["dres"] = _bits(dres)
+                fields.update(residual=_bits(residual.detach()), residual_out=_bits(residual_out.detach()),
+                              grad_residual_ref=_bits(residual.grad))
+            fields.update(grad_x_ref=_bits(x.grad), grad_weight_ref=_bits(weight.grad))
+            np.savez_compressed(HERE / f"{name}.npz", **fields)
         print(name, (tokens, hidden))
     return 0
 

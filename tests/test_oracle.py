@@ -133,3 +133,67 @@ def test_oracle_paged_attention_matches_reference_fixtures(path):
         case["q"], case["k"], case["v"], case["block_tables"], case["context_lengths"], float(case["scale"]), dtype
     )
     oracle.assert_attention(out, case["out_ref"], out32, dtype)
+
+
+# ----------------------------------------------------------------- gradients
+@pytest.mark.parametrize("path", golden_cases("grad_silu"), ids=lambda p: p.stem)
+def test_oracle_silu_mul_backward_matches_reference_autograd(path):
+    case = _load(path)
+    dt = str(case["dtype"])
+    got = oracle.silu_mul_backward(case["dy"], case["gate"], case["up"], dt)
+    oracle.assert_gradient(got["grad_gate"], case["grad_gate_ref"], got["grad_gate_fp32"], got["grad_gate_scale"], dt)
+    oracle.assert_gradient(got["grad_up"], case["grad_up_ref"], got["grad_up_fp32"], got["grad_up_scale"], dt)
+
+
+@pytest.mark.parametrize("path", golden_cases("grad_rms"), ids=lambda p: p.stem)
+def test_oracle_rms_norm_backward_matches_reference_autograd(path):
+    case = _load(path)
+    dt = str(case["dtype"])
+    got = oracle.rms_norm_backward(case["dy"], case["x"], case["weight"], float(case["eps"]), dt)
+    oracle.assert_gradient(got["grad_x"], case["grad_x_ref"], got["grad_x_fp32"], got["grad_x_scale"], dt)
+    oracle.assert_gradient(
+        got["grad_weight"], case["grad_weight_ref"], got["grad_weight_fp32"], got["grad_weight_scale"], dt
+    )
+
+
+@pytest.mark.parametrize("path", golden_cases("grad_add_rms"), ids=lambda p: p.stem)
+def test_oracle_add_rms_norm_backward_matches_reference_autograd(path):
+    case = _load(path)
+    dt = str(case["dtype"])
+    dres = case.get("dres")
+    got = oracle.add_rms_norm_backward(case["dy"], dres, case["residual_out"], case["weight"], float(case["eps"]), dt)
+    oracle.assert_gradient(got["grad_x"], case["grad_x_ref"], got["grad_x_fp32"], got["grad_x_scale"], dt)
+    # both inputs of the add receive the same gradient
+    assert np.array_equal(case["grad_x_ref"], case["grad_residual_ref"])
+    oracle.assert_gradient(
+        got["grad_weight"], case["grad_weight_ref"], got["grad_weight_fp32"], got["grad_weight_scale"], dt
+    )
+
+
+def test_gradient_gate_detects_planted_errors():
+    case = _load(golden_cases("grad_rms_bf16_t4")[0])
+    got = oracle.rms_norm_backward(case["dy"], case["x"], case["weight"], float(case["eps"]), "bf16")
+    # An error of 1 % of the terms' magnitude (what a wrong term in the formula gives),
+    # planted in the oracle's own output.
+    wrong = oracle.round_to(got["grad_x_fp32"] + 0.01 * got["grad_x_scale"], "bf16")
+    with pytest.raises(AssertionError):
+        oracle.assert_gradient(wrong, case["grad_x_ref"], got["grad_x_fp32"], got["grad_x_scale"], "bf16")
+    two_steps = got["grad_weight"].copy()
+    two_steps[5] += 2
+    with pytest.raises(AssertionError):
+        oracle.assert_gradient(
+            two_steps, case["grad_weight_ref"], got["grad_weight_fp32"], got["grad_weight_scale"], "bf16"
+        )
+
+
+def test_silu_backward_specials_follow_the_reference():
+    """inf / -inf / NaN gates give NaN gradients where the reference's graph does, and the
+    saturated ends of the sigmoid give the reference's zeros and signs."""
+
+    case = _load(golden_cases("grad_silu_bf16_t8")[0])
+    got = oracle.silu_mul_backward(case["dy"], case["gate"], case["up"], "bf16")
+    for key in ("grad_gate", "grad_up"):
+        mine, ref = got[key][0, :8], case[f"{key}_ref"][0, :8]
+        nan = oracle._is_nan(ref, "bf16")
+        assert np.array_equal(oracle._is_nan(mine, "bf16"), nan)  # NaN payloads may differ
+        assert np.array_equal(mine[~nan], ref[~nan])
