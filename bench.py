@@ -29,6 +29,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -421,8 +422,11 @@ def suite(args, dist: Dist, ext, peaks):
     results = {}
     stream = torch.cuda.current_stream()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    wanted = re.compile(args.suite_filter).search if args.suite_filter else (lambda name: True)
 
     def gemm_case(name, m, n, k, dtype, dist_name, seed, iters, scaling="replica", graph=False):
+        if not wanted(name):
+            return
         a = seeded((m, k), seed, dist_name, dtype)
         b = seeded((k, n), seed + 1, dist_name, dtype)
         c = torch.empty(m, n, dtype=a.dtype, device="cuda")
@@ -468,6 +472,8 @@ def suite(args, dist: Dist, ext, peaks):
         del a, b, c
 
     def gemv_case(name, m, n, k, dtype, seed, iters):
+        if not wanted(name):
+            return
         ws = [seeded((n, k), seed + r, f"normal/{k}", dtype) for r in range(ROTATE)]
         x = seeded((m, k), seed, "normal", dtype)
         out = torch.empty(m, n, dtype=x.dtype, device="cuda")
@@ -504,10 +510,20 @@ def suite(args, dist: Dist, ext, peaks):
         del ws
 
     def neighbour_case(name, op, tokens, hidden, dtype, seed):
-        """silu_mul / rms_norm / add_rms_norm: HBM streams (bytes each launch must move)."""
+        """silu_mul / rms_norm / add_rms_norm and their backward passes: HBM streams (bytes
+        each launch must move: every input read once, every output written once)."""
 
+        if not wanted(name):
+            return
         elems = tokens * hidden
-        per_set = {"silu_mul": 3, "rms_norm": 2, "add_rms_norm": 4}[op] * elems * 2 + (hidden * 2 if op != "silu_mul" else 0)
+        streams = {
+            "silu_mul": 3, "rms_norm": 2, "add_rms_norm": 4,
+            "silu_mul_backward": 5,  # dy, gate, up -> grad_gate, grad_up
+            "rms_norm_backward": 3,  # dy, x -> grad_x (+ weight in, grad_weight out)
+            "add_rms_norm_backward": 5,  # dy, residual_out, d(residual_out) -> grad_x, grad_residual
+        }[op]
+        vectors = {"silu_mul": 0, "silu_mul_backward": 0, "rms_norm_backward": 2, "add_rms_norm_backward": 2}.get(op, 1)
+        per_set = streams * elems * 2 + vectors * hidden * 2
         # Enough rotated input sets that a replay cycle touches > 2 x L2 (decode-sized cases
         # stay L2-resident whatever: they are launch-latency bound and reported as such).
         sets = max(2, min(64, -(-300_000_000 // per_set)))
@@ -516,12 +532,20 @@ def suite(args, dist: Dist, ext, peaks):
         a = [torch.randn((tokens, hidden), generator=gen, device="cuda").to(tdt) for _ in range(sets)]
         b = [torch.randn((tokens, hidden), generator=gen, device="cuda").to(tdt) for _ in range(sets)]
         w = (1 + 0.1 * torch.randn((hidden,), generator=gen, device="cuda")).to(tdt)
+        c = [torch.randn((tokens, hidden), generator=gen, device="cuda").to(tdt) for _ in range(sets)] if op in (
+            "silu_mul_backward", "add_rms_norm_backward") else None
         if op == "silu_mul":
             step = lambda i: ext.silu_mul(a[i % sets], b[i % sets])  # noqa: E731
         elif op == "rms_norm":
             step = lambda i: ext.rms_norm(a[i % sets], w, 1e-6)  # noqa: E731
-        else:
+        elif op == "add_rms_norm":
             step = lambda i: ext.add_rms_norm(a[i % sets], b[i % sets], w, 1e-6)  # noqa: E731
+        elif op == "silu_mul_backward":
+            step = lambda i: ext.silu_mul_backward(a[i % sets], b[i % sets], c[i % sets])  # noqa: E731
+        elif op == "rms_norm_backward":
+            step = lambda i: ext.rms_norm_backward(a[i % sets], b[i % sets], w, 1e-6, True)  # noqa: E731
+        else:
+            step = lambda i: ext.add_rms_norm_backward(a[i % sets], c[i % sets], b[i % sets], w, 1e-6, True)  # noqa: E731
         for i in range(3):
             step(i)
         torch.cuda.synchronize()
@@ -555,11 +579,13 @@ def suite(args, dist: Dist, ext, peaks):
             "timing": f"CUDA graph of {launches} launches over {sets} input sets"
             + (" (L2-resident: launch-latency bound)" if per_set * sets < 256_000_000 else ""),
         }
-        del a, b
+        del a, b, c
 
     def paged_case(name, batch, hq, hkv, ctx, d, bs, dtype, seed):
         """Paged decode attention: bytes = the K/V cache positions every sequence reads."""
 
+        if not wanted(name):
+            return
         tdt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
         maxb = -(-ctx // bs)
         kv_bytes = batch * ctx * hkv * d * 2 * 2
@@ -615,6 +641,8 @@ def suite(args, dist: Dist, ext, peaks):
     def ffn_swiglu_case(name, m, n, k, dtype, iters):
         """Fused FFN-up + SwiGLU: both products (2 x 2MNK FLOP) and the epilogue, one kernel."""
 
+        if not wanted(name):
+            return
         gen = torch.Generator(device="cuda").manual_seed(3)
         tdt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
         a = (torch.randn((m, k), generator=gen, device="cuda") / 64).to(tdt)
@@ -661,6 +689,10 @@ def suite(args, dist: Dist, ext, peaks):
     neighbour_case("add_rms_norm_prefill_t2048_h4096_bf16", "add_rms_norm", 2048, 4096, "bf16", 54)
     neighbour_case("add_rms_norm_prefill_t1024_h8192_bf16", "add_rms_norm", 1024, 8192, "bf16", 55)
     neighbour_case("rms_norm_prefill_t2048_h4096_bf16", "rms_norm", 2048, 4096, "bf16", 56)
+    neighbour_case("swiglu_backward_t1024_h11008_bf16", "silu_mul_backward", 1024, 11008, "bf16", 57)
+    neighbour_case("rms_norm_backward_t2048_h4096_bf16", "rms_norm_backward", 2048, 4096, "bf16", 58)
+    neighbour_case("add_rms_norm_backward_t2048_h4096_bf16", "add_rms_norm_backward", 2048, 4096, "bf16", 59)
+    neighbour_case("rms_norm_backward_decode_h4096_bf16", "rms_norm_backward", 1, 4096, "bf16", 60)
     # Paged decode attention, the reference's workload cases (paged_attention_decode-1.0.yaml).
     paged_case("paged_b1_gqa32x8_c4096_d128_bf16", 1, 32, 8, 4096, 128, 16, "bf16", 60)
     paged_case("paged_b8_gqa32x8_c1024_d128_bf16", 8, 32, 8, 1024, 128, 16, "bf16", 61)
@@ -850,6 +882,7 @@ def main(argv=None) -> int:
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--quick", action="store_true", help="skip the optional 8192^3 suite entry")
     parser.add_argument("--no-suite", action="store_true")
+    parser.add_argument("--suite-filter", default=None, help="regex: run only the suite entries it matches")
     args = parser.parse_args(argv)
 
     if args.impl == "reference":

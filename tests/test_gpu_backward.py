@@ -32,13 +32,16 @@ def _check_norm(got_x, got_w, ref, dt, ref_x_bits=None, ref_w_bits=None):
     """Kernel gradients against the oracle (bits + fp32 + scales), and, when given, against
     the reference's own rounded gradients with the oracle's fp32 values and scales."""
 
-    oracle.assert_gradient(to_bits(got_x), ref["grad_x"], ref["grad_x_fp32"], ref["grad_x_scale"], dt)
+    inter = ref.get("grad_x_intermediate")
+    oracle.assert_gradient(to_bits(got_x), ref["grad_x"], ref["grad_x_fp32"], ref["grad_x_scale"], dt, intermediate=inter)
     if got_w is not None:
         oracle.assert_gradient(
             to_bits(got_w), ref["grad_weight"], ref["grad_weight_fp32"], ref["grad_weight_scale"], dt
         )
     if ref_x_bits is not None:
-        oracle.assert_gradient(to_bits(got_x), ref_x_bits, ref["grad_x_fp32"], ref["grad_x_scale"], dt)
+        oracle.assert_gradient(
+            to_bits(got_x), ref_x_bits, ref["grad_x_fp32"], ref["grad_x_scale"], dt, intermediate=inter
+        )
     if ref_w_bits is not None and got_w is not None:
         oracle.assert_gradient(
             to_bits(got_w), ref_w_bits, ref["grad_weight_fp32"], ref["grad_weight_scale"], dt
@@ -251,13 +254,27 @@ def test_gemm_swiglu_backward_is_the_composition_gradient():
     ad, bd = a.cuda().requires_grad_(True), b.cuda().requires_grad_(True)
     rk.gemm_swiglu(ad, bd).backward(dy.cuda())
 
-    y_bits, _ = oracle.gemm(to_bits(a), to_bits(b), "bf16")
-    ref = oracle.silu_mul_backward(to_bits(dy), y_bits[:, :n], y_bits[:, n:], "bf16")
-    dyy = np.concatenate([ref["grad_gate"], ref["grad_up"]], axis=1)
-    ga_bits, ga32 = oracle.gemm(dyy, np.ascontiguousarray(to_bits(b).T), "bf16")
-    gb_bits, gb32 = oracle.gemm(np.ascontiguousarray(to_bits(a).T), dyy, "bf16")
-    oracle.assert_parity(to_bits(ad.grad), ga_bits, ga32, "bf16")
-    oracle.assert_parity(to_bits(bd.grad), gb_bits, gb32, "bf16")
+    # The same steps through the binding (deterministic kernels: the autograd path must
+    # give identical bits), each step checked against the oracle on its own inputs.
+    ext = _native.extension()
+    y = ext.gemm(a.cuda(), b.cuda(), 0)
+    y_bits, y32 = oracle.gemm(to_bits(a), to_bits(b), "bf16")
+    oracle.assert_parity(to_bits(y), y_bits, y32, "bf16")
+    dg, du = ext.silu_mul_backward(dy.cuda(), y[:, :n].contiguous(), y[:, n:].contiguous())
+    yk = to_bits(y)
+    ref = oracle.silu_mul_backward(to_bits(dy), yk[:, :n], yk[:, n:], "bf16")
+    oracle.assert_gradient(to_bits(dg), ref["grad_gate"], ref["grad_gate_fp32"], ref["grad_gate_scale"], "bf16")
+    oracle.assert_gradient(to_bits(du), ref["grad_up"], ref["grad_up_fp32"], ref["grad_up_scale"], "bf16")
+    dyy = torch.cat([dg, du], dim=1)
+    ga = ext.gemm_views(dyy, b.cuda().t(), None, 0)
+    gb = ext.gemm_views(a.cuda().t(), dyy, None, 0)
+    assert torch.equal(ga.view(torch.int16), ad.grad.view(torch.int16))
+    assert torch.equal(gb.view(torch.int16), bd.grad.view(torch.int16))
+    dyy_bits = to_bits(dyy)
+    ga_bits, ga32 = oracle.gemm(dyy_bits, np.ascontiguousarray(to_bits(b).T), "bf16")
+    gb_bits, gb32 = oracle.gemm(np.ascontiguousarray(to_bits(a).T), dyy_bits, "bf16")
+    oracle.assert_parity(to_bits(ga), ga_bits, ga32, "bf16")
+    oracle.assert_parity(to_bits(gb), gb_bits, gb32, "bf16")
 
 
 def test_nt_layout_inside_autograd_repro():
