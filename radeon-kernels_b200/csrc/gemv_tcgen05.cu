@@ -97,15 +97,6 @@ __device__ __forceinline__ bool try_wait_cluster(uint32_t bar, uint32_t parity) 
   return mbar_try_wait_cluster(bar, parity);
 }
 
-__device__ __forceinline__ float4 ld_cluster_v4(uint32_t cluster_addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(cluster_addr)
-               : "memory");
-  return v;
-}
-
 __device__ __forceinline__ void epilogue_bar_sync() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }

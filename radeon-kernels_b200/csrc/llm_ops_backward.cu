@@ -20,11 +20,15 @@
 // (grid-stride over rows) with dy and x of the row held in registers between the two
 // row sums (sum of squares, sum of dy*w*x) and the gradient stores.  The weight gradient
 // is a column sum over rows: each CTA accumulates its rows' dy * (x * r) in shared memory
-// (one fp32 slot per column, each owned by one thread, so no atomics), writes one fp32
-// partial row to the caller's workspace, and a second kernel adds the partial rows in CTA
-// order -- deterministic for a given shape and device.
+// (one fp32 slot per column, each owned by one thread, so no atomics); the CTAs of a
+// thread-block cluster of 8 then add their accumulators through distributed shared memory
+// (rank r sums column slice r over the 8 CTAs in rank order) and write one fp32 partial
+// row per cluster to the caller's workspace, and a second kernel adds the partial rows in
+// cluster order -- deterministic for a given shape and device.  (One partial row per CTA
+// made the second kernel the larger of the two: 24 us for 1184 partial rows of 4096.)
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include "rk_device.cuh"
@@ -35,6 +39,7 @@ namespace {
 
 constexpr int BWD_CACHE = 4;          // 16-byte vectors of dy and of x per thread in registers
 constexpr int MAX_DW_HIDDEN = 49152;  // shared-memory weight-gradient accumulators (192 KiB)
+constexpr int DW_CLUSTER = 8;         // CTAs whose accumulators are added before the write-out
 
 std::atomic<int> g_bwd_ctas_per_sm{0};  // tuning override of the row kernel's CTAs per SM
 
@@ -163,22 +168,33 @@ __device__ __forceinline__ uint32_t pass2_pair(uint32_t dy2, uint32_t x2, uint32
 // One CTA per row, grid-stride.  x is the normalised tensor's input (rms_norm) or
 // residual_out (add_rms_norm).  ADD: dres (nullable: no residual_out gradient) is added to
 // the rounded input gradient and the sum is stored to dx and, when non-null, dres_out.
-// DW: the CTA's weight-gradient partial row goes to dw_partial[blockIdx.x * hidden ...];
-// shared memory holds `hidden` fp32 accumulators, for 16-byte vectors laid out lane-major
-// (slot k * nv + v for column 8 v + k) so a warp's accesses are conflict-free.
+// DW (launched in clusters of DW_CLUSTER CTAs, grid a multiple of it): shared memory holds
+// `hidden` fp32 accumulators in column order; after the rows, the cluster's sum goes to
+// dw_partial[(blockIdx.x / DW_CLUSTER) * hidden ...].  Every thread reaches both cluster
+// barriers (no early exit), and the second keeps each CTA's shared memory alive until the
+// other CTAs of its cluster have read it.
 template <typename T, bool ADD, bool VEC, bool DW, int ROW_THREADS>
 __global__ void __launch_bounds__(ROW_THREADS)
     rms_norm_backward_kernel(const T* __restrict__ dy, const T* __restrict__ x,
                              const T* __restrict__ weight, const T* __restrict__ dres,
                              T* __restrict__ dx, T* __restrict__ dres_out,
                              float* __restrict__ dw_partial, int64_t rows, int hidden, float eps) {
-  extern __shared__ float sdw[];
+  extern __shared__ __align__(16) float sdw[];
   __shared__ float2 scratch[ROW_THREADS / 32];
+  const int nv = hidden / 8;
+  // Weight-gradient accumulators: registers for the register-cached vectors of a row
+  // (columns 8 v .. 8 v + 7 of vector v = threadIdx.x + k * ROW_THREADS), shared memory for
+  // the rest (longer rows, scalar path), which therefore starts at zero.
+  float dwreg[BWD_CACHE][8];
+#pragma unroll
+  for (int k = 0; k < BWD_CACHE; ++k)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwreg[k][j] = 0.f;
+  const int cached_cols = VEC ? 8 * BWD_CACHE * ROW_THREADS : 0;
   if (DW)
-    for (int i = threadIdx.x; i < hidden; i += ROW_THREADS) sdw[i] = 0.f;
+    for (int i = cached_cols + threadIdx.x; i < hidden; i += ROW_THREADS) sdw[i] = 0.f;
   pdl_begin();
   const float inv_h = 1.0f / static_cast<float>(hidden);
-  const int nv = hidden / 8;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const size_t base = static_cast<size_t>(row) * hidden;
     float sq = 0.f, c = 0.f;
@@ -220,26 +236,37 @@ __global__ void __launch_bounds__(ROW_THREADS)
       const uint4* e4 = ADD && dres != nullptr ? reinterpret_cast<const uint4*>(dres + base) : nullptr;
       uint4* o4 = reinterpret_cast<uint4*>(dx + base);
       uint4* ro4 = ADD && dres_out != nullptr ? reinterpret_cast<uint4*>(dres_out + base) : nullptr;
-      auto store = [&](int v, const uint4& d, const uint4& xv) {
+      auto store = [&](int v, const uint4& d, const uint4& xv, float* acc) {
         const uint4 w = __ldg(w4 + v);
         const bool has = e4 != nullptr;
         const uint4 e = has ? ld_stream_v4(e4 + v) : make_uint4(0u, 0u, 0u, 0u);
-        float* s = sdw + v;  // slot k * nv + v for column 8 v + k
         uint4 o;
-        o.x = pass2_pair<T, ADD, DW>(d.x, xv.x, w.x, e.x, has, r, q, s, s + nv);
-        o.y = pass2_pair<T, ADD, DW>(d.y, xv.y, w.y, e.y, has, r, q, s + 2 * nv, s + 3 * nv);
-        o.z = pass2_pair<T, ADD, DW>(d.z, xv.z, w.z, e.z, has, r, q, s + 4 * nv, s + 5 * nv);
-        o.w = pass2_pair<T, ADD, DW>(d.w, xv.w, w.w, e.w, has, r, q, s + 6 * nv, s + 7 * nv);
+        o.x = pass2_pair<T, ADD, DW>(d.x, xv.x, w.x, e.x, has, r, q, acc + 0, acc + 1);
+        o.y = pass2_pair<T, ADD, DW>(d.y, xv.y, w.y, e.y, has, r, q, acc + 2, acc + 3);
+        o.z = pass2_pair<T, ADD, DW>(d.z, xv.z, w.z, e.z, has, r, q, acc + 4, acc + 5);
+        o.w = pass2_pair<T, ADD, DW>(d.w, xv.w, w.w, e.w, has, r, q, acc + 6, acc + 7);
         o4[v] = o;
         if (ro4 != nullptr) ro4[v] = o;
       };
 #pragma unroll
       for (int k = 0; k < BWD_CACHE; ++k) {
         const int v = threadIdx.x + k * ROW_THREADS;
-        if (v < nv) store(v, dcache[k], xcache[k]);
+        if (v < nv) store(v, dcache[k], xcache[k], dwreg[k]);
       }
-      for (int v = threadIdx.x + BWD_CACHE * ROW_THREADS; v < nv; v += ROW_THREADS)
-        store(v, d4[v], x4[v]);
+      for (int v = threadIdx.x + BWD_CACHE * ROW_THREADS; v < nv; v += ROW_THREADS) {
+        float acc[8];
+        float4* s4 = reinterpret_cast<float4*>(sdw) + 2 * v;  // columns 8 v .. 8 v + 7
+        if (DW) {
+          const float4 lo = s4[0], hi = s4[1];
+          acc[0] = lo.x, acc[1] = lo.y, acc[2] = lo.z, acc[3] = lo.w;
+          acc[4] = hi.x, acc[5] = hi.y, acc[6] = hi.z, acc[7] = hi.w;
+        }
+        store(v, d4[v], x4[v], acc);
+        if (DW) {
+          s4[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+          s4[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        }
+      }
     } else {
       for (int i = threadIdx.x; i < hidden; i += ROW_THREADS) {
         const float d = to_f32(dy[base + i]), xv = to_f32(x[base + i]);
@@ -262,29 +289,68 @@ __global__ void __launch_bounds__(ROW_THREADS)
     }
   }
   if (DW) {
-    __syncthreads();
-    float* part = dw_partial + static_cast<size_t>(blockIdx.x) * hidden;
-    for (int i = threadIdx.x; i < hidden; i += ROW_THREADS)
-      part[i] = VEC ? sdw[(i & 7) * nv + (i >> 3)] : sdw[i];
+    if (VEC) {
+#pragma unroll
+      for (int k = 0; k < BWD_CACHE; ++k) {
+        const int v = threadIdx.x + k * ROW_THREADS;
+        if (v < nv) {
+          float4* s4 = reinterpret_cast<float4*>(sdw) + 2 * v;
+          s4[0] = make_float4(dwreg[k][0], dwreg[k][1], dwreg[k][2], dwreg[k][3]);
+          s4[1] = make_float4(dwreg[k][4], dwreg[k][5], dwreg[k][6], dwreg[k][7]);
+        }
+      }
+    }
+    cluster_sync_all();  // every CTA of the cluster has finished accumulating
+    const uint32_t rank = cluster_ctarank();
+    float* part = dw_partial + static_cast<size_t>(blockIdx.x / DW_CLUSTER) * hidden;
+    const uint32_t base = smem_u32(sdw);
+    if (VEC) {
+      // hidden % 8 == 0: float4 slices, rank r takes float4 columns [r * per, (r + 1) * per).
+      const int n4 = hidden / 4;
+      const int per = (n4 + DW_CLUSTER - 1) / DW_CLUSTER;
+      const int end = min(n4, static_cast<int>(rank + 1) * per);
+      for (int i = static_cast<int>(rank) * per + threadIdx.x; i < end; i += ROW_THREADS) {
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < DW_CLUSTER; ++q) {
+          const float4 v = ld_cluster_v4(map_to_rank(base + 16u * i, q));
+          t.x += v.x, t.y += v.y, t.z += v.z, t.w += v.w;
+        }
+        reinterpret_cast<float4*>(part)[i] = t;
+      }
+    } else {
+      const int per = (hidden + DW_CLUSTER - 1) / DW_CLUSTER;
+      const int end = min(hidden, static_cast<int>(rank + 1) * per);
+      for (int i = static_cast<int>(rank) * per + threadIdx.x; i < end; i += ROW_THREADS) {
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < DW_CLUSTER; ++q) t += ld_cluster_f32(map_to_rank(base + 4u * i, q));
+        part[i] = t;
+      }
+    }
+    cluster_sync_all();  // peers are done reading this CTA's accumulators
   }
 }
 
-// dw[col] = sum over the partial rows in CTA order, rounded once.  32 columns x 8 groups
-// per CTA: group g adds a fixed contiguous range of partial rows, then the group sums are
+// dw[col] = sum over the partial rows in cluster order, rounded once.  32 columns x
+// REDUCE_GROUPS groups per CTA: group g adds a fixed contiguous range of partial rows
+// (all its loads independent, so they are in flight together), then the group sums are
 // added in group order.
+constexpr int REDUCE_GROUPS = 32;
+
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32 * REDUCE_GROUPS)
     weight_grad_reduce_kernel(const float* __restrict__ partial, int parts, int hidden,
                               T* __restrict__ dw) {
-  __shared__ float acc[8][33];
+  __shared__ float acc[REDUCE_GROUPS][33];
   const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
   pdl_begin();
-  const int per = (parts + 7) / 8;
+  const int per = (parts + REDUCE_GROUPS - 1) / REDUCE_GROUPS;
   float s = 0.f;
   if (col < hidden) {
     const int p0 = grp * per, p1 = min(parts, p0 + per);
-#pragma unroll 4
+#pragma unroll 8
     for (int p = p0; p < p1; ++p) s += partial[static_cast<size_t>(p) * hidden + col];
   }
   acc[grp][lane] = s;
@@ -292,7 +358,7 @@ __global__ void __launch_bounds__(256)
   if (grp == 0 && col < hidden) {
     float t = 0.f;
 #pragma unroll
-    for (int g = 0; g < 8; ++g) t += acc[g][lane];
+    for (int g = 0; g < REDUCE_GROUPS; ++g) t += acc[g][lane];
     dw[col] = from_f32<T>(t);
   }
 }
@@ -328,13 +394,26 @@ int bwd_threads(int64_t rows, int64_t hidden) {
   return threads;
 }
 
-// CTAs of the row kernel: with a weight gradient every CTA writes a partial row, so the
-// grid is held to 1024 threads per SM; without, up to 2048 threads per SM.
+// CTAs of the row kernel: up to 2048 threads per SM, one row each, more rows walked
+// grid-stride.  With a weight gradient the grid is a multiple of the cluster size (CTAs
+// past the last row only add zeros).
 int bwd_grid(int64_t rows, int threads, bool dw) {
+  const int sms = device_sm_count();
   int per_sm = g_bwd_ctas_per_sm.load();
-  if (per_sm <= 0) per_sm = (dw ? 1024 : 2048) / threads;
-  const int64_t cap = static_cast<int64_t>(device_sm_count()) * per_sm;
-  return static_cast<int>(rows < cap ? rows : cap);
+  if (per_sm <= 0) per_sm = 2048 / threads;
+  const int64_t cap = static_cast<int64_t>(sms) * per_sm;
+  int64_t grid = rows < cap ? rows : cap;
+  if (dw) {
+    // About four rows per CTA once there are enough rows for every SM: the cluster
+    // sum and the partial-row write are paid once per CTA.
+    if (g_bwd_ctas_per_sm.load() <= 0) {
+      const int64_t quarter = (rows + 3) / 4;
+      const int64_t floor_rows = rows < sms ? rows : sms;
+      grid = std::min(grid, std::max(quarter, floor_rows));
+    }
+    grid = (grid + DW_CLUSTER - 1) / DW_CLUSTER * DW_CLUSTER;
+  }
+  return static_cast<int>(grid);
 }
 
 template <typename T, bool ADD, bool DW, int THREADS>
@@ -349,7 +428,8 @@ cudaError_t launch_bwd_rows(bool vec, int grid, const void* dy, const void* x, c
                                                static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  return launch_kernel(kernel, dim3(grid), dim3(THREADS), smem, s, 0, static_cast<const T*>(dy),
+  return launch_kernel(kernel, dim3(grid), dim3(THREADS), smem, s, DW ? DW_CLUSTER : 0,
+                       static_cast<const T*>(dy),
                        static_cast<const T*>(x), static_cast<const T*>(w),
                        static_cast<const T*>(dres), static_cast<T*>(dx), static_cast<T*>(dres_out),
                        partial, rows, static_cast<int>(hidden), eps);
@@ -381,10 +461,11 @@ rk_status rms_norm_backward_typed(const void* dy, const void* x, const void* w, 
   const int threads = bwd_threads(rows, hidden);
   const int grid = bwd_grid(rows, threads, want_dw);
   float* partial = static_cast<float*>(workspace);
+  const int parts = grid / DW_CLUSTER;
   if (want_dw) {
     if (hidden > MAX_DW_HIDDEN) return RK_ERR_UNSUPPORTED;
     if (workspace == nullptr ||
-        workspace_bytes < static_cast<size_t>(grid) * static_cast<size_t>(hidden) * sizeof(float) ||
+        workspace_bytes < static_cast<size_t>(parts) * static_cast<size_t>(hidden) * sizeof(float) ||
         !aligned16(workspace))
       return RK_ERR_INVALID_ARGUMENT;
   }
@@ -395,7 +476,7 @@ rk_status rms_norm_backward_typed(const void* dy, const void* x, const void* w, 
   note_launch();
   if (e != cudaSuccess || !want_dw) return cuda_status(e);
   e = launch_kernel(weight_grad_reduce_kernel<T>, dim3(static_cast<unsigned>((hidden + 31) / 32)),
-                    dim3(256), 0, s, 0, static_cast<const float*>(partial), grid,
+                    dim3(32 * REDUCE_GROUPS), 0, s, 0, static_cast<const float*>(partial), parts,
                     static_cast<int>(hidden), static_cast<T*>(dw));
   note_launch();
   return cuda_status(e);
@@ -408,7 +489,7 @@ void norm_backward_set_ctas_per_sm(int ctas) { g_bwd_ctas_per_sm.store(ctas); }
 size_t rms_norm_backward_workspace_bytes(int64_t tokens, int64_t hidden) {
   if (tokens <= 0 || hidden <= 0) return 0;
   const int grid = bwd_grid(tokens, bwd_threads(tokens, hidden), true);
-  return static_cast<size_t>(grid) * static_cast<size_t>(hidden) * sizeof(float);
+  return static_cast<size_t>(grid / DW_CLUSTER) * static_cast<size_t>(hidden) * sizeof(float);
 }
 
 rk_status silu_mul_backward_launch(const void* dy, const void* gate, const void* up, void* dgate,
