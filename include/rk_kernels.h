@@ -318,6 +318,25 @@ RK_API rk_status rk_add_rms_norm_backward(const void* grad_out, const void* grad
                                           float eps, rk_dtype dt, void* workspace,
                                           size_t workspace_bytes, rk_stream_t stream);
 
+/*
+ * Scaled dot-product self-attention (prefill), inference only: for every batch b, query
+ * head h and query position q,
+ *   out[b,h,q,:] = sum_k softmax_k(scale * Q[b,h,q,:] . K[b,g,k,:]) V[b,g,k,:],
+ * g = h / (query_heads / kv_heads), keys k < sequence (and k <= q when is_causal), fp32
+ * softmax and accumulation, output rounded once.  query/out: [batch, query_heads,
+ * sequence, head_dim], key/value: [batch, kv_heads, sequence, head_dim], contiguous, 16-byte
+ * aligned, of dtype `dt`; head_dim 64, 128 or 256; query_heads % kv_heads == 0; scale > 0
+ * and finite.  Replaces the reference's rk.sdpa (src/radeon_kernels/ops/sdpa/api.py:102-118),
+ * which runs torch's scaled_dot_product_attention (ops/sdpa/reference.py:39-57; its manifest,
+ * dispatch/sdpa-1.0.json, has no native entry).  tcgen05 flash attention: one CTA per
+ * 128-row query tile and head, S = Q K^T and O += P V on the tensor cores, P rounded to the
+ * dtype between them.
+ */
+RK_API rk_status rk_sdpa(const void* query, const void* key, const void* value, void* out,
+                         int64_t batch, int64_t query_heads, int64_t kv_heads,
+                         int64_t sequence, int64_t head_dim, int is_causal, float scale,
+                         rk_dtype dt, rk_stream_t stream);
+
 /* Static description of a status code; never NULL. */
 RK_API const char* rk_status_string(rk_status status);
 

@@ -83,3 +83,21 @@ def paged_attention_decode_reference(
     scores = scores.masked_fill(~valid.unsqueeze(1), float("-inf"))
     probabilities = torch_module.softmax(scores, dim=-1, dtype=torch_module.float32)
     return torch_module.einsum("bht,bthd->bhd", probabilities, values).to(dtype=query.dtype)
+
+
+def sdpa_reference(torch_module: Any, query: Any, key: Any, value: Any, is_causal: bool, scale: float) -> Any:
+    """The reference's fp32 self-attention definition (ops/sdpa/reference.py:13-36): K and V
+    repeated to the query heads, fp32 scores times scale, causal mask from tril, fp32
+    softmax, probabilities times V, cast to the query dtype."""
+
+    group = int(query.shape[1]) // int(key.shape[1])
+    keys = key.repeat_interleave(group, dim=1).float() if group > 1 else key.float()
+    values = value.repeat_interleave(group, dim=1).float() if group > 1 else value.float()
+    scores = torch_module.matmul(query.float(), keys.transpose(-2, -1)) * scale
+    if is_causal:
+        seq = int(query.shape[2])
+        keep = torch_module.ones((seq, seq), device=query.device, dtype=torch_module.bool).tril()
+        scores = scores.masked_fill(~keep, float("-inf"))
+    probabilities = torch_module.softmax(scores, dim=-1, dtype=torch_module.float32)
+    return torch_module.matmul(probabilities, values).to(dtype=query.dtype)
+

@@ -384,6 +384,20 @@ rk_status rk_add_rms_norm_backward(const void* grad_out, const void* grad_residu
                                   reinterpret_cast<cudaStream_t>(stream));
 }
 
+rk_status rk_sdpa(const void* query, const void* key, const void* value, void* out, int64_t batch,
+                  int64_t query_heads, int64_t kv_heads, int64_t sequence, int64_t head_dim,
+                  int is_causal, float scale, rk_dtype dt, rk_stream_t stream) {
+  if (!valid_dtype(dt) || batch < 1 || query_heads < 1 || kv_heads < 1 || sequence < 1 ||
+      query_heads % kv_heads != 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256) ||
+      !(scale > 0.0f && scale <= 3.4e38f))
+    return RK_ERR_INVALID_ARGUMENT;
+  if (query == nullptr || key == nullptr || value == nullptr || out == nullptr)
+    return RK_ERR_INVALID_ARGUMENT;
+  if (current_device_info() == nullptr) return RK_ERR_NO_DEVICE;
+  return sdpa_launch(query, key, value, out, batch, query_heads, kv_heads, sequence, head_dim,
+                     is_causal != 0, scale, dt, reinterpret_cast<cudaStream_t>(stream));
+}
+
 void rk_norm_backward_set_ctas_per_sm(int ctas_per_sm) {
   norm_backward_set_ctas_per_sm(ctas_per_sm >= 1 && ctas_per_sm <= 32 ? ctas_per_sm : 0);
 }

@@ -126,6 +126,10 @@ rk_status rms_norm_backward_launch(const void* dy, const void* x, const void* w,
                                    void* workspace, size_t workspace_bytes, cudaStream_t s);
 size_t rms_norm_backward_workspace_bytes(int64_t tokens, int64_t hidden);
 void norm_backward_set_ctas_per_sm(int ctas);
+// Prefill attention (sdpa_tcgen05.cu).
+rk_status sdpa_launch(const void* q, const void* k, const void* v, void* out, int64_t B,
+                      int64_t Hq, int64_t Hkv, int64_t S, int64_t D, bool causal, float scale,
+                      rk_dtype dt, cudaStream_t s);
 
 rk_status gather_column_blocks_launch(const void* blocks, void* out, int64_t G, int64_t M,
                                       int64_t N, rk_dtype dt, cudaStream_t s);

@@ -58,6 +58,33 @@ inline rk_status encode_tmap_2d(CUtensorMap* map, const void* base, rk_dtype dt,
   return RK_ERR_UNSUPPORTED;
 }
 
+// Tensor map over a stack of `depth` row-major [rows, inner] matrices of 16-bit elements
+// (dense: matrix i starts rows * inner elements after matrix i - 1), read in boxes of
+// [1, box_rows, box_inner] with the 128-byte swizzle.  Rows past the end of a matrix read
+// as zero (no spill into the next matrix).
+inline rk_status encode_tmap_3d(CUtensorMap* map, const void* base, rk_dtype dt, int64_t inner,
+                                int64_t rows, int64_t depth, uint32_t box_inner,
+                                uint32_t box_rows) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (fn == nullptr) return RK_ERR_CUDA;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(depth)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(inner) * 2,
+                                 static_cast<cuuint64_t>(inner) * static_cast<cuuint64_t>(rows) * 2};
+  const cuuint32_t box[3] = {box_inner, box_rows, 1};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  const CUtensorMapDataType t =
+      dt == RK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUresult r = fn(map, t, 3, const_cast<void*>(base), dims, strides, box, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) return RK_OK;
+  note_error("cuTensorMapEncodeTiled failed (CUresult " + std::to_string(static_cast<int>(r)) +
+             ") for a [" + std::to_string(depth) + ", " + std::to_string(rows) + ", " +
+             std::to_string(inner) + "] stack");
+  return RK_ERR_UNSUPPORTED;
+}
+
 // Encoding a tensor map costs about a microsecond of host time per call; decode loops
 // call the same GEMV on the same weight and activation buffers every step, so recently
 // encoded maps are kept in a small process-wide cache keyed by every encoded field.

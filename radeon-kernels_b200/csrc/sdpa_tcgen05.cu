@@ -1,0 +1,453 @@
+// sdpa_tcgen05.cu -- scaled dot-product self-attention (prefill) on the tcgen05 tensor cores.
+//
+//   out[b, h, q, :] = softmax_k(scale * Q[b,h,q,:] . K[b,g(h),k,:], causal mask) @ V[b,g(h)]
+//
+// Semantics of the reference's operator (src/radeon_kernels/ops/sdpa/api.py:22-118,
+// reference.py:13-36): [batch, heads, sequence, head_dim] tensors, equal query and key
+// lengths, GQA head g(h) = h / (Hq / Hkv), optional causal mask (key <= query), fp32 softmax
+// and accumulation, output rounded once to the input dtype.  The reference computes it
+// with torch's SDPA (its dispatch manifest has no native entry, dispatch/sdpa-1.0.json); its
+// HIP candidate walks keys one at a time per query row (benchmarks/sdpa/native_sdpa.hip).
+//
+// One CTA per (128-row query tile, query head, batch), 128 threads (4 warps), flash-style:
+//   * thread 0 issues the TMA loads -- the Q tile once, K and V tiles of 128 keys in a ring
+//     of STAGES buffers, through 3-D tensor maps over the [batch*heads, S, D] stacks, so rows
+//     past the sequence read as zero instead of the next head's -- and the MMAs;
+//   * S = Q K^T (M = 128, N = 128 keys, K = head_dim) into TMEM columns [0, 128): Q and K
+//     are K-major 128-byte-swizzled tiles straight from TMA;
+//   * each thread owns one query row (TMEM lane): it reads its 128 scores, applies the
+//     scale (in base 2) and the masks, updates the running max and sum in fp32 (online
+//     softmax), rescales its row of O in TMEM when the max moved (warp-uniform), and writes
+//     P = exp2(s - m) rounded to the dtype into shared memory in the K-major swizzled
+//     layout the next MMA reads;
+//   * O += P V (M = 128, N = head_dim, K = 128 keys) into TMEM columns [128, 128 + D): V is
+//     an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
+//   * epilogue: O / l rounded to the dtype, one 64-byte row segment per store.
+// The sum l adds the rounded P values the MMA uses.  Every wait is bounded (status word on
+// expiry) and made CTA-uniform; before TMEM is released every MMA and bulk copy this CTA
+// issued has completed.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <mutex>
+#include <type_traits>
+
+#include "rk_device.cuh"
+#include "rk_internal.h"
+#include "rk_tma.h"
+
+namespace rk {
+namespace sdpa {
+
+constexpr int BM = 128;  // query rows per CTA
+constexpr int BN = 128;  // keys per tile
+constexpr int THREADS = 128;
+constexpr int UMMA_K = 16;
+
+template <int D>
+struct Cfg {
+  static constexpr int CHUNKS = D / 64;              // 64-element (128-byte) column chunks
+  static constexpr int Q_BYTES = CHUNKS * BM * 128;  // Q tile: CHUNKS x [128 rows x 128 B]
+  static constexpr int K_BYTES = CHUNKS * BN * 128;  // K tile: same layout, 128 keys
+  static constexpr int V_BYTES = BN * D * 2;         // V tile: [2 key blocks][CHUNKS][64 x 128 B]
+  static constexpr int P_BYTES = BM * BN * 2;        // P: 2 key chunks x [128 rows x 128 B]
+  static constexpr int STAGES = D == 256 ? 1 : 2;    // 227 KB of shared memory per CTA
+  static constexpr int TMEM_COLS = D == 64 ? 256 : (D == 128 ? 256 : 512);  // S + O
+  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES) + P_BYTES + 256;
+  static_assert(D == 64 || D == 128 || D == 256, "head_dim");
+};
+
+struct __align__(8) Bars {
+  uint64_t q_full;
+  uint64_t k_full[2];
+  uint64_t v_full[2];
+  uint64_t s_done;
+  uint64_t o_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+};
+
+struct Params {
+  int seq;          // S (query and key length)
+  int hq, hkv;      // heads
+  int group;        // hq / hkv
+  int q_tiles;      // ceil(S / BM)
+  int causal;
+  float scale_log2;  // scale * log2(e)
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(THREADS, 1)
+    sdpa_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                const __grid_constant__ CUtensorMap tmap_v, T* __restrict__ out, Params p,
+                KernelCtl ctl) {
+  using C = Cfg<D>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* sk = sq + C::Q_BYTES;
+  uint8_t* sv = sk + STAGES * C::K_BYTES;
+  uint8_t* sp = sv + STAGES * C::V_BYTES;
+  Bars* bars = reinterpret_cast<Bars*>(sp + C::P_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  // Heavier (later, under the causal mask) query tiles first.
+  const int qtile = p.q_tiles - 1 - static_cast<int>(blockIdx.x);
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const int kv_head = head / p.group;
+  const int q_mat = batch * p.hq + head;      // matrix index in the [B*Hq, S, D] stack
+  const int kv_mat = batch * p.hkv + kv_head;  // and in the [B*Hkv, S, D] stacks
+  const int k_tiles_all = (p.seq + BN - 1) / BN;
+  const int n_tiles = p.causal ? min(k_tiles_all, qtile + 1) : k_tiles_all;
+  const int row = threadIdx.x;  // TMEM lane and query row within the tile
+  const int q_pos = qtile * BM + row;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars->q_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars->k_full[s]), 1);
+      mbar_init(smem_u32(&bars->v_full[s]), 1);
+    }
+    mbar_init(smem_u32(&bars->s_done), 1);
+    mbar_init(smem_u32(&bars->o_done), 1);
+    mbar_init(smem_u32(&bars->drain), 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&bars->tmem_base), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);  // this warp's lanes
+  const uint32_t t_s = t_lane;        // S: columns [0, 128)
+  const uint32_t t_o = t_lane + 128;  // O: columns [128, 128 + D)
+  pdl_begin();  // global memory is touched only after this
+
+  // Bulk-copy bookkeeping (thread 0): loads issued into each stage, and those waited for.
+  uint32_t k_issued[2] = {0, 0}, v_issued[2] = {0, 0}, k_used[2] = {0, 0}, v_used[2] = {0, 0};
+  bool q_issued = false, q_used = false;
+  auto load_k = [&](int t) {
+    const int st = t % STAGES;
+    const uint32_t bar = smem_u32(&bars->k_full[st]);
+    mbar_arrive_expect_tx(bar, C::K_BYTES);
+#pragma unroll
+    for (int c = 0; c < C::CHUNKS; ++c)
+      tma_load_3d(smem_u32(sk + st * C::K_BYTES + c * BN * 128), &tmap_k, bar, c * 64, t * BN,
+                  kv_mat);
+    ++k_issued[st];
+  };
+  auto load_v = [&](int t) {
+    const int st = t % STAGES;
+    const uint32_t bar = smem_u32(&bars->v_full[st]);
+    mbar_arrive_expect_tx(bar, C::V_BYTES);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+      for (int c = 0; c < C::CHUNKS; ++c)
+        tma_load_3d(smem_u32(sv + st * C::V_BYTES + (kb * C::CHUNKS + c) * 8192), &tmap_v, bar,
+                    c * 64, t * BN + kb * 64, kv_mat);
+    ++v_issued[st];
+  };
+  if (threadIdx.x == 0) {
+    const uint32_t bar = smem_u32(&bars->q_full);
+    mbar_arrive_expect_tx(bar, C::Q_BYTES);
+#pragma unroll
+    for (int c = 0; c < C::CHUNKS; ++c)
+      tma_load_3d(smem_u32(sq + c * BM * 128), &tmap_q, bar, c * 64, qtile * BM, q_mat);
+    q_issued = true;
+    for (int t = 0; t < STAGES && t < n_tiles; ++t) {
+      load_k(t);
+      load_v(t);
+    }
+  }
+
+  constexpr uint32_t IDESC_S =
+      umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, BN, false, false);
+  constexpr uint32_t IDESC_O =
+      umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, D, false, true);
+  int never = 0;
+  bool ok = true;
+  float m_run = -INFINITY, l_run = 0.f;
+  int issued_mma = 0;  // thread 0: tcgen05.commit groups issued
+
+  for (int j = 0; j < n_tiles && ok; ++j) {
+    const int st = j % STAGES;
+    // ---- S = Q K_j^T (thread 0)
+    if (threadIdx.x == 0) {
+      bool got = true;
+      if (j == 0) got = q_used = mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, &never);
+      got = got && mbar_wait_bounded(smem_u32(&bars->k_full[st]), k_used[st] & 1u, ctl.timeout_ns,
+                                     &never);
+      if (got) {
+        ++k_used[st];
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(sq), k0 = smem_u32(sk + st * C::K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / UMMA_K; ++kk) {
+          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          tc_mma_f16(tmem, umma_desc_sw128(q0 + off, 16, 1024), umma_desc_sw128(k0 + off, 16, 1024),
+                     IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&bars->s_done));
+        ++issued_mma;
+      } else {
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_PRODUCER);
+      }
+      ok = got;
+    }
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    // ---- scores of this thread's row
+    bool got = mbar_wait_bounded(smem_u32(&bars->s_done), j & 1, ctl.timeout_ns, &never);
+    ok = __syncthreads_and(got);
+    if (!ok) {
+      if (threadIdx.x == 0) atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_MMA);
+      break;
+    }
+    tc_fence_after();
+    // K_j is no longer needed: refill its stage with K_{j+STAGES}.
+    if (threadIdx.x == 0 && j + STAGES < n_tiles) load_k(j + STAGES);
+    const int key0 = j * BN;
+    const bool diag = p.causal && key0 + BN > qtile * BM;  // some keys lie above this row's
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_s + c * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int key = key0 + c * 32 + i;
+        const bool masked = key >= p.seq || (diag && key > q_pos);
+        const float s = masked ? -INFINITY : __uint_as_float(r[i]) * p.scale_log2;
+        mx = fmaxf(mx, s);
+      }
+    }
+    const float m_new = fmaxf(m_run, mx);
+    const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a row with no key yet
+    const float alpha = exp2f(m_run - m_use);
+
+    // ---- P V_{j-1} must be done: P is overwritten and O rescaled below.
+    if (j > 0) {
+      got = mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, &never);
+      ok = __syncthreads_and(got);
+      if (!ok) {
+        if (threadIdx.x == 0) atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_MMA);
+        break;
+      }
+      tc_fence_after();
+      if (threadIdx.x == 0 && j - 1 + STAGES < n_tiles) load_v(j - 1 + STAGES);
+      // Rescale this warp's rows of O when any of their maxima moved.
+      if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_o + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32x32b_x32(t_o + c * 32, r);
+        }
+        tmem_st_wait();
+      }
+    }
+
+    // ---- P = exp2(s - m), rounded, into the K-major swizzled operand tile
+    float psum = 0.f;
+    uint8_t* prow = sp + row * 128;
+#pragma unroll
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_s + c * 32, r);
+      tmem_ld_wait();
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        float e[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int key = key0 + c * 32 + i + h;
+          const bool masked = key >= p.seq || (diag && key > q_pos);
+          e[h] = masked ? 0.f : exp2f(__uint_as_float(r[i + h]) * p.scale_log2 - m_use);
+        }
+        packed[i / 2] = Pack2<T>::from_floats(e[0], e[1]);
+        const float2 back = Pack2<T>::to_floats(packed[i / 2]);
+        psum += back.x + back.y;
+      }
+      // Keys c*32 .. c*32+31 = chunk c/2, 16-byte units (c%2)*4 .. +3, swizzled by row.
+      uint8_t* chunk = prow + (c >> 1) * (BM * 128);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int unit = (c & 1) * 4 + u;
+        *reinterpret_cast<uint4*>(chunk + ((unit ^ (row & 7)) << 4)) =
+            make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+      }
+    }
+    l_run = l_run * alpha + psum;
+    m_run = m_new;
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    // ---- O += P V_j (thread 0)
+    if (threadIdx.x == 0) {
+      tc_fence_after();
+      got = mbar_wait_bounded(smem_u32(&bars->v_full[st]), v_used[st] & 1u, ctl.timeout_ns, &never);
+      if (got) {
+        ++v_used[st];
+        const uint32_t p0 = smem_u32(sp), v0 = smem_u32(sv + st * C::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / UMMA_K; ++kk) {
+          const uint64_t a = umma_desc_sw128(p0 + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t b =
+              umma_desc_sw128(v0 + (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048, 8192, 1024);
+          tc_mma_f16(tmem + 128, a, b, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&bars->o_done));
+        ++issued_mma;
+      } else {
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_PRODUCER);
+      }
+      ok = got;
+    }
+    ok = __syncthreads_and(ok);
+  }
+
+  // ---- epilogue: O / l
+  if (ok && n_tiles > 0) {
+    const bool got =
+        mbar_wait_bounded(smem_u32(&bars->o_done), (n_tiles - 1) & 1, ctl.timeout_ns, &never);
+    ok = __syncthreads_and(got);
+    if (ok) {
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      T* orow = out + (static_cast<size_t>(q_mat) * p.seq + q_pos) * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_o + c * 32, r);
+        tmem_ld_wait();
+        if (q_pos < p.seq) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 v;
+            v.x = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 0]) * inv, __uint_as_float(r[8 * q + 1]) * inv);
+            v.y = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv);
+            v.z = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv);
+            v.w = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * q) = v;
+          }
+        }
+      }
+    } else if (threadIdx.x == 0) {
+      atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_EPILOGUE);
+    }
+  }
+
+  // ---- drain: every MMA and bulk copy issued by this CTA completes before exit.
+  if (threadIdx.x == 0) {
+    if (issued_mma > 0) {
+      tc_commit(smem_u32(&bars->drain));
+      if (!mbar_wait_bounded(smem_u32(&bars->drain), 0, ctl.timeout_ns, &never))
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    }
+    if (q_issued && !q_used &&
+        !mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, &never))
+      atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    for (int s = 0; s < STAGES; ++s) {
+      // Loads issued but never waited for: wait for the last one of each stage.
+      if (k_issued[s] > k_used[s] &&
+          !mbar_wait_bounded(smem_u32(&bars->k_full[s]), (k_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+      if (v_issued[s] > v_used[s] &&
+          !mbar_wait_bounded(smem_u32(&bars->v_full[s]), (v_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace sdpa
+
+namespace {
+template <typename T, int D>
+rk_status launch_sdpa(const void* q, const void* k, const void* v, void* out, int64_t B,
+                      int64_t Hq, int64_t Hkv, int64_t S, bool causal, float scale, rk_dtype dt,
+                      cudaStream_t s) {
+  using C = sdpa::Cfg<D>;
+  CUtensorMap tq, tk, tv;
+  rk_status st = encode_tmap_3d(&tq, q, dt, D, S, B * Hq, 64, sdpa::BM);
+  if (st != RK_OK) return st;
+  if ((st = encode_tmap_3d(&tk, k, dt, D, S, B * Hkv, 64, sdpa::BN)) != RK_OK) return st;
+  if ((st = encode_tmap_3d(&tv, v, dt, D, S, B * Hkv, 64, 64)) != RK_OK) return st;
+  LaunchCtl lc;
+  if ((st = launch_ctl(&lc)) != RK_OK) return st;
+  KernelCtl ctl{lc.status, lc.timeout_ns, 0};
+
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(sdpa::sdpa_kernel<T, D>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
+
+  sdpa::Params p;
+  p.seq = static_cast<int>(S);
+  p.hq = static_cast<int>(Hq);
+  p.hkv = static_cast<int>(Hkv);
+  p.group = static_cast<int>(Hq / Hkv);
+  p.q_tiles = static_cast<int>((S + sdpa::BM - 1) / sdpa::BM);
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = static_cast<float>(static_cast<double>(scale) * 1.4426950408889634);
+  const dim3 grid(static_cast<unsigned>(p.q_tiles), static_cast<unsigned>(Hq),
+                  static_cast<unsigned>(B));
+  const cudaError_t e = launch_kernel(sdpa::sdpa_kernel<T, D>, grid, dim3(sdpa::THREADS), C::SMEM, s,
+                                      0, tq, tk, tv, static_cast<T*>(out), p, ctl);
+  note_launch();
+  return cuda_status(e);
+}
+
+template <typename T>
+rk_status launch_sdpa_d(const void* q, const void* k, const void* v, void* out, int64_t B,
+                        int64_t Hq, int64_t Hkv, int64_t S, int64_t D, bool causal, float scale,
+                        rk_dtype dt, cudaStream_t s) {
+  switch (D) {
+    case 64: return launch_sdpa<T, 64>(q, k, v, out, B, Hq, Hkv, S, causal, scale, dt, s);
+    case 128: return launch_sdpa<T, 128>(q, k, v, out, B, Hq, Hkv, S, causal, scale, dt, s);
+    case 256: return launch_sdpa<T, 256>(q, k, v, out, B, Hq, Hkv, S, causal, scale, dt, s);
+  }
+  return RK_ERR_UNSUPPORTED;
+}
+}  // namespace
+
+rk_status sdpa_launch(const void* q, const void* k, const void* v, void* out, int64_t B,
+                      int64_t Hq, int64_t Hkv, int64_t S, int64_t D, bool causal, float scale,
+                      rk_dtype dt, cudaStream_t s) {
+  if (device_cc_major() != 10) return RK_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return RK_ERR_UNSUPPORTED;
+  // TMA coordinates and the kernel's matrix and row indices are 32-bit.
+  if (S + sdpa::BM > (1ll << 31) || B * Hq > (1ll << 31)) return RK_ERR_UNSUPPORTED;
+  if (Hq > 65535 || B > 65535) return RK_ERR_UNSUPPORTED;
+  if (dt == RK_DTYPE_BF16)
+    return launch_sdpa_d<__nv_bfloat16>(q, k, v, out, B, Hq, Hkv, S, D, causal, scale, dt, s);
+  return launch_sdpa_d<__half>(q, k, v, out, B, Hq, Hkv, S, D, causal, scale, dt, s);
+}
+
+}  // namespace rk

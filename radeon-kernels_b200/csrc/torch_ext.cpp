@@ -318,6 +318,30 @@ std::vector<at::Tensor> add_rms_norm(const at::Tensor& input, const at::Tensor& 
   return {out, residual_out};
 }
 
+// Prefill attention (rk_sdpa): query [B, Hq, S, D], key/value [B, Hkv, S, D].
+at::Tensor sdpa(const at::Tensor& query, const at::Tensor& key, const at::Tensor& value,
+                bool is_causal, double scale) {
+  check_rows(query, "query", 4);
+  check_rows(key, "key", 4);
+  check_rows(value, "value", 4);
+  TORCH_CHECK(query.device() == key.device() && key.device() == value.device(),
+              "query, key and value must share a device");
+  TORCH_CHECK(query.scalar_type() == key.scalar_type() && key.scalar_type() == value.scalar_type(),
+              "query, key and value must share a dtype");
+  TORCH_CHECK(key.sizes() == value.sizes(), "key and value must have the same shape");
+  TORCH_CHECK(query.size(0) == key.size(0) && query.size(2) == key.size(2) &&
+                  query.size(3) == key.size(3),
+              "query and key must share batch, sequence and head_dim");
+  c10::cuda::CUDAGuard guard(query.device());
+  auto out = at::empty_like(query);
+  check_status(rk_sdpa(query.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(),
+                       query.size(0), query.size(1), key.size(1), query.size(2), query.size(3),
+                       is_causal ? 1 : 0, static_cast<float>(scale), dtype_of(query, "query"),
+                       current_stream(query)),
+               "rk_sdpa");
+  return out;
+}
+
 // ------------------------------------------------------------------ backward passes
 std::vector<at::Tensor> silu_mul_backward(const at::Tensor& grad, const at::Tensor& gate,
                                           const at::Tensor& up) {
@@ -455,6 +479,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("eps"));
   m.def("add_rms_norm", &add_rms_norm, "residual add + row RMS normalisation -> [out, residual_out]",
         py::arg("input"), py::arg("residual"), py::arg("weight"), py::arg("eps"));
+  m.def("sdpa", &sdpa, "scaled dot-product self-attention (prefill)", py::arg("query"),
+        py::arg("key"), py::arg("value"), py::arg("is_causal"), py::arg("scale"));
   m.def("silu_mul_backward", &silu_mul_backward, "gradients of silu(gate) * up -> [grad_gate, grad_up]",
         py::arg("grad"), py::arg("gate"), py::arg("up"));
   m.def("rms_norm_backward", &rms_norm_backward, "rms_norm gradients -> [grad_input, grad_weight]",

@@ -26,6 +26,7 @@ SELECTED_RMS_NORM = "cuda/rms_norm"
 SELECTED_ADD_RMS_NORM = "cuda/add_rms_norm"
 SELECTED_GEMM_SWIGLU = "cuda/gemm_swiglu"
 SELECTED_PAGED_ATTENTION = "cuda/paged_attention_decode"
+SELECTED_SDPA = "cuda/sdpa"
 
 
 def _contiguous(tensor: Any) -> Any:
@@ -272,3 +273,9 @@ def paged_attention_decode(
     """rk_paged_attention_decode (inference only; the front-end rejects autograd inputs)."""
 
     return _native.extension().paged_attention_decode(query, key_cache, value_cache, block_tables, context_lengths, scale)
+
+
+def sdpa(torch_module: Any, query: Any, key: Any, value: Any, is_causal: bool, scale: float) -> Any:
+    """rk_sdpa (inference only; the front-end rejects autograd and non-contiguous inputs)."""
+
+    return _native.extension().sdpa(query, key, value, is_causal, scale)

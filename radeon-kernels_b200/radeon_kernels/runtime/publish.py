@@ -32,6 +32,7 @@ ENTRYPOINTS = {
     ("add_rms_norm", "1.0"): ("add_rms_norm", "rk-sm100a-add_rms_norm"),
     ("gemm_swiglu", "1.0"): ("gemm_swiglu", "rk-sm100a-gemm_swiglu"),
     ("paged_attention_decode", "1.0"): ("paged_attention_decode", "rk-sm100a-paged_attention_decode"),
+    ("sdpa", "1.0"): ("sdpa", "rk-sm100a-sdpa"),
 }
 
 

@@ -14,6 +14,8 @@ by calling the reference package itself:
   (ops/gemv/reference.py:6-15)
 * paged decode attention: ``ops.paged_attention.reference.paged_attention_decode_reference``
   (paged_attention/reference.py:8-47)
+* self-attention: ``ops.sdpa.reference.sdpa_reference`` (sdpa/reference.py:13-36), inputs
+  drawn U[-0.125, 0.125) as the reference's SDPA benchmark draws them (benchmark.py:75-78)
 * SwiGLU, RMSNorm, residual add + RMSNorm (the decode neighbours):
   ``ops.swiglu.reference.silu_mul_reference`` (swiglu/reference.py:6-9),
   ``ops.rms_norm.reference.rms_norm_reference`` (rms_norm/reference.py:6-10),
@@ -91,6 +93,16 @@ GRAD_CASES = [
     ("grad_add_rms_bf16_t2_h16392_long_row", "add_rms_norm", "bf16", 2, 16392, 78, 1e-6, ""),
 ]
 
+# Self-attention (ops.sdpa.reference.sdpa_reference): name, dtype, batch, query_heads,
+# kv_heads, sequence, head_dim, causal, scale (None: 1/sqrt(head_dim)), seed
+SDPA_CASES = [
+    ("sdpa_bf16_b1_mha2_s37_d64_causal", "bf16", 1, 2, 2, 37, 64, True, None, 80),
+    ("sdpa_fp16_b2_gqa4x2_s130_d128_causal", "fp16", 2, 4, 2, 130, 128, True, None, 81),
+    ("sdpa_bf16_b1_gqa8x1_s200_d128_noncausal", "bf16", 1, 8, 1, 200, 128, False, 0.05, 82),
+    ("sdpa_fp16_b1_mha2_s64_d256_causal", "fp16", 1, 2, 2, 64, 256, True, None, 83),
+    ("sdpa_bf16_b1_gqa4x2_s260_d64_noncausal", "bf16", 1, 4, 2, 260, 64, False, None, 84),
+]
+
 # name, dtype, batch, query_heads, kv_heads, head_dim, block_size, num_blocks, max_blocks,
 # context lengths, index dtype, scale (None: 1/sqrt(head_dim)), seed
 PAGED_CASES = [
@@ -130,6 +142,7 @@ def main(argv: list[str] | None = None) -> int:
     from radeon_kernels.ops.gemv.reference import gemv_fallback, gemv_reference
     from radeon_kernels.ops.paged_attention.reference import paged_attention_decode_reference
     from radeon_kernels.ops.rms_norm.reference import rms_norm_reference
+    from radeon_kernels.ops.sdpa.reference import sdpa_reference
     from radeon_kernels.ops.swiglu.reference import silu_mul_reference
     from radeon_kernels.providers import torch_fallback
 
@@ -219,6 +232,19 @@ def main(argv: list[str] | None = None) -> int:
         fields["out_fp32"] = exact.numpy()
         np.savez_compressed(HERE / f"{name}.npz", **fields)
         print(name, (tokens, hidden))
+
+    for name, dt, batch, hq, hkv, seq, d, causal, scale, seed in SDPA_CASES:
+        gen = torch.Generator().manual_seed(seed)
+        q = (torch.rand((batch, hq, seq, d), generator=gen) * 0.25 - 0.125).to(dtypes[dt])
+        k = (torch.rand((batch, hkv, seq, d), generator=gen) * 0.25 - 0.125).to(dtypes[dt])
+        v = (torch.rand((batch, hkv, seq, d), generator=gen) * 0.25 - 0.125).to(dtypes[dt])
+        eff_scale = 1.0 / d**0.5 if scale is None else scale
+        out = sdpa_reference(torch, q, k, v, causal, eff_scale)
+        np.savez_compressed(
+            HERE / f"{name}.npz", dtype=dt, q=_bits(q), k=_bits(k), v=_bits(v), is_causal=np.bool_(causal),
+            scale=np.float64(eff_scale), out_ref=_bits(out),
+        )
+        print(name, tuple(out.shape))
 
     for name, operator, dt, tokens, hidden, seed, param, flags in GRAD_CASES:
         gen = torch.Generator().manual_seed(seed)

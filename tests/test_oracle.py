@@ -135,6 +135,30 @@ def test_oracle_paged_attention_matches_reference_fixtures(path):
     oracle.assert_attention(out, case["out_ref"], out32, dtype)
 
 
+@pytest.mark.parametrize("path", golden_cases("sdpa"), ids=lambda p: p.stem)
+def test_oracle_sdpa_matches_reference_fixtures(path):
+    case = _load(path)
+    dtype = str(case["dtype"])
+    out, out32 = oracle.sdpa(case["q"], case["k"], case["v"], bool(case["is_causal"]), float(case["scale"]), dtype)
+    oracle.assert_attention(out, case["out_ref"], out32, dtype)
+
+
+@pytest.mark.parametrize("path", golden_cases("sdpa"), ids=lambda p: p.stem)
+def test_reference_path_sdpa_reproduces_the_reference_bits(path):
+    """oracle.reference_path.sdpa_reference (the contract's reference entrypoint) on CPU gives
+    the reference function's own output bit for bit."""
+
+    import torch
+
+    from oracle import reference_path
+
+    case = _load(path)
+    dt = {"bf16": torch.bfloat16, "fp16": torch.float16}[str(case["dtype"])]
+    t = lambda bits: torch.from_numpy(bits.view(np.int16).copy()).view(dt)  # noqa: E731
+    out = reference_path.sdpa_reference(torch, t(case["q"]), t(case["k"]), t(case["v"]), bool(case["is_causal"]), float(case["scale"]))
+    assert np.array_equal(out.view(torch.int16).numpy().view(np.uint16), case["out_ref"])
+
+
 # ----------------------------------------------------------------- gradients
 @pytest.mark.parametrize("path", golden_cases("grad_silu"), ids=lambda p: p.stem)
 def test_oracle_silu_mul_backward_matches_reference_autograd(path):
