@@ -10,20 +10,21 @@
 // HIP candidate walks keys one at a time per query row (benchmarks/sdpa/native_sdpa.hip).
 //
 // One CTA per (128-row query tile, query head, batch), 128 threads (4 warps), flash-style:
-//   * thread 0 issues the TMA loads -- the Q tile once, K and V tiles of 128 keys in a ring
+//   * thread 0 issues the TMA loads -- the Q tile once, K and V tiles of BN keys (128; 64
+//     for head_dim 256, to fit shared memory) in a ring
 //     of STAGES buffers, through 3-D tensor maps over the [batch*heads, S, D] stacks, so rows
 //     past the sequence read as zero instead of the next head's -- and the MMAs;
-//   * S = Q K^T (M = 128, N = 128 keys, K = head_dim) into TMEM columns [0, 128): Q and K
+//   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into TMEM columns [0, BN): Q and K
 //     are K-major 128-byte-swizzled tiles straight from TMA;
 //   * each thread owns one query row (TMEM lane): it reads its 128 scores, applies the
 //     scale (in base 2) and the masks, updates the running max and sum in fp32 (online
 //     softmax), rescales its row of O in TMEM when the max moved (warp-uniform), and writes
-//     P = exp2(s - m) rounded to the dtype into shared memory in the K-major swizzled
-//     layout the next MMA reads;
-//   * O += P V (M = 128, N = head_dim, K = 128 keys) into TMEM columns [128, 128 + D): V is
+//     P = exp2(s - m) into shared memory in the K-major swizzled layout the next MMA reads:
+//     rounded to fp16, or for bf16 as two bf16 terms P_hi + P_lo (see Cfg::SPLIT);
+//   * O += P V (M = 128, N = head_dim, K = BN keys) into TMEM columns [128, 128 + D): V is
 //     an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
 //   * epilogue: O / l rounded to the dtype, one 64-byte row segment per store.
-// The sum l adds the rounded P values the MMA uses.  Every wait is bounded (status word on
+// The sum l adds the P values the MMAs use (P_hi + P_lo for bf16).  Every wait is bounded (status word on
 // expiry) and made CTA-uniform; before TMEM is released every MMA and bulk copy this CTA
 // issued has completed.
 #include <cuda.h>
@@ -41,21 +42,28 @@ namespace rk {
 namespace sdpa {
 
 constexpr int BM = 128;  // query rows per CTA
-constexpr int BN = 128;  // keys per tile
 constexpr int THREADS = 128;
 constexpr int UMMA_K = 16;
 
-template <int D>
+// SPLIT (bf16): P is stored as P_hi + P_lo, both bf16, and O += P_hi V + P_lo V, so the
+// probabilities keep ~16 significant bits instead of bf16's 8 (rounding P alone moved the
+// output by up to 4.5e-3 of its maximum on near-uniform attention); fp16 P keeps 11 bits
+// and is used as is.
+template <typename T, int D>
 struct Cfg {
+  static constexpr bool SPLIT = std::is_same<T, __nv_bfloat16>::value;
+  static constexpr int BN = D == 256 ? 64 : 128;      // keys per tile (shared-memory budget)
   static constexpr int CHUNKS = D / 64;              // 64-element (128-byte) column chunks
   static constexpr int Q_BYTES = CHUNKS * BM * 128;  // Q tile: CHUNKS x [128 rows x 128 B]
-  static constexpr int K_BYTES = CHUNKS * BN * 128;  // K tile: same layout, 128 keys
-  static constexpr int V_BYTES = BN * D * 2;         // V tile: [2 key blocks][CHUNKS][64 x 128 B]
-  static constexpr int P_BYTES = BM * BN * 2;        // P: 2 key chunks x [128 rows x 128 B]
-  static constexpr int STAGES = D == 256 ? 1 : 2;    // 227 KB of shared memory per CTA
-  static constexpr int TMEM_COLS = D == 64 ? 256 : (D == 128 ? 256 : 512);  // S + O
-  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES) + P_BYTES + 256;
+  static constexpr int K_BYTES = CHUNKS * BN * 128;  // K tile: same layout, BN keys
+  static constexpr int V_BYTES = BN * D * 2;         // V tile: [BN/64 key blocks][CHUNKS][64 x 128 B]
+  static constexpr int P_BYTES = BM * BN * 2;        // P: BN/64 key chunks x [128 rows x 128 B]
+  static constexpr int STAGES = 2;
+  static constexpr int TMEM_COLS = D == 256 ? 512 : 256;  // S at [0, BN), O at [128, 128 + D)
+  static constexpr int SMEM =
+      1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES) + (SPLIT ? 2 : 1) * P_BYTES + 256;
   static_assert(D == 64 || D == 128 || D == 256, "head_dim");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 struct __align__(8) Bars {
@@ -82,8 +90,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     sdpa_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                 const __grid_constant__ CUtensorMap tmap_v, T* __restrict__ out, Params p,
                 KernelCtl ctl) {
-  using C = Cfg<D>;
+  using C = Cfg<T, D>;
   constexpr int STAGES = C::STAGES;
+  constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -91,7 +100,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sk = sq + C::Q_BYTES;
   uint8_t* sv = sk + STAGES * C::K_BYTES;
   uint8_t* sp = sv + STAGES * C::V_BYTES;
-  Bars* bars = reinterpret_cast<Bars*>(sp + C::P_BYTES);
+  uint8_t* sp_lo = sp + C::P_BYTES;  // SPLIT only
+  Bars* bars = reinterpret_cast<Bars*>(sp + (C::SPLIT ? 2 : 1) * C::P_BYTES);
 
   const int warp = threadIdx.x >> 5;
   // Heavier (later, under the causal mask) query tiles first.
@@ -101,7 +111,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int q_mat = batch * p.hq + head;      // matrix index in the [B*Hq, S, D] stack
   const int kv_mat = batch * p.hkv + kv_head;  // and in the [B*Hkv, S, D] stacks
   const int k_tiles_all = (p.seq + BN - 1) / BN;
-  const int n_tiles = p.causal ? min(k_tiles_all, qtile + 1) : k_tiles_all;
+  // Causal: the key tiles up to this query tile's last row.
+  const int n_tiles = p.causal ? min(k_tiles_all, (qtile + 1) * (BM / BN)) : k_tiles_all;
   const int row = threadIdx.x;  // TMEM lane and query row within the tile
   const int q_pos = qtile * BM + row;
 
@@ -150,7 +161,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t bar = smem_u32(&bars->v_full[st]);
     mbar_arrive_expect_tx(bar, C::V_BYTES);
 #pragma unroll
-    for (int kb = 0; kb < 2; ++kb)
+    for (int kb = 0; kb < BN / 64; ++kb)
 #pragma unroll
       for (int c = 0; c < C::CHUNKS; ++c)
         tma_load_3d(smem_u32(sv + st * C::V_BYTES + (kb * C::CHUNKS + c) * 8192), &tmap_v, bar,
@@ -193,9 +204,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t q0 = smem_u32(sq), k0 = smem_u32(sk + st * C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / UMMA_K; ++kk) {
-          const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          tc_mma_f16(tmem, umma_desc_sw128(q0 + off, 16, 1024), umma_desc_sw128(k0 + off, 16, 1024),
-                     IDESC_S, kk > 0 ? 1u : 0u);
+          const uint32_t off_q = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          const uint32_t off_k = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          tc_mma_f16(tmem, umma_desc_sw128(q0 + off_q, 16, 1024),
+                     umma_desc_sw128(k0 + off_k, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
         }
         tc_commit(smem_u32(&bars->s_done));
         ++issued_mma;
@@ -261,15 +273,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
 
-    // ---- P = exp2(s - m), rounded, into the K-major swizzled operand tile
+    // ---- P = exp2(s - m), rounded (SPLIT: hi + lo), into the K-major swizzled operand tile
     float psum = 0.f;
-    uint8_t* prow = sp + row * 128;
 #pragma unroll
     for (int c = 0; c < BN / 32; ++c) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(t_s + c * 32, r);
       tmem_ld_wait();
-      uint32_t packed[16];
+      uint32_t hi[16], lo[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
         float e[2];
@@ -279,17 +290,26 @@ __global__ void __launch_bounds__(THREADS, 1)
           const bool masked = key >= p.seq || (diag && key > q_pos);
           e[h] = masked ? 0.f : exp2f(__uint_as_float(r[i + h]) * p.scale_log2 - m_use);
         }
-        packed[i / 2] = Pack2<T>::from_floats(e[0], e[1]);
-        const float2 back = Pack2<T>::to_floats(packed[i / 2]);
-        psum += back.x + back.y;
+        hi[i / 2] = Pack2<T>::from_floats(e[0], e[1]);
+        const float2 h2 = Pack2<T>::to_floats(hi[i / 2]);
+        if (C::SPLIT) {
+          lo[i / 2] = Pack2<T>::from_floats(e[0] - h2.x, e[1] - h2.y);
+          const float2 l2 = Pack2<T>::to_floats(lo[i / 2]);
+          psum += (h2.x + l2.x) + (h2.y + l2.y);
+        } else {
+          psum += h2.x + h2.y;
+        }
       }
       // Keys c*32 .. c*32+31 = chunk c/2, 16-byte units (c%2)*4 .. +3, swizzled by row.
-      uint8_t* chunk = prow + (c >> 1) * (BM * 128);
+      const int chunk_off = (c >> 1) * (BM * 128) + row * 128;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int unit = (c & 1) * 4 + u;
-        *reinterpret_cast<uint4*>(chunk + ((unit ^ (row & 7)) << 4)) =
-            make_uint4(packed[4 * u], packed[4 * u + 1], packed[4 * u + 2], packed[4 * u + 3]);
+        const int unit_off = chunk_off + ((((c & 1) * 4 + u) ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(sp + unit_off) =
+            make_uint4(hi[4 * u], hi[4 * u + 1], hi[4 * u + 2], hi[4 * u + 3]);
+        if (C::SPLIT)
+          *reinterpret_cast<uint4*>(sp_lo + unit_off) =
+              make_uint4(lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
       }
     }
     l_run = l_run * alpha + psum;
@@ -304,13 +324,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       got = mbar_wait_bounded(smem_u32(&bars->v_full[st]), v_used[st] & 1u, ctl.timeout_ns, &never);
       if (got) {
         ++v_used[st];
-        const uint32_t p0 = smem_u32(sp), v0 = smem_u32(sv + st * C::V_BYTES);
+        const uint32_t p0 = smem_u32(sp), plo0 = smem_u32(sp_lo), v0 = smem_u32(sv + st * C::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BN / UMMA_K; ++kk) {
-          const uint64_t a = umma_desc_sw128(p0 + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+          const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint64_t b =
               umma_desc_sw128(v0 + (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048, 8192, 1024);
-          tc_mma_f16(tmem + 128, a, b, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          tc_mma_f16(tmem + 128, umma_desc_sw128(p0 + a_off, 16, 1024), b, IDESC_O,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+          if (C::SPLIT) tc_mma_f16(tmem + 128, umma_desc_sw128(plo0 + a_off, 16, 1024), b, IDESC_O, 1u);
         }
         tc_commit(smem_u32(&bars->o_done));
         ++issued_mma;
@@ -388,11 +410,11 @@ template <typename T, int D>
 rk_status launch_sdpa(const void* q, const void* k, const void* v, void* out, int64_t B,
                       int64_t Hq, int64_t Hkv, int64_t S, bool causal, float scale, rk_dtype dt,
                       cudaStream_t s) {
-  using C = sdpa::Cfg<D>;
+  using C = sdpa::Cfg<T, D>;
   CUtensorMap tq, tk, tv;
   rk_status st = encode_tmap_3d(&tq, q, dt, D, S, B * Hq, 64, sdpa::BM);
   if (st != RK_OK) return st;
-  if ((st = encode_tmap_3d(&tk, k, dt, D, S, B * Hkv, 64, sdpa::BN)) != RK_OK) return st;
+  if ((st = encode_tmap_3d(&tk, k, dt, D, S, B * Hkv, 64, C::BN)) != RK_OK) return st;
   if ((st = encode_tmap_3d(&tv, v, dt, D, S, B * Hkv, 64, 64)) != RK_OK) return st;
   LaunchCtl lc;
   if ((st = launch_ctl(&lc)) != RK_OK) return st;
@@ -443,7 +465,7 @@ rk_status sdpa_launch(const void* q, const void* k, const void* v, void* out, in
   if (device_cc_major() != 10) return RK_ERR_UNSUPPORTED;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return RK_ERR_UNSUPPORTED;
   // TMA coordinates and the kernel's matrix and row indices are 32-bit.
-  if (S + sdpa::BM > (1ll << 31) || B * Hq > (1ll << 31)) return RK_ERR_UNSUPPORTED;
+  if (S + 2 * sdpa::BM > (1ll << 31) || B * Hq > (1ll << 31)) return RK_ERR_UNSUPPORTED;
   if (Hq > 65535 || B > 65535) return RK_ERR_UNSUPPORTED;
   if (dt == RK_DTYPE_BF16)
     return launch_sdpa_d<__nv_bfloat16>(q, k, v, out, B, Hq, Hkv, S, D, causal, scale, dt, s);
