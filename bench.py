@@ -670,6 +670,66 @@ def suite(args, dist: Dist, ext, peaks):
         }
         del a, b
 
+    def sdpa_case(name, b, hq, hkv, seq, d, causal, dtype, seed):
+        """Prefill self-attention: FLOP counted as the reference's benchmark counts them
+        (4 * batch * heads * head_dim * attended pairs, benchmarks/sdpa/benchmark.py:164-167).
+        torch's scaled_dot_product_attention -- the reference's own fallback on a GPU
+        (ops/sdpa/reference.py:39-57) -- is timed on the same inputs for comparison."""
+
+        if not wanted(name):
+            return
+        import torch.nn.functional as F
+
+        tdt = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
+        per_set = (b * hq * seq * d + 2 * b * hkv * seq * d + b * hq * seq * d) * 2
+        sets = max(2, min(32, -(-300_000_000 // per_set)))
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        draw = lambda shape: (torch.rand(shape, generator=gen, device="cuda") * 0.25 - 0.125).to(tdt)  # noqa: E731
+        qkv = [(draw((b, hq, seq, d)), draw((b, hkv, seq, d)), draw((b, hkv, seq, d))) for _ in range(sets)]
+        scale = d ** -0.5
+
+        def graph_time(step):
+            for i in range(3):
+                step(i)
+            torch.cuda.synchronize()
+            launches = max(20, sets)
+            g = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream()
+            cap.wait_stream(stream)
+            with torch.cuda.stream(cap):
+                with torch.cuda.graph(g, stream=cap):
+                    for i in range(launches):
+                        step(i)
+            stream.wait_stream(cap)
+            torch.cuda.synchronize()
+            g.replay()
+            torch.cuda.synchronize()
+            reps = 10
+            ms = time_loop(lambda i: g.replay(), reps, stream) / (reps * launches)
+            del g
+            return ms
+
+        ms = graph_time(lambda i: ext.sdpa(*qkv[i % sets], causal, scale))
+        torch_ms = graph_time(lambda i: F.scaled_dot_product_attention(
+            *qkv[i % sets], is_causal=causal, scale=scale, enable_gqa=hq != hkv))
+        dist.barrier()
+        ms = dist.max(ms)
+        pairs = seq * (seq + 1) // 2 if causal else seq * seq
+        tflops = 4.0 * b * hq * d * pairs / (ms / 1e3) / 1e12
+        results[name] = {
+            "unit": "TFLOP/s",
+            "value": round(tflops * dist.world, 2),
+            "per_gpu": round(tflops, 2),
+            "us": round(ms * 1e3, 2),
+            "torch_sdpa_us": round(torch_ms * 1e3, 2),
+            "roofline_frac": round(tflops / peaks["bf16_tflops"], 4),
+            "scaling": "replica",
+            "shape": {"batch": b, "query_heads": hq, "kv_heads": hkv, "sequence": seq, "head_dim": d, "causal": causal},
+            "dtype": dtype,
+            "timing": f"CUDA graph over {sets} input sets (small cases: launch and latency bound)",
+        }
+        del qkv
+
     def cool_down():
         # Let the power/clock state recover between long GEMM cases so one case's
         # power capping does not leak into the next measurement.
@@ -699,6 +759,14 @@ def suite(args, dist: Dist, ext, peaks):
     paged_case("paged_b16_gqa32x8_c2048_d128_bf16", 16, 32, 8, 2048, 128, 16, "bf16", 62)
     paged_case("paged_b4_mha16_c2048_d64_bf16", 4, 16, 16, 2048, 64, 32, "bf16", 63)
     paged_case("paged_b4_gqa32x8_c1024_d256_bf16", 4, 32, 8, 1024, 256, 16, "bf16", 64)
+    # Prefill attention, the reference's workload cases (benchmarks/workloads/sdpa-1.0.yaml),
+    # plus one long-sequence case that is tensor-core rather than latency bound.
+    sdpa_case("sdpa_b1_mha16_s128_d64_causal_bf16", 1, 16, 16, 128, 64, True, "bf16", 70)
+    sdpa_case("sdpa_b1_gqa32x8_s512_d128_causal_bf16", 1, 32, 8, 512, 128, True, "bf16", 71)
+    sdpa_case("sdpa_b4_gqa32x8_s128_d128_causal_bf16", 4, 32, 8, 128, 128, True, "bf16", 72)
+    sdpa_case("sdpa_b1_mha16_s256_d64_full_bf16", 1, 16, 16, 256, 64, False, "bf16", 73)
+    sdpa_case("sdpa_b2_gqa16x4_s256_d256_causal_bf16", 2, 16, 4, 256, 256, True, "bf16", 74)
+    sdpa_case("sdpa_b4_gqa32x8_s4096_d128_causal_bf16", 4, 32, 8, 4096, 128, True, "bf16", 75)
     gemm_case("c1_gemm_1024_bf16", 1024, 1024, 1024, "bf16", "uniform", 0, 10, graph=True)
     cool_down()
     gemm_case("c4_gemm_ffn_up_fp16", 4096, 14336, 4096, "fp16", "normal64", 3, 10)
@@ -819,6 +887,8 @@ PROFILE_CASES = {
     "add_rms_norm_prefill": ("add_rms_norm", 2048, 4096, 0, "bf16", "normal"),
     "ffn_swiglu": ("gemm_swiglu", 4096, 14336, 4096, "fp16", "normal64"),
     "paged_b16_c2048": ("paged", 16, 2048, 0, "bf16", "normal"),
+    "rms_norm_backward_prefill": ("rms_norm_backward", 2048, 4096, 0, "bf16", "normal"),
+    "sdpa_b4_s4096": ("sdpa", 4, 4096, 128, "bf16", "normal"),  # GQA 32 x 8, causal
 }
 
 
@@ -853,6 +923,16 @@ def run_profile(args) -> int:
         a = seeded((m, k), 1, dist_name, dtype)
         b = seeded((k, 2 * n), 2, dist_name, dtype)
         launch = lambda: ext.gemm_swiglu(a, b, 0)  # noqa: E731
+    elif kind == "rms_norm_backward":  # with the weight gradient
+        dy = seeded((m, n), 1, dist_name, dtype)
+        x = seeded((m, n), 2, dist_name, dtype)
+        w = seeded((n,), 3, dist_name, dtype)
+        launch = lambda: ext.rms_norm_backward(dy, x, w, 1e-6, True)  # noqa: E731
+    elif kind == "sdpa":  # m = batch, n = sequence, k = head_dim; 32 query heads over 8 KV heads
+        q = seeded((m, 32, n, k), 1, dist_name, dtype)
+        kk = seeded((m, 8, n, k), 2, dist_name, dtype)
+        v = seeded((m, 8, n, k), 3, dist_name, dtype)
+        launch = lambda: ext.sdpa(q, kk, v, True, k ** -0.5)  # noqa: E731
     elif kind == "add_rms_norm":
         x = seeded((m, n), 1, dist_name, dtype)
         r = seeded((m, n), 2, dist_name, dtype)
