@@ -9,22 +9,27 @@
 // with torch's SDPA (its dispatch manifest has no native entry, dispatch/sdpa-1.0.json); its
 // HIP candidate walks keys one at a time per query row (benchmarks/sdpa/native_sdpa.hip).
 //
-// One CTA per (128-row query tile, query head, batch), 128 threads (4 warps), flash-style:
+// One CTA per (128-row query tile, query head, batch), 512 threads (16 warps), flash-style:
 //   * thread 0 issues the TMA loads -- the Q tile once, K and V tiles of BN keys (128; 64
 //     for head_dim 256, to fit shared memory) in a ring
 //     of STAGES buffers, through 3-D tensor maps over the [batch*heads, S, D] stacks, so rows
 //     past the sequence read as zero instead of the next head's -- and the MMAs;
 //   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into TMEM columns [0, BN): Q and K
 //     are K-major 128-byte-swizzled tiles straight from TMA;
-//   * each thread owns one query row (TMEM lane): it reads its 128 scores, applies the
-//     scale (in base 2) and the masks, updates the running max and sum in fp32 (online
-//     softmax), rescales its row of O in TMEM when the max moved (warp-uniform), and writes
-//     P = exp2(s - m) into shared memory in the K-major swizzled layout the next MMA reads:
-//     rounded to fp16, or for bf16 as two bf16 terms P_hi + P_lo (see Cfg::SPLIT);
+//   * four warps share each 32-row TMEM lane quarter, each thread a quarter of its row's
+//     scores: it applies the scale (in base 2) and the masks, the row maximum is combined
+//     through four spare TMEM columns in a fixed order, and the online softmax (fp32) rescales the
+//     thread's quarter of the O row in TMEM only when the maximum grew by more than 2^8
+//     (lazy rescaling); P = 2^(s - m) (hardware ex2) goes to shared memory in the K-major
+//     swizzled layout the next MMA reads: rounded to fp16, or for bf16 as two bf16 terms
+//     P_hi + P_lo (see Cfg::SPLIT).  (One warp per lane quarter, 128 scores per thread,
+//     spent about 9 us per key tile on the dependent softmax chain.);
 //   * O += P V (M = 128, N = head_dim, K = BN keys) into TMEM columns [128, 128 + D): V is
 //     an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
-//   * epilogue: O / l rounded to the dtype, one 64-byte row segment per store.
-// The sum l adds the P values the MMAs use (P_hi + P_lo for bf16).  Every wait is bounded (status word on
+//   * epilogue: O / l rounded to the dtype; l is the four warps' shares added in order.
+// The sum l adds the P values the MMAs use (P_hi + P_lo for bf16).  Thread 0 issues S_{j+1}
+// before P V_j, so the softmax of tile j+1 overlaps the tail of P V_j; one S buffer serves
+// (S_{j+1} is issued after every thread has read S_j).  Every wait is bounded (status word on
 // expiry) and made CTA-uniform; before TMEM is released every MMA and bulk copy this CTA
 // issued has completed.
 #include <cuda.h>
@@ -42,7 +47,7 @@ namespace rk {
 namespace sdpa {
 
 constexpr int BM = 128;  // query rows per CTA
-constexpr int THREADS = 128;
+constexpr int THREADS = 512;
 constexpr int UMMA_K = 16;
 
 // SPLIT (bf16): P is stored as P_hi + P_lo, both bf16, and O += P_hi V + P_lo V, so the
@@ -59,7 +64,7 @@ struct Cfg {
   static constexpr int V_BYTES = BN * D * 2;         // V tile: [BN/64 key blocks][CHUNKS][64 x 128 B]
   static constexpr int P_BYTES = BM * BN * 2;        // P: BN/64 key chunks x [128 rows x 128 B]
   static constexpr int STAGES = 2;
-  static constexpr int TMEM_COLS = D == 256 ? 512 : 256;  // S at [0, BN), O at [128, 128 + D)
+  static constexpr int TMEM_COLS = 512;  // S, O and the row-exchange columns
   static constexpr int SMEM =
       1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES) + (SPLIT ? 2 : 1) * P_BYTES + 256;
   static_assert(D == 64 || D == 128 || D == 256, "head_dim");
@@ -74,6 +79,7 @@ struct __align__(8) Bars {
   uint64_t o_done;
   uint64_t drain;
   uint32_t tmem_base;
+  int abort;  // set when a wait gave up; every later wait returns at once
 };
 
 struct Params {
@@ -98,12 +104,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                                              ~uintptr_t(1023));
   uint8_t* sq = smem;
   uint8_t* sk = sq + C::Q_BYTES;
-  uint8_t* sv = sk + STAGES * C::K_BYTES;
-  uint8_t* sp = sv + STAGES * C::V_BYTES;
+  uint8_t* sv_s = sk + STAGES * C::K_BYTES;
+  uint8_t* sp = sv_s + STAGES * C::V_BYTES;
   uint8_t* sp_lo = sp + C::P_BYTES;  // SPLIT only
   Bars* bars = reinterpret_cast<Bars*>(sp + (C::SPLIT ? 2 : 1) * C::P_BYTES);
 
-  const int warp = threadIdx.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Four warps share each 32-row TMEM lane quarter; each takes a quarter of the columns.
+  const int quarter = warp & 3, slice = warp >> 2;
+  constexpr int SLICE = BN / 4;  // score columns per thread
+  constexpr int OSL = D / 4;     // output columns per thread
   // Heavier (later, under the causal mask) query tiles first.
   const int qtile = p.q_tiles - 1 - static_cast<int>(blockIdx.x);
   const int head = blockIdx.y, batch = blockIdx.z;
@@ -113,7 +123,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int k_tiles_all = (p.seq + BN - 1) / BN;
   // Causal: the key tiles up to this query tile's last row.
   const int n_tiles = p.causal ? min(k_tiles_all, (qtile + 1) * (BM / BN)) : k_tiles_all;
-  const int row = threadIdx.x;  // TMEM lane and query row within the tile
+  const int row = quarter * 32 + lane;  // TMEM lane and query row within the tile
   const int q_pos = qtile * BM + row;
 
   if (threadIdx.x == 0) {
@@ -125,6 +135,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     mbar_init(smem_u32(&bars->s_done), 1);
     mbar_init(smem_u32(&bars->o_done), 1);
     mbar_init(smem_u32(&bars->drain), 1);
+    bars->abort = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_q);
     tma_prefetch_desc(&tmap_k);
@@ -138,9 +149,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);  // this warp's lanes
-  const uint32_t t_s = t_lane;        // S: columns [0, 128)
-  const uint32_t t_o = t_lane + 128;  // O: columns [128, 128 + D)
+  const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);  // this warp's lanes
+  // TMEM columns: S [0, BN), O [O_COL, O_COL + D), exchange slots [X_COL, X_COL + 8).
+  constexpr int O_COL = 2 * BN, X_COL = 384;
+  static_assert(O_COL + D <= X_COL, "TMEM column plan");
+  const uint32_t t_s = t_lane;
+  const uint32_t t_o = t_lane + O_COL;
+  const uint32_t t_x = t_lane + X_COL;
   pdl_begin();  // global memory is touched only after this
 
   // Bulk-copy bookkeeping (thread 0): loads issued into each stage, and those waited for.
@@ -164,7 +179,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int kb = 0; kb < BN / 64; ++kb)
 #pragma unroll
       for (int c = 0; c < C::CHUNKS; ++c)
-        tma_load_3d(smem_u32(sv + st * C::V_BYTES + (kb * C::CHUNKS + c) * 8192), &tmap_v, bar,
+        tma_load_3d(smem_u32(sv_s + st * C::V_BYTES + (kb * C::CHUNKS + c) * 8192), &tmap_v, bar,
                     c * 64, t * BN + kb * 64, kv_mat);
     ++v_issued[st];
   };
@@ -186,125 +201,157 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr uint32_t IDESC_O =
       umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, D, false, true);
   int never = 0;
-  bool ok = true;
-  float m_run = -INFINITY, l_run = 0.f;
+  volatile int* abort = &bars->abort;
+  // A wait that gives up records why and sets the abort flag; the CTA then runs on without
+  // issuing more work (every later wait returns at once), so every thread keeps reaching
+  // every barrier, and the output is not written.
+  auto fail = [&](uint32_t code) {
+    *abort = 1;
+    if ((threadIdx.x & 31) == 0) atomicOr(ctl.status, code);
+  };
+  // Row state (identical in the four warps that share a row): the maximum the exponentials
+  // are taken against, and this warp's share of the row sum.
+  float m_use = -INFINITY, l_part = 0.f;
   int issued_mma = 0;  // thread 0: tcgen05.commit groups issued
 
-  for (int j = 0; j < n_tiles && ok; ++j) {
-    const int st = j % STAGES;
-    // ---- S = Q K_j^T (thread 0)
-    if (threadIdx.x == 0) {
-      bool got = true;
-      if (j == 0) got = q_used = mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, &never);
-      got = got && mbar_wait_bounded(smem_u32(&bars->k_full[st]), k_used[st] & 1u, ctl.timeout_ns,
-                                     &never);
-      if (got) {
-        ++k_used[st];
-        tc_fence_after();
-        const uint32_t q0 = smem_u32(sq), k0 = smem_u32(sk + st * C::K_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < D / UMMA_K; ++kk) {
-          const uint32_t off_q = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint32_t off_k = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          tc_mma_f16(tmem, umma_desc_sw128(q0 + off_q, 16, 1024),
-                     umma_desc_sw128(k0 + off_k, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(smem_u32(&bars->s_done));
-        ++issued_mma;
-      } else {
-        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_PRODUCER);
-      }
-      ok = got;
+  // Thread 0: S_t = Q K_t^T into the S columns (the previous S has been read).
+  auto issue_s = [&](int t) {
+    const int st = t % STAGES;
+    bool got = true;
+    if (t == 0) got = q_used = mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, abort);
+    got = got && mbar_wait_bounded(smem_u32(&bars->k_full[st]), k_used[st] & 1u, ctl.timeout_ns, abort);
+    if (!got) {
+      fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+      return;
     }
-    ok = __syncthreads_and(ok);
-    if (!ok) break;
-    // ---- scores of this thread's row
-    bool got = mbar_wait_bounded(smem_u32(&bars->s_done), j & 1, ctl.timeout_ns, &never);
-    ok = __syncthreads_and(got);
-    if (!ok) {
-      if (threadIdx.x == 0) atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_MMA);
-      break;
-    }
+    ++k_used[st];
     tc_fence_after();
-    // K_j is no longer needed: refill its stage with K_{j+STAGES}.
-    if (threadIdx.x == 0 && j + STAGES < n_tiles) load_k(j + STAGES);
-    const int key0 = j * BN;
-    const bool diag = p.causal && key0 + BN > qtile * BM;  // some keys lie above this row's
-    float mx = -INFINITY;
+    const uint32_t q0 = smem_u32(sq), k0 = smem_u32(sk + st * C::K_BYTES);
 #pragma unroll
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(t_s + c * 32, r);
+    for (int kk = 0; kk < D / UMMA_K; ++kk) {
+      const uint32_t off_q = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+      const uint32_t off_k = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+      tc_mma_f16(tmem, umma_desc_sw128(q0 + off_q, 16, 1024), umma_desc_sw128(k0 + off_k, 16, 1024),
+                 IDESC_S, kk > 0 ? 1u : 0u);
+    }
+    tc_commit(smem_u32(&bars->s_done));
+    ++issued_mma;
+  };
+  // Thread 0: O += P V_t (P in shared memory, V_t in its stage).
+  auto issue_pv = [&](int t) {
+    const int st = t % STAGES;
+    if (!mbar_wait_bounded(smem_u32(&bars->v_full[st]), v_used[st] & 1u, ctl.timeout_ns, abort)) {
+      fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+      return;
+    }
+    ++v_used[st];
+    const uint32_t p0 = smem_u32(sp), plo0 = smem_u32(sp_lo), v0 = smem_u32(sv_s + st * C::V_BYTES);
+#pragma unroll
+    for (int kk = 0; kk < BN / UMMA_K; ++kk) {
+      const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+      const uint64_t b = umma_desc_sw128(v0 + (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048, 8192, 1024);
+      tc_mma_f16(tmem + O_COL, umma_desc_sw128(p0 + a_off, 16, 1024), b, IDESC_O,
+                 (t > 0 || kk > 0) ? 1u : 0u);
+      if (C::SPLIT) tc_mma_f16(tmem + O_COL, umma_desc_sw128(plo0 + a_off, 16, 1024), b, IDESC_O, 1u);
+    }
+    tc_commit(smem_u32(&bars->o_done));
+    ++issued_mma;
+  };
+
+  if (threadIdx.x == 0) issue_s(0);
+  // Keys this row may attend: below the sequence end and, causal, up to the row itself.
+  const int key_limit = p.causal ? min(p.seq, q_pos + 1) : p.seq;
+
+  // Per tile j: S_j is issued before P V_{j-1} (end of the previous iteration), so the
+  // softmax of tile j starts as soon as S_j lands while P V_{j-1} still runs; each thread
+  // waits for P V_{j-1} only before it overwrites P or rescales O.
+  for (int j = 0; j < n_tiles; ++j) {
+    if (!mbar_wait_bounded(smem_u32(&bars->s_done), j & 1, ctl.timeout_ns, abort))
+      fail(RK_DEV_ERR_TIMEOUT_MMA);
+    tc_fence_after();
+    // K_j's stage is free again.
+    if (threadIdx.x == 0 && !*abort && j + STAGES < n_tiles) load_k(j + STAGES);
+    const int valid = key_limit - (j * BN + slice * SLICE);  // keys i < valid are attended
+    float sv[SLICE];
+    float mx = -INFINITY;
+    {
+      uint32_t r[SLICE];
+#pragma unroll
+      for (int c = 0; c < SLICE / 16; ++c)
+        tmem_ld_32x32b_x16(t_s + slice * SLICE + c * 16, *reinterpret_cast<uint32_t(*)[16]>(r + c * 16));
       tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int key = key0 + c * 32 + i;
-        const bool masked = key >= p.seq || (diag && key > q_pos);
-        const float s = masked ? -INFINITY : __uint_as_float(r[i]) * p.scale_log2;
-        mx = fmaxf(mx, s);
+      for (int i = 0; i < SLICE; ++i) {
+        sv[i] = i < valid ? __uint_as_float(r[i]) * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, sv[i]);
       }
     }
-    const float m_new = fmaxf(m_run, mx);
-    const float m_use = m_new == -INFINITY ? 0.f : m_new;  // a row with no key yet
-    const float alpha = exp2f(m_run - m_use);
+    // Row maximum over the four warps of the lane quarter, through four spare TMEM columns.
+    tmem_st_32x32b_x1(t_x + slice, __float_as_uint(mx));
+    tmem_st_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    float m_tile;
+    {
+      uint32_t r[4];
+      tmem_ld_32x32b_x4(t_x, r);
+      tmem_ld_wait();
+      m_tile = fmaxf(fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                     fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3])));
+    }
+    // Lazy rescaling: the exponentials keep the old maximum until the row maximum exceeds
+    // it by more than 2^8 (P <= 256, exact enough in fp16 and in bf16 hi + lo).
+    float alpha = 1.f;
+    if (m_tile > m_use + 8.f) {
+      alpha = ex2_approx(m_use - m_tile);  // 0 for the first keys of the row
+      m_use = m_tile;
+    }
+    const float m_sub = m_use == -INFINITY ? 0.f : m_use;
 
-    // ---- P V_{j-1} must be done: P is overwritten and O rescaled below.
-    if (j > 0) {
-      got = mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, &never);
-      ok = __syncthreads_and(got);
-      if (!ok) {
-        if (threadIdx.x == 0) atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_MMA);
-        break;
+    // ---- P = 2^(s - m), rounded (SPLIT: hi + lo), kept in registers for now.  The row sum
+    // adds the fp32 values (within 2^-16 of hi + lo; fp16 P within 2^-11).
+    float psum = 0.f;
+    uint32_t hi[SLICE / 2], lo[SLICE / 2];
+#pragma unroll
+    for (int i = 0; i < SLICE; i += 2) {
+      const float e0 = ex2_approx(sv[i] - m_sub), e1 = ex2_approx(sv[i + 1] - m_sub);
+      psum += e0 + e1;
+      hi[i / 2] = Pack2<T>::from_floats(e0, e1);
+      if (C::SPLIT) {
+        const float2 h2 = Pack2<T>::to_floats(hi[i / 2]);
+        lo[i / 2] = Pack2<T>::from_floats(e0 - h2.x, e1 - h2.y);
       }
+    }
+    l_part = l_part * alpha + psum;
+
+    // ---- P V_{j-1} must be done before P is overwritten and O rescaled.
+    if (j > 0) {
+      if (!mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, abort))
+        fail(RK_DEV_ERR_TIMEOUT_MMA);
       tc_fence_after();
-      if (threadIdx.x == 0 && j - 1 + STAGES < n_tiles) load_v(j - 1 + STAGES);
-      // Rescale this warp's rows of O when any of their maxima moved.
-      if (__any_sync(0xffffffffu, alpha != 1.0f)) {
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(t_o + c * 32, r);
+      if (threadIdx.x == 0 && !*abort && j - 1 + STAGES < n_tiles) load_v(j - 1 + STAGES);
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < OSL / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st_32x32b_x32(t_o + c * 32, r);
+          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32x32b_x16(t_o + slice * OSL + c * 16, r);
         }
         tmem_st_wait();
       }
     }
-
-    // ---- P = exp2(s - m), rounded (SPLIT: hi + lo), into the K-major swizzled operand tile
-    float psum = 0.f;
+    {
+      // This thread's keys: 64-key chunk kf / 64, 16-byte units (kf % 64) / 8 onwards,
+      // swizzled by row.
+      const int kf = slice * SLICE;
+      const int chunk_off = (kf >> 6) * (BM * 128) + row * 128;
 #pragma unroll
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(t_s + c * 32, r);
-      tmem_ld_wait();
-      uint32_t hi[16], lo[16];
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        float e[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int key = key0 + c * 32 + i + h;
-          const bool masked = key >= p.seq || (diag && key > q_pos);
-          e[h] = masked ? 0.f : exp2f(__uint_as_float(r[i + h]) * p.scale_log2 - m_use);
-        }
-        hi[i / 2] = Pack2<T>::from_floats(e[0], e[1]);
-        const float2 h2 = Pack2<T>::to_floats(hi[i / 2]);
-        if (C::SPLIT) {
-          lo[i / 2] = Pack2<T>::from_floats(e[0] - h2.x, e[1] - h2.y);
-          const float2 l2 = Pack2<T>::to_floats(lo[i / 2]);
-          psum += (h2.x + l2.x) + (h2.y + l2.y);
-        } else {
-          psum += h2.x + h2.y;
-        }
-      }
-      // Keys c*32 .. c*32+31 = chunk c/2, 16-byte units (c%2)*4 .. +3, swizzled by row.
-      const int chunk_off = (c >> 1) * (BM * 128) + row * 128;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int unit_off = chunk_off + ((((c & 1) * 4 + u) ^ (row & 7)) << 4);
+      for (int u = 0; u < SLICE / 8; ++u) {
+        const int unit_off = chunk_off + (((((kf & 63) >> 3) + u) ^ (row & 7)) << 4);
         *reinterpret_cast<uint4*>(sp + unit_off) =
             make_uint4(hi[4 * u], hi[4 * u + 1], hi[4 * u + 2], hi[4 * u + 3]);
         if (C::SPLIT)
@@ -312,66 +359,52 @@ __global__ void __launch_bounds__(THREADS, 1)
               make_uint4(lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
       }
     }
-    l_run = l_run * alpha + psum;
-    m_run = m_new;
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
 
-    // ---- O += P V_j (thread 0)
-    if (threadIdx.x == 0) {
+    // ---- thread 0: S_{j+1} first (the next softmax waits for it), then P V_j.
+    if (threadIdx.x == 0 && !*abort) {
       tc_fence_after();
-      got = mbar_wait_bounded(smem_u32(&bars->v_full[st]), v_used[st] & 1u, ctl.timeout_ns, &never);
-      if (got) {
-        ++v_used[st];
-        const uint32_t p0 = smem_u32(sp), plo0 = smem_u32(sp_lo), v0 = smem_u32(sv + st * C::V_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < BN / UMMA_K; ++kk) {
-          const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint64_t b =
-              umma_desc_sw128(v0 + (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048, 8192, 1024);
-          tc_mma_f16(tmem + 128, umma_desc_sw128(p0 + a_off, 16, 1024), b, IDESC_O,
-                     (j > 0 || kk > 0) ? 1u : 0u);
-          if (C::SPLIT) tc_mma_f16(tmem + 128, umma_desc_sw128(plo0 + a_off, 16, 1024), b, IDESC_O, 1u);
-        }
-        tc_commit(smem_u32(&bars->o_done));
-        ++issued_mma;
-      } else {
-        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_PRODUCER);
-      }
-      ok = got;
+      if (j + 1 < n_tiles) issue_s(j + 1);
+      if (!*abort) issue_pv(j);
     }
-    ok = __syncthreads_and(ok);
   }
 
-  // ---- epilogue: O / l
-  if (ok && n_tiles > 0) {
-    const bool got =
-        mbar_wait_bounded(smem_u32(&bars->o_done), (n_tiles - 1) & 1, ctl.timeout_ns, &never);
-    ok = __syncthreads_and(got);
-    if (ok) {
-      tc_fence_after();
-      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-      T* orow = out + (static_cast<size_t>(q_mat) * p.seq + q_pos) * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_o + c * 32, r);
-        tmem_ld_wait();
-        if (q_pos < p.seq) {
+  // ---- epilogue: O / l  (l = the four warps' shares, added in slice order)
+  if (!mbar_wait_bounded(smem_u32(&bars->o_done), (n_tiles - 1) & 1, ctl.timeout_ns, abort))
+    fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
+  tc_fence_after();
+  tmem_st_32x32b_x1(t_x + 4 + slice, __float_as_uint(l_part));
+  tmem_st_wait();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  {
+    uint32_t lr[4];
+    tmem_ld_32x32b_x4(t_x + 4, lr);
+    tmem_ld_wait();
+    const float l = ((__uint_as_float(lr[0]) + __uint_as_float(lr[1])) + __uint_as_float(lr[2])) +
+                    __uint_as_float(lr[3]);
+    const float inv = l > 0.f ? 1.0f / l : 0.f;
+    const bool store = q_pos < p.seq && !*abort;
+    T* orow = out + (static_cast<size_t>(q_mat) * p.seq + q_pos) * D + slice * OSL;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 v;
-            v.x = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 0]) * inv, __uint_as_float(r[8 * q + 1]) * inv);
-            v.y = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv);
-            v.z = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv);
-            v.w = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * q) = v;
-          }
+    for (int c = 0; c < OSL / 16; ++c) {
+      uint32_t r[16];
+      tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
+      tmem_ld_wait();
+      if (store) {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          uint4 v;
+          v.x = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 0]) * inv, __uint_as_float(r[8 * q + 1]) * inv);
+          v.y = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv);
+          v.z = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv);
+          v.w = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c * 16 + 8 * q) = v;
         }
       }
-    } else if (threadIdx.x == 0) {
-      atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_EPILOGUE);
     }
   }
 
