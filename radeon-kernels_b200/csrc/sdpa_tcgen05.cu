@@ -27,9 +27,9 @@
 //   * O += P V (M = 128, N = head_dim, K = BN keys) into TMEM columns [128, 128 + D): V is
 //     an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
 //   * epilogue: O / l rounded to the dtype; l is the four warps' shares added in order.
-// The sum l adds the P values the MMAs use (P_hi + P_lo for bf16).  Thread 0 issues S_{j+1}
-// before P V_j, so the softmax of tile j+1 overlaps the tail of P V_j; one S buffer serves
-// (S_{j+1} is issued after every thread has read S_j).  Every wait is bounded (status word on
+// The row sum l adds the fp32 exponentials.  Two S buffers in TMEM: thread 0 issues S_{j+1}
+// as soon as S_j has landed, so the scores of the next tile are computed during this tile's
+// softmax, and P V_j overlaps the next tile's exponentials.  Every wait is bounded (status word on
 // expiry) and made CTA-uniform; before TMEM is released every MMA and bulk copy this CTA
 // issued has completed.
 #include <cuda.h>
@@ -75,7 +75,7 @@ struct __align__(8) Bars {
   uint64_t q_full;
   uint64_t k_full[2];
   uint64_t v_full[2];
-  uint64_t s_done;
+  uint64_t s_done[2];  // one per S buffer (tile t: buffer t & 1)
   uint64_t o_done;
   uint64_t drain;
   uint32_t tmem_base;
@@ -132,7 +132,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(smem_u32(&bars->k_full[s]), 1);
       mbar_init(smem_u32(&bars->v_full[s]), 1);
     }
-    mbar_init(smem_u32(&bars->s_done), 1);
+    mbar_init(smem_u32(&bars->s_done[0]), 1);
+    mbar_init(smem_u32(&bars->s_done[1]), 1);
     mbar_init(smem_u32(&bars->o_done), 1);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
@@ -150,10 +151,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);  // this warp's lanes
-  // TMEM columns: S [0, BN), O [O_COL, O_COL + D), exchange slots [X_COL, X_COL + 8).
+  // TMEM columns: S buffers [0, BN) and [BN, 2 BN), O [O_COL, O_COL + D), exchange slots
+  // [X_COL, X_COL + 8).
   constexpr int O_COL = 2 * BN, X_COL = 384;
   static_assert(O_COL + D <= X_COL, "TMEM column plan");
-  const uint32_t t_s = t_lane;
   const uint32_t t_o = t_lane + O_COL;
   const uint32_t t_x = t_lane + X_COL;
   pdl_begin();  // global memory is touched only after this
@@ -214,7 +215,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   float m_use = -INFINITY, l_part = 0.f;
   int issued_mma = 0;  // thread 0: tcgen05.commit groups issued
 
-  // Thread 0: S_t = Q K_t^T into the S columns (the previous S has been read).
+  // Thread 0: S_t = Q K_t^T into S buffer t & 1 (whose previous tile, t - 2, every thread
+  // has read: S_t is issued after the barrier that closes tile t - 1).
   auto issue_s = [&](int t) {
     const int st = t % STAGES;
     bool got = true;
@@ -231,10 +233,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int kk = 0; kk < D / UMMA_K; ++kk) {
       const uint32_t off_q = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
       const uint32_t off_k = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-      tc_mma_f16(tmem, umma_desc_sw128(q0 + off_q, 16, 1024), umma_desc_sw128(k0 + off_k, 16, 1024),
-                 IDESC_S, kk > 0 ? 1u : 0u);
+      tc_mma_f16(tmem + (t & 1) * BN, umma_desc_sw128(q0 + off_q, 16, 1024),
+                 umma_desc_sw128(k0 + off_k, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
     }
-    tc_commit(smem_u32(&bars->s_done));
+    tc_commit(smem_u32(&bars->s_done[t & 1]));
     ++issued_mma;
   };
   // Thread 0: O += P V_t (P in shared memory, V_t in its stage).
@@ -262,15 +264,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   // Keys this row may attend: below the sequence end and, causal, up to the row itself.
   const int key_limit = p.causal ? min(p.seq, q_pos + 1) : p.seq;
 
-  // Per tile j: S_j is issued before P V_{j-1} (end of the previous iteration), so the
-  // softmax of tile j starts as soon as S_j lands while P V_{j-1} still runs; each thread
-  // waits for P V_{j-1} only before it overwrites P or rescales O.
+  // Per tile j: S_{j+1} is issued as soon as S_j has landed, into the other S buffer, so the
+  // tensor core computes the next scores during this tile's softmax; P V_{j-1} runs under
+  // its first half too -- each thread waits for it only before it overwrites P or rescales O.
   for (int j = 0; j < n_tiles; ++j) {
-    if (!mbar_wait_bounded(smem_u32(&bars->s_done), j & 1, ctl.timeout_ns, abort))
+    if (!mbar_wait_bounded(smem_u32(&bars->s_done[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort))
       fail(RK_DEV_ERR_TIMEOUT_MMA);
     tc_fence_after();
-    // K_j's stage is free again.
-    if (threadIdx.x == 0 && !*abort && j + STAGES < n_tiles) load_k(j + STAGES);
+    if (threadIdx.x == 0 && !*abort) {
+      if (j + STAGES < n_tiles) load_k(j + STAGES);  // K_j's stage is free again
+      if (j + 1 < n_tiles) issue_s(j + 1);
+    }
+    const uint32_t t_s = t_lane + (j & 1) * BN;
     const int valid = key_limit - (j * BN + slice * SLICE);  // keys i < valid are attended
     float sv[SLICE];
     float mx = -INFINITY;
@@ -363,11 +368,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
     __syncthreads();
 
-    // ---- thread 0: S_{j+1} first (the next softmax waits for it), then P V_j.
+    // ---- thread 0: O += P V_j.
     if (threadIdx.x == 0 && !*abort) {
       tc_fence_after();
-      if (j + 1 < n_tiles) issue_s(j + 1);
-      if (!*abort) issue_pv(j);
+      issue_pv(j);
     }
   }
 
