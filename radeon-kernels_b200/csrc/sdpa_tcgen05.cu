@@ -47,7 +47,8 @@ namespace rk {
 namespace sdpa {
 
 constexpr int BM = 128;  // query rows per CTA
-constexpr int THREADS = 512;
+constexpr int SOFTMAX_WARPS = 16;
+constexpr int THREADS = 32 * (SOFTMAX_WARPS + 1);  // + the producer warp
 constexpr int UMMA_K = 16;
 
 // SPLIT (bf16): P is stored as P_hi + P_lo, both bf16, and O += P_hi V + P_lo V, so the
@@ -77,6 +78,7 @@ struct __align__(8) Bars {
   uint64_t v_full[2];
   uint64_t s_done[2];  // one per S buffer (tile t: buffer t & 1)
   uint64_t o_done;
+  uint64_t p_full;  // one arrival per softmax warp: P_t is in shared memory
   uint64_t drain;
   uint32_t tmem_base;
   int abort;  // set when a wait gave up; every later wait returns at once
@@ -90,6 +92,11 @@ struct Params {
   int causal;
   float scale_log2;  // scale * log2(e)
 };
+
+// Named barrier of the four softmax warps that share TMEM lane quarter q (ids 1..4).
+__device__ __forceinline__ void quarter_sync(int q) {
+  asm volatile("bar.sync %0, 128;" ::"r"(q + 1) : "memory");
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -110,8 +117,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   Bars* bars = reinterpret_cast<Bars*>(sp + (C::SPLIT ? 2 : 1) * C::P_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Four warps share each 32-row TMEM lane quarter; each takes a quarter of the columns.
-  const int quarter = warp & 3, slice = warp >> 2;
+  const bool producer = warp == SOFTMAX_WARPS;  // TMA + MMA issue (one lane)
+  // Softmax warps: four share each 32-row TMEM lane quarter, each a quarter of the columns.
+  const int quarter = warp & 3, slice = (warp >> 2) & 3;
   constexpr int SLICE = BN / 4;  // score columns per thread
   constexpr int OSL = D / 4;     // output columns per thread
   // Heavier (later, under the causal mask) query tiles first.
@@ -131,10 +139,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&bars->k_full[s]), 1);
       mbar_init(smem_u32(&bars->v_full[s]), 1);
+      mbar_init(smem_u32(&bars->s_done[s]), 1);
     }
-    mbar_init(smem_u32(&bars->s_done[0]), 1);
-    mbar_init(smem_u32(&bars->s_done[1]), 1);
     mbar_init(smem_u32(&bars->o_done), 1);
+    mbar_init(smem_u32(&bars->p_full), SOFTMAX_WARPS);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
     fence_barrier_init();
@@ -150,52 +158,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);  // this warp's lanes
   // TMEM columns: S buffers [0, BN) and [BN, 2 BN), O [O_COL, O_COL + D), exchange slots
-  // [X_COL, X_COL + 8).
+  // [X_COL, X_COL + 12): row maxima by tile parity (2 x 4) and the row-sum shares (4).
   constexpr int O_COL = 2 * BN, X_COL = 384;
   static_assert(O_COL + D <= X_COL, "TMEM column plan");
+  const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);  // this warp's lanes
   const uint32_t t_o = t_lane + O_COL;
   const uint32_t t_x = t_lane + X_COL;
   pdl_begin();  // global memory is touched only after this
-
-  // Bulk-copy bookkeeping (thread 0): loads issued into each stage, and those waited for.
-  uint32_t k_issued[2] = {0, 0}, v_issued[2] = {0, 0}, k_used[2] = {0, 0}, v_used[2] = {0, 0};
-  bool q_issued = false, q_used = false;
-  auto load_k = [&](int t) {
-    const int st = t % STAGES;
-    const uint32_t bar = smem_u32(&bars->k_full[st]);
-    mbar_arrive_expect_tx(bar, C::K_BYTES);
-#pragma unroll
-    for (int c = 0; c < C::CHUNKS; ++c)
-      tma_load_3d(smem_u32(sk + st * C::K_BYTES + c * BN * 128), &tmap_k, bar, c * 64, t * BN,
-                  kv_mat);
-    ++k_issued[st];
-  };
-  auto load_v = [&](int t) {
-    const int st = t % STAGES;
-    const uint32_t bar = smem_u32(&bars->v_full[st]);
-    mbar_arrive_expect_tx(bar, C::V_BYTES);
-#pragma unroll
-    for (int kb = 0; kb < BN / 64; ++kb)
-#pragma unroll
-      for (int c = 0; c < C::CHUNKS; ++c)
-        tma_load_3d(smem_u32(sv_s + st * C::V_BYTES + (kb * C::CHUNKS + c) * 8192), &tmap_v, bar,
-                    c * 64, t * BN + kb * 64, kv_mat);
-    ++v_issued[st];
-  };
-  if (threadIdx.x == 0) {
-    const uint32_t bar = smem_u32(&bars->q_full);
-    mbar_arrive_expect_tx(bar, C::Q_BYTES);
-#pragma unroll
-    for (int c = 0; c < C::CHUNKS; ++c)
-      tma_load_3d(smem_u32(sq + c * BM * 128), &tmap_q, bar, c * 64, qtile * BM, q_mat);
-    q_issued = true;
-    for (int t = 0; t < STAGES && t < n_tiles; ++t) {
-      load_k(t);
-      load_v(t);
-    }
-  }
 
   constexpr uint32_t IDESC_S =
       umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, BN, false, false);
@@ -203,190 +173,260 @@ __global__ void __launch_bounds__(THREADS, 1)
       umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, D, false, true);
   int never = 0;
   volatile int* abort = &bars->abort;
-  // A wait that gives up records why and sets the abort flag; the CTA then runs on without
-  // issuing more work (every later wait returns at once), so every thread keeps reaching
-  // every barrier, and the output is not written.
+  // A wait that gives up records why and sets the abort flag; every later wait returns at
+  // once and no more work is issued, so every thread still reaches every barrier, and the
+  // output is not written.
   auto fail = [&](uint32_t code) {
     *abort = 1;
-    if ((threadIdx.x & 31) == 0) atomicOr(ctl.status, code);
-  };
-  // Row state (identical in the four warps that share a row): the maximum the exponentials
-  // are taken against, and this warp's share of the row sum.
-  float m_use = -INFINITY, l_part = 0.f;
-  int issued_mma = 0;  // thread 0: tcgen05.commit groups issued
-
-  // Thread 0: S_t = Q K_t^T into S buffer t & 1 (whose previous tile, t - 2, every thread
-  // has read: S_t is issued after the barrier that closes tile t - 1).
-  auto issue_s = [&](int t) {
-    const int st = t % STAGES;
-    bool got = true;
-    if (t == 0) got = q_used = mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, abort);
-    got = got && mbar_wait_bounded(smem_u32(&bars->k_full[st]), k_used[st] & 1u, ctl.timeout_ns, abort);
-    if (!got) {
-      fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
-      return;
-    }
-    ++k_used[st];
-    tc_fence_after();
-    const uint32_t q0 = smem_u32(sq), k0 = smem_u32(sk + st * C::K_BYTES);
-#pragma unroll
-    for (int kk = 0; kk < D / UMMA_K; ++kk) {
-      const uint32_t off_q = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-      const uint32_t off_k = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-      tc_mma_f16(tmem + (t & 1) * BN, umma_desc_sw128(q0 + off_q, 16, 1024),
-                 umma_desc_sw128(k0 + off_k, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-    }
-    tc_commit(smem_u32(&bars->s_done[t & 1]));
-    ++issued_mma;
-  };
-  // Thread 0: O += P V_t (P in shared memory, V_t in its stage).
-  auto issue_pv = [&](int t) {
-    const int st = t % STAGES;
-    if (!mbar_wait_bounded(smem_u32(&bars->v_full[st]), v_used[st] & 1u, ctl.timeout_ns, abort)) {
-      fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
-      return;
-    }
-    ++v_used[st];
-    const uint32_t p0 = smem_u32(sp), plo0 = smem_u32(sp_lo), v0 = smem_u32(sv_s + st * C::V_BYTES);
-#pragma unroll
-    for (int kk = 0; kk < BN / UMMA_K; ++kk) {
-      const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-      const uint64_t b = umma_desc_sw128(v0 + (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048, 8192, 1024);
-      tc_mma_f16(tmem + O_COL, umma_desc_sw128(p0 + a_off, 16, 1024), b, IDESC_O,
-                 (t > 0 || kk > 0) ? 1u : 0u);
-      if (C::SPLIT) tc_mma_f16(tmem + O_COL, umma_desc_sw128(plo0 + a_off, 16, 1024), b, IDESC_O, 1u);
-    }
-    tc_commit(smem_u32(&bars->o_done));
-    ++issued_mma;
+    atomicOr(ctl.status, code);
   };
 
-  if (threadIdx.x == 0) issue_s(0);
-  // Keys this row may attend: below the sequence end and, causal, up to the row itself.
-  const int key_limit = p.causal ? min(p.seq, q_pos + 1) : p.seq;
+  if (producer) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      // Bulk-copy bookkeeping: loads issued into each stage, and those waited for.
+      uint32_t k_issued[2] = {0, 0}, v_issued[2] = {0, 0}, k_used[2] = {0, 0}, v_used[2] = {0, 0};
+      bool q_used = false;
+      int issued_mma = 0;
+      auto load_k = [&](int t) {
+        const int st = t % STAGES;
+        const uint32_t bar = smem_u32(&bars->k_full[st]);
+        mbar_arrive_expect_tx(bar, C::K_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_3d(smem_u32(sk + st * C::K_BYTES + c * BN * 128), &tmap_k, bar, c * 64, t * BN,
+                      kv_mat);
+        ++k_issued[st];
+      };
+      auto load_v = [&](int t) {
+        const int st = t % STAGES;
+        const uint32_t bar = smem_u32(&bars->v_full[st]);
+        mbar_arrive_expect_tx(bar, C::V_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < BN / 64; ++kb)
+#pragma unroll
+          for (int c = 0; c < C::CHUNKS; ++c)
+            tma_load_3d(smem_u32(sv_s + st * C::V_BYTES + (kb * C::CHUNKS + c) * 8192), &tmap_v, bar,
+                        c * 64, t * BN + kb * 64, kv_mat);
+        ++v_issued[st];
+      };
+      // S_t = Q K_t^T into S buffer t & 1.
+      auto issue_s = [&](int t) {
+        const int st = t % STAGES;
+        bool got = true;
+        if (t == 0) got = q_used = mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, abort);
+        got = got && mbar_wait_bounded(smem_u32(&bars->k_full[st]), k_used[st] & 1u, ctl.timeout_ns, abort);
+        if (!got) return fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+        ++k_used[st];
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(sq), k0 = smem_u32(sk + st * C::K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / UMMA_K; ++kk) {
+          const uint32_t off_q = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          const uint32_t off_k = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
+          tc_mma_f16(tmem + (t & 1) * BN, umma_desc_sw128(q0 + off_q, 16, 1024),
+                     umma_desc_sw128(k0 + off_k, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&bars->s_done[t & 1]));
+        ++issued_mma;
+      };
+      // O += P_t V_t.
+      auto issue_pv = [&](int t) {
+        const int st = t % STAGES;
+        if (!mbar_wait_bounded(smem_u32(&bars->v_full[st]), v_used[st] & 1u, ctl.timeout_ns, abort))
+          return fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+        ++v_used[st];
+        tc_fence_after();
+        const uint32_t p0 = smem_u32(sp), plo0 = smem_u32(sp_lo), v0 = smem_u32(sv_s + st * C::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / UMMA_K; ++kk) {
+          const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+          const uint64_t b =
+              umma_desc_sw128(v0 + (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048, 8192, 1024);
+          tc_mma_f16(tmem + O_COL, umma_desc_sw128(p0 + a_off, 16, 1024), b, IDESC_O,
+                     (t > 0 || kk > 0) ? 1u : 0u);
+          if (C::SPLIT) tc_mma_f16(tmem + O_COL, umma_desc_sw128(plo0 + a_off, 16, 1024), b, IDESC_O, 1u);
+        }
+        tc_commit(smem_u32(&bars->o_done));
+        ++issued_mma;
+      };
 
-  // Per tile j: S_{j+1} is issued as soon as S_j has landed, into the other S buffer, so the
-  // tensor core computes the next scores during this tile's softmax; P V_{j-1} runs under
-  // its first half too -- each thread waits for it only before it overwrites P or rescales O.
-  for (int j = 0; j < n_tiles; ++j) {
-    if (!mbar_wait_bounded(smem_u32(&bars->s_done[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort))
-      fail(RK_DEV_ERR_TIMEOUT_MMA);
-    tc_fence_after();
-    if (threadIdx.x == 0 && !*abort) {
-      if (j + STAGES < n_tiles) load_k(j + STAGES);  // K_j's stage is free again
-      if (j + 1 < n_tiles) issue_s(j + 1);
-    }
-    const uint32_t t_s = t_lane + (j & 1) * BN;
-    const int valid = key_limit - (j * BN + slice * SLICE);  // keys i < valid are attended
-    float sv[SLICE];
-    float mx = -INFINITY;
-    {
-      uint32_t r[SLICE];
+      {
+        const uint32_t bar = smem_u32(&bars->q_full);
+        mbar_arrive_expect_tx(bar, C::Q_BYTES);
 #pragma unroll
-      for (int c = 0; c < SLICE / 16; ++c)
-        tmem_ld_32x32b_x16(t_s + slice * SLICE + c * 16, *reinterpret_cast<uint32_t(*)[16]>(r + c * 16));
-      tmem_ld_wait();
-#pragma unroll
-      for (int i = 0; i < SLICE; ++i) {
-        sv[i] = i < valid ? __uint_as_float(r[i]) * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[i]);
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_3d(smem_u32(sq + c * BM * 128), &tmap_q, bar, c * 64, qtile * BM, q_mat);
+      }
+      for (int t = 0; t < STAGES && t < n_tiles; ++t) {
+        load_k(t);
+        load_v(t);
+      }
+      issue_s(0);
+      for (int j = 0; j < n_tiles && !*abort; ++j) {
+        // V_{j+1} into the stage of V_{j-1}, once P V_{j-1} has completed.
+        if (j >= 1 && j + 1 < n_tiles) {
+          if (!mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, abort)) {
+            fail(RK_DEV_ERR_TIMEOUT_MMA);
+            break;
+          }
+          load_v(j + 1);
+        }
+        // S_{j+1} into the buffer of S_{j-1}: every softmax warp has read it (they wrote
+        // P_{j-1}, which P V_{j-1} consumed before this iteration).
+        if (j + 1 < n_tiles) issue_s(j + 1);
+        // K_{j+2} into the stage of K_j, once S_j has completed.
+        if (j + 2 < n_tiles && !*abort) {
+          if (!mbar_wait_bounded(smem_u32(&bars->s_done[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort)) {
+            fail(RK_DEV_ERR_TIMEOUT_MMA);
+            break;
+          }
+          load_k(j + 2);
+        }
+        // P_j from all sixteen softmax warps, then O += P_j V_j.
+        if (*abort) break;
+        if (!mbar_wait_bounded(smem_u32(&bars->p_full), j & 1, ctl.timeout_ns, abort)) {
+          fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+          break;
+        }
+        issue_pv(j);
+      }
+      // ---- drain: every MMA and bulk copy issued by this CTA completes before exit.
+      if (issued_mma > 0) {
+        tc_commit(smem_u32(&bars->drain));
+        if (!mbar_wait_bounded(smem_u32(&bars->drain), 0, ctl.timeout_ns, &never))
+          atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+      }
+      if (!q_used && !mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, &never))
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+      for (int s = 0; s < STAGES; ++s) {
+        // Loads issued but never waited for: wait for the last one of each stage.
+        if (k_issued[s] > k_used[s] &&
+            !mbar_wait_bounded(smem_u32(&bars->k_full[s]), (k_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
+          atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+        if (v_issued[s] > v_used[s] &&
+            !mbar_wait_bounded(smem_u32(&bars->v_full[s]), (v_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
+          atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
       }
     }
-    // Row maximum over the four warps of the lane quarter, through four spare TMEM columns.
-    tmem_st_32x32b_x1(t_x + slice, __float_as_uint(mx));
-    tmem_st_wait();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    float m_tile;
-    {
-      uint32_t r[4];
-      tmem_ld_32x32b_x4(t_x, r);
-      tmem_ld_wait();
-      m_tile = fmaxf(fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1])),
-                     fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3])));
-    }
-    // Lazy rescaling: the exponentials keep the old maximum until the row maximum exceeds
-    // it by more than 2^8 (P <= 256, exact enough in fp16 and in bf16 hi + lo).
-    float alpha = 1.f;
-    if (m_tile > m_use + 8.f) {
-      alpha = ex2_approx(m_use - m_tile);  // 0 for the first keys of the row
-      m_use = m_tile;
-    }
-    const float m_sub = m_use == -INFINITY ? 0.f : m_use;
-
-    // ---- P = 2^(s - m), rounded (SPLIT: hi + lo), kept in registers for now.  The row sum
-    // adds the fp32 values (within 2^-16 of hi + lo; fp16 P within 2^-11).
-    float psum = 0.f;
-    uint32_t hi[SLICE / 2], lo[SLICE / 2];
-#pragma unroll
-    for (int i = 0; i < SLICE; i += 2) {
-      const float e0 = ex2_approx(sv[i] - m_sub), e1 = ex2_approx(sv[i + 1] - m_sub);
-      psum += e0 + e1;
-      hi[i / 2] = Pack2<T>::from_floats(e0, e1);
-      if (C::SPLIT) {
-        const float2 h2 = Pack2<T>::to_floats(hi[i / 2]);
-        lo[i / 2] = Pack2<T>::from_floats(e0 - h2.x, e1 - h2.y);
-      }
-    }
-    l_part = l_part * alpha + psum;
-
-    // ---- P V_{j-1} must be done before P is overwritten and O rescaled.
-    if (j > 0) {
-      if (!mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, abort))
+  } else {
+    // -------------------------------------------------------------- softmax
+    // Row state (identical in the four warps that share a row): the maximum the
+    // exponentials are taken against, and this warp's share of the row sum.
+    float m_use = -INFINITY, l_part = 0.f;
+    const int key_limit = p.causal ? min(p.seq, q_pos + 1) : p.seq;  // keys this row attends
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!mbar_wait_bounded(smem_u32(&bars->s_done[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort))
         fail(RK_DEV_ERR_TIMEOUT_MMA);
       tc_fence_after();
-      if (threadIdx.x == 0 && !*abort && j - 1 + STAGES < n_tiles) load_v(j - 1 + STAGES);
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      const uint32_t t_s = t_lane + (j & 1) * BN;
+      const int valid = key_limit - (j * BN + slice * SLICE);  // keys i < valid are attended
+      float sv[SLICE];
+      float mx = -INFINITY;
+      {
+        uint32_t r[SLICE];
 #pragma unroll
-        for (int c = 0; c < OSL / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
-          tmem_ld_wait();
+        for (int c = 0; c < SLICE / 16; ++c)
+          tmem_ld_32x32b_x16(t_s + slice * SLICE + c * 16, *reinterpret_cast<uint32_t(*)[16]>(r + c * 16));
+        tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st_32x32b_x16(t_o + slice * OSL + c * 16, r);
+        for (int i = 0; i < SLICE; ++i) {
+          sv[i] = i < valid ? __uint_as_float(r[i]) * p.scale_log2 : -INFINITY;
+          mx = fmaxf(mx, sv[i]);
         }
-        tmem_st_wait();
       }
-    }
-    {
-      // This thread's keys: 64-key chunk kf / 64, 16-byte units (kf % 64) / 8 onwards,
-      // swizzled by row.
-      const int kf = slice * SLICE;
-      const int chunk_off = (kf >> 6) * (BM * 128) + row * 128;
-#pragma unroll
-      for (int u = 0; u < SLICE / 8; ++u) {
-        const int unit_off = chunk_off + (((((kf & 63) >> 3) + u) ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(sp + unit_off) =
-            make_uint4(hi[4 * u], hi[4 * u + 1], hi[4 * u + 2], hi[4 * u + 3]);
-        if (C::SPLIT)
-          *reinterpret_cast<uint4*>(sp_lo + unit_off) =
-              make_uint4(lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-
-    // ---- thread 0: O += P V_j.
-    if (threadIdx.x == 0 && !*abort) {
+      // Row maximum over the four warps of the lane quarter, through TMEM slots of this
+      // tile's parity (a warp writes tile j+2's slots only after the barrier of tile j+1,
+      // which its peers reach after reading tile j's).
+      const uint32_t xs = t_x + (j & 1) * 4;
+      tmem_st_32x32b_x1(xs + slice, __float_as_uint(mx));
+      tmem_st_wait();
+      tc_fence_before();
+      quarter_sync(quarter);
       tc_fence_after();
-      issue_pv(j);
-    }
-  }
+      float m_tile;
+      {
+        uint32_t r[4];
+        tmem_ld_32x32b_x4(xs, r);
+        tmem_ld_wait();
+        m_tile = fmaxf(fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                       fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3])));
+      }
+      // Lazy rescaling: the exponentials keep the old maximum until the row maximum
+      // exceeds it by more than 2^8 (P <= 256, exact enough in fp16 and in bf16 hi + lo).
+      float alpha = 1.f;
+      if (m_tile > m_use + 8.f) {
+        alpha = ex2_approx(m_use - m_tile);  // 0 for the first keys of the row
+        m_use = m_tile;
+      }
+      const float m_sub = m_use == -INFINITY ? 0.f : m_use;
 
-  // ---- epilogue: O / l  (l = the four warps' shares, added in slice order)
-  if (!mbar_wait_bounded(smem_u32(&bars->o_done), (n_tiles - 1) & 1, ctl.timeout_ns, abort))
-    fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
-  tc_fence_after();
-  tmem_st_32x32b_x1(t_x + 4 + slice, __float_as_uint(l_part));
-  tmem_st_wait();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  {
+      // P = 2^(s - m), rounded (SPLIT: hi + lo), in registers until P V_{j-1} is done.  The
+      // row sum adds the fp32 values (within 2^-16 of hi + lo; fp16 P within 2^-11).
+      float psum = 0.f;
+      uint32_t hi[SLICE / 2], lo[SLICE / 2];
+#pragma unroll
+      for (int i = 0; i < SLICE; i += 2) {
+        const float e0 = ex2_approx(sv[i] - m_sub), e1 = ex2_approx(sv[i + 1] - m_sub);
+        psum += e0 + e1;
+        hi[i / 2] = Pack2<T>::from_floats(e0, e1);
+        if (C::SPLIT) {
+          const float2 h2 = Pack2<T>::to_floats(hi[i / 2]);
+          lo[i / 2] = Pack2<T>::from_floats(e0 - h2.x, e1 - h2.y);
+        }
+      }
+      l_part = l_part * alpha + psum;
+
+      if (j > 0) {
+        if (!mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, abort))
+          fail(RK_DEV_ERR_TIMEOUT_MMA);
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < OSL / 16; ++c) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st_32x32b_x16(t_o + slice * OSL + c * 16, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      {
+        // This thread's keys: 64-key chunk kf / 64, 16-byte units (kf % 64) / 8 onwards,
+        // swizzled by row.
+        const int kf = slice * SLICE;
+        const int chunk_off = (kf >> 6) * (BM * 128) + row * 128;
+#pragma unroll
+        for (int u = 0; u < SLICE / 8; ++u) {
+          const int unit_off = chunk_off + (((((kf & 63) >> 3) + u) ^ (row & 7)) << 4);
+          *reinterpret_cast<uint4*>(sp + unit_off) =
+              make_uint4(hi[4 * u], hi[4 * u + 1], hi[4 * u + 2], hi[4 * u + 3]);
+          if (C::SPLIT)
+            *reinterpret_cast<uint4*>(sp_lo + unit_off) =
+                make_uint4(lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
+        }
+      }
+      // P_j (and O's rescaling) of this warp is in place: one arrival per warp.
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->p_full));
+    }
+
+    // ---- epilogue: O / l  (l = the four warps' shares, added in slice order)
+    if (!mbar_wait_bounded(smem_u32(&bars->o_done), (n_tiles - 1) & 1, ctl.timeout_ns, abort))
+      fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
+    tc_fence_after();
+    tmem_st_32x32b_x1(t_x + 8 + slice, __float_as_uint(l_part));
+    tmem_st_wait();
+    tc_fence_before();
+    quarter_sync(quarter);
+    tc_fence_after();
     uint32_t lr[4];
-    tmem_ld_32x32b_x4(t_x + 4, lr);
+    tmem_ld_32x32b_x4(t_x + 8, lr);
     tmem_ld_wait();
     const float l = ((__uint_as_float(lr[0]) + __uint_as_float(lr[1])) + __uint_as_float(lr[2])) +
                     __uint_as_float(lr[3]);
@@ -412,26 +452,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
 
-  // ---- drain: every MMA and bulk copy issued by this CTA completes before exit.
-  if (threadIdx.x == 0) {
-    if (issued_mma > 0) {
-      tc_commit(smem_u32(&bars->drain));
-      if (!mbar_wait_bounded(smem_u32(&bars->drain), 0, ctl.timeout_ns, &never))
-        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
-    }
-    if (q_issued && !q_used &&
-        !mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, &never))
-      atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
-    for (int s = 0; s < STAGES; ++s) {
-      // Loads issued but never waited for: wait for the last one of each stage.
-      if (k_issued[s] > k_used[s] &&
-          !mbar_wait_bounded(smem_u32(&bars->k_full[s]), (k_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
-        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
-      if (v_issued[s] > v_used[s] &&
-          !mbar_wait_bounded(smem_u32(&bars->v_full[s]), (v_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
-        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
-    }
-  }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
