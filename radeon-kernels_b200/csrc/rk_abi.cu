@@ -44,6 +44,16 @@ thread_local std::string g_last_error;
 DeviceInfo* current_device_info() {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  // Make the device's primary context current on this thread.  A thread whose device was
+  // never set explicitly (PyTorch's autograd worker threads, for instance: device 0 is
+  // already "current", so no cudaSetDevice happens) has no current driver context until
+  // its first runtime launch, and the driver calls made here before any launch --
+  // cuTensorMapEncodeTiled -- then fail with CUDA_ERROR_INVALID_CONTEXT.
+  thread_local int bound_device = -1;
+  if (bound_device != dev) {
+    if (cudaSetDevice(dev) != cudaSuccess) return nullptr;
+    bound_device = dev;
+  }
   DeviceInfo* d = &g_devices[dev];
   std::call_once(d->once, [d, dev] {
     cudaDeviceProp prop;

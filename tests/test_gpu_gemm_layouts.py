@@ -9,6 +9,8 @@ the C oracle fed the logical (materialised) operands.  Outputs land inside a sen
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -195,3 +197,35 @@ def test_gemv_backward_and_transposed_weight():
     out2 = rk.gemv(x.cuda(), w_view)
     o_bits, o32 = oracle.gemm(to_bits(x), to_bits(w.t().contiguous()), "bf16")
     oracle.assert_parity(to_bits(out2), o_bits, o32, "bf16")
+
+
+def test_fresh_thread_encodes_tensor_maps():
+    """A thread that never set its device (as PyTorch's autograd workers) calls the library
+    first: the tensor-map encode must find a current context.  Shapes no other test uses, so
+    no cached map hides the encode."""
+
+    import threading
+
+    import torch
+
+    a, b, a_stored, b_stored = _operands("nt", 72, 136, 104, "bf16")
+    a_dev, b_dev = a_stored.cuda(), b_stored.cuda()
+    c = torch.empty(72, 136, dtype=torch.bfloat16, device="cuda")
+    torch.cuda.synchronize()
+    result = {}
+
+    lib = _native.library()
+    ptrs = [ctypes.c_void_p(t.data_ptr()) for t in (a_dev, b_dev, c)]
+
+    def run():  # no torch call on this thread: the library is its first CUDA user
+        result["status"] = lib.rk_gemm_layout(*ptrs, 72, 136, 104, 1, 1, GEMM["tc_1sm"], None)
+        result["error"] = lib.rk_last_error()
+
+    worker = threading.Thread(target=run)
+    worker.start()
+    worker.join()
+    assert result["status"] == _native.RK_OK, result
+    torch.cuda.synchronize()
+    c_bits, c32 = oracle.gemm(to_bits(a), to_bits(b), "bf16")
+    oracle.assert_parity(to_bits(c), c_bits, c32, "bf16")
+
