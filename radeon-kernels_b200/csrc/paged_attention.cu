@@ -31,6 +31,8 @@
 // (benchmarks/paged_attention/native_paged_attention.hip:192-283).
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include <cmath>
 
 #include "rk_device.cuh"
@@ -351,13 +353,25 @@ rk_status launch_d(Params prm, const Plan& pl, int64_t head_dim, cudaStream_t s)
 
 }  // namespace pa
 
+namespace {
+std::atomic<int> g_paged_path{0};  // 0 automatic, 1 CUDA cores, 2 tensor cores
+}  // namespace
+
+void paged_attention_set_path(int path) { g_paged_path.store(path >= 0 && path <= 2 ? path : 0); }
+
+// The larger of the two kernels' needs: which kernel runs also depends on pointers and
+// dtype, which this query does not see.
 size_t paged_attention_workspace_bytes(int64_t batch, int64_t hq, int64_t hkv, int64_t head_dim,
                                        int64_t max_blocks, int64_t block_size) {
   if (batch <= 0 || hq <= 0 || hkv <= 0 || hq % hkv != 0 || max_blocks <= 0 || block_size <= 0)
     return 0;
-  const pa::Plan pl = pa::plan(batch, hq, hkv, max_blocks * block_size, device_sm_count());
-  if (pl.partitions == 1) return 0;
-  return static_cast<size_t>(batch) * hq * pl.partitions * (head_dim + 2) * sizeof(float);
+  const int64_t max_ctx = max_blocks * block_size;
+  const pa::Plan pl = pa::plan(batch, hq, hkv, max_ctx, device_sm_count());
+  int tc_parts = 1, tc_tokens = 0;
+  paged_attention_tc_plan(batch, hkv, max_ctx, device_sm_count(), &tc_parts, &tc_tokens);
+  const int parts = pl.partitions > tc_parts ? pl.partitions : tc_parts;
+  if (parts == 1) return 0;
+  return static_cast<size_t>(batch) * hq * parts * (head_dim + 2) * sizeof(float);
 }
 
 rk_status paged_attention_launch(const void* query, const void* key_cache, const void* value_cache,
@@ -394,6 +408,54 @@ rk_status paged_attention_launch(const void* query, const void* key_cache, const
   prm.part_tokens = pl.part_tokens;
   prm.scale = scale;
   const bool bf16 = dt == RK_DTYPE_BF16;
+  const int path = g_paged_path.load();
+  const bool tc_ok = paged_attention_tc_supported(key_cache, value_cache, hq, hkv, head_dim, block_size);
+  if (path == 2 && !tc_ok) return RK_ERR_UNSUPPORTED;
+  if (tc_ok && path != 1) {
+    // Tensor-core kernel; its partitions (whole 128-position tiles) go through the same
+    // workspace layout and merge kernel.
+    PagedTcArgs a{};
+    a.q = query;
+    a.k = key_cache;
+    a.v = value_cache;
+    a.tables = block_tables;
+    a.lens = context_lengths;
+    a.out = out;
+    a.batch = batch;
+    a.hq = hq;
+    a.hkv = hkv;
+    a.head_dim = head_dim;
+    a.num_blocks = num_blocks;
+    a.block_size = block_size;
+    a.max_blocks = max_blocks;
+    a.index_bits = index_bits;
+    a.scale = scale;
+    a.dt = dt;
+    paged_attention_tc_plan(batch, hkv, max_blocks * block_size, device_sm_count(), &a.partitions,
+                            &a.part_tokens);
+    if (a.partitions > 1) {
+      a.part_acc = static_cast<float*>(workspace);
+      a.part_ml = static_cast<float*>(workspace) + batch * hq * a.partitions * head_dim;
+    }
+    if (batch > 65535 || hkv > 65535) return RK_ERR_UNSUPPORTED;
+    rk_status st = paged_attention_tc_launch(a, s);
+    if (st != RK_OK || a.partitions == 1) return st;
+    prm.partitions = a.partitions;
+    prm.part_acc = a.part_acc;
+    prm.part_ml = a.part_ml;
+    cudaError_t e = cudaSuccess;
+    switch (head_dim) {
+      case 64:
+        e = bf16 ? launch_kernel(pa::paged_merge_kernel<__nv_bfloat16, 64>, dim3(static_cast<unsigned>(batch * hq)), dim3(64), 0, s, 0, prm)
+                 : launch_kernel(pa::paged_merge_kernel<__half, 64>, dim3(static_cast<unsigned>(batch * hq)), dim3(64), 0, s, 0, prm);
+        break;
+      default:
+        e = bf16 ? launch_kernel(pa::paged_merge_kernel<__nv_bfloat16, 128>, dim3(static_cast<unsigned>(batch * hq)), dim3(128), 0, s, 0, prm)
+                 : launch_kernel(pa::paged_merge_kernel<__half, 128>, dim3(static_cast<unsigned>(batch * hq)), dim3(128), 0, s, 0, prm);
+    }
+    note_launch();
+    return cuda_status(e);
+  }
   if (index_bits == 32)
     return bf16 ? pa::launch_d<__nv_bfloat16, int32_t>(prm, pl, head_dim, s)
                 : pa::launch_d<__half, int32_t>(prm, pl, head_dim, s);

@@ -408,6 +408,8 @@ rk_status rk_sdpa(const void* query, const void* key, const void* value, void* o
                      is_causal != 0, scale, dt, reinterpret_cast<cudaStream_t>(stream));
 }
 
+void rk_paged_attention_set_path(int path) { paged_attention_set_path(path); }
+
 void rk_norm_backward_set_ctas_per_sm(int ctas_per_sm) {
   norm_backward_set_ctas_per_sm(ctas_per_sm >= 1 && ctas_per_sm <= 32 ? ctas_per_sm : 0);
 }

@@ -126,6 +126,23 @@ rk_status rms_norm_backward_launch(const void* dy, const void* x, const void* w,
                                    void* workspace, size_t workspace_bytes, cudaStream_t s);
 size_t rms_norm_backward_workspace_bytes(int64_t tokens, int64_t hidden);
 void norm_backward_set_ctas_per_sm(int ctas);
+// Paged decode attention on the tensor cores (paged_attention_tc.cu).
+struct PagedTcArgs {
+  const void *q, *k, *v, *tables, *lens;
+  void* out;
+  float *part_acc, *part_ml;
+  int64_t batch, hq, hkv, head_dim, num_blocks, block_size, max_blocks;
+  int partitions, part_tokens, index_bits;
+  float scale;
+  rk_dtype dt;
+};
+bool paged_attention_tc_supported(const void* key_cache, const void* value_cache, int64_t hq,
+                                  int64_t hkv, int64_t head_dim, int64_t block_size);
+void paged_attention_tc_plan(int64_t batch, int64_t hkv, int64_t max_ctx, int sms, int* partitions,
+                             int* part_tokens);
+rk_status paged_attention_tc_launch(const PagedTcArgs& a, cudaStream_t s);
+void paged_attention_set_path(int path);  // 0 automatic, 1 CUDA cores, 2 tensor cores
+
 // Prefill attention (sdpa_tcgen05.cu).
 rk_status sdpa_launch(const void* q, const void* k, const void* v, void* out, int64_t B,
                       int64_t Hq, int64_t Hkv, int64_t S, int64_t D, bool causal, float scale,

@@ -490,6 +490,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "add_rms_norm gradients -> [grad_input, grad_residual, grad_weight]", py::arg("grad"),
         py::arg("grad_residual_out"), py::arg("residual_out"), py::arg("weight"), py::arg("eps"),
         py::arg("weight_grad") = true);
+  m.def("paged_attention_set_path", [](int path) { rk_paged_attention_set_path(path); });
   m.def("norm_backward_set_ctas_per_sm", [](int c) { rk_norm_backward_set_ctas_per_sm(c); });
   m.def("device_status", &device_status, "read and clear the device status word");
   m.def("set_wait_timeout_ns", [](uint64_t ns) { rk_set_wait_timeout_ns(ns); });

@@ -85,6 +85,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_rms_norm_backward.restype = cint
     lib.rk_add_rms_norm_backward.argtypes = [vp] * 7 + [i64, i64, ctypes.c_float, cint, vp, ctypes.c_size_t, vp]
     lib.rk_add_rms_norm_backward.restype = cint
+    lib.rk_paged_attention_set_path.argtypes = [cint]
+    lib.rk_paged_attention_set_path.restype = None
     lib.rk_norm_backward_set_ctas_per_sm.argtypes = [cint]
     lib.rk_norm_backward_set_ctas_per_sm.restype = None
     lib.rk_gemv.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, vp]
