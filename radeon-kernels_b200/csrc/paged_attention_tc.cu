@@ -13,15 +13,18 @@
 // so each thread owns one position (TMEM lane) for the softmax -- a handful of exponentials
 // per tile -- and one output dimension (O^T lane) for the rescaling and the epilogue.
 //
-// One CTA (128 threads) per (context partition, KV head, sequence) serves every query head
-// of the GQA group (padded to N = 16; the padding rows of Q are zero).  Warp 0 streams the
-// partition's 128-position tiles: one TMA box per cache block and 64-dim chunk, through a
+// One CTA per (context partition, KV head, sequence) serves every query head of the GQA
+// group (padded to N = 16; the padding rows of Q are zero): four softmax warps, a load warp
+// and an MMA warp that meet on mbarriers only.  The load warp streams the partition's
+// 128-position tiles: one TMA box per cache block and 64-dim chunk, through a
 // 4-D tensor map over [num_blocks, block_size, kv_heads, head_dim]; a block index that is out
 // of range, or a block past the context, is loaded from the out-of-range coordinate
 // num_blocks, which reads as zero (no fault, no stale bytes, full byte count), and its
 // positions are masked; an out-of-range index inside the context is reported through the
 // status word (RK_DEV_ERR_BAD_INDEX), as the CUDA-core kernel does.  A ring of STAGES tiles
-// keeps the HBM stream going while the softmax runs.  Online softmax per head in fp32
+// keeps the HBM stream going while the softmax runs.  (A first version with the loads and
+// MMAs issued from the softmax warps between CTA barriers took 4-5 us per tile, slower than
+// the CUDA-core kernel.)  Online softmax per head in fp32
 // (base 2, hardware ex2), lazy rescaling of O^T (only when a head's maximum grows by more
 // than 2^8); bf16 probabilities as P_hi + P_lo (two MMAs) so they keep ~16 significant bits.
 // Partition results go to the workspace in the CUDA-core kernel's format (natural-log
@@ -44,7 +47,7 @@ namespace patc {
 
 constexpr int TILE = 128;  // positions per tile (TMEM lanes, MMA M)
 constexpr int NG = 16;     // query heads per CTA, padded (MMA N)
-constexpr int THREADS = 128;
+constexpr int THREADS = 192;  // 4 softmax warps, a load warp, an MMA warp
 constexpr int UMMA_K = 16;
 constexpr float LN2 = 0.6931471805599453f;
 
@@ -60,7 +63,7 @@ struct Cfg {
   static constexpr int P_BYTES = 2 * NG * 128;         // P^T: 2 position chunks x [16 x 128 B]
   static constexpr int TMEM_COLS = 64;                 // S^T x 2 (16 each), O^T (16)
   static constexpr int SMEM = 1024 + STAGES * (K_BYTES + V_BYTES) + Q_BYTES +
-                              (SPLIT ? 2 : 1) * P_BYTES + 2048;
+                              2 * (SPLIT ? 2 : 1) * P_BYTES + 2048;  // P^T by tile parity
   static_assert(D == 64 || D == 128, "head_dim");
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
@@ -79,16 +82,24 @@ struct Params {
 };
 
 struct __align__(8) Bars {
-  uint64_t kv_full[4];
-  uint64_t s_done[2];
-  uint64_t o_done;
+  uint64_t kv_full[4];   // TMA: tile in the stage
+  uint64_t kv_empty[4];  // MMA commit: the stage's tile is no longer read
+  uint64_t s_done[2];    // MMA commit: S^T buffer holds the tile's scores
+  uint64_t p_full[2];    // one arrival per softmax warp: P^T_t written (buffer t & 1)
+  uint64_t o_done[2];    // MMA commit: O^T += V^T P^T_t done (t & 1)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  uint8_t valid[4][16];  // per stage: block j of the tile holds attended positions
-  float red[4][NG];      // per-warp per-head reductions
+  float red[2][4][NG];  // per-warp per-head maxima, by tile parity
+  float red_l[4][NG];   // per-warp per-head sums (epilogue)
 };
 
+// Named barrier of the four softmax warps (id 1).
+__device__ __forceinline__ void softmax_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Warps 0-3: softmax (thread = position = TMEM lane; for O^T, thread = output dimension);
+// warp 4: bulk loads; warp 5: MMA issue.  They meet on mbarriers only, so the loads run
+// STAGES - 1 tiles ahead of the softmax and nothing waits on a CTA-wide barrier per tile.
 template <typename T, typename Index, int D>
 __global__ void __launch_bounds__(THREADS, 1)
     paged_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -101,25 +112,29 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* sk = smem;                          // STAGES x K tile
   uint8_t* sv = sk + STAGES * C::K_BYTES;      // STAGES x V tile
   uint8_t* sq = sv + STAGES * C::V_BYTES;      // Q^T
-  uint8_t* sp = sq + C::Q_BYTES;               // P^T (hi)
-  uint8_t* sp_lo = sp + C::P_BYTES;            // P^T (lo, SPLIT)
-  Bars* bars = reinterpret_cast<Bars*>(sp + (C::SPLIT ? 2 : 1) * C::P_BYTES);
+  uint8_t* sp = sq + C::Q_BYTES;  // P^T buffers: [parity][hi, lo]
+  constexpr int P_SET = (C::SPLIT ? 2 : 1) * C::P_BYTES;
+  Bars* bars = reinterpret_cast<Bars*>(sp + 2 * P_SET);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int part = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int h0 = kvh * p.group;
   const int G = p.group;  // real heads of this CTA (<= NG)
   const int bs = p.block_size;
-  const int blocks_per_tile = TILE / bs;
-
   const Index* tables = static_cast<const Index*>(p.tables) + static_cast<int64_t>(b) * p.max_blocks;
   const int t_begin = part * p.part_tokens;
 
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(smem_u32(&bars->kv_full[s]), 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&bars->kv_full[s]), 1);
+      mbar_init(smem_u32(&bars->kv_empty[s]), 1);
+    }
     mbar_init(smem_u32(&bars->s_done[0]), 1);
     mbar_init(smem_u32(&bars->s_done[1]), 1);
-    mbar_init(smem_u32(&bars->o_done), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars->p_full[s]), 4);
+      mbar_init(smem_u32(&bars->o_done[s]), 1);
+    }
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
     fence_barrier_init();
@@ -141,7 +156,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   constexpr int O_COL = 2 * NG;
   pdl_begin();  // global memory is touched only after this
   int64_t ctx64 = static_cast<int64_t>(static_cast<const Index*>(p.lens)[b]);
@@ -170,245 +184,275 @@ __global__ void __launch_bounds__(THREADS, 1)
     atomicOr(ctl.status, code);
   };
 
-  // ---- loads (warp 0): tile t into stage t % STAGES; lane j loads the tile's block j.
-  uint32_t issued[4] = {0, 0, 0, 0};  // lane 0's count of loads per stage
-  auto load_tile = [&](int t) {
-    const int st = t % STAGES;
-    const uint32_t bar = smem_u32(&bars->kv_full[st]);
-    if (lane == 0) {
-      mbar_arrive_expect_tx(bar, C::LOAD_BYTES);
-      ++issued[st];
-    }
-    __syncwarp();
-    if (lane < blocks_per_tile) {
-      const int pos = t_begin + t * TILE + lane * bs;  // first position of block `lane`
-      int blk = p.num_blocks;                           // out of range: reads as zero
-      bool valid = false;
-      if (pos < t_end) {
-        const int64_t idx = static_cast<int64_t>(tables[pos / bs]);
-        if (idx >= 0 && idx < p.num_blocks) {
-          blk = static_cast<int>(idx);
-          valid = true;
-        } else {
-          atomicOr(ctl.status, RK_DEV_ERR_BAD_INDEX);
+  if (warp == 4) {
+    // ------------------------------------------------------------ loads
+    uint32_t issued[4] = {0, 0, 0, 0};
+    const int blocks_per_tile = TILE / bs;
+    for (int t = 0; t < n_tiles; ++t) {
+      const int st = t % STAGES;
+      bool ok = true;
+      if (lane == 0 && t >= STAGES)
+        ok = mbar_wait_bounded(smem_u32(&bars->kv_empty[st]), ((t / STAGES) - 1) & 1, ctl.timeout_ns, abort);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+        break;
+      }
+      const uint32_t bar = smem_u32(&bars->kv_full[st]);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar, C::LOAD_BYTES);
+        ++issued[st];
+      }
+      __syncwarp();
+      if (lane < blocks_per_tile) {
+        const int pos = t_begin + t * TILE + lane * bs;  // first position of block `lane`
+        int blk = p.num_blocks;                           // out of range: reads as zero
+        if (pos < t_end) {
+          const int64_t idx = static_cast<int64_t>(tables[pos / bs]);
+          if (idx >= 0 && idx < p.num_blocks)
+            blk = static_cast<int>(idx);
+          else
+            atomicOr(ctl.status, RK_DEV_ERR_BAD_INDEX);
         }
-      }
-      bars->valid[st][lane] = valid ? 1 : 0;
 #pragma unroll
-      for (int c = 0; c < C::CHUNKS; ++c) {
-        const uint32_t off = c * (TILE * 128) + lane * bs * 128;
-        tma_load_4d(smem_u32(sk + st * C::K_BYTES + off), &tmap_k, bar, c * 64, kvh, 0, blk);
-        tma_load_4d(smem_u32(sv + st * C::V_BYTES + off), &tmap_v, bar, c * 64, kvh, 0, blk);
-      }
-    }
-  };
-  if (warp == 0)
-    for (int t = 0; t < STAGES - 1 && t < n_tiles; ++t) load_tile(t);
-
-  constexpr uint32_t IDESC_S = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, TILE, NG, false, false);
-  constexpr uint32_t IDESC_O = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, TILE, NG, true, false);
-  int issued_mma = 0;
-  uint32_t used[4] = {0, 0, 0, 0};  // thread 0's waits per stage
-  auto issue_s = [&](int t) {       // thread 0: S^T_t = K_t Q^T into buffer t & 1
-    const int st = t % STAGES;
-    if (!mbar_wait_bounded(smem_u32(&bars->kv_full[st]), used[st] & 1u, ctl.timeout_ns, abort))
-      return fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
-    ++used[st];
-    tc_fence_after();
-    const uint32_t k0 = smem_u32(sk + st * C::K_BYTES), q0 = smem_u32(sq);
-#pragma unroll
-    for (int kk = 0; kk < D / UMMA_K; ++kk) {
-      const uint32_t off_k = (kk >> 2) * (TILE * 128) + (kk & 3) * 32;
-      const uint32_t off_q = (kk >> 2) * (NG * 128) + (kk & 3) * 32;
-      tc_mma_f16(tmem + (t & 1) * NG, umma_desc_sw128(k0 + off_k, 16, 1024),
-                 umma_desc_sw128(q0 + off_q, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-    }
-    tc_commit(smem_u32(&bars->s_done[t & 1]));
-    ++issued_mma;
-  };
-  auto issue_pv = [&](int t) {  // thread 0: O^T += V_t^T P_t^T
-    const int st = t % STAGES;
-    const uint32_t v0 = smem_u32(sv + st * C::V_BYTES), p0 = smem_u32(sp), plo0 = smem_u32(sp_lo);
-#pragma unroll
-    for (int kk = 0; kk < TILE / UMMA_K; ++kk) {
-      const uint64_t a = umma_desc_sw128(v0 + kk * 2048, TILE * 128, 1024);
-      const uint32_t off_p = (kk >> 2) * (NG * 128) + (kk & 3) * 32;
-      tc_mma_f16(tmem + O_COL, a, umma_desc_sw128(p0 + off_p, 16, 1024), IDESC_O,
-                 (t > 0 || kk > 0) ? 1u : 0u);
-      if (C::SPLIT) tc_mma_f16(tmem + O_COL, a, umma_desc_sw128(plo0 + off_p, 16, 1024), IDESC_O, 1u);
-    }
-    tc_commit(smem_u32(&bars->o_done));
-    ++issued_mma;
-  };
-
-  if (tid == 0 && n_tiles > 0) issue_s(0);
-  __syncthreads();  // the stage-0 validity flags are visible
-
-  // Per-head row state (identical in every thread): the maximum the exponentials use.
-  float m_use[NG], l_part[NG];
-#pragma unroll
-  for (int g = 0; g < NG; ++g) {
-    m_use[g] = -INFINITY;
-    l_part[g] = 0.f;
-  }
-  for (int j = 0; j < n_tiles; ++j) {
-    const int st = j % STAGES;
-    if (!mbar_wait_bounded(smem_u32(&bars->s_done[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort))
-      fail(RK_DEV_ERR_TIMEOUT_MMA);
-    tc_fence_after();
-    // This thread's position: row `tid` of the tile.
-    const int pos = t_begin + j * TILE + tid;
-    const bool attended = pos < t_end && bars->valid[st][tid / bs] != 0;
-    float s[NG];
-    {
-      uint32_t r[16];
-      tmem_ld_32x32b_x16(t_lane + (j & 1) * NG, r);
-      tmem_ld_wait();
-#pragma unroll
-      for (int g = 0; g < NG; ++g) s[g] = attended && g < G ? __uint_as_float(r[g]) * p.scale_log2 : -INFINITY;
-    }
-    // Per-head maximum over the tile: warp shuffles, then the four warps in order.
-#pragma unroll
-    for (int g = 0; g < NG; ++g) {
-      if (g < G) {  // G is uniform over the CTA
-        float v = s[g];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) bars->red[warp][g] = v;
-      }
-    }
-    __syncthreads();
-    float alpha[NG];
-    bool rescale = false;
-#pragma unroll
-    for (int g = 0; g < NG; ++g) {
-      alpha[g] = 1.f;
-      if (g < G) {
-        const float mt = fmaxf(fmaxf(bars->red[0][g], bars->red[1][g]), fmaxf(bars->red[2][g], bars->red[3][g]));
-        if (mt > m_use[g] + 8.f) {  // lazy rescaling: P <= 256
-          alpha[g] = ex2_approx(m_use[g] - mt);
-          m_use[g] = mt;
-          rescale = true;
+        for (int c = 0; c < C::CHUNKS; ++c) {
+          const uint32_t off = c * (TILE * 128) + lane * bs * 128;
+          tma_load_4d(smem_u32(sk + st * C::K_BYTES + off), &tmap_k, bar, c * 64, kvh, 0, blk);
+          tma_load_4d(smem_u32(sv + st * C::V_BYTES + off), &tmap_v, bar, c * 64, kvh, 0, blk);
         }
       }
     }
-    // P for this position (zero for padding heads and masked positions).
-    uint32_t hi[NG / 2], lo[NG / 2];
-#pragma unroll
-    for (int g = 0; g < NG; g += 2) {
-      float e[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float m = m_use[g + h] == -INFINITY ? 0.f : m_use[g + h];
-        e[h] = ex2_approx(s[g + h] - m);
-        l_part[g + h] = l_part[g + h] * alpha[g + h] + e[h];
-      }
-      hi[g / 2] = Pack2<T>::from_floats(e[0], e[1]);
-      if (C::SPLIT) {
-        const float2 h2 = Pack2<T>::to_floats(hi[g / 2]);
-        lo[g / 2] = Pack2<T>::from_floats(e[0] - h2.x, e[1] - h2.y);
-      }
-    }
-    // P V_{j-1} must be done before P^T is overwritten, O^T rescaled, or the stage refilled.
-    if (j > 0) {
-      if (!mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, abort))
-        fail(RK_DEV_ERR_TIMEOUT_MMA);
-      tc_fence_after();
-      if (rescale) {  // uniform: every thread holds the same maxima
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(t_lane + O_COL, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int g = 0; g < NG; ++g) r[g] = __float_as_uint(__uint_as_float(r[g]) * alpha[g]);
-        tmem_st_32x32b_x16(t_lane + O_COL, r);
-        tmem_st_wait();
-      }
-    }
-    if (warp == 0) {
-      // load_tile synchronises the warp: decide for all 32 lanes at once.
-      const bool go = __all_sync(0xffffffffu, *abort == 0);
-      if (go && j + STAGES - 1 < n_tiles) load_tile(j + STAGES - 1);
-    }
-    // P^T: row g = head, positions along K; this thread writes position `tid` of each row.
-    {
-      const int c = tid >> 6, within = tid & 63;
-#pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        const uint32_t off = c * (NG * 128) + g * 128 + ((((within >> 3) ^ (g & 7))) << 4) + (within & 7) * 2;
-        const uint32_t hv = (g & 1) ? (hi[g / 2] >> 16) : (hi[g / 2] & 0xffffu);
-        *reinterpret_cast<uint16_t*>(sp + off) = static_cast<uint16_t>(hv);
-        if (C::SPLIT) {
-          const uint32_t lv = (g & 1) ? (lo[g / 2] >> 16) : (lo[g / 2] & 0xffffu);
-          *reinterpret_cast<uint16_t*>(sp_lo + off) = static_cast<uint16_t>(lv);
+    // No bulk copy may still be landing when the CTA exits: wait for the last load of
+    // each stage (earlier ones completed before that stage was refilled).
+    if (lane == 0)
+      for (int s = 0; s < STAGES; ++s)
+        if (issued[s] > 0 &&
+            !mbar_wait_bounded(smem_u32(&bars->kv_full[s]), (issued[s] - 1) & 1u, ctl.timeout_ns, &never))
+          atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t IDESC_S = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, TILE, NG, false, false);
+      constexpr uint32_t IDESC_O = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, TILE, NG, true, false);
+      int issued_mma = 0;
+      auto issue_s = [&](int t) -> bool {  // S^T_t = K_t Q^T into buffer t & 1
+        const int st = t % STAGES;
+        if (!mbar_wait_bounded(smem_u32(&bars->kv_full[st]), (t / STAGES) & 1, ctl.timeout_ns, abort)) {
+          fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+          return false;
         }
-      }
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && !*abort) {
-      tc_fence_after();
-      issue_pv(j);
-      if (j + 1 < n_tiles) issue_s(j + 1);
-    }
-  }
-
-  // ---- epilogue: per-head sums over the 128 positions, then O^T row d = tid.
-  if (n_tiles > 0 &&
-      !mbar_wait_bounded(smem_u32(&bars->o_done), (n_tiles - 1) & 1, ctl.timeout_ns, abort))
-    fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
-  tc_fence_after();
-  __syncthreads();  // every thread has read the last maxima from `red`
+        tc_fence_after();
+        const uint64_t dk = umma_desc_sw128(smem_u32(sk + st * C::K_BYTES), 16, 1024);
+        const uint64_t dq = umma_desc_sw128(smem_u32(sq), 16, 1024);
 #pragma unroll
-  for (int g = 0; g < NG; ++g) {
-    if (g < G) {
-      float v = l_part[g];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) bars->red[warp][g] = v;
-    }
-  }
-  __syncthreads();
-  float o_row[NG];
-  if (n_tiles > 0) {
-    uint32_t r[16];
-    tmem_ld_32x32b_x16(t_lane + O_COL, r);
-    tmem_ld_wait();
-#pragma unroll
-    for (int g = 0; g < NG; ++g) o_row[g] = __uint_as_float(r[g]);
-  } else {
-#pragma unroll
-    for (int g = 0; g < NG; ++g) o_row[g] = 0.f;
-  }
-  if (tid < D && !*abort) {
-    for (int g = 0; g < G; ++g) {
-      const float l = ((bars->red[0][g] + bars->red[1][g]) + bars->red[2][g]) + bars->red[3][g];
-      const int64_t head = static_cast<int64_t>(b) * p.hq + h0 + g;
-      if (p.partitions == 1) {
-        static_cast<T*>(p.out)[head * D + tid] = from_f32<T>(o_row[g] / l);  // 0/0 = NaN for ctx 0
-      } else {
-        const int64_t slot = head * p.partitions + part;
-        p.part_acc[slot * D + tid] = o_row[g];
-        if (tid == 0) {
-          p.part_ml[2 * slot] = m_use[g] == -INFINITY ? -INFINITY : m_use[g] * LN2;
-          p.part_ml[2 * slot + 1] = l;
+        for (int kk = 0; kk < D / UMMA_K; ++kk) {
+          const uint32_t off_k = (kk >> 2) * (TILE * 128) + (kk & 3) * 32;
+          const uint32_t off_q = (kk >> 2) * (NG * 128) + (kk & 3) * 32;
+          tc_mma_f16(tmem + (t & 1) * NG, umma_desc_advance(dk, off_k), umma_desc_advance(dq, off_q),
+                     IDESC_S, kk > 0 ? 1u : 0u);
         }
+        tc_commit(smem_u32(&bars->s_done[t & 1]));
+        ++issued_mma;
+        return true;
+      };
+      bool ok = issue_s(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        // S^T_{j+1} into the buffer of S^T_{j-1}, which the softmax warps read before P_{j-1}.
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        if (!mbar_wait_bounded(smem_u32(&bars->p_full[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort)) {
+          fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+          break;
+        }
+        tc_fence_after();
+        const int st = j % STAGES;
+        const uint64_t dv = umma_desc_sw128(smem_u32(sv + st * C::V_BYTES), TILE * 128, 1024);
+        const uint64_t dp = umma_desc_sw128(smem_u32(sp + (j & 1) * P_SET), 16, 1024);
+        const uint64_t dplo = umma_desc_sw128(smem_u32(sp + (j & 1) * P_SET + C::P_BYTES), 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < TILE / UMMA_K; ++kk) {
+          const uint64_t a = umma_desc_advance(dv, kk * 2048);
+          const uint32_t off_p = (kk >> 2) * (NG * 128) + (kk & 3) * 32;
+          tc_mma_f16(tmem + O_COL, a, umma_desc_advance(dp, off_p), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          if (C::SPLIT) tc_mma_f16(tmem + O_COL, a, umma_desc_advance(dplo, off_p), IDESC_O, 1u);
+        }
+        tc_commit(smem_u32(&bars->o_done[j & 1]));
+        tc_commit(smem_u32(&bars->kv_empty[st]));
+        ++issued_mma;
       }
-    }
-  }
-
-  // ---- drain: every MMA and bulk copy issued by this CTA completes before exit.
-  if (tid == 0) {
-    if (issued_mma > 0) {
+      // Every MMA completes before TMEM is released.
       tc_commit(smem_u32(&bars->drain));
       if (!mbar_wait_bounded(smem_u32(&bars->drain), 0, ctl.timeout_ns, &never))
         atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+      (void)issued_mma;
     }
-    for (int s = 0; s < STAGES; ++s)
-      if (issued[s] > used[s] &&
-          !mbar_wait_bounded(smem_u32(&bars->kv_full[s]), (issued[s] - 1) & 1u, ctl.timeout_ns, &never))
-        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+  } else {
+    // ------------------------------------------------------------ softmax
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // Per-head state (identical in every softmax thread): the maximum the exponentials use.
+    float m_use[NG], l_part[NG];
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      m_use[g] = -INFINITY;
+      l_part[g] = 0.f;
+    }
+    // Block-table entry of this thread's position, fetched one tile ahead.
+    auto entry_ok = [&](int pos) -> bool {
+      if (pos >= t_end) return false;
+      const int64_t idx = static_cast<int64_t>(tables[pos / bs]);
+      return idx >= 0 && idx < p.num_blocks;
+    };
+    bool ok_next = n_tiles > 0 && entry_ok(t_begin + tid);
+    for (int j = 0; j < n_tiles; ++j) {
+      const bool attended = ok_next;
+      if (j + 1 < n_tiles) ok_next = entry_ok(t_begin + (j + 1) * TILE + tid);
+      if (!mbar_wait_bounded(smem_u32(&bars->s_done[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort))
+        fail(RK_DEV_ERR_TIMEOUT_MMA);
+      tc_fence_after();
+      float s[NG];
+      {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(t_lane + (j & 1) * NG, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < NG; ++g) s[g] = attended && g < G ? __uint_as_float(r[g]) * p.scale_log2 : -INFINITY;
+      }
+      // Per-head maximum over the tile: warp shuffles, then the four warps in order (slots
+      // of this tile's parity: a warp rewrites them two tiles on, after the barrier of the
+      // tile between, which its peers reach only once they have read them).
+      float (*red)[NG] = bars->red[j & 1];
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        if (g < G) {  // G is uniform over the CTA
+          float v = s[g];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+          if (lane == 0) red[warp][g] = v;
+        }
+      }
+      softmax_sync();
+      float alpha[NG];
+      bool rescale = false;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        alpha[g] = 1.f;
+        if (g < G) {
+          const float mt = fmaxf(fmaxf(red[0][g], red[1][g]), fmaxf(red[2][g], red[3][g]));
+          if (mt > m_use[g] + 8.f) {  // lazy rescaling: P <= 256
+            alpha[g] = ex2_approx(m_use[g] - mt);
+            m_use[g] = mt;
+            rescale = true;
+          }
+        }
+      }
+      // P for this position (zero for padding heads and masked positions).
+      uint32_t hi[NG / 2], lo[NG / 2];
+#pragma unroll
+      for (int g = 0; g < NG; g += 2) {
+        float e[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float m = m_use[g + h] == -INFINITY ? 0.f : m_use[g + h];
+          e[h] = ex2_approx(s[g + h] - m);
+          l_part[g + h] = l_part[g + h] * alpha[g + h] + e[h];
+        }
+        hi[g / 2] = Pack2<T>::from_floats(e[0], e[1]);
+        if (C::SPLIT) {
+          const float2 h2 = Pack2<T>::to_floats(hi[g / 2]);
+          lo[g / 2] = Pack2<T>::from_floats(e[0] - h2.x, e[1] - h2.y);
+        }
+      }
+      // P^T buffer j & 1 was read by P V_{j-2}; a rescaling of O^T needs every earlier
+      // P V done (they complete in order: P V_{j-1} is enough).  Neither usually waits:
+      // the softmax of tile j does not depend on P V_{j-1} otherwise.
+      if (j >= 2) {
+        if (!mbar_wait_bounded(smem_u32(&bars->o_done[j & 1]), ((j - 2) >> 1) & 1, ctl.timeout_ns, abort))
+          fail(RK_DEV_ERR_TIMEOUT_MMA);
+      }
+      if (j > 0 && rescale) {  // uniform: every softmax thread holds the same maxima
+        if (!mbar_wait_bounded(smem_u32(&bars->o_done[(j - 1) & 1]), ((j - 1) >> 1) & 1, ctl.timeout_ns, abort))
+          fail(RK_DEV_ERR_TIMEOUT_MMA);
+        tc_fence_after();
+        {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_lane + O_COL, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int g = 0; g < NG; ++g) r[g] = __float_as_uint(__uint_as_float(r[g]) * alpha[g]);
+          tmem_st_32x32b_x16(t_lane + O_COL, r);
+          tmem_st_wait();
+        }
+      }
+      tc_fence_after();
+      // P^T: row g = head, positions along K; this thread writes position `tid` of each row.
+      {
+        uint8_t* sp_hi = sp + (j & 1) * P_SET;
+        uint8_t* sp_lo = sp_hi + C::P_BYTES;
+        const int c = tid >> 6, within = tid & 63;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          const uint32_t off = c * (NG * 128) + g * 128 + (((within >> 3) ^ (g & 7)) << 4) + (within & 7) * 2;
+          const uint32_t hv = (g & 1) ? (hi[g / 2] >> 16) : (hi[g / 2] & 0xffffu);
+          *reinterpret_cast<uint16_t*>(sp_hi + off) = static_cast<uint16_t>(hv);
+          if (C::SPLIT) {
+            const uint32_t lv = (g & 1) ? (lo[g / 2] >> 16) : (lo[g / 2] & 0xffffu);
+            *reinterpret_cast<uint16_t*>(sp_lo + off) = static_cast<uint16_t>(lv);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[j & 1]));
+    }
+
+    // ---- epilogue: per-head sums over the 128 positions, then O^T row d = tid.
+    if (n_tiles > 0 &&
+        !mbar_wait_bounded(smem_u32(&bars->o_done[(n_tiles - 1) & 1]), ((n_tiles - 1) >> 1) & 1,
+                           ctl.timeout_ns, abort))
+      fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
+    tc_fence_after();
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      if (g < G) {
+        float v = l_part[g];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) bars->red_l[warp][g] = v;
+      }
+    }
+    softmax_sync();
+    float o_row[NG];
+    if (n_tiles > 0) {
+      uint32_t r[16];
+      tmem_ld_32x32b_x16(t_lane + O_COL, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int g = 0; g < NG; ++g) o_row[g] = __uint_as_float(r[g]);
+    } else {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) o_row[g] = 0.f;
+    }
+    if (tid < D && !*abort) {
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        if (g < G) {
+          const float l = ((bars->red_l[0][g] + bars->red_l[1][g]) + bars->red_l[2][g]) + bars->red_l[3][g];
+          const int64_t head = static_cast<int64_t>(b) * p.hq + h0 + g;
+          if (p.partitions == 1) {
+            static_cast<T*>(p.out)[head * D + tid] = from_f32<T>(o_row[g] / l);  // 0/0 = NaN for ctx 0
+          } else {
+            const int64_t slot = head * p.partitions + part;
+            p.part_acc[slot * D + tid] = o_row[g];
+            if (tid == 0) {
+              p.part_ml[2 * slot] = m_use[g] == -INFINITY ? -INFINITY : m_use[g] * LN2;
+              p.part_ml[2 * slot + 1] = l;
+            }
+          }
+        }
+      }
+    }
   }
+
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

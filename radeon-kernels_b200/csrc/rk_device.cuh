@@ -389,6 +389,13 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
+// The start-address field is the descriptor's low 14 bits (address >> 4): the descriptor of
+// an operand `bytes` further on is desc + (bytes >> 4), as long as the address stays below
+// 256 KiB (all shared memory does).  MMA loops build one descriptor per tile and add.
+__device__ __forceinline__ uint64_t umma_desc_advance(uint64_t desc, uint32_t bytes) {
+  return desc + static_cast<uint64_t>(bytes >> 4);
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 //   [4,6) D format (1 = f32)  [7,10) A format  [10,13) B format (0 = f16, 1 = bf16)
 //   [15] A major (0 = K)      [16] B major (1 = MN)

@@ -219,13 +219,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!got) return fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
         ++k_used[st];
         tc_fence_after();
-        const uint32_t q0 = smem_u32(sq), k0 = smem_u32(sk + st * C::K_BYTES);
+        const uint64_t dq = umma_desc_sw128(smem_u32(sq), 16, 1024);
+        const uint64_t dk = umma_desc_sw128(smem_u32(sk + st * C::K_BYTES), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < D / UMMA_K; ++kk) {
           const uint32_t off_q = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint32_t off_k = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          tc_mma_f16(tmem + (t & 1) * BN, umma_desc_sw128(q0 + off_q, 16, 1024),
-                     umma_desc_sw128(k0 + off_k, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          tc_mma_f16(tmem + (t & 1) * BN, umma_desc_advance(dq, off_q), umma_desc_advance(dk, off_k),
+                     IDESC_S, kk > 0 ? 1u : 0u);
         }
         tc_commit(smem_u32(&bars->s_done[t & 1]));
         ++issued_mma;
@@ -237,15 +238,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           return fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
         ++v_used[st];
         tc_fence_after();
-        const uint32_t p0 = smem_u32(sp), plo0 = smem_u32(sp_lo), v0 = smem_u32(sv_s + st * C::V_BYTES);
+        const uint64_t dp = umma_desc_sw128(smem_u32(sp), 16, 1024);
+        const uint64_t dplo = umma_desc_sw128(smem_u32(sp_lo), 16, 1024);
+        const uint64_t dv = umma_desc_sw128(smem_u32(sv_s + st * C::V_BYTES), 8192, 1024);
 #pragma unroll
         for (int kk = 0; kk < BN / UMMA_K; ++kk) {
           const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint64_t b =
-              umma_desc_sw128(v0 + (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048, 8192, 1024);
-          tc_mma_f16(tmem + O_COL, umma_desc_sw128(p0 + a_off, 16, 1024), b, IDESC_O,
-                     (t > 0 || kk > 0) ? 1u : 0u);
-          if (C::SPLIT) tc_mma_f16(tmem + O_COL, umma_desc_sw128(plo0 + a_off, 16, 1024), b, IDESC_O, 1u);
+          const uint64_t b = umma_desc_advance(dv, (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048);
+          tc_mma_f16(tmem + O_COL, umma_desc_advance(dp, a_off), b, IDESC_O, (t > 0 || kk > 0) ? 1u : 0u);
+          if (C::SPLIT) tc_mma_f16(tmem + O_COL, umma_desc_advance(dplo, a_off), b, IDESC_O, 1u);
         }
         tc_commit(smem_u32(&bars->o_done));
         ++issued_mma;
