@@ -409,7 +409,7 @@ rk_status paged_attention_launch(const void* query, const void* key_cache, const
   prm.scale = scale;
   const bool bf16 = dt == RK_DTYPE_BF16;
   const int path = g_paged_path.load();
-  const bool tc_ok = paged_attention_tc_supported(key_cache, value_cache, hq, hkv, head_dim, block_size);
+  const bool tc_ok = paged_attention_tc_supported(query, key_cache, value_cache, hq, hkv, head_dim, block_size);
   if (path == 2 && !tc_ok) return RK_ERR_UNSUPPORTED;
   if (tc_ok && path != 1) {
     // Tensor-core kernel; its partitions (whole 128-position tiles) go through the same

@@ -136,8 +136,8 @@ struct PagedTcArgs {
   float scale;
   rk_dtype dt;
 };
-bool paged_attention_tc_supported(const void* key_cache, const void* value_cache, int64_t hq,
-                                  int64_t hkv, int64_t head_dim, int64_t block_size);
+bool paged_attention_tc_supported(const void* query, const void* key_cache, const void* value_cache,
+                                  int64_t hq, int64_t hkv, int64_t head_dim, int64_t block_size);
 void paged_attention_tc_plan(int64_t batch, int64_t hkv, int64_t max_ctx, int sms, int* partitions,
                              int* part_tokens);
 rk_status paged_attention_tc_launch(const PagedTcArgs& a, cudaStream_t s);

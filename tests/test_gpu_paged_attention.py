@@ -149,13 +149,19 @@ def test_reference_workloads(batch, hq, hkv, ctx, d, bs, dtype, index, kernel):
 
 
 # Shapes at the tensor-core kernel's edges: 8- and 128-position blocks, MHA, a 16-head
-# group, contexts ending inside a tile, many partitions (long context, one sequence).
+# group, contexts ending inside a tile, many partitions (long context, one sequence), and
+# groups of 2, 3, 6 and 8 heads (the kernel rounds a group up to 1, 4, 8 or 16 heads; with
+# fewer than 16 query heads a Q box holds only the tensor's rows).
 EDGES = [
     (2, 8, 8, 300, 128, 8),
     (2, 16, 1, 1000, 128, 128),
     (3, 4, 4, 129, 64, 64),
     (1, 32, 2, 8191, 128, 32),
     (5, 8, 2, 1, 64, 16),
+    (2, 6, 2, 700, 128, 16),
+    (3, 16, 2, 515, 64, 32),
+    (2, 12, 2, 260, 128, 64),
+    (2, 4, 2, 333, 128, 16),
 ]
 
 
@@ -176,6 +182,29 @@ def test_tensor_core_edges(batch, hq, hkv, ctx, d, bs, dtype, kernel):
         to_bits(q), to_bits(k), to_bits(v), tables.numpy(), lens.numpy(), 1.0 / math.sqrt(d), dtype
     )
     _gate(kernel, out, ref, ref32, dtype)
+
+
+def test_many_items_per_cta_with_empty_sequences(kernel):
+    """More (sequence, KV head) pairs than SMs, ragged lengths with empty sequences among
+    them: the tensor-core kernel's CTAs walk several items each, some without tiles."""
+    import torch
+
+    batch, hq, hkv, d, bs, ctx = 300, 16, 2, 128, 16, 300
+    q, k, v, tables, _ = _random_case(torch, batch, hq, hkv, ctx, d, bs, "bf16", seed=11)
+    gen = torch.Generator().manual_seed(12)
+    lens = torch.randint(0, ctx + 1, (batch,), generator=gen, dtype=torch.int32)
+    lens[::7] = 0
+    st, out, _ = run_abi(q.cuda(), k.cuda(), v.cuda(), tables.to(torch.int32).cuda(), lens.cuda(), 0.088, "bf16")
+    assert st == _native.RK_OK
+    torch.cuda.synchronize()
+    assert device_status() == _native.RK_OK
+    ref, ref32 = oracle.paged_attention_decode(
+        to_bits(q), to_bits(k), to_bits(v), tables.numpy(), lens.numpy(), 0.088, "bf16"
+    )
+    live = (lens > 0).numpy()
+    live_t = torch.from_numpy(live).to(out.device)
+    _gate(kernel, out[live_t], ref[live], ref32[live], "bf16")
+    assert bool(torch.isnan(out[~live_t].float()).all())
 
 
 def test_lengths_zero_and_beyond_the_table_and_bad_block_indices(kernel):
