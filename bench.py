@@ -603,26 +603,41 @@ def suite(args, dist: Dist, ext, peaks):
             cases.append((q, k, v, tables, lens))
         scale = d ** -0.5
         step = lambda i: ext.paged_attention_decode(*cases[i % sets], scale)  # noqa: E731
-        for i in range(3):
-            step(i)
-        torch.cuda.synchronize()
         launches = max(20, sets)
-        g = torch.cuda.CUDAGraph()
-        cap = torch.cuda.Stream()
-        cap.wait_stream(stream)
-        with torch.cuda.stream(cap):
-            with torch.cuda.graph(g, stream=cap):
-                for i in range(launches):
+        from radeon_kernels import _native
+
+        lib = _native.library()
+
+        def time_path(path):
+            # The kernel choice is read when a call is launched, so a graph captured under a
+            # path keeps that kernel.
+            lib.rk_paged_attention_set_path(path)
+            try:
+                for i in range(3):
                     step(i)
-        stream.wait_stream(cap)
-        torch.cuda.synchronize()
-        g.replay()
-        torch.cuda.synchronize()
-        reps = 10
-        ms = time_loop(lambda i: g.replay(), reps, stream) / (reps * launches)
-        del g
-        dist.barrier()
-        ms = dist.max(ms)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                cap = torch.cuda.Stream()
+                cap.wait_stream(stream)
+                with torch.cuda.stream(cap):
+                    with torch.cuda.graph(g, stream=cap):
+                        for i in range(launches):
+                            step(i)
+                stream.wait_stream(cap)
+                torch.cuda.synchronize()
+                g.replay()
+                torch.cuda.synchronize()
+                reps = 10
+                t = time_loop(lambda i: g.replay(), reps, stream) / (reps * launches)
+                del g
+            finally:
+                lib.rk_paged_attention_set_path(0)
+            dist.barrier()
+            return dist.max(t)
+
+        ms = time_path(0)
+        ms_cuda_cores = time_path(1)
+        tc_auto = d in (64, 128) and hq // hkv <= 16 and bs in (8, 16, 32, 64, 128) and not (hq == hkv and d == 64)
         gbs = (kv_bytes + io_bytes) / (ms / 1e3) / 1e9
         results[name] = {
             "unit": "GB/s",
@@ -632,6 +647,8 @@ def suite(args, dist: Dist, ext, peaks):
             "roofline_frac": round(gbs / peaks["hbm_gbs"], 4),
             "scaling": "replica",
             "shape": {"batch": batch, "query_heads": hq, "kv_heads": hkv, "context": ctx, "head_dim": d, "block_size": bs},
+            "kernel": "tcgen05" if tc_auto else "cuda cores",
+            "cuda_cores_us": round(ms_cuda_cores * 1e3, 2),
             "dtype": dtype,
             "timing": f"CUDA graph of {launches} launches over {sets} caches"
             + (" (L2-resident: latency bound)" if kv_bytes * sets < 256_000_000 else ""),
@@ -759,6 +776,9 @@ def suite(args, dist: Dist, ext, peaks):
     paged_case("paged_b16_gqa32x8_c2048_d128_bf16", 16, 32, 8, 2048, 128, 16, "bf16", 62)
     paged_case("paged_b4_mha16_c2048_d64_bf16", 4, 16, 16, 2048, 64, 32, "bf16", 63)
     paged_case("paged_b4_gqa32x8_c1024_d256_bf16", 4, 32, 8, 1024, 256, 16, "bf16", 64)
+    # Larger batches: HBM-bound (about 0.5 GB of cache per call).
+    paged_case("paged_b64_gqa32x8_c2048_d128_bf16", 64, 32, 8, 2048, 128, 16, "bf16", 65)
+    paged_case("paged_b8_mha32_c4096_d128_bf16", 8, 32, 32, 4096, 128, 16, "bf16", 66)
     # Prefill attention, the reference's workload cases (benchmarks/workloads/sdpa-1.0.yaml),
     # plus one long-sequence case that is tensor-core rather than latency bound.
     sdpa_case("sdpa_b1_mha16_s128_d64_causal_bf16", 1, 16, 16, 128, 64, True, "bf16", 70)
@@ -887,6 +907,7 @@ PROFILE_CASES = {
     "add_rms_norm_prefill": ("add_rms_norm", 2048, 4096, 0, "bf16", "normal"),
     "ffn_swiglu": ("gemm_swiglu", 4096, 14336, 4096, "fp16", "normal64"),
     "paged_b16_c2048": ("paged", 16, 2048, 0, "bf16", "normal"),
+    "paged_b16_c2048_cuda_cores": ("paged", 16, 2048, 1, "bf16", "normal"),  # k: kernel choice
     "rms_norm_backward_prefill": ("rms_norm_backward", 2048, 4096, 0, "bf16", "normal"),
     "sdpa_b4_s4096": ("sdpa", 4, 4096, 128, "bf16", "normal"),  # GQA 32 x 8, causal
 }
@@ -911,7 +932,8 @@ def run_profile(args) -> int:
         gate = seeded((m, n), 1, dist_name, dtype)
         up = seeded((m, n), 2, dist_name, dtype)
         launch = lambda: ext.silu_mul(gate, up)  # noqa: E731
-    elif kind == "paged":  # m = batch, n = context; GQA 32 x 8, head_dim 128, block 16
+    elif kind == "paged":  # m = batch, n = context; GQA 32 x 8, head_dim 128, block 16; k = path
+        _native.library().rk_paged_attention_set_path(k)
         maxb = -(-n // 16)
         q = seeded((m, 32, 128), 1, dist_name, dtype)
         kc = seeded((m * maxb, 16, 8, 128), 2, dist_name, dtype)

@@ -357,9 +357,10 @@ RK_API void rk_gemm_set_tile_n(int tile_n);
 RK_API void rk_norm_set_threads(int threads_per_row);
 
 /* Kernel choice of rk_paged_attention_decode: 0 automatic (the tcgen05 kernel for head_dim
- * 64/128, up to 16 query heads per KV head and block sizes 8-128 in powers of two; the
- * CUDA-core kernel otherwise), 1 always the CUDA-core kernel, 2 the tcgen05 kernel
- * (RK_ERR_UNSUPPORTED where it does not apply).  Process-wide; for tests and tuning. */
+ * 64/128, up to 16 query heads per KV head and block sizes 8-128 in powers of two, except
+ * head_dim-64 MHA; the CUDA-core kernel otherwise), 1 always the CUDA-core kernel, 2 the
+ * tcgen05 kernel (RK_ERR_UNSUPPORTED where it does not apply).  Process-wide; for tests and
+ * tuning. */
 RK_API void rk_paged_attention_set_path(int path);
 
 /* Tuning hook for the rms_norm backward row kernel: CTAs per SM (1..32); 0 restores the

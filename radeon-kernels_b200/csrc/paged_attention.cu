@@ -411,7 +411,11 @@ rk_status paged_attention_launch(const void* query, const void* key_cache, const
   const int path = g_paged_path.load();
   const bool tc_ok = paged_attention_tc_supported(query, key_cache, value_cache, hq, hkv, head_dim, block_size);
   if (path == 2 && !tc_ok) return RK_ERR_UNSUPPORTED;
-  if (tc_ok && path != 1) {
+  // Automatic choice: the tensor-core kernel wherever it applies except head_dim-64 MHA, where
+  // the CUDA-core kernel measured faster (no query heads share a K/V tile, and V^T is padded
+  // to the MMA's 128 rows).
+  const bool tc_auto = tc_ok && !(hq == hkv && head_dim == 64);
+  if (path == 2 || (path == 0 && tc_auto)) {
     // Tensor-core kernel; its partitions (whole 128-position tiles) go through the same
     // workspace layout and merge kernel.
     PagedTcArgs a{};

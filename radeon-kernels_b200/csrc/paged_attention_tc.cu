@@ -385,13 +385,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       constexpr uint32_t IDESC_S = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, TILE, NG, false, false);
       constexpr uint32_t IDESC_O = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, TILE, C::PN, true, false);
       // Cursor over this CTA's tiles: item, its tile count, tile j in it, non-empty item
-      // count ne, tile count g.
+      // count ne, tile count g, and the context length of the item after (read one item
+      // ahead, so moving to the next item does not wait for a global load).
       struct Cur {
         int item, n, j, ne, g;
+        Index len_next;
       };
       auto seek = [&](Cur& c) {  // from c.item on, to the first item with tiles
         for (; c.item < p.items; c.item += gridDim.x) {
-          c.n = make_item(p, c.item, lens[item_sequence(p, c.item)]).n_tiles;
+          const Index len = c.len_next;
+          const int nxt = c.item + static_cast<int>(gridDim.x);
+          c.len_next = nxt < p.items ? lens[item_sequence(p, nxt)] : Index(0);
+          c.n = make_item(p, c.item, len).n_tiles;
           if (c.n > 0) return;
         }
       };
@@ -430,7 +435,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (c.j + 1 == c.n) tc_commit(smem_u32(&bars->q_empty[qb]));
         return true;
       };
-      Cur cs{static_cast<int>(blockIdx.x), 0, 0, 0, 0};
+      Cur cs{static_cast<int>(blockIdx.x), 0, 0, 0, 0,
+             static_cast<int>(blockIdx.x) < p.items ? lens[item_sequence(p, blockIdx.x)] : Index(0)};
       seek(cs);
       Cur cp = cs;
       bool ok = true;
