@@ -9,29 +9,34 @@
 // with torch's SDPA (its dispatch manifest has no native entry, dispatch/sdpa-1.0.json); its
 // HIP candidate walks keys one at a time per query row (benchmarks/sdpa/native_sdpa.hip).
 //
-// One CTA per (128-row query tile, query head, batch), 512 threads (16 warps), flash-style:
-//   * thread 0 issues the TMA loads -- the Q tile once, K and V tiles of BN keys (128; 64
-//     for head_dim 256, to fit shared memory) in a ring
-//     of STAGES buffers, through 3-D tensor maps over the [batch*heads, S, D] stacks, so rows
-//     past the sequence read as zero instead of the next head's -- and the MMAs;
-//   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into TMEM columns [0, BN): Q and K
+// One CTA per (128-row query tile, query head, batch), 544 threads (16 softmax warps and a
+// producer warp), flash-style:
+//   * one producer thread issues the TMA loads -- the Q tile once, K and V tiles of BN keys
+//     (128; 64 for head_dim 256, to fit shared memory) in two-stage rings, through 3-D
+//     tensor maps over the [batch*heads, S, D] stacks, so rows past the sequence read as zero
+//     instead of the next head's -- and the MMAs;
+//   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into one of two TMEM buffers: Q and K
 //     are K-major 128-byte-swizzled tiles straight from TMA;
 //   * four warps share each 32-row TMEM lane quarter, each thread a quarter of its row's
-//     scores: it applies the scale (in base 2) and the masks, the row maximum is combined
-//     through four spare TMEM columns in a fixed order, and the online softmax (fp32) rescales the
-//     thread's quarter of the O row in TMEM only when the maximum grew by more than 2^8
-//     (lazy rescaling); P = 2^(s - m) (hardware ex2) goes to shared memory in the K-major
-//     swizzled layout the next MMA reads: rounded to fp16, or for bf16 as two bf16 terms
-//     P_hi + P_lo (see Cfg::SPLIT).  (One warp per lane quarter, 128 scores per thread,
-//     spent about 9 us per key tile on the dependent softmax chain.);
-//   * O += P V (M = 128, N = head_dim, K = BN keys) into TMEM columns [128, 128 + D): V is
-//     an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
+//     scores: masks on the raw scores (skipped when every row of the warp attends every key
+//     of its slice), tree maximum, the row maximum combined over the four warps in a fixed
+//     order, the scale folded into one FMA before the hardware ex2, online softmax in fp32
+//     that rescales the thread's quarter of the O row in TMEM only when the maximum grew by
+//     more than 2^8 (lazy rescaling).  P = 2^(s - m) is rounded to fp16, or for bf16 kept as
+//     two bf16 terms P_hi + P_lo (see Cfg::SPLIT);
+//   * 128-key tiles: P is written over its S buffer in TMEM (tcgen05.st, two 16-bit values
+//     per column) and O += P V takes A from TMEM, so the softmax never waits for the
+//     previous tile's P V except to rescale O; 64-key tiles write P to shared memory in the
+//     K-major swizzled layout instead;
+//   * O += P V (M = 128, N = head_dim, K = BN keys) into TMEM columns past the S buffers: V
+//     is an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
 //   * epilogue: O / l rounded to the dtype; l is the four warps' shares added in order.
-// The row sum l adds the fp32 exponentials.  Two S buffers in TMEM: thread 0 issues S_{j+1}
-// as soon as S_j has landed, so the scores of the next tile are computed during this tile's
-// softmax, and P V_j overlaps the next tile's exponentials.  Every wait is bounded (status word on
-// expiry) and made CTA-uniform; before TMEM is released every MMA and bulk copy this CTA
-// issued has completed.
+// The row sum l adds the fp32 exponentials.  The producer loads K_{j+2} first in each
+// iteration, then issues S_{j+1} (scores of the next tile during this tile's softmax), the
+// next V, and P V_j.  Each MMA instruction costs ~156 SM cycles whatever N up to 256, so a
+// 128 x 128 tile (8 + 8 MMAs, 8 more for bf16's P_lo) is bound by the tensor pipe's
+// instruction rate.  Every wait is bounded (status word on expiry) and made CTA-uniform;
+// before TMEM is released every MMA and bulk copy this CTA issued has completed.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -51,10 +56,12 @@ constexpr int SOFTMAX_WARPS = 16;
 constexpr int THREADS = 32 * (SOFTMAX_WARPS + 1);  // + the producer warp
 constexpr int UMMA_K = 16;
 
-// SPLIT (bf16): P is stored as P_hi + P_lo, both bf16, and O += P_hi V + P_lo V, so the
-// probabilities keep ~16 significant bits instead of bf16's 8 (rounding P alone moved the
-// output by up to 4.5e-3 of its maximum on near-uniform attention); fp16 P keeps 11 bits
-// and is used as is.
+// SPLIT (bf16): P is stored as P_hi + P_lo, both bf16 (P_hi: P with its low 16 bits
+// cleared; P_lo: the rest, rounded), and O += P_hi V + P_lo V, so the probabilities keep ~16
+// significant bits instead of bf16's 8.  Rounding P alone measured 4.5e-3 of the output's
+// maximum on near-uniform attention, and 4.45e-3 on two of the reference fixtures even with
+// the row sum taken over the rounded values; the gate is 4e-3.  fp16 P keeps 11 bits and is
+// used as is.
 template <typename T, int D>
 struct Cfg {
   static constexpr bool SPLIT = std::is_same<T, __nv_bfloat16>::value;
@@ -63,22 +70,37 @@ struct Cfg {
   static constexpr int Q_BYTES = CHUNKS * BM * 128;  // Q tile: CHUNKS x [128 rows x 128 B]
   static constexpr int K_BYTES = CHUNKS * BN * 128;  // K tile: same layout, BN keys
   static constexpr int V_BYTES = BN * D * 2;         // V tile: [BN/64 key blocks][CHUNKS][64 x 128 B]
-  static constexpr int P_BYTES = BM * BN * 2;        // P: BN/64 key chunks x [128 rows x 128 B]
-  static constexpr int STAGES = 2;
-  static constexpr int TMEM_COLS = 512;  // S, O and the row-exchange columns
-  static constexpr int SMEM =
-      1024 + Q_BYTES + STAGES * (K_BYTES + V_BYTES) + (SPLIT ? 2 : 1) * P_BYTES + 256;
+  // 128-key tiles: P overwrites S in TMEM and P V reads it from there (no shared-memory
+  // P, no proxy fence, and the softmax does not wait for the previous P V).  64-key tiles
+  // (head_dim 256) keep P in shared memory in the K-major swizzled layout.
+  static constexpr bool P_TMEM = BN == 128;
+  static constexpr int P_BYTES = P_TMEM ? 0 : BM * BN * 2;  // P: BN/64 key chunks x [128 rows x 128 B]
+  // S / P buffers in TMEM: tile t uses buffer t % NBUF, so S_{t+1} needs P V_{t+1-NBUF}
+  // done; K_t's stage is free once S_{t-KSTAGES} has completed, V_t's once P V_{t-VSTAGES}
+  // has.  Deeper rings (three buffers, three K or V stages) measured no faster: every tile
+  // costs 24 (bf16) or 16 (fp16) MMA instructions of N <= 128 at ~156 cycles each, and the
+  // tensor pipe is busy with them; shorter sequences lost 5-10 % to the longer prologue.
+  static constexpr int NBUF = 2;
+  static constexpr int KSTAGES = 2;
+  static constexpr int VSTAGES = 2;
+  // 128-key tiles: the per-row maximum and sum are exchanged in shared memory; head_dim 256
+  // (no shared memory to spare): in TMEM columns past O.
+  static constexpr bool X_SMEM = P_TMEM;
+  static constexpr int X_BYTES = X_SMEM ? 2 * 4 * BM * 4 : 0;  // [tile parity][slice][row] floats
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int SMEM = 1024 + Q_BYTES + KSTAGES * K_BYTES + VSTAGES * V_BYTES +
+                              (SPLIT ? 2 : 1) * P_BYTES + X_BYTES + 256;
   static_assert(D == 64 || D == 128 || D == 256, "head_dim");
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 struct __align__(8) Bars {
   uint64_t q_full;
-  uint64_t k_full[2];
-  uint64_t v_full[2];
-  uint64_t s_done[2];  // one per S buffer (tile t: buffer t & 1)
-  uint64_t o_done;
-  uint64_t p_full;  // one arrival per softmax warp: P_t is in shared memory
+  uint64_t k_full[3];
+  uint64_t v_full[3];
+  uint64_t s_done[3];   // S_t complete (barrier t % NBUF)
+  uint64_t pv_done[3];  // P V_t complete (barrier t % NBUF)
+  uint64_t p_full;      // one arrival per softmax warp: P_t written
   uint64_t drain;
   uint32_t tmem_base;
   int abort;  // set when a wait gave up; every later wait returns at once
@@ -104,17 +126,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const __grid_constant__ CUtensorMap tmap_v, T* __restrict__ out, Params p,
                 KernelCtl ctl) {
   using C = Cfg<T, D>;
-  constexpr int STAGES = C::STAGES;
+  constexpr int KSTAGES = C::KSTAGES, VSTAGES = C::VSTAGES, NBUF = C::NBUF;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sq = smem;
   uint8_t* sk = sq + C::Q_BYTES;
-  uint8_t* sv_s = sk + STAGES * C::K_BYTES;
-  uint8_t* sp = sv_s + STAGES * C::V_BYTES;
-  uint8_t* sp_lo = sp + C::P_BYTES;  // SPLIT only
-  Bars* bars = reinterpret_cast<Bars*>(sp + (C::SPLIT ? 2 : 1) * C::P_BYTES);
+  uint8_t* sv_s = sk + KSTAGES * C::K_BYTES;
+  uint8_t* sp = sv_s + VSTAGES * C::V_BYTES;  // shared-memory P (64-key tiles only)
+  uint8_t* sp_lo = sp + C::P_BYTES;           // SPLIT only
+  float* xch = reinterpret_cast<float*>(sp + (C::SPLIT ? 2 : 1) * C::P_BYTES);  // X_SMEM only
+  Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(xch) + C::X_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool producer = warp == SOFTMAX_WARPS;  // TMA + MMA issue (one lane)
@@ -136,12 +159,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars->q_full), 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&bars->k_full[s]), 1);
-      mbar_init(smem_u32(&bars->v_full[s]), 1);
+    for (int s = 0; s < KSTAGES; ++s) mbar_init(smem_u32(&bars->k_full[s]), 1);
+    for (int s = 0; s < VSTAGES; ++s) mbar_init(smem_u32(&bars->v_full[s]), 1);
+    for (int s = 0; s < NBUF; ++s) {
       mbar_init(smem_u32(&bars->s_done[s]), 1);
+      mbar_init(smem_u32(&bars->pv_done[s]), 1);
     }
-    mbar_init(smem_u32(&bars->o_done), 1);
     mbar_init(smem_u32(&bars->p_full), SOFTMAX_WARPS);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
@@ -158,10 +181,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  // TMEM columns: S buffers [0, BN) and [BN, 2 BN), O [O_COL, O_COL + D), exchange slots
-  // [X_COL, X_COL + 12): row maxima by tile parity (2 x 4) and the row-sum shares (4).
-  constexpr int O_COL = 2 * BN, X_COL = 384;
-  static_assert(O_COL + D <= X_COL, "TMEM column plan");
+  // TMEM columns: S / P buffers [b BN, (b + 1) BN) for b < NBUF, O [O_COL, O_COL + D), and
+  // with the exchange in TMEM, slots [X_COL, X_COL + 12): row maxima by tile parity (2 x 4)
+  // and the row-sum shares (4).
+  constexpr int O_COL = NBUF * BN, X_COL = O_COL + D;
+  static_assert(X_COL + (C::X_SMEM ? 0 : 12) <= C::TMEM_COLS, "TMEM column plan");
   const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);  // this warp's lanes
   const uint32_t t_o = t_lane + O_COL;
   const uint32_t t_x = t_lane + X_COL;
@@ -180,16 +204,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     *abort = 1;
     atomicOr(ctl.status, code);
   };
+  // Completion of S_t / P V_t: barrier t % NBUF, its (t / NBUF)-th phase.  Every wait below
+  // is for a tile whose barrier's next completion cannot happen before the wait returns.
+  auto wait_s = [&](int t, volatile int* ab) {
+    return mbar_wait_bounded(smem_u32(&bars->s_done[t % NBUF]), (t / NBUF) & 1, ctl.timeout_ns, ab);
+  };
+  auto wait_pv = [&](int t, volatile int* ab) {
+    return mbar_wait_bounded(smem_u32(&bars->pv_done[t % NBUF]), (t / NBUF) & 1, ctl.timeout_ns, ab);
+  };
 
   if (producer) {
     if (lane == 0) {
       // ------------------------------------------------------------ producer
       // Bulk-copy bookkeeping: loads issued into each stage, and those waited for.
-      uint32_t k_issued[2] = {0, 0}, v_issued[2] = {0, 0}, k_used[2] = {0, 0}, v_used[2] = {0, 0};
+      uint32_t k_issued[KSTAGES] = {}, v_issued[VSTAGES] = {}, k_used[KSTAGES] = {}, v_used[VSTAGES] = {};
       bool q_used = false;
       int issued_mma = 0;
       auto load_k = [&](int t) {
-        const int st = t % STAGES;
+        const int st = t % KSTAGES;
         const uint32_t bar = smem_u32(&bars->k_full[st]);
         mbar_arrive_expect_tx(bar, C::K_BYTES);
 #pragma unroll
@@ -199,7 +231,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         ++k_issued[st];
       };
       auto load_v = [&](int t) {
-        const int st = t % STAGES;
+        const int st = t % VSTAGES;
         const uint32_t bar = smem_u32(&bars->v_full[st]);
         mbar_arrive_expect_tx(bar, C::V_BYTES);
 #pragma unroll
@@ -210,9 +242,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                         c * 64, t * BN + kb * 64, kv_mat);
         ++v_issued[st];
       };
-      // S_t = Q K_t^T into S buffer t & 1.
+      // S_t = Q K_t^T into S buffer t % NBUF.
       auto issue_s = [&](int t) {
-        const int st = t % STAGES;
+        const int st = t % KSTAGES;
         bool got = true;
         if (t == 0) got = q_used = mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, abort);
         got = got && mbar_wait_bounded(smem_u32(&bars->k_full[st]), k_used[st] & 1u, ctl.timeout_ns, abort);
@@ -225,30 +257,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kk = 0; kk < D / UMMA_K; ++kk) {
           const uint32_t off_q = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint32_t off_k = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-          tc_mma_f16(tmem + (t & 1) * BN, umma_desc_advance(dq, off_q), umma_desc_advance(dk, off_k),
+          tc_mma_f16(tmem + (t % NBUF) * BN, umma_desc_advance(dq, off_q), umma_desc_advance(dk, off_k),
                      IDESC_S, kk > 0 ? 1u : 0u);
         }
-        tc_commit(smem_u32(&bars->s_done[t & 1]));
+        tc_commit(smem_u32(&bars->s_done[t % NBUF]));
         ++issued_mma;
       };
-      // O += P_t V_t.
+      // O += P_t V_t.  128-key tiles: P_t read from TMEM where the softmax warps wrote it over
+      // S_t (P_hi in the buffer's first BN/2 columns, P_lo in the next BN/2).
       auto issue_pv = [&](int t) {
-        const int st = t % STAGES;
+        const int st = t % VSTAGES;
         if (!mbar_wait_bounded(smem_u32(&bars->v_full[st]), v_used[st] & 1u, ctl.timeout_ns, abort))
           return fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
         ++v_used[st];
         tc_fence_after();
+        const uint32_t t_p = tmem + (t % NBUF) * BN;
+        const uint64_t dv = umma_desc_sw128(smem_u32(sv_s + st * C::V_BYTES), 8192, 1024);
         const uint64_t dp = umma_desc_sw128(smem_u32(sp), 16, 1024);
         const uint64_t dplo = umma_desc_sw128(smem_u32(sp_lo), 16, 1024);
-        const uint64_t dv = umma_desc_sw128(smem_u32(sv_s + st * C::V_BYTES), 8192, 1024);
 #pragma unroll
         for (int kk = 0; kk < BN / UMMA_K; ++kk) {
-          const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
           const uint64_t b = umma_desc_advance(dv, (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048);
-          tc_mma_f16(tmem + O_COL, umma_desc_advance(dp, a_off), b, IDESC_O, (t > 0 || kk > 0) ? 1u : 0u);
-          if (C::SPLIT) tc_mma_f16(tmem + O_COL, umma_desc_advance(dplo, a_off), b, IDESC_O, 1u);
+          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+          if constexpr (C::P_TMEM) {
+            tc_mma_f16_ts(tmem + O_COL, t_p + kk * (UMMA_K / 2), b, IDESC_O, acc);
+            if (C::SPLIT) tc_mma_f16_ts(tmem + O_COL, t_p + BN / 2 + kk * (UMMA_K / 2), b, IDESC_O, 1u);
+          } else {
+            const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+            tc_mma_f16(tmem + O_COL, umma_desc_advance(dp, a_off), b, IDESC_O, acc);
+            if (C::SPLIT) tc_mma_f16(tmem + O_COL, umma_desc_advance(dplo, a_off), b, IDESC_O, 1u);
+          }
         }
-        tc_commit(smem_u32(&bars->o_done));
+        tc_commit(smem_u32(&bars->pv_done[t % NBUF]));
         ++issued_mma;
       };
 
@@ -259,30 +299,35 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 0; c < C::CHUNKS; ++c)
           tma_load_3d(smem_u32(sq + c * BM * 128), &tmap_q, bar, c * 64, qtile * BM, q_mat);
       }
-      for (int t = 0; t < STAGES && t < n_tiles; ++t) {
-        load_k(t);
-        load_v(t);
-      }
+      for (int t = 0; t < KSTAGES && t < n_tiles; ++t) load_k(t);
+      for (int t = 0; t < VSTAGES && t < n_tiles; ++t) load_v(t);
       issue_s(0);
       for (int j = 0; j < n_tiles && !*abort; ++j) {
-        // V_{j+1} into the stage of V_{j-1}, once P V_{j-1} has completed.
-        if (j >= 1 && j + 1 < n_tiles) {
-          if (!mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, abort)) {
+        // K_{j+KSTAGES} into the stage of K_j, once S_j (issued a tile ago) has completed:
+        // first, so that the load is in flight while S_{j+1} waits for K_{j+1}.
+        if (j + KSTAGES < n_tiles) {
+          if (!wait_s(j, abort)) {
             fail(RK_DEV_ERR_TIMEOUT_MMA);
             break;
           }
-          load_v(j + 1);
+          load_k(j + KSTAGES);
         }
-        // S_{j+1} into the buffer of S_{j-1}: every softmax warp has read it (they wrote
-        // P_{j-1}, which P V_{j-1} consumed before this iteration).
-        if (j + 1 < n_tiles) issue_s(j + 1);
-        // K_{j+2} into the stage of K_j, once S_j has completed.
-        if (j + 2 < n_tiles && !*abort) {
-          if (!mbar_wait_bounded(smem_u32(&bars->s_done[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort)) {
+        // S_{j+1} into buffer (j+1) % NBUF once P V_{j+1-NBUF}, the last reader of that
+        // buffer's P, has completed (the softmax warps read S before writing P over it).
+        if (j + 1 < n_tiles && !*abort) {
+          if (j + 1 >= NBUF && !wait_pv(j + 1 - NBUF, abort)) {
             fail(RK_DEV_ERR_TIMEOUT_MMA);
             break;
           }
-          load_k(j + 2);
+          issue_s(j + 1);
+        }
+        // V_{j-1+VSTAGES} into the stage of V_{j-1}, once P V_{j-1} has completed.
+        if (j >= 1 && j - 1 + VSTAGES < n_tiles && !*abort) {
+          if (!wait_pv(j - 1, abort)) {
+            fail(RK_DEV_ERR_TIMEOUT_MMA);
+            break;
+          }
+          load_v(j - 1 + VSTAGES);
         }
         // P_j from all sixteen softmax warps, then O += P_j V_j.
         if (*abort) break;
@@ -300,15 +345,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       if (!q_used && !mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, &never))
         atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
-      for (int s = 0; s < STAGES; ++s) {
-        // Loads issued but never waited for: wait for the last one of each stage.
+      // Loads issued but never waited for: wait for the last one of each stage.
+      for (int s = 0; s < KSTAGES; ++s)
         if (k_issued[s] > k_used[s] &&
             !mbar_wait_bounded(smem_u32(&bars->k_full[s]), (k_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
           atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+      for (int s = 0; s < VSTAGES; ++s)
         if (v_issued[s] > v_used[s] &&
             !mbar_wait_bounded(smem_u32(&bars->v_full[s]), (v_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
           atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
-      }
     }
   } else {
     // -------------------------------------------------------------- softmax
@@ -317,42 +362,62 @@ __global__ void __launch_bounds__(THREADS, 1)
     float m_use = -INFINITY, l_part = 0.f;
     const int key_limit = p.causal ? min(p.seq, q_pos + 1) : p.seq;  // keys this row attends
     for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait_bounded(smem_u32(&bars->s_done[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort))
-        fail(RK_DEV_ERR_TIMEOUT_MMA);
+      if (!wait_s(j, abort)) fail(RK_DEV_ERR_TIMEOUT_MMA);
       tc_fence_after();
-      const uint32_t t_s = t_lane + (j & 1) * BN;
+      const uint32_t t_s = t_lane + (j % NBUF) * BN;
       const int valid = key_limit - (j * BN + slice * SLICE);  // keys i < valid are attended
+      // Raw scores (the scale is applied with the maximum below); masked keys are -inf.  A
+      // warp whose rows all attend every key of its slice skips the mask.
       float sv[SLICE];
-      float mx = -INFINITY;
       {
         uint32_t r[SLICE];
 #pragma unroll
         for (int c = 0; c < SLICE / 16; ++c)
           tmem_ld_32x32b_x16(t_s + slice * SLICE + c * 16, *reinterpret_cast<uint32_t(*)[16]>(r + c * 16));
         tmem_ld_wait();
+        if (__all_sync(0xffffffffu, valid >= SLICE)) {
 #pragma unroll
-        for (int i = 0; i < SLICE; ++i) {
-          sv[i] = i < valid ? __uint_as_float(r[i]) * p.scale_log2 : -INFINITY;
-          mx = fmaxf(mx, sv[i]);
+          for (int i = 0; i < SLICE; ++i) sv[i] = __uint_as_float(r[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < SLICE; ++i) sv[i] = i < valid ? __uint_as_float(r[i]) : -INFINITY;
         }
       }
-      // Row maximum over the four warps of the lane quarter, through TMEM slots of this
-      // tile's parity (a warp writes tile j+2's slots only after the barrier of tile j+1,
-      // which its peers reach after reading tile j's).
-      const uint32_t xs = t_x + (j & 1) * 4;
-      tmem_st_32x32b_x1(xs + slice, __float_as_uint(mx));
-      tmem_st_wait();
-      tc_fence_before();
-      quarter_sync(quarter);
-      tc_fence_after();
-      float m_tile;
+      float mx;
       {
+        float t[SLICE / 2];
+#pragma unroll
+        for (int i = 0; i < SLICE / 2; ++i) t[i] = fmaxf(sv[i], sv[i + SLICE / 2]);
+#pragma unroll
+        for (int w = SLICE / 4; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) t[i] = fmaxf(t[i], t[i + w]);
+        mx = t[0];
+      }
+      // Row maximum over the four warps of the lane quarter, through slots of this tile's
+      // parity (a warp writes tile j+2's slots only after the barrier of tile j+1, which its
+      // peers reach after reading tile j's).
+      float m_raw;
+      if constexpr (C::X_SMEM) {
+        float* xs = xch + (j & 1) * 4 * BM;
+        xs[slice * BM + row] = mx;
+        quarter_sync(quarter);
+        m_raw = fmaxf(fmaxf(xs[row], xs[BM + row]), fmaxf(xs[2 * BM + row], xs[3 * BM + row]));
+      } else {
+        const uint32_t xs = t_x + (j & 1) * 4;
+        tmem_st_32x32b_x1(xs + slice, __float_as_uint(mx));
+        tmem_st_wait();
+        tc_fence_before();
+        quarter_sync(quarter);
+        tc_fence_after();
         uint32_t r[4];
         tmem_ld_32x32b_x4(xs, r);
         tmem_ld_wait();
-        m_tile = fmaxf(fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1])),
-                       fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3])));
+        m_raw = fmaxf(fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1])),
+                      fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3])));
       }
+      // The scale is positive, so the maximum of the scaled scores is the scaled maximum.
+      const float m_tile = m_raw * p.scale_log2;
       // Lazy rescaling: the exponentials keep the old maximum until the row maximum
       // exceeds it by more than 2^8 (P <= 256, exact enough in fp16 and in bf16 hi + lo).
       float alpha = 1.f;
@@ -362,40 +427,65 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       const float m_sub = m_use == -INFINITY ? 0.f : m_use;
 
-      // P = 2^(s - m), rounded (SPLIT: hi + lo), in registers until P V_{j-1} is done.  The
-      // row sum adds the fp32 values (within 2^-16 of hi + lo; fp16 P within 2^-11).
-      float psum = 0.f;
+      // P = 2^(s scale - m) (one FMA, hardware ex2), packed two keys per 32-bit word.  bf16:
+      // P_hi = P with the low 16 bits cleared (exact), P_lo = P - P_hi rounded to bf16, so
+      // P_hi + P_lo keeps ~16 significant bits; fp16: P rounded once.  The row sum adds the
+      // fp32 values.
       uint32_t hi[SLICE / 2], lo[SLICE / 2];
+      float e[SLICE];
+#pragma unroll
+      for (int i = 0; i < SLICE; ++i) e[i] = ex2_approx(fmaf(sv[i], p.scale_log2, -m_sub));
 #pragma unroll
       for (int i = 0; i < SLICE; i += 2) {
-        const float e0 = ex2_approx(sv[i] - m_sub), e1 = ex2_approx(sv[i + 1] - m_sub);
-        psum += e0 + e1;
-        hi[i / 2] = Pack2<T>::from_floats(e0, e1);
-        if (C::SPLIT) {
-          const float2 h2 = Pack2<T>::to_floats(hi[i / 2]);
-          lo[i / 2] = Pack2<T>::from_floats(e0 - h2.x, e1 - h2.y);
+        if constexpr (C::SPLIT) {
+          const uint32_t b0 = __float_as_uint(e[i]), b1 = __float_as_uint(e[i + 1]);
+          hi[i / 2] = __byte_perm(b0, b1, 0x7632);
+          lo[i / 2] = Pack2<T>::from_floats(e[i] - __uint_as_float(b0 & 0xFFFF0000u),
+                                            e[i + 1] - __uint_as_float(b1 & 0xFFFF0000u));
+        } else {
+          hi[i / 2] = Pack2<T>::from_floats(e[i], e[i + 1]);
         }
+      }
+      float psum;
+      {
+        float t[SLICE / 2];
+#pragma unroll
+        for (int i = 0; i < SLICE / 2; ++i) t[i] = e[i] + e[i + SLICE / 2];
+#pragma unroll
+        for (int w = SLICE / 4; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) t[i] = t[i] + t[i + w];
+        psum = t[0];
       }
       l_part = l_part * alpha + psum;
 
-      if (j > 0) {
-        if (!mbar_wait_bounded(smem_u32(&bars->o_done), (j - 1) & 1, ctl.timeout_ns, abort))
-          fail(RK_DEV_ERR_TIMEOUT_MMA);
+      // O is rescaled (rarely, with lazy rescaling) once P V_{j-1} has completed; with P in
+      // TMEM nothing else here waits for the previous tile's P V (a shared-memory P buffer
+      // is free only once P V_{j-1} has read it).
+      const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha != 1.f);
+      if (j > 0 && (rescale || !C::P_TMEM)) {
+        if (!wait_pv(j - 1, abort)) fail(RK_DEV_ERR_TIMEOUT_MMA);
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      }
+      if (rescale) {
 #pragma unroll
-          for (int c = 0; c < OSL / 16; ++c) {
-            uint32_t r[16];
-            tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
-            tmem_ld_wait();
+        for (int c = 0; c < OSL / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
+          tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st_32x32b_x16(t_o + slice * OSL + c * 16, r);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32x32b_x16(t_o + slice * OSL + c * 16, r);
         }
       }
-      {
+      if constexpr (C::P_TMEM) {
+        // P_j over S_j in TMEM: this thread's keys [slice * SLICE, + SLICE) are SLICE / 2
+        // packed columns from slice * SLICE / 2 (P_lo BN / 2 columns further).  Every warp of
+        // the quarter read its scores before the barrier above, so none is overwritten unread.
+        static_assert(SLICE == 32, "score columns per thread");
+        tmem_st_32x32b_x16(t_s + slice * (SLICE / 2), hi);
+        if (C::SPLIT) tmem_st_32x32b_x16(t_s + BN / 2 + slice * (SLICE / 2), lo);
+      } else {
         // This thread's keys: 64-key chunk kf / 64, 16-byte units (kf % 64) / 8 onwards,
         // swizzled by row.
         const int kf = slice * SLICE;
@@ -409,28 +499,37 @@ __global__ void __launch_bounds__(THREADS, 1)
             *reinterpret_cast<uint4*>(sp_lo + unit_off) =
                 make_uint4(lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
         }
+        fence_proxy_async_smem();
       }
+      tmem_st_wait();
       // P_j (and O's rescaling) of this warp is in place: one arrival per warp.
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars->p_full));
     }
 
     // ---- epilogue: O / l  (l = the four warps' shares, added in slice order)
-    if (!mbar_wait_bounded(smem_u32(&bars->o_done), (n_tiles - 1) & 1, ctl.timeout_ns, abort))
-      fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
+    if (!wait_pv(n_tiles - 1, abort)) fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
     tc_fence_after();
-    tmem_st_32x32b_x1(t_x + 8 + slice, __float_as_uint(l_part));
-    tmem_st_wait();
-    tc_fence_before();
-    quarter_sync(quarter);
-    tc_fence_after();
-    uint32_t lr[4];
-    tmem_ld_32x32b_x4(t_x + 8, lr);
-    tmem_ld_wait();
-    const float l = ((__uint_as_float(lr[0]) + __uint_as_float(lr[1])) + __uint_as_float(lr[2])) +
-                    __uint_as_float(lr[3]);
+    float l;
+    if constexpr (C::X_SMEM) {
+      // The slots of parity n_tiles & 1: last written for tile n_tiles - 2, whose readers
+      // passed the barrier of tile n_tiles - 1 before this warp did.
+      float* xs = xch + (n_tiles & 1) * 4 * BM;
+      xs[slice * BM + row] = l_part;
+      quarter_sync(quarter);
+      l = ((xs[row] + xs[BM + row]) + xs[2 * BM + row]) + xs[3 * BM + row];
+    } else {
+      tmem_st_32x32b_x1(t_x + 8 + slice, __float_as_uint(l_part));
+      tmem_st_wait();
+      tc_fence_before();
+      quarter_sync(quarter);
+      tc_fence_after();
+      uint32_t lr[4];
+      tmem_ld_32x32b_x4(t_x + 8, lr);
+      tmem_ld_wait();
+      l = ((__uint_as_float(lr[0]) + __uint_as_float(lr[1])) + __uint_as_float(lr[2])) + __uint_as_float(lr[3]);
+    }
     const float inv = l > 0.f ? 1.0f / l : 0.f;
     const bool store = q_pos < p.seq && !*abort;
     T* orow = out + (static_cast<size_t>(q_mat) * p.seq + q_pos) * D + slice * OSL;

@@ -115,6 +115,23 @@ def test_sdpa_long_and_ragged_sequences(shape, dtype):
     oracle.assert_attention(to_bits(out), ref, ref32, dtype, rounded_p=True)
 
 
+@pytest.mark.parametrize("q_scale", [0.0, 1e-3, 3e-2])
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_sdpa_near_uniform_attention(q_scale, dtype):
+    """Scores near zero: every probability of a row is close to the same value, so a
+    rounding of P that moves them all the same way must cancel in O / l (the row sum adds
+    the probabilities as rounded for P V).  q_scale 0: exactly uniform attention."""
+
+    b, hq, hkv, s, d = 1, 4, 2, 1500, 128
+    q, k, v = _inputs(b, hq, hkv, s, d, dtype, seed=int(q_scale * 1e4) + 3, dist="normal")
+    q = (q.float() * q_scale).to(q.dtype)
+    scale = 1 / math.sqrt(d)
+    for causal in (False, True):
+        out = _native.extension().sdpa(q.cuda(), k.cuda(), v.cuda(), causal, scale)
+        ref, ref32 = oracle.sdpa(to_bits(q), to_bits(k), to_bits(v), causal, scale, dtype)
+        oracle.assert_attention(to_bits(out), ref, ref32, dtype, rounded_p=True)
+
+
 def test_sdpa_is_deterministic_and_propagates_non_finite_values():
     import torch
 
