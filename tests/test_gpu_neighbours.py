@@ -108,6 +108,9 @@ def test_add_rms_norm_matches_reference_fixtures(path):
 # The reference's workload cases (benchmarks/workloads/swiglu-1.0.yaml, add_rms_norm-1.0.yaml).
 SILU_WORKLOADS = [(1, 11008), (128, 11008), (1024, 11008), (512, 28672)]
 NORM_WORKLOADS = [(1, 4096), (128, 4096), (2048, 4096), (1024, 8192)]
+# Prefill rows walked two (or three, past the resident capacity) per CTA, with a CTA left a
+# single row: 1201 rows; 12000 rows of 1024.
+NORM_WORKLOADS += [(1201, 2048), (12000, 1024)]
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "fp16"])
