@@ -361,7 +361,9 @@ template <typename T, bool ADD, int THREADS>
 cudaError_t launch_rows(bool vec, int64_t rows, const void* x, const void* residual,
                         const void* weight, void* out, void* residual_out, int64_t hidden,
                         float eps, cudaStream_t s) {
-  if (vec && hidden / 8 <= static_cast<int64_t>(ROW_CACHE) * THREADS &&
+  // rms_norm only: add_rms_norm already overlaps its reads with the residual_out stores of
+  // the first pass, and measured no faster (slower at 1024 x 8192) with two rows per CTA.
+  if (!ADD && vec && hidden / 8 <= static_cast<int64_t>(ROW_CACHE) * THREADS &&
       rows >= 4ll * device_sm_count()) {
     // Prefill: at least NORM_PIPE_RPC rows per CTA, within the resident capacity.
     const int64_t cap = static_cast<int64_t>(device_sm_count()) * (2048 / THREADS);
