@@ -53,7 +53,9 @@ namespace sdpa {
 
 constexpr int BM = 128;  // query rows per CTA
 constexpr int SOFTMAX_WARPS = 16;
-constexpr int THREADS = 32 * (SOFTMAX_WARPS + 1);  // + the producer warp
+// + an MMA-issue warp, a K (and Q) load warp and a V load warp, meeting on mbarriers only.
+constexpr int MMA_WARP = SOFTMAX_WARPS, K_WARP = SOFTMAX_WARPS + 1, V_WARP = SOFTMAX_WARPS + 2;
+constexpr int THREADS = 32 * (SOFTMAX_WARPS + 3);
 constexpr int UMMA_K = 16;
 
 // SPLIT (bf16): P is stored as P_hi + P_lo, both bf16 (P_hi: P with its low 16 bits
@@ -80,8 +82,8 @@ struct Cfg {
   // has.  Deeper rings (three buffers, three K or V stages) measured no faster: every tile
   // costs 24 (bf16) or 16 (fp16) MMA instructions of N <= 128 at ~156 cycles each, and the
   // tensor pipe is busy with them; shorter sequences lost 5-10 % to the longer prologue.
-  static constexpr int NBUF = 2;
-  static constexpr int KSTAGES = 2;
+  static constexpr int NBUF = P_TMEM ? 3 : 2;
+  static constexpr int KSTAGES = P_TMEM ? 3 : 2;
   static constexpr int VSTAGES = 2;
   // 128-key tiles: the per-row maximum and sum are exchanged in shared memory; head_dim 256
   // (no shared memory to spare): in TMEM columns past O.
@@ -97,10 +99,12 @@ struct Cfg {
 struct __align__(8) Bars {
   uint64_t q_full;
   uint64_t k_full[3];
+  uint64_t k_empty[3];  // MMA commit: the score MMAs no longer read the stage's K tile
   uint64_t v_full[3];
+  uint64_t v_empty[3];  // MMA commit: P V no longer reads the stage's V tile
   uint64_t s_done[3];   // S_t complete (barrier t % NBUF)
   uint64_t pv_done[3];  // P V_t complete (barrier t % NBUF)
-  uint64_t p_full;      // one arrival per softmax warp: P_t written
+  uint64_t p_full[2];   // one arrival per softmax warp: P_t written (barrier t & 1)
   uint64_t drain;
   uint32_t tmem_base;
   int abort;  // set when a wait gave up; every later wait returns at once
@@ -140,7 +144,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(xch) + C::X_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool producer = warp == SOFTMAX_WARPS;  // TMA + MMA issue (one lane)
   // Softmax warps: four share each 32-row TMEM lane quarter, each a quarter of the columns.
   const int quarter = warp & 3, slice = (warp >> 2) & 3;
   constexpr int SLICE = BN / 4;  // score columns per thread
@@ -159,13 +162,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars->q_full), 1);
-    for (int s = 0; s < KSTAGES; ++s) mbar_init(smem_u32(&bars->k_full[s]), 1);
-    for (int s = 0; s < VSTAGES; ++s) mbar_init(smem_u32(&bars->v_full[s]), 1);
+    for (int s = 0; s < KSTAGES; ++s) {
+      mbar_init(smem_u32(&bars->k_full[s]), 1);
+      mbar_init(smem_u32(&bars->k_empty[s]), 1);
+    }
+    for (int s = 0; s < VSTAGES; ++s) {
+      mbar_init(smem_u32(&bars->v_full[s]), 1);
+      mbar_init(smem_u32(&bars->v_empty[s]), 1);
+    }
     for (int s = 0; s < NBUF; ++s) {
       mbar_init(smem_u32(&bars->s_done[s]), 1);
       mbar_init(smem_u32(&bars->pv_done[s]), 1);
     }
-    mbar_init(smem_u32(&bars->p_full), SOFTMAX_WARPS);
+    for (int s = 0; s < 2; ++s) mbar_init(smem_u32(&bars->p_full[s]), SOFTMAX_WARPS);
     mbar_init(smem_u32(&bars->drain), 1);
     bars->abort = 0;
     fence_barrier_init();
@@ -213,43 +222,69 @@ __global__ void __launch_bounds__(THREADS, 1)
     return mbar_wait_bounded(smem_u32(&bars->pv_done[t % NBUF]), (t / NBUF) & 1, ctl.timeout_ns, ab);
   };
 
-  if (producer) {
+  if (warp == K_WARP || warp == V_WARP) {
     if (lane == 0) {
-      // ------------------------------------------------------------ producer
-      // Bulk-copy bookkeeping: loads issued into each stage, and those waited for.
-      uint32_t k_issued[KSTAGES] = {}, v_issued[VSTAGES] = {}, k_used[KSTAGES] = {}, v_used[VSTAGES] = {};
-      bool q_used = false;
-      int issued_mma = 0;
-      auto load_k = [&](int t) {
-        const int st = t % KSTAGES;
-        const uint32_t bar = smem_u32(&bars->k_full[st]);
-        mbar_arrive_expect_tx(bar, C::K_BYTES);
+      // ------------------------------------------------------------ loads
+      // K (and Q) through one warp, V through another, each ring refilled as soon as its
+      // consumer MMAs have completed: a K stage after S_{t-KSTAGES}, a V stage after
+      // P V_{t-VSTAGES}.
+      const bool is_k = warp == K_WARP;
+      const int stages = is_k ? KSTAGES : VSTAGES;
+      uint64_t* full = is_k ? bars->k_full : bars->v_full;
+      uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
+      uint32_t issued[3] = {0, 0, 0};
+      if (is_k) {
+        const uint32_t bar = smem_u32(&bars->q_full);
+        mbar_arrive_expect_tx(bar, C::Q_BYTES);
 #pragma unroll
         for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_3d(smem_u32(sk + st * C::K_BYTES + c * BN * 128), &tmap_k, bar, c * 64, t * BN,
-                      kv_mat);
-        ++k_issued[st];
-      };
-      auto load_v = [&](int t) {
-        const int st = t % VSTAGES;
-        const uint32_t bar = smem_u32(&bars->v_full[st]);
-        mbar_arrive_expect_tx(bar, C::V_BYTES);
-#pragma unroll
-        for (int kb = 0; kb < BN / 64; ++kb)
+          tma_load_3d(smem_u32(sq + c * BM * 128), &tmap_q, bar, c * 64, qtile * BM, q_mat);
+      }
+      for (int t = 0; t < n_tiles; ++t) {
+        const int st = t % stages;
+        if (t >= stages &&
+            !mbar_wait_bounded(smem_u32(&empty[st]), ((t / stages) - 1) & 1, ctl.timeout_ns, abort)) {
+          fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+          break;
+        }
+        const uint32_t bar = smem_u32(&full[st]);
+        if (is_k) {
+          mbar_arrive_expect_tx(bar, C::K_BYTES);
 #pragma unroll
           for (int c = 0; c < C::CHUNKS; ++c)
-            tma_load_3d(smem_u32(sv_s + st * C::V_BYTES + (kb * C::CHUNKS + c) * 8192), &tmap_v, bar,
-                        c * 64, t * BN + kb * 64, kv_mat);
-        ++v_issued[st];
-      };
+            tma_load_3d(smem_u32(sk + st * C::K_BYTES + c * BN * 128), &tmap_k, bar, c * 64, t * BN, kv_mat);
+        } else {
+          mbar_arrive_expect_tx(bar, C::V_BYTES);
+#pragma unroll
+          for (int kb = 0; kb < BN / 64; ++kb)
+#pragma unroll
+            for (int c = 0; c < C::CHUNKS; ++c)
+              tma_load_3d(smem_u32(sv_s + st * C::V_BYTES + (kb * C::CHUNKS + c) * 8192), &tmap_v, bar,
+                          c * 64, t * BN + kb * 64, kv_mat);
+        }
+        ++issued[st];
+      }
+      // No bulk copy may still be landing when the CTA exits: wait for the last load of each
+      // stage (earlier ones completed before the stage was refilled) and for Q.
+      for (int st = 0; st < stages; ++st)
+        if (issued[st] > 0 &&
+            !mbar_wait_bounded(smem_u32(&full[st]), (issued[st] - 1) & 1u, ctl.timeout_ns, &never))
+          atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+      if (is_k && !mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, &never))
+        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
+    }
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issue
+      int issued_mma = 0;
       // S_t = Q K_t^T into S buffer t % NBUF.
-      auto issue_s = [&](int t) {
+      auto issue_s = [&](int t) -> bool {
         const int st = t % KSTAGES;
-        bool got = true;
-        if (t == 0) got = q_used = mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, abort);
-        got = got && mbar_wait_bounded(smem_u32(&bars->k_full[st]), k_used[st] & 1u, ctl.timeout_ns, abort);
-        if (!got) return fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
-        ++k_used[st];
+        if ((t == 0 && !mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, abort)) ||
+            !mbar_wait_bounded(smem_u32(&bars->k_full[st]), (t / KSTAGES) & 1, ctl.timeout_ns, abort)) {
+          fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+          return false;
+        }
         tc_fence_after();
         const uint64_t dq = umma_desc_sw128(smem_u32(sq), 16, 1024);
         const uint64_t dk = umma_desc_sw128(smem_u32(sk + st * C::K_BYTES), 16, 1024);
@@ -261,15 +296,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                      IDESC_S, kk > 0 ? 1u : 0u);
         }
         tc_commit(smem_u32(&bars->s_done[t % NBUF]));
+        tc_commit(smem_u32(&bars->k_empty[st]));
         ++issued_mma;
+        return true;
       };
       // O += P_t V_t.  128-key tiles: P_t read from TMEM where the softmax warps wrote it over
       // S_t (P_hi in the buffer's first BN/2 columns, P_lo in the next BN/2).
-      auto issue_pv = [&](int t) {
+      auto issue_pv = [&](int t) -> bool {
         const int st = t % VSTAGES;
-        if (!mbar_wait_bounded(smem_u32(&bars->v_full[st]), v_used[st] & 1u, ctl.timeout_ns, abort))
-          return fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
-        ++v_used[st];
+        if (!mbar_wait_bounded(smem_u32(&bars->v_full[st]), (t / VSTAGES) & 1, ctl.timeout_ns, abort)) {
+          fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
+          return false;
+        }
         tc_fence_after();
         const uint32_t t_p = tmem + (t % NBUF) * BN;
         const uint64_t dv = umma_desc_sw128(smem_u32(sv_s + st * C::V_BYTES), 8192, 1024);
@@ -289,71 +327,34 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         tc_commit(smem_u32(&bars->pv_done[t % NBUF]));
+        tc_commit(smem_u32(&bars->v_empty[st]));
         ++issued_mma;
+        return true;
       };
-
-      {
-        const uint32_t bar = smem_u32(&bars->q_full);
-        mbar_arrive_expect_tx(bar, C::Q_BYTES);
-#pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_3d(smem_u32(sq + c * BM * 128), &tmap_q, bar, c * 64, qtile * BM, q_mat);
-      }
-      for (int t = 0; t < KSTAGES && t < n_tiles; ++t) load_k(t);
-      for (int t = 0; t < VSTAGES && t < n_tiles; ++t) load_v(t);
-      issue_s(0);
-      for (int j = 0; j < n_tiles && !*abort; ++j) {
-        // K_{j+KSTAGES} into the stage of K_j, once S_j (issued a tile ago) has completed:
-        // first, so that the load is in flight while S_{j+1} waits for K_{j+1}.
-        if (j + KSTAGES < n_tiles) {
-          if (!wait_s(j, abort)) {
-            fail(RK_DEV_ERR_TIMEOUT_MMA);
-            break;
-          }
-          load_k(j + KSTAGES);
-        }
+      bool ok = issue_s(0);
+      for (int j = 0; j < n_tiles && ok && !*abort; ++j) {
         // S_{j+1} into buffer (j+1) % NBUF once P V_{j+1-NBUF}, the last reader of that
         // buffer's P, has completed (the softmax warps read S before writing P over it).
-        if (j + 1 < n_tiles && !*abort) {
+        if (j + 1 < n_tiles) {
           if (j + 1 >= NBUF && !wait_pv(j + 1 - NBUF, abort)) {
             fail(RK_DEV_ERR_TIMEOUT_MMA);
             break;
           }
-          issue_s(j + 1);
-        }
-        // V_{j-1+VSTAGES} into the stage of V_{j-1}, once P V_{j-1} has completed.
-        if (j >= 1 && j - 1 + VSTAGES < n_tiles && !*abort) {
-          if (!wait_pv(j - 1, abort)) {
-            fail(RK_DEV_ERR_TIMEOUT_MMA);
-            break;
-          }
-          load_v(j - 1 + VSTAGES);
+          if (!issue_s(j + 1)) break;
         }
         // P_j from all sixteen softmax warps, then O += P_j V_j.
-        if (*abort) break;
-        if (!mbar_wait_bounded(smem_u32(&bars->p_full), j & 1, ctl.timeout_ns, abort)) {
+        if (!mbar_wait_bounded(smem_u32(&bars->p_full[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort)) {
           fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
           break;
         }
-        issue_pv(j);
+        if (!issue_pv(j)) break;
       }
-      // ---- drain: every MMA and bulk copy issued by this CTA completes before exit.
+      // ---- drain: every MMA this CTA issued completes before TMEM is released.
       if (issued_mma > 0) {
         tc_commit(smem_u32(&bars->drain));
         if (!mbar_wait_bounded(smem_u32(&bars->drain), 0, ctl.timeout_ns, &never))
           atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
       }
-      if (!q_used && !mbar_wait_bounded(smem_u32(&bars->q_full), 0, ctl.timeout_ns, &never))
-        atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
-      // Loads issued but never waited for: wait for the last one of each stage.
-      for (int s = 0; s < KSTAGES; ++s)
-        if (k_issued[s] > k_used[s] &&
-            !mbar_wait_bounded(smem_u32(&bars->k_full[s]), (k_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
-          atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
-      for (int s = 0; s < VSTAGES; ++s)
-        if (v_issued[s] > v_used[s] &&
-            !mbar_wait_bounded(smem_u32(&bars->v_full[s]), (v_issued[s] - 1) & 1u, ctl.timeout_ns, &never))
-          atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_DRAIN);
     }
   } else {
     // -------------------------------------------------------------- softmax
@@ -505,7 +506,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // P_j (and O's rescaling) of this warp is in place: one arrival per warp.
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars->p_full));
+      if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[j & 1]));
     }
 
     // ---- epilogue: O / l  (l = the four warps' shares, added in slice order)
