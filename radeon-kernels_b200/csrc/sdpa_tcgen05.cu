@@ -9,14 +9,14 @@
 // with torch's SDPA (its dispatch manifest has no native entry, dispatch/sdpa-1.0.json); its
 // HIP candidate walks keys one at a time per query row (benchmarks/sdpa/native_sdpa.hip).
 //
-// One CTA per (128-row query tile, query head, batch), 544 threads (16 softmax warps and a
-// producer warp), flash-style:
-//   * one producer thread issues the TMA loads -- the Q tile once, K and V tiles of BN keys
-//     (128; 64 for head_dim 256, to fit shared memory) in two-stage rings, through 3-D
-//     tensor maps over the [batch*heads, S, D] stacks, so rows past the sequence read as zero
-//     instead of the next head's -- and the MMAs;
-//   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into one of two TMEM buffers: Q and K
-//     are K-major 128-byte-swizzled tiles straight from TMA;
+// One CTA per (128-row query tile, query head, batch), 608 threads (16 softmax warps, an
+// MMA-issue warp and two load warps), flash-style:
+//   * TMA loads -- the Q tile once, K and V tiles of BN keys (128; 64 for head_dim 256, to fit
+//     shared memory) in rings of three (K) and two (V) stages (two and two at head_dim 256),
+//     through 3-D tensor maps over the [batch*heads, S, D] stacks, so rows past the sequence
+//     read as zero instead of the next head's;
+//   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into one of three TMEM buffers (two at
+//     head_dim 256): Q and K are K-major 128-byte-swizzled tiles straight from TMA;
 //   * four warps share each 32-row TMEM lane quarter, each thread a quarter of its row's
 //     scores: masks on the raw scores (skipped when every row of the warp attends every key
 //     of its slice), tree maximum, the row maximum combined over the four warps in a fixed
@@ -31,12 +31,15 @@
 //   * O += P V (M = 128, N = head_dim, K = BN keys) into TMEM columns past the S buffers: V
 //     is an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
 //   * epilogue: O / l rounded to the dtype; l is the four warps' shares added in order.
-// The row sum l adds the fp32 exponentials.  The producer loads K_{j+2} first in each
-// iteration, then issues S_{j+1} (scores of the next tile during this tile's softmax), the
-// next V, and P V_j.  Each MMA instruction costs ~156 SM cycles whatever N up to 256, so a
-// 128 x 128 tile (8 + 8 MMAs, 8 more for bf16's P_lo) is bound by the tensor pipe's
-// instruction rate.  Every wait is bounded (status word on expiry) and made CTA-uniform;
-// before TMEM is released every MMA and bulk copy this CTA issued has completed.
+// The row sum l adds the fp32 exponentials.  Three more warps feed them, meeting on
+// mbarriers only: one loads Q and the K ring, one the V ring (each stage refilled as soon as
+// its consumer MMAs complete), one issues the MMAs -- S_{j+1} as soon as its K tile has
+// landed and its TMEM buffer's last P V has completed, then P V_j once the sixteen softmax
+// warps have written P_j.  Back-to-back tcgen05.mma instructions of M = 128, K = 16 run at
+// 64 cycles for N = 128 (the tensor pipe's full rate), so a 128 x 128 bf16 tile's 24 MMAs
+// need ~0.8 us; the softmax warps (~1.4 us per tile, most of it the 16 K hardware ex2 at 16
+// per clock per SM) set the pace.  Every wait is bounded (status word on expiry) and made
+// CTA-uniform; before TMEM is released every MMA and bulk copy this CTA issued has completed.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -79,9 +82,8 @@ struct Cfg {
   static constexpr int P_BYTES = P_TMEM ? 0 : BM * BN * 2;  // P: BN/64 key chunks x [128 rows x 128 B]
   // S / P buffers in TMEM: tile t uses buffer t % NBUF, so S_{t+1} needs P V_{t+1-NBUF}
   // done; K_t's stage is free once S_{t-KSTAGES} has completed, V_t's once P V_{t-VSTAGES}
-  // has.  Deeper rings (three buffers, three K or V stages) measured no faster: every tile
-  // costs 24 (bf16) or 16 (fp16) MMA instructions of N <= 128 at ~156 cycles each, and the
-  // tensor pipe is busy with them; shorter sequences lost 5-10 % to the longer prologue.
+  // has.  Three buffers and three K stages pay off only with the separate load and MMA
+  // warps (with one producer thread doing everything in turn they measured no faster).
   static constexpr int NBUF = P_TMEM ? 3 : 2;
   static constexpr int KSTAGES = P_TMEM ? 3 : 2;
   static constexpr int VSTAGES = 2;
