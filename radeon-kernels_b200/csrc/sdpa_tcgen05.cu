@@ -9,7 +9,7 @@
 // with torch's SDPA (its dispatch manifest has no native entry, dispatch/sdpa-1.0.json); its
 // HIP candidate walks keys one at a time per query row (benchmarks/sdpa/native_sdpa.hip).
 //
-// One CTA per (128-row query tile, query head, batch), 608 threads (16 softmax warps, an
+// One CTA per (128-row query tile, query head, batch), 352 threads (8 softmax warps, an
 // MMA-issue warp and two load warps), flash-style:
 //   * TMA loads -- the Q tile once, K and V tiles of BN keys (128; 64 for head_dim 256, to fit
 //     shared memory) in rings of three (K) and two (V) stages (two and two at head_dim 256),
@@ -17,9 +17,8 @@
 //     read as zero instead of the next head's;
 //   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into one of three TMEM buffers (two at
 //     head_dim 256): Q and K are K-major 128-byte-swizzled tiles straight from TMA;
-//   * four warps share each 32-row TMEM lane quarter, each thread a quarter of its row's
-//     scores: masks on the raw scores (skipped when every row of the warp attends every key
-//     of its slice), tree maximum, the row maximum combined over the four warps in a fixed
+//   * two warps share each 32-row TMEM lane quarter, each thread half of its row's scores: masks on the raw scores (skipped when every row of the warp attends every key
+//     of its slice), tree maximum, the row maximum combined over the two warps in a fixed
 //     order, the scale folded into one FMA before the hardware ex2, online softmax in fp32
 //     that rescales the thread's quarter of the O row in TMEM only when the maximum grew by
 //     more than 2^8 (lazy rescaling).  P = 2^(s - m) is rounded to fp16, or for bf16 kept as
@@ -30,11 +29,11 @@
 //     K-major swizzled layout instead;
 //   * O += P V (M = 128, N = head_dim, K = BN keys) into TMEM columns past the S buffers: V
 //     is an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
-//   * epilogue: O / l rounded to the dtype; l is the four warps' shares added in order.
+//   * epilogue: O / l rounded to the dtype; l is the two warps' shares added in order.
 // The row sum l adds the fp32 exponentials.  Three more warps feed them, meeting on
 // mbarriers only: one loads Q and the K ring, one the V ring (each stage refilled as soon as
 // its consumer MMAs complete), one issues the MMAs -- S_{j+1} as soon as its K tile has
-// landed and its TMEM buffer's last P V has completed, then P V_j once the sixteen softmax
+// landed and its TMEM buffer's last P V has completed, then P V_j once the eight softmax
 // warps have written P_j.  Back-to-back tcgen05.mma instructions of M = 128, K = 16 run at
 // 64 cycles for N = 128 (the tensor pipe's full rate), so a 128 x 128 bf16 tile's 24 MMAs
 // need ~0.8 us; the softmax warps (~1.4 us per tile, most of it the 16 K hardware ex2 at 16
@@ -55,7 +54,12 @@ namespace rk {
 namespace sdpa {
 
 constexpr int BM = 128;  // query rows per CTA
-constexpr int SOFTMAX_WARPS = 16;
+// Two softmax warps per TMEM lane quarter (64 score columns per thread at 128-key tiles):
+// measured 2-5 % faster than four (32 columns each) on every benchmark shape -- half the
+// cross-warp exchange, and each thread's per-tile bookkeeping spread over twice the scores.
+constexpr int SOFTMAX_WARPS = 8;
+constexpr int NSL = SOFTMAX_WARPS / 4;  // warps (column slices) per TMEM lane quarter
+static_assert(NSL == 2 || NSL == 4, "softmax warps");
 // + an MMA-issue warp, a K (and Q) load warp and a V load warp, meeting on mbarriers only.
 constexpr int MMA_WARP = SOFTMAX_WARPS, K_WARP = SOFTMAX_WARPS + 1, V_WARP = SOFTMAX_WARPS + 2;
 constexpr int THREADS = 32 * (SOFTMAX_WARPS + 3);
@@ -90,7 +94,7 @@ struct Cfg {
   // 128-key tiles: the per-row maximum and sum are exchanged in shared memory; head_dim 256
   // (no shared memory to spare): in TMEM columns past O.
   static constexpr bool X_SMEM = P_TMEM;
-  static constexpr int X_BYTES = X_SMEM ? 2 * 4 * BM * 4 : 0;  // [tile parity][slice][row] floats
+  static constexpr int X_BYTES = X_SMEM ? 2 * NSL * BM * 4 : 0;  // [tile parity][slice][row] floats
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM = 1024 + Q_BYTES + KSTAGES * K_BYTES + VSTAGES * V_BYTES +
                               (SPLIT ? 2 : 1) * P_BYTES + X_BYTES + 256;
@@ -121,9 +125,9 @@ struct Params {
   float scale_log2;  // scale * log2(e)
 };
 
-// Named barrier of the four softmax warps that share TMEM lane quarter q (ids 1..4).
+// Named barrier of the NSL softmax warps that share TMEM lane quarter q (ids 1..4).
 __device__ __forceinline__ void quarter_sync(int q) {
-  asm volatile("bar.sync %0, 128;" ::"r"(q + 1) : "memory");
+  asm volatile("bar.sync %0, %1;" ::"r"(q + 1), "n"(32 * NSL) : "memory");
 }
 
 template <typename T, int D>
@@ -147,9 +151,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Softmax warps: four share each 32-row TMEM lane quarter, each a quarter of the columns.
-  const int quarter = warp & 3, slice = (warp >> 2) & 3;
-  constexpr int SLICE = BN / 4;  // score columns per thread
-  constexpr int OSL = D / 4;     // output columns per thread
+  const int quarter = warp & 3, slice = warp >> 2;
+  constexpr int SLICE = BN / NSL;  // score columns per thread
+  constexpr int OSL = D / NSL;     // output columns per thread
   // Heavier (later, under the causal mask) query tiles first.
   const int qtile = p.q_tiles - 1 - static_cast<int>(blockIdx.x);
   const int head = blockIdx.y, batch = blockIdx.z;
@@ -344,7 +348,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           if (!issue_s(j + 1)) break;
         }
-        // P_j from all sixteen softmax warps, then O += P_j V_j.
+        // P_j from all eight softmax warps, then O += P_j V_j.
         if (!mbar_wait_bounded(smem_u32(&bars->p_full[j & 1]), (j >> 1) & 1, ctl.timeout_ns, abort)) {
           fail(RK_DEV_ERR_TIMEOUT_PRODUCER);
           break;
@@ -360,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // -------------------------------------------------------------- softmax
-    // Row state (identical in the four warps that share a row): the maximum the
+    // Row state (identical in the two warps that share a row): the maximum the
     // exponentials are taken against, and this warp's share of the row sum.
     float m_use = -INFINITY, l_part = 0.f;
     const int key_limit = p.causal ? min(p.seq, q_pos + 1) : p.seq;  // keys this row attends
@@ -397,15 +401,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int i = 0; i < w; ++i) t[i] = fmaxf(t[i], t[i + w]);
         mx = t[0];
       }
-      // Row maximum over the four warps of the lane quarter, through slots of this tile's
+      // Row maximum over the two warps of the lane quarter, through slots of this tile's
       // parity (a warp writes tile j+2's slots only after the barrier of tile j+1, which its
       // peers reach after reading tile j's).
       float m_raw;
       if constexpr (C::X_SMEM) {
-        float* xs = xch + (j & 1) * 4 * BM;
+        float* xs = xch + (j & 1) * NSL * BM;
         xs[slice * BM + row] = mx;
         quarter_sync(quarter);
-        m_raw = fmaxf(fmaxf(xs[row], xs[BM + row]), fmaxf(xs[2 * BM + row], xs[3 * BM + row]));
+        m_raw = xs[row];
+#pragma unroll
+        for (int q = 1; q < NSL; ++q) m_raw = fmaxf(m_raw, xs[q * BM + row]);
       } else {
         const uint32_t xs = t_x + (j & 1) * 4;
         tmem_st_32x32b_x1(xs + slice, __float_as_uint(mx));
@@ -416,8 +422,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t r[4];
         tmem_ld_32x32b_x4(xs, r);
         tmem_ld_wait();
-        m_raw = fmaxf(fmaxf(__uint_as_float(r[0]), __uint_as_float(r[1])),
-                      fmaxf(__uint_as_float(r[2]), __uint_as_float(r[3])));
+        m_raw = __uint_as_float(r[0]);  // only the NSL slots written this tile
+#pragma unroll
+        for (int q = 1; q < NSL; ++q) m_raw = fmaxf(m_raw, __uint_as_float(r[q]));
       }
       // The scale is positive, so the maximum of the scaled scores is the scaled maximum.
       const float m_tile = m_raw * p.scale_log2;
@@ -485,9 +492,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         // P_j over S_j in TMEM: this thread's keys [slice * SLICE, + SLICE) are SLICE / 2
         // packed columns from slice * SLICE / 2 (P_lo BN / 2 columns further).  Every warp of
         // the quarter read its scores before the barrier above, so none is overwritten unread.
-        static_assert(SLICE == 32, "score columns per thread");
-        tmem_st_32x32b_x16(t_s + slice * (SLICE / 2), hi);
-        if (C::SPLIT) tmem_st_32x32b_x16(t_s + BN / 2 + slice * (SLICE / 2), lo);
+        static_assert(SLICE == 32 || SLICE == 64, "score columns per thread");
+        if constexpr (SLICE == 32) {
+          tmem_st_32x32b_x16(t_s + slice * (SLICE / 2), hi);
+          if (C::SPLIT) tmem_st_32x32b_x16(t_s + BN / 2 + slice * (SLICE / 2), lo);
+        } else {
+          tmem_st_32x32b_x32(t_s + slice * (SLICE / 2), hi);
+          if (C::SPLIT) tmem_st_32x32b_x32(t_s + BN / 2 + slice * (SLICE / 2), lo);
+        }
       } else {
         // This thread's keys: 64-key chunk kf / 64, 16-byte units (kf % 64) / 8 onwards,
         // swizzled by row.
@@ -511,17 +523,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[j & 1]));
     }
 
-    // ---- epilogue: O / l  (l = the four warps' shares, added in slice order)
+    // ---- epilogue: O / l  (l = the two warps' shares, added in slice order)
     if (!wait_pv(n_tiles - 1, abort)) fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
     tc_fence_after();
     float l;
     if constexpr (C::X_SMEM) {
       // The slots of parity n_tiles & 1: last written for tile n_tiles - 2, whose readers
       // passed the barrier of tile n_tiles - 1 before this warp did.
-      float* xs = xch + (n_tiles & 1) * 4 * BM;
+      float* xs = xch + (n_tiles & 1) * NSL * BM;
       xs[slice * BM + row] = l_part;
       quarter_sync(quarter);
-      l = ((xs[row] + xs[BM + row]) + xs[2 * BM + row]) + xs[3 * BM + row];
+      l = xs[row];
+#pragma unroll
+      for (int q = 1; q < NSL; ++q) l += xs[q * BM + row];
     } else {
       tmem_st_32x32b_x1(t_x + 8 + slice, __float_as_uint(l_part));
       tmem_st_wait();
@@ -531,7 +545,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t lr[4];
       tmem_ld_32x32b_x4(t_x + 8, lr);
       tmem_ld_wait();
-      l = ((__uint_as_float(lr[0]) + __uint_as_float(lr[1])) + __uint_as_float(lr[2])) + __uint_as_float(lr[3]);
+      l = __uint_as_float(lr[0]);
+#pragma unroll
+      for (int q = 1; q < NSL; ++q) l += __uint_as_float(lr[q]);
     }
     const float inv = l > 0.f ? 1.0f / l : 0.f;
     const bool store = q_pos < p.seq && !*abort;
