@@ -441,31 +441,40 @@ __global__ void __launch_bounds__(THREADS, 1)
       // P_hi = P with the low 16 bits cleared (exact), P_lo = P - P_hi rounded to bf16, so
       // P_hi + P_lo keeps ~16 significant bits; fp16: P rounded once.  The row sum adds the
       // fp32 values.
+      // Packed fp32 pairs (fma.rn.f32x2, add.rn.f32x2) for the scale and the sums: the loop
+      // is issue-bound, and each lane rounds as the scalar operation would.
       uint32_t hi[SLICE / 2], lo[SLICE / 2];
       float e[SLICE];
+      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_sub, -m_sub);
 #pragma unroll
-      for (int i = 0; i < SLICE; ++i) e[i] = ex2_approx(fmaf(sv[i], p.scale_log2, -m_sub));
+      for (int i = 0; i < SLICE; i += 2) {
+        const float2 x = ffma2(make_float2(sv[i], sv[i + 1]), sc2, nm2);
+        e[i] = ex2_approx(x.x);
+        e[i + 1] = ex2_approx(x.y);
+      }
 #pragma unroll
       for (int i = 0; i < SLICE; i += 2) {
         if constexpr (C::SPLIT) {
           const uint32_t b0 = __float_as_uint(e[i]), b1 = __float_as_uint(e[i + 1]);
           hi[i / 2] = __byte_perm(b0, b1, 0x7632);
-          lo[i / 2] = Pack2<T>::from_floats(e[i] - __uint_as_float(b0 & 0xFFFF0000u),
-                                            e[i + 1] - __uint_as_float(b1 & 0xFFFF0000u));
+          const float2 r = fadd2(make_float2(e[i], e[i + 1]), make_float2(-__uint_as_float(b0 & 0xFFFF0000u),
+                                                                          -__uint_as_float(b1 & 0xFFFF0000u)));
+          lo[i / 2] = Pack2<T>::from_floats(r.x, r.y);
         } else {
           hi[i / 2] = Pack2<T>::from_floats(e[i], e[i + 1]);
         }
       }
       float psum;
       {
-        float t[SLICE / 2];
+        float2 t[SLICE / 4];
 #pragma unroll
-        for (int i = 0; i < SLICE / 2; ++i) t[i] = e[i] + e[i + SLICE / 2];
+        for (int i = 0; i < SLICE / 4; ++i)
+          t[i] = fadd2(make_float2(e[2 * i], e[2 * i + 1]), make_float2(e[2 * i + SLICE / 2], e[2 * i + 1 + SLICE / 2]));
 #pragma unroll
-        for (int w = SLICE / 4; w >= 1; w >>= 1)
+        for (int w = SLICE / 8; w >= 1; w >>= 1)
 #pragma unroll
-          for (int i = 0; i < w; ++i) t[i] = t[i] + t[i + w];
-        psum = t[0];
+          for (int i = 0; i < w; ++i) t[i] = fadd2(t[i], t[i + w]);
+        psum = t[0].x + t[0].y;
       }
       l_part = l_part * alpha + psum;
 
