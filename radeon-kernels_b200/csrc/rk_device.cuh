@@ -298,6 +298,14 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   return unpack_f2(d);
 }
 
+// Three-input maximum in one instruction (max.f32 with three sources; a NaN input is
+// ignored as by fmaxf unless every input is NaN).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // ------------------------------------------------------------ clusters
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

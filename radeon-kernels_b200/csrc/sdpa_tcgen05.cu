@@ -392,14 +392,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       float mx;
       {
-        float t[SLICE / 2];
+        // Four independent chains of three-input maxima (about half the instructions of a
+        // two-input tree; the maximum is exact in any order).
+        float a4[4] = {sv[0], sv[1], sv[2], sv[3]};
 #pragma unroll
-        for (int i = 0; i < SLICE / 2; ++i) t[i] = fmaxf(sv[i], sv[i + SLICE / 2]);
-#pragma unroll
-        for (int w = SLICE / 4; w >= 1; w >>= 1)
-#pragma unroll
-          for (int i = 0; i < w; ++i) t[i] = fmaxf(t[i], t[i + w]);
-        mx = t[0];
+        for (int i = 4; i < SLICE; i += 2) a4[(i / 2) % 4] = fmax3(a4[(i / 2) % 4], sv[i], sv[i + 1]);
+        mx = fmax3(fmaxf(a4[0], a4[1]), a4[2], a4[3]);
       }
       // Row maximum over the two warps of the lane quarter, through slots of this tile's
       // parity (a warp writes tile j+2's slots only after the barrier of tile j+1, which its
