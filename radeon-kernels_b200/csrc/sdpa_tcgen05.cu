@@ -15,21 +15,25 @@
 //     shared memory) in rings of three (K) and two (V) stages (two and two at head_dim 256),
 //     through 3-D tensor maps over the [batch*heads, S, D] stacks, so rows past the sequence
 //     read as zero instead of the next head's;
-//   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into one of three TMEM buffers (two at
-//     head_dim 256): Q and K are K-major 128-byte-swizzled tiles straight from TMA;
-//   * two warps share each 32-row TMEM lane quarter, each thread half of its row's scores: masks on the raw scores (skipped when every row of the warp attends every key
-//     of its slice), tree maximum, the row maximum combined over the two warps in a fixed
-//     order, the scale folded into one FMA before the hardware ex2, online softmax in fp32
-//     that rescales the thread's quarter of the O row in TMEM only when the maximum grew by
-//     more than 2^8 (lazy rescaling).  P = 2^(s - m) is rounded to fp16, or for bf16 kept as
-//     two bf16 terms P_hi + P_lo (see Cfg::SPLIT);
-//   * 128-key tiles: P is written over its S buffer in TMEM (tcgen05.st, two 16-bit values
-//     per column) and O += P V takes A from TMEM, so the softmax never waits for the
-//     previous tile's P V except to rescale O; 64-key tiles write P to shared memory in the
-//     K-major swizzled layout instead;
+//   * S = Q K^T (M = 128, N = BN keys, K = head_dim) into one of three TMEM buffers at
+//     head_dim 64, two otherwise: Q and K are K-major 128-byte-swizzled tiles from TMA;
+//   * two warps share each 32-row TMEM lane quarter, each thread half of its row's scores:
+//     masks on the raw scores (skipped when every row of the warp attends every key of its
+//     slice), tree maximum, the scale folded into one FMA before the hardware ex2, online
+//     softmax in fp32 that rescales O in TMEM only when the maximum grew by more than 2^8
+//     (lazy rescaling).  P = 2^(s - m) is rounded to fp16, or for bf16 kept as two bf16
+//     terms P_hi + P_lo (see Cfg::SPLIT);
+//   * 128-key tiles: each warp keeps its own maximum, sum and O accumulator over its half of
+//     the keys (Cfg::SPLIT_O), so the two warps of a quarter never wait for each other in the
+//     key loop; P is written over the warp's own S columns in TMEM (tcgen05.st, two 16-bit
+//     values per column) and O += P V takes A from TMEM, so the softmax never waits for the
+//     previous tile's P V except to rescale O.  64-key tiles (head_dim 256) exchange the row
+//     maximum every tile, share one O and write P to shared memory in the K-major swizzled
+//     layout;
 //   * O += P V (M = 128, N = head_dim, K = BN keys) into TMEM columns past the S buffers: V
 //     is an MN-major operand (row-major [keys, head_dim] tiles, as a GEMM's B);
-//   * epilogue: O / l rounded to the dtype; l is the two warps' shares added in order.
+//   * epilogue: the warps' partial results merged in slice order (O = sum w_q O_q, l = sum
+//     w_q l_q, w_q = 2^(m_q - m)), O / l rounded to the dtype.
 // The row sum l adds the fp32 exponentials.  Three more warps feed them, meeting on
 // mbarriers only: one loads Q and the K ring, one the V ring (each stage refilled as soon as
 // its consumer MMAs complete), one issues the MMAs -- S_{j+1} as soon as its K tile has
@@ -84,17 +88,26 @@ struct Cfg {
   // (head_dim 256) keep P in shared memory in the K-major swizzled layout.
   static constexpr bool P_TMEM = BN == 128;
   static constexpr int P_BYTES = P_TMEM ? 0 : BM * BN * 2;  // P: BN/64 key chunks x [128 rows x 128 B]
+  // SPLIT_O (128-key tiles): each column slice (warp) of a lane quarter keeps its own O
+  // accumulator in TMEM and its own running maximum and sum over its keys, and the slices
+  // are combined once, in the epilogue (as split-K partitions are merged).  The warps of a
+  // quarter then never wait for each other inside the key loop (no per-tile exchange of the
+  // row maximum); the P V MMAs are the same, each K step adding into its slice's O.
+  // head_dim 256 (no TMEM for a second O) exchanges the maximum every tile.
+  static constexpr bool SPLIT_O = P_TMEM;
+  static constexpr int N_O = SPLIT_O ? NSL : 1;  // O accumulators
   // S / P buffers in TMEM: tile t uses buffer t % NBUF, so S_{t+1} needs P V_{t+1-NBUF}
   // done; K_t's stage is free once S_{t-KSTAGES} has completed, V_t's once P V_{t-VSTAGES}
-  // has.  Three buffers and three K stages pay off only with the separate load and MMA
-  // warps (with one producer thread doing everything in turn they measured no faster).
-  static constexpr int NBUF = P_TMEM ? 3 : 2;
+  // has.  Three buffers where TMEM holds them next to the O accumulators (head_dim 64),
+  // else two.
+  static constexpr int NBUF = P_TMEM && 3 * BN + N_O * D <= 512 ? 3 : 2;
   static constexpr int KSTAGES = P_TMEM ? 3 : 2;
   static constexpr int VSTAGES = 2;
-  // 128-key tiles: the per-row maximum and sum are exchanged in shared memory; head_dim 256
-  // (no shared memory to spare): in TMEM columns past O.
+  // The per-row maximum and sum: 128-key tiles exchange them once, in the epilogue, in
+  // shared memory; head_dim 256 (no shared memory to spare) every tile, in TMEM columns
+  // past O.
   static constexpr bool X_SMEM = P_TMEM;
-  static constexpr int X_BYTES = X_SMEM ? 2 * NSL * BM * 4 : 0;  // [tile parity][slice][row] floats
+  static constexpr int X_BYTES = X_SMEM ? 2 * NSL * BM * 4 : 0;  // [max, sum][slice][row] floats
   static constexpr int TMEM_COLS = 512;
   static constexpr int SMEM = 1024 + Q_BYTES + KSTAGES * K_BYTES + VSTAGES * V_BYTES +
                               (SPLIT ? 2 : 1) * P_BYTES + X_BYTES + 256;
@@ -196,10 +209,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  // TMEM columns: S / P buffers [b BN, (b + 1) BN) for b < NBUF, O [O_COL, O_COL + D), and
-  // with the exchange in TMEM, slots [X_COL, X_COL + 12): row maxima by tile parity (2 x 4)
-  // and the row-sum shares (4).
-  constexpr int O_COL = NBUF * BN, X_COL = O_COL + D;
+  // TMEM columns: S / P buffers [b BN, (b + 1) BN) for b < NBUF, O accumulator o at
+  // [O_COL + o D, O_COL + (o + 1) D), and with the exchange in TMEM, slots [X_COL, X_COL +
+  // 12): row maxima by tile parity (2 x 4) and the row-sum shares (4).
+  constexpr int O_COL = NBUF * BN, X_COL = O_COL + C::N_O * D;
   static_assert(X_COL + (C::X_SMEM ? 0 : 12) <= C::TMEM_COLS, "TMEM column plan");
   const uint32_t t_lane = tmem + (static_cast<uint32_t>(quarter * 32) << 16);  // this warp's lanes
   const uint32_t t_o = t_lane + O_COL;
@@ -307,7 +320,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       // O += P_t V_t.  128-key tiles: P_t read from TMEM where the softmax warps wrote it over
-      // S_t (P_hi in the buffer's first BN/2 columns, P_lo in the next BN/2).
+      // S_t, each slice within its own SLICE score columns (P_hi in the first SLICE/2, P_lo in
+      // the next SLICE/2), each K step adding into its slice's O.
       auto issue_pv = [&](int t) -> bool {
         const int st = t % VSTAGES;
         if (!mbar_wait_bounded(smem_u32(&bars->v_full[st]), (t / VSTAGES) & 1, ctl.timeout_ns, abort)) {
@@ -322,11 +336,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / UMMA_K; ++kk) {
           const uint64_t b = umma_desc_advance(dv, (kk >> 2) * (C::CHUNKS * 8192) + (kk & 3) * 2048);
-          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
           if constexpr (C::P_TMEM) {
-            tc_mma_f16_ts(tmem + O_COL, t_p + kk * (UMMA_K / 2), b, IDESC_O, acc);
-            if (C::SPLIT) tc_mma_f16_ts(tmem + O_COL, t_p + BN / 2 + kk * (UMMA_K / 2), b, IDESC_O, 1u);
+            constexpr int STEPS = SLICE / UMMA_K;  // K steps per slice
+            const int sl = kk / STEPS, u = kk % STEPS;
+            const uint32_t o = tmem + O_COL + sl * D, a = t_p + sl * SLICE + u * (UMMA_K / 2);
+            const uint32_t acc = (t > 0 || u > 0) ? 1u : 0u;
+            tc_mma_f16_ts(o, a, b, IDESC_O, acc);
+            if (C::SPLIT) tc_mma_f16_ts(o, a + SLICE / 2, b, IDESC_O, 1u);
           } else {
+            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
             const uint32_t a_off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
             tc_mma_f16(tmem + O_COL, umma_desc_advance(dp, a_off), b, IDESC_O, acc);
             if (C::SPLIT) tc_mma_f16(tmem + O_COL, umma_desc_advance(dplo, a_off), b, IDESC_O, 1u);
@@ -364,8 +382,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // -------------------------------------------------------------- softmax
-    // Row state (identical in the two warps that share a row): the maximum the
-    // exponentials are taken against, and this warp's share of the row sum.
+    // Row state: the maximum the exponentials are taken against (SPLIT_O: of this warp's
+    // keys; otherwise of the row, identical in the warps that share it) and this warp's share
+    // of the row sum.
     float m_use = -INFINITY, l_part = 0.f;
     const int key_limit = p.causal ? min(p.seq, q_pos + 1) : p.seq;  // keys this row attends
     for (int j = 0; j < n_tiles; ++j) {
@@ -399,17 +418,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int i = 4; i < SLICE; i += 2) a4[(i / 2) % 4] = fmax3(a4[(i / 2) % 4], sv[i], sv[i + 1]);
         mx = fmax3(fmaxf(a4[0], a4[1]), a4[2], a4[3]);
       }
-      // Row maximum over the two warps of the lane quarter, through slots of this tile's
-      // parity (a warp writes tile j+2's slots only after the barrier of tile j+1, which its
-      // peers reach after reading tile j's).
+      // SPLIT_O: this slice's own maximum.  Otherwise the row maximum over the warps of the
+      // lane quarter, through TMEM slots of this tile's parity (a warp writes tile j+2's slots
+      // only after the barrier of tile j+1, which its peers reach after reading tile j's).
       float m_raw;
-      if constexpr (C::X_SMEM) {
-        float* xs = xch + (j & 1) * NSL * BM;
-        xs[slice * BM + row] = mx;
-        quarter_sync(quarter);
-        m_raw = xs[row];
-#pragma unroll
-        for (int q = 1; q < NSL; ++q) m_raw = fmaxf(m_raw, xs[q * BM + row]);
+      if constexpr (C::SPLIT_O) {
+        m_raw = mx;
       } else {
         const uint32_t xs = t_x + (j & 1) * 4;
         tmem_st_32x32b_x1(xs + slice, __float_as_uint(mx));
@@ -485,27 +499,30 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc_fence_after();
       }
       if (rescale) {
+        // SPLIT_O: this slice's whole O; otherwise its OSL columns of the shared O.
+        constexpr int RCOLS = C::SPLIT_O ? D : OSL;
+        const uint32_t t_r = t_o + slice * RCOLS;
 #pragma unroll
-        for (int c = 0; c < OSL / 16; ++c) {
+        for (int c = 0; c < RCOLS / 16; ++c) {
           uint32_t r[16];
-          tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
+          tmem_ld_32x32b_x16(t_r + c * 16, r);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st_32x32b_x16(t_o + slice * OSL + c * 16, r);
+          tmem_st_32x32b_x16(t_r + c * 16, r);
         }
       }
       if constexpr (C::P_TMEM) {
-        // P_j over S_j in TMEM: this thread's keys [slice * SLICE, + SLICE) are SLICE / 2
-        // packed columns from slice * SLICE / 2 (P_lo BN / 2 columns further).  Every warp of
-        // the quarter read its scores before the barrier above, so none is overwritten unread.
+        // P_j over S_j in TMEM, within this warp's own score columns [slice * SLICE, +
+        // SLICE), all read above: keys k, k + 1 packed in column slice * SLICE + k / 2 (P_hi),
+        // P_lo SLICE / 2 columns further.  No other warp reads or writes these columns.
         static_assert(SLICE == 32 || SLICE == 64, "score columns per thread");
         if constexpr (SLICE == 32) {
-          tmem_st_32x32b_x16(t_s + slice * (SLICE / 2), hi);
-          if (C::SPLIT) tmem_st_32x32b_x16(t_s + BN / 2 + slice * (SLICE / 2), lo);
+          tmem_st_32x32b_x16(t_s + slice * SLICE, hi);
+          if (C::SPLIT) tmem_st_32x32b_x16(t_s + slice * SLICE + SLICE / 2, lo);
         } else {
-          tmem_st_32x32b_x32(t_s + slice * (SLICE / 2), hi);
-          if (C::SPLIT) tmem_st_32x32b_x32(t_s + BN / 2 + slice * (SLICE / 2), lo);
+          tmem_st_32x32b_x32(t_s + slice * SLICE, hi);
+          if (C::SPLIT) tmem_st_32x32b_x32(t_s + slice * SLICE + SLICE / 2, lo);
         }
       } else {
         // This thread's keys: 64-key chunk kf / 64, 16-byte units (kf % 64) / 8 onwards,
@@ -530,19 +547,28 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(smem_u32(&bars->p_full[j & 1]));
     }
 
-    // ---- epilogue: O / l  (l = the two warps' shares, added in slice order)
+    // ---- epilogue: O / l  (SPLIT_O: O = sum_q w_q O_q and l = sum_q w_q l_q over the
+    // slices q in order, w_q = 2^(m_q - m) with m the row maximum; otherwise l = the warps'
+    // shares added in slice order)
     if (!wait_pv(n_tiles - 1, abort)) fail(RK_DEV_ERR_TIMEOUT_EPILOGUE);
     tc_fence_after();
     float l;
+    float w[C::N_O];
     if constexpr (C::X_SMEM) {
-      // The slots of parity n_tiles & 1: last written for tile n_tiles - 2, whose readers
-      // passed the barrier of tile n_tiles - 1 before this warp did.
-      float* xs = xch + (n_tiles & 1) * NSL * BM;
-      xs[slice * BM + row] = l_part;
+      // Shared-memory slots [max | sum][slice][row], written only here.
+      xch[slice * BM + row] = m_use;
+      xch[(NSL + slice) * BM + row] = l_part;
       quarter_sync(quarter);
-      l = xs[row];
+      float m = xch[row];
 #pragma unroll
-      for (int q = 1; q < NSL; ++q) l += xs[q * BM + row];
+      for (int q = 1; q < NSL; ++q) m = fmaxf(m, xch[q * BM + row]);
+      l = 0.f;
+#pragma unroll
+      for (int q = 0; q < NSL; ++q) {
+        const float mq = xch[q * BM + row];
+        w[q] = mq == -INFINITY ? 0.f : ex2_approx(mq - m);  // a slice with no attended key adds 0
+        l += w[q] * xch[(NSL + q) * BM + row];
+      }
     } else {
       tmem_st_32x32b_x1(t_x + 8 + slice, __float_as_uint(l_part));
       tmem_st_wait();
@@ -555,6 +581,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       l = __uint_as_float(lr[0]);
 #pragma unroll
       for (int q = 1; q < NSL; ++q) l += __uint_as_float(lr[q]);
+      w[0] = 1.f;
     }
     const float inv = l > 0.f ? 1.0f / l : 0.f;
     const bool store = q_pos < p.seq && !*abort;
@@ -563,7 +590,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int c = 0; c < OSL / 16; ++c) {
       uint32_t r[16];
       tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
-      tmem_ld_wait();
+      if constexpr (C::SPLIT_O) {
+        uint32_t r2[NSL - 1][16];
+#pragma unroll
+        for (int q = 1; q < NSL; ++q) tmem_ld_32x32b_x16(t_o + q * D + slice * OSL + c * 16, r2[q - 1]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float v = w[0] * __uint_as_float(r[i]);
+#pragma unroll
+          for (int q = 1; q < NSL; ++q) v = fmaf(w[q], __uint_as_float(r2[q - 1][i]), v);
+          r[i] = __float_as_uint(v);
+        }
+      } else {
+        tmem_ld_wait();
+      }
       if (store) {
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
