@@ -9,12 +9,17 @@
 //     across 148 SMs to cover HBM latency);
 //   * x (at most 32 x K x 2 bytes) stays in L2/L1 and is read with __ldg;
 //     one 16-byte x vector feeds ROWS rows;
+//   * M >= 2: each weight word is widened to fp32 once and feeds every row of x
+//     through packed FMAs (fma.rn.f32x2), so the work per weight element grows by
+//     one FMA lane per row of x, not by a widening and a scalar FMA;
 //   * fp32 accumulation, warp-shuffle tree reduction;
 //   * split-K inside the CTA: the 8 warps form (8/KS) row groups x KS K-slices
 //     and the KS partial sums are added in a fixed order through shared
 //     memory -- deterministic, no workspace, no second launch.  KS grows when
 //     N is too small to give every SM enough rows.
-// No tensor cores: at M <= 16 the kernel is bound by HBM bandwidth.
+// No tensor cores.  HBM-bound at M = 1; from M = 3 the automatic choice is the tcgen05
+// skinny kernel (gemv_tcgen05.cu), which keeps the weight stream at HBM speed while the
+// FMA work here grows with M.
 //
 // Role of the reference: replaces gemv_wave_kernel / gemv_packed_kernel /
 // gemv_lds_kernel (benchmarks/gemv/native_gemv.hip:30-203), whose lanes
@@ -59,6 +64,33 @@ __device__ __forceinline__ void fma_vec(float (&acc)[MB][ROWS], const uint4 (&w)
       const float2 wf = Pack2<T>::to_floats(ws[p]);
       acc[m][r] = fmaf(wf.x, xf.x, acc[m][r]);
       acc[m][r] = fmaf(wf.y, xf.y, acc[m][r]);
+    }
+  }
+}
+
+// M >= 2: one 16-byte vector of each of ROWS weight rows against the x vectors of every
+// row m < M at the same k.  Each weight word is widened once and feeds all M rows through
+// packed fp32 FMAs (fma.rn.f32x2: even and odd k accumulate in the two halves of acc, added
+// at the end), so the per-element work is one FMA lane per row of x plus a shared widening.
+template <typename T, int MB, int ROWS>
+__device__ __forceinline__ void fma_rows(float2 (&acc)[MB][ROWS], const uint4 (&w)[ROWS],
+                                         const uint4 (&xv)[MB], int M) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    float2 wf[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      const uint32_t ws[4] = {w[r].x, w[r].y, w[r].z, w[r].w};
+      wf[r] = Pack2<T>::to_floats(ws[p]);
+    }
+#pragma unroll
+    for (int m = 0; m < MB; ++m) {
+      if (m < M) {
+        const uint32_t xs[4] = {xv[m].x, xv[m].y, xv[m].z, xv[m].w};
+        const float2 xf = Pack2<T>::to_floats(xs[p]);
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) acc[m][r] = ffma2(wf[r], xf, acc[m][r]);
+      }
     }
   }
 }
@@ -136,11 +168,15 @@ __global__ void __launch_bounds__(GEMV_THREADS)
       const int row = row_begin + min(i0 + r, rows - 1);  // duplicates are never stored
       wrow[r] = reinterpret_cast<const uint4*>(W + static_cast<size_t>(row) * K);
     }
-    float acc[MB][ROWS];
+    float acc[MB][ROWS];    // M = 1
+    float2 acc2[MB][ROWS];  // M >= 2 (even / odd k)
 #pragma unroll
     for (int m = 0; m < MB; ++m)
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) acc[m][r] = 0.f;
+      for (int r = 0; r < ROWS; ++r) {
+        acc[m][r] = 0.f;
+        acc2[m][r] = make_float2(0.f, 0.f);
+      }
 
     for (int v = v0 + lane; v < v1; v += 32 * UNROLL) {
       uint4 w[UNROLL][ROWS];
@@ -154,10 +190,15 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 #pragma unroll
       for (int u = 0; u < UNROLL; ++u) {
         if (v + 32 * u < v1) {
+          if constexpr (MB == 1) {
+            fma_vec<T, MB, ROWS>(acc, w[u], __ldg(xrow + v + 32 * u), 0);
+          } else {
+            uint4 xv[MB];
 #pragma unroll
-          for (int m = 0; m < MB; ++m)
-            if (m < M)
-              fma_vec<T, MB, ROWS>(acc, w[u], __ldg(xrow + static_cast<size_t>(m) * KV + v + 32 * u), m);
+            for (int m = 0; m < MB; ++m)
+              xv[m] = m < M ? __ldg(xrow + static_cast<size_t>(m) * KV + v + 32 * u) : make_uint4(0, 0, 0, 0);
+            fma_rows<T, MB, ROWS>(acc2, w[u], xv, M);
+          }
         }
       }
     }
@@ -166,7 +207,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 #pragma unroll
     for (int m = 0; m < MB; ++m)
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) vals[m * ROWS + r] = acc[m][r];
+      for (int r = 0; r < ROWS; ++r) vals[m * ROWS + r] = MB == 1 ? acc[m][r] : acc2[m][r].x + acc2[m][r].y;
     const float sum = warp_reduce_scatter<V>(vals, lane);
     const int idx = lane >> (5 - LOGV);  // value index this lane now holds
     if ((lane & ((1 << (5 - LOGV)) - 1)) == 0) {

@@ -287,6 +287,27 @@ def test_gemv_tunings_agree(rows, ks):
     oracle.assert_parity(to_bits(out), o_bits, o32, "bf16")
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("m", [2, 3, 4, 5, 8, 16])
+@pytest.mark.parametrize("n, k", [(1000, 2048), (37, 8200), (513, 4104), (64, 14336)])
+def test_gemv_stream_skinny_m(m, n, k, dtype):
+    """The CUDA-core stream kernel at M >= 2 (shared widening, packed FMAs, two pipeline
+    stages up to M = 4): K slices of odd and ragged vector counts per lane, so the second
+    stage runs past the slice end, against the oracle."""
+    import torch
+
+    gen = torch.Generator().manual_seed(100 + m)
+    x = seeded((m, k), 100 + m, "normal", dtype, gen)
+    w = seeded((n, k), 100 + m, f"normal/{k}", dtype, gen)
+    o_bits, o32 = oracle.gemv(to_bits(x), to_bits(w), dtype)
+    buf, out = _guarded(torch, m, n, dtype)
+    assert abi_gemv(x.cuda(), w.cuda(), out, GEMV["stream"], dtype) == _native.RK_OK
+    torch.cuda.synchronize()
+    assert device_status() == _native.RK_OK
+    assert _guards_intact(buf), "kernel wrote outside out"
+    oracle.assert_parity(to_bits(out), o_bits, o32, dtype)
+
+
 @pytest.mark.parametrize("cluster", [1, 2, 4, 8])
 @pytest.mark.parametrize("m", [1, 5, 16, 17, 32])
 def test_gemv_tensor_core_cluster_split_k(cluster, m):
