@@ -362,6 +362,20 @@ rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M,
     // Split K across the CTA's warps while each slice keeps >= 2 vectors per lane.
     ks = 8;
     while (ks > 1 && kv / ks < 64) ks /= 2;
+    if (ks == 8) {
+      // A lane walks its slice in steps of 32 x UNROLL vectors; a short slice that leaves
+      // much of its last step empty keeps fewer loads in flight.  Take 4 slices instead of 8
+      // when 8 would give at most two steps and 4 fill them clearly better (K = 4096: 64 of
+      // 128 vectors with 8 slices, measured 7-17 % slower; K = 11008: 172 of 256, 3-9 %);
+      // otherwise 8 (K = 8192, 14336: as fast; K = 28672, four steps: 8 measured 3.5 %
+      // faster at M = 1 although 4 slices would fill their steps exactly).
+      const int64_t step = 32 * (rows >= 4 ? 2 : 4);
+      auto idle = [&](int64_t c) {
+        const int64_t per = (kv + c - 1) / c, cap = (per + step - 1) / step * step;
+        return static_cast<double>(cap - per) / static_cast<double>(cap);
+      };
+      if ((kv / 8 + step - 1) / step <= 2 && idle(4) < idle(8) - 0.02) ks = 4;
+    }
   }
   ks = ks >= 8 ? 8 : (ks >= 4 ? 4 : (ks >= 2 ? 2 : 1));
   StreamLaunch L = dt == RK_DTYPE_BF16 ? pick<__nv_bfloat16>(mb, rows, ks) : pick<__half>(mb, rows, ks);
