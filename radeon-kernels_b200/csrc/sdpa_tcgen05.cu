@@ -586,34 +586,43 @@ __global__ void __launch_bounds__(THREADS, 1)
     const float inv = l > 0.f ? 1.0f / l : 0.f;
     const bool store = q_pos < p.seq && !*abort;
     T* orow = out + (static_cast<size_t>(q_mat) * p.seq + q_pos) * D + slice * OSL;
+    // Two 16-column chunks per TMEM round trip (their loads issued together, one wait).
+    constexpr int CPW = OSL / 16 >= 2 ? 2 : 1;
 #pragma unroll
-    for (int c = 0; c < OSL / 16; ++c) {
-      uint32_t r[16];
-      tmem_ld_32x32b_x16(t_o + slice * OSL + c * 16, r);
-      if constexpr (C::SPLIT_O) {
-        uint32_t r2[NSL - 1][16];
+    for (int c0 = 0; c0 < OSL / 16; c0 += CPW) {
+      uint32_t r[CPW][16];
+      uint32_t r2[C::SPLIT_O ? CPW * (NSL - 1) : 1][16];
 #pragma unroll
-        for (int q = 1; q < NSL; ++q) tmem_ld_32x32b_x16(t_o + q * D + slice * OSL + c * 16, r2[q - 1]);
-        tmem_ld_wait();
+      for (int u = 0; u < CPW; ++u) {
+        tmem_ld_32x32b_x16(t_o + slice * OSL + (c0 + u) * 16, r[u]);
+        if constexpr (C::SPLIT_O) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v = w[0] * __uint_as_float(r[i]);
-#pragma unroll
-          for (int q = 1; q < NSL; ++q) v = fmaf(w[q], __uint_as_float(r2[q - 1][i]), v);
-          r[i] = __float_as_uint(v);
+          for (int q = 1; q < NSL; ++q)
+            tmem_ld_32x32b_x16(t_o + q * D + slice * OSL + (c0 + u) * 16, r2[u * (NSL - 1) + q - 1]);
         }
-      } else {
-        tmem_ld_wait();
       }
-      if (store) {
+      tmem_ld_wait();
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          uint4 v;
-          v.x = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 0]) * inv, __uint_as_float(r[8 * q + 1]) * inv);
-          v.y = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 2]) * inv, __uint_as_float(r[8 * q + 3]) * inv);
-          v.z = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 4]) * inv, __uint_as_float(r[8 * q + 5]) * inv);
-          v.w = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 6]) * inv, __uint_as_float(r[8 * q + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + c * 16 + 8 * q) = v;
+      for (int u = 0; u < CPW; ++u) {
+        if constexpr (C::SPLIT_O) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float v = w[0] * __uint_as_float(r[u][i]);
+#pragma unroll
+            for (int q = 1; q < NSL; ++q) v = fmaf(w[q], __uint_as_float(r2[u * (NSL - 1) + q - 1][i]), v);
+            r[u][i] = __float_as_uint(v);
+          }
+        }
+        if (store) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint4 v;
+            v.x = Pack2<T>::from_floats(__uint_as_float(r[u][8 * q + 0]) * inv, __uint_as_float(r[u][8 * q + 1]) * inv);
+            v.y = Pack2<T>::from_floats(__uint_as_float(r[u][8 * q + 2]) * inv, __uint_as_float(r[u][8 * q + 3]) * inv);
+            v.z = Pack2<T>::from_floats(__uint_as_float(r[u][8 * q + 4]) * inv, __uint_as_float(r[u][8 * q + 5]) * inv);
+            v.w = Pack2<T>::from_floats(__uint_as_float(r[u][8 * q + 6]) * inv, __uint_as_float(r[u][8 * q + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + (c0 + u) * 16 + 8 * q) = v;
+          }
         }
       }
     }
