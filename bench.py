@@ -2,22 +2,26 @@
 
 Metric (BASELINE.json): "GEMM TFLOP/s & GEMV HBM GB/s per B200, % roofline, at 1/2/4/8 GPUs".
 
-Headline workload -- BASELINE config 2, decode GEMV ``x[1,8192] @ W[8192,8192]^T`` bf16:
-a *step* is one ``rk_gemv`` over one weight matrix (128 MiB).  Steps rotate over several
-weight matrices (4 x 128 MiB > the 126 MB L2) so every step streams its weight from HBM;
-``value`` = weight+activation bytes of all steps on all ranks / the device time of the
-timed region (max over ranks).  With N GPUs every rank streams its own 8192-row block of
-an N x 8192-row weight (N-row sharding, weak scaling, no data-path collective).
+Headline workload -- BASELINE config 2, decode GEMV ``x[1,8192] @ W[8192,8192]^T`` bf16,
+strong-scaled: a *step* is one product over the whole 8192 x 8192 weight (128 MiB).
+  * N = 1: one ``rk_gemv`` launch per step.
+  * N > 1: the weight is split by rows, rank r holding rows [r*8192/N, (r+1)*8192/N); a
+    step is one ``rk_gemv_allgather`` launch per rank, which streams the rank's block and
+    stores its slice of the output into every rank's full ``out[1, 8192]`` over NVLink, so
+    the output all-gather is inside the timed step.
+Steps rotate over several weight sets (more than 2 x 126 MB of L2 per rank) so every step
+streams its weight from HBM; ``value`` = the bytes of all steps (the whole weight plus x and
+out per step) / the device time of the timed region (max over ranks).
 
-``e2e``: the same GEMV through the public ``radeon_kernels.gemv`` call (dispatch, pack
-winner) with the step's activation copied host->device from pinned memory and the result
-copied back every step.  At N=1 the steps are captured from those calls into a CUDA graph
-whose copies run on forked streams and overlap neighbouring kernels (``eager_serial``
-keeps the serialised per-call figure); at N>1 the per-rank output blocks are
-all-gathered (NCCL) first, as a caller that needs the full output would, eagerly.
+``e2e``: the same step through the public API -- ``radeon_kernels.gemv`` at N = 1,
+``radeon_kernels.distributed.ShardedGemv(..., gather=True)`` at N > 1 -- with the step's
+activation copied host->device from pinned memory and the full result copied back every
+step, the steps captured into a CUDA graph.
 
 ``suite``: the other BASELINE configs measured in the same run (GEMM TFLOP/s with the
-tcgen05 kernel, FFN-down GEMV at M = 1/4/16), each with its roofline fraction.
+tcgen05 kernels, FFN-down GEMV at M = 1/4/16, the decode neighbours), each with its
+roofline fraction; at N > 1 config 5 runs with B split into N column blocks, compute-only
+and with the fused all-gather, next to the NCCL all-gather it replaces.
 
 ``--impl reference`` times the reference's own path for the same workload on the host
 CPU cores (``oracle/reference_path.py``: ``torch.mm`` as in providers/torch_fallback.py /
@@ -42,6 +46,7 @@ sys.path.insert(0, str(REPO / "radeon-kernels_b200"))
 sys.path.insert(0, str(REPO))
 
 METRIC = "GEMM TFLOP/s & GEMV HBM GB/s per B200, % roofline, at 1/2/4/8 GPUs"
+DATA = "synthetic (seeded torch.Generator, BASELINE config 2 distributions: x~N(0,1), W~N(0,1/8192))"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 ROTATE = 4  # weight matrices cycled through by the headline loop
 
@@ -212,62 +217,164 @@ def time_loop(fn, steps: int, stream) -> float:
     return start.elapsed_time(stop)
 
 
-def headline(args, dist: Dist, ext, peaks, peak_kind):
-    """Config 2 decode GEMV, kernel-only, inputs resident; CUDA graph of the launch loop."""
+L2_BYTES = 126 * 1024 * 1024
+HEAD_M, HEAD_N, HEAD_K = 1, 8192, 8192
+
+
+def rotation(block_bytes: int) -> int:
+    """Weight sets a rank cycles through: at least ROTATE, and more than 2 x L2 in total."""
+
+    return max(ROTATE, -(-2 * L2_BYTES // block_bytes) + 1)
+
+
+def headline_config(world: int) -> dict:
+    """The workload description both arms print (the driver compares them)."""
+
+    return {
+        "workload": "gemv-decode-bf16-m1-n8192-k8192 (BASELINE config 2), x @ W^T over the whole "
+        "8192 x 8192 weight per step; N > 1: weight rows split over the N GPUs, output all-gathered "
+        "inside the step",
+        "m": HEAD_M,
+        "n": HEAD_N,
+        "k": HEAD_K,
+        "n_per_gpu": HEAD_N // world,
+        "l2": "inputs larger than L2: weight sets rotated per step, > 2 x 126 MB per GPU",
+        "parallelism": "single GPU" if world == 1 else f"weight-row shards x{world} + fused NVLink all-gather",
+    }
+
+
+def capture_graph(step, count: int, stream, offset: int = 0):
+    """CUDA graph of `count` calls step(offset + i), captured on a side stream."""
 
     import torch
 
-    m, n, k = 1, 8192, 8192
-    dtype = "bf16"
-    weights = [seeded((n, k), 100 + 17 * dist.rank + r, "normal/8192", dtype) for r in range(ROTATE)]
-    x = seeded((m, k), 1, "normal", dtype)
-    out = torch.empty(m, n, dtype=x.dtype, device="cuda")
-    stream = torch.cuda.current_stream()
-
-    def step(i):
-        ext.gemv_out(x, weights[i % ROTATE], out, 0)
-
-    for i in range(max(args.warmup, 3)):
-        step(i)
-    torch.cuda.synchronize()
-
-    # Capture a block of launches into a CUDA graph: decode loops replay graphs, and the
-    # graph removes the per-launch host overhead from the measurement of the kernel.
-    block = 40
     graph = torch.cuda.CUDAGraph()
-    capture_stream = torch.cuda.Stream()
-    capture_stream.wait_stream(stream)
-    with torch.cuda.stream(capture_stream):
-        with torch.cuda.graph(graph, stream=capture_stream):
-            for i in range(block):
-                step(i)
-    stream.wait_stream(capture_stream)
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(count):
+                step(offset + i)
+    stream.wait_stream(cap)
     torch.cuda.synchronize()
-    for _ in range(2):
-        graph.replay()
-    torch.cuda.synchronize()
+    return graph
 
-    replays = max(1, args.steps // block)
-    steps = replays * block
+
+class ExactReplay:
+    """Runs exactly `steps` calls of `step` as replays of (at most) two captured graphs."""
+
+    def __init__(self, step, steps: int, stream, block: int = 40):
+        self.block = max(1, min(block, steps))
+        self.full = steps // self.block
+        self.main = capture_graph(step, self.block, stream)
+        rest = steps - self.full * self.block
+        self.tail = capture_graph(step, rest, stream, offset=self.full * self.block) if rest else None
+
+    def __call__(self, _i=0):
+        for _ in range(self.full):
+            self.main.replay()
+        if self.tail is not None:
+            self.tail.replay()
+
+    def release(self):
+        self.main = self.tail = None
+
+
+def timed_region(run, dist: Dist, stream) -> tuple[float, float]:
+    """(max-over-ranks ms, this rank's ms) of one call of run(), barrier + sync on both sides."""
+
+    import torch
+
     dist.barrier()
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    for _ in range(replays):
-        graph.replay()
+    run()
     stop.record(stream)
     stop.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
-    ms_local = start.elapsed_time(stop)
-    ms = dist.max(ms_local)
+    local = start.elapsed_time(stop)
+    return dist.max(local), local
+
+
+def sharded_weights(dist: Dist, dtype: str = "bf16"):
+    rows = HEAD_N // dist.world
+    count = rotation(rows * HEAD_K * 2)
+    return [seeded((rows, HEAD_K), 100 + 17 * dist.rank + r, "normal/8192", dtype) for r in range(count)]
+
+
+def headline(args, dist: Dist, ext, peaks, peak_kind):
+    """Config 2 decode GEMV, kernel-only, inputs resident; CUDA graphs of the launch loop.
+
+    N = 1: ``rk_gemv`` over the full weight.  N > 1: ``rk_gemv_allgather`` over this rank's
+    row block (the fused all-gather), exactly ``--steps`` launches per rank; the plain
+    ``rk_gemv`` of the block alone is timed too, so the exchange's share is visible.
+    """
+
+    import torch
+
+    m, k = HEAD_M, HEAD_K
+    rows = HEAD_N // dist.world
+    weights = sharded_weights(dist)
+    x = seeded((m, k), 1, "normal", "bf16")
+    stream = torch.cuda.current_stream()
+    local_out = torch.empty(m, rows, dtype=x.dtype, device="cuda")
+
+    def compute_only(i):
+        ext.gemv_out(x, weights[i % len(weights)], local_out, 0)
+
+    exchange = None
+    if dist.world > 1:
+        from radeon_kernels.distributed.peer import PeerExchange, fused_path_available
+
+        if not fused_path_available(x):
+            raise RuntimeError("bench: the fused all-gather needs every rank on its own NVLink-connected GPU")
+        exchange = PeerExchange((m, HEAD_N), x.dtype)
+
+        def step(i):
+            ext.gemv_allgather(x, weights[i % len(weights)], exchange.output, exchange.out_ptrs,
+                               exchange.ctl_ptrs, exchange.rank, exchange.timeout_ns)
+    else:
+        step = compute_only
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    if exchange is not None:
+        # The gathered output equals the single-GPU kernel's on the concatenated weight blocks.
+        local = ext.gemv_out(x, weights[(max(args.warmup, 3) - 1) % len(weights)],
+                             torch.empty(m, rows, dtype=x.dtype, device="cuda"), 2)
+        mine = exchange.output[:, dist.rank * rows:(dist.rank + 1) * rows]
+        if not torch.equal(mine.view(torch.int16), local.view(torch.int16)):
+            raise RuntimeError("bench: the fused all-gather output differs from the local GEMV")
+
+    steps = args.steps
+    runner = ExactReplay(step, steps, stream)
+    runner()  # warm replay
+    torch.cuda.synchronize()
+    ms, ms_local = timed_region(runner, dist, stream)
+    runner.release()
     per_launch_s = ms_local / 1e3 / steps
-    bytes_step = gemv_bytes(m, n, k)
-    value = bytes_step * steps * dist.world / (ms / 1e3) / 1e9
-    achieved = bytes_step / per_launch_s / 1e9
-    del graph
-    return {
+
+    compute = None
+    if exchange is not None:
+        plain = ExactReplay(compute_only, steps, stream)
+        plain()
+        torch.cuda.synchronize()
+        c_ms, _ = timed_region(plain, dist, stream)
+        plain.release()
+        compute = {"us_per_step": round(c_ms * 1e3 / steps, 3),
+                   "what": "rk_gemv over the rank's row block alone (no exchange), same rotation"}
+
+    bytes_step = gemv_bytes(m, HEAD_N, k)  # the whole logical problem, per step
+    # Per-rank algorithmic HBM bytes of one launch: the weight block and x read, the full
+    # output written into this rank's memory (its own block and every peer's).
+    rank_bytes = (rows * k + m * k + m * HEAD_N) * 2
+    value = bytes_step * steps / (ms / 1e3) / 1e9
+    achieved = rank_bytes / per_launch_s / 1e9
+    result = {
         "value": value,
         "ms_per_step": ms / steps,
         "steps": steps,
@@ -278,9 +385,19 @@ def headline(args, dist: Dist, ext, peaks, peak_kind):
             "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 4),
             "peak_source": peak_kind,
+            "kernel": "gemv_stream_kernel" + ("<PEER> (rk_gemv_allgather)" if exchange is not None else " (rk_gemv)"),
+            "bytes_per_launch": rank_bytes,
         },
         "bytes_per_step": bytes_step,
+        "weight_sets_per_rank": len(weights),
+        "launch": f"CUDA graphs replayed for exactly {steps} launches per rank (blocks of {runner.block})",
     }
+    if compute is not None:
+        result["compute_only"] = compute
+        result["exchange_us_per_step"] = round(ms * 1e3 / steps - compute["us_per_step"], 3)
+    if exchange is not None:
+        exchange.close()
+    return result
 
 
 E2E_GRAPH_STEPS = 16  # independent steps captured in one CUDA graph (multiple of ROTATE)
@@ -289,63 +406,53 @@ E2E_GRAPH_STEPS = 16  # independent steps captured in one CUDA graph (multiple o
 def e2e(args, dist: Dist):
     """The same GEMV through the public API with host buffers, copies inside the region.
 
-    Every step copies its activation host->device from pinned memory, calls
-    ``radeon_kernels.gemv`` (validation, dispatch, pack winner) and copies the result back
-    into pinned memory.  At N = 1 the reported value comes from a CUDA graph captured from
-    those calls: 16 independent steps, H2D copies on a forked copy stream and each D2H
-    on a second stream right after its kernel, so copy-engine latency overlaps neighbouring
+    Every step copies its activation host->device from pinned memory, calls the public API
+    (validation, dispatch, pack winner) and copies the full result back into pinned memory.
+    N = 1: ``radeon_kernels.gemv``; the reported value comes from a CUDA graph captured from
+    those calls: 16 independent steps, H2D copies on a forked copy stream and each D2H on a
+    second stream right after its kernel, so copy-engine latency overlaps neighbouring
     kernels; ``eager_serial`` is the same step issued eagerly with copy, kernel and copy
-    serialised on one stream (the per-call latency).  At N > 1 each step also all-gathers
-    the rank blocks (NCCL) and runs eagerly (no NCCL inside a graph).
+    serialised on one stream (the per-call latency).  N > 1: ``ShardedGemv(..., gather=True)``
+    (the fused all-gather kernel), copy in, kernel and copy out on one stream -- the gathered
+    output buffer is rewritten by the next call, so its copy must finish first -- captured
+    into a CUDA graph of 16 steps.
     """
+
+    if dist.world > 1:
+        return e2e_sharded(args, dist)
 
     import torch
 
     import radeon_kernels as rk
-    from radeon_kernels.distributed import all_gather_columns
 
-    m, n, k = 1, 8192, 8192
-    weights = [seeded((n, k), 100 + 17 * dist.rank + r, "normal/8192", "bf16") for r in range(ROTATE)]
+    m, n, k = HEAD_M, HEAD_N, HEAD_K
+    weights = [seeded((n, k), 100 + r, "normal/8192", "bf16") for r in range(ROTATE)]
     bytes_step = gemv_bytes(m, n, k)
     stream = torch.cuda.current_stream()
 
     def rate(ms, steps):
-        return round(bytes_step * steps * dist.world / (ms / 1e3) / 1e9, 1)
+        return round(bytes_step * steps / (ms / 1e3) / 1e9, 1)
 
-    # Eager, serialised: copy in, GEMV, (all-gather), copy out, one stream.
+    # Eager, serialised: copy in, GEMV, copy out, one stream.
     x_host = seeded((m, k), 1, "normal", "bf16", device="cpu").pin_memory()
-    out_host = torch.empty((m, n * dist.world), dtype=torch.bfloat16).pin_memory()
+    out_host = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
     x_dev = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
-    full = torch.empty((m, n * dist.world), dtype=torch.bfloat16, device="cuda") if dist.world > 1 else None
 
     def step(i):
         x_dev.copy_(x_host, non_blocking=True)
-        y = rk.gemv(x_dev, weights[i % ROTATE])
-        if dist.world > 1:
-            out_host.copy_(all_gather_columns(y, out=full), non_blocking=True)
-        else:
-            out_host.copy_(y, non_blocking=True)
+        out_host.copy_(rk.gemv(x_dev, weights[i % ROTATE]), non_blocking=True)
 
     for i in range(max(args.warmup, 3)):
         step(i)
     torch.cuda.synchronize()
     selected = rk.get_last_dispatch()["selected"]
-    eager_steps = max(args.e2e_steps // (1 if dist.world > 1 else 4), 10)
+    eager_steps = max(args.e2e_steps // 4, 10)
     dist.barrier()
     torch.cuda.synchronize()
     eager_ms = dist.max(time_loop(step, eager_steps, stream))
     dist.barrier()
     eager = {"value": rate(eager_ms, eager_steps), "ms_per_step": round(eager_ms / eager_steps, 5)}
-    result = {
-        "unit": "GB/s",
-        "h2d_bytes_per_step": m * k * 2,
-        "d2h_bytes_per_step": m * n * dist.world * 2,
-    }
-    if dist.world > 1:
-        result.update(eager)
-        result["path"] = (f"eager: H2D copy, radeon_kernels.gemv -> {selected}, NCCL all-gather + "
-                          "rk_gather_column_blocks, D2H copy; one stream")
-        return result
+    result = {"unit": "GB/s", "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * 2}
 
     G = E2E_GRAPH_STEPS
     xs_host = seeded((G, m, k), 2, "normal", "bf16", device="cpu").pin_memory()
@@ -412,6 +519,52 @@ def e2e(args, dist: Dist):
         "eager_serial": eager,
     })
     return result
+
+
+def e2e_sharded(args, dist: Dist):
+    """N > 1: H2D copy, ShardedGemv(gather=True) (fused all-gather kernel), D2H copy of the
+    full output, one stream, 16 steps per CUDA graph, replayed."""
+
+    import torch
+
+    from radeon_kernels.distributed import ShardedGemv
+
+    m, n, k = HEAD_M, HEAD_N, HEAD_K
+    weights = sharded_weights(dist)
+    operators = [ShardedGemv(w, n_total=n) for w in weights]
+    stream = torch.cuda.current_stream()
+    G = E2E_GRAPH_STEPS
+    xs_host = seeded((G, m, k), 2, "normal", "bf16", device="cpu").pin_memory()
+    outs_host = torch.empty((G, m, n), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
+
+    def step(i):
+        x_dev.copy_(xs_host[i % G], non_blocking=True)
+        y = operators[i % len(operators)](x_dev, gather=True)
+        outs_host[i % G].copy_(y, non_blocking=True)
+
+    for i in range(max(args.warmup, 3, len(operators))):
+        step(i)  # the first gathered call of each operator sets up its exchange (collective)
+    torch.cuda.synchronize()
+    graph = capture_graph(step, G, stream)
+    graph.replay()
+    torch.cuda.synchronize()
+    replays = max(args.e2e_steps // G, 10)
+    ms, _ = timed_region(lambda: [graph.replay() for _ in range(replays)], dist, stream)
+    del graph
+    for op in operators:
+        op.close()
+    steps = replays * G
+    return {
+        "unit": "GB/s",
+        "h2d_bytes_per_step": m * k * 2,
+        "d2h_bytes_per_step": m * n * 2,
+        "value": round(gemv_bytes(m, n, k) * steps / (ms / 1e3) / 1e9, 1),
+        "ms_per_step": round(ms / steps, 5),
+        "path": (f"CUDA graph of {G} captured steps on one stream: pinned H2D copy, "
+                 "radeon_kernels.distributed.ShardedGemv(gather=True) -> rk_gemv_allgather, "
+                 "pinned D2H copy of the full output"),
+    }
 
 
 def suite(args, dist: Dist, ext, peaks):
@@ -747,6 +900,86 @@ def suite(args, dist: Dist, ext, peaks):
         }
         del qkv
 
+    def c5_sharded_case(name, iters):
+        """BASELINE config 5 with B split into N column blocks (strong scaling): the local
+        product alone, the fused all-gather kernel (rk_gemm_allgather: every tile stored into
+        every rank's C over NVLink while the next tile accumulates), and the NCCL form it
+        replaces (local product, all_gather_into_tensor, rk_gather_column_blocks)."""
+
+        if not wanted(name):
+            return
+        import torch.distributed as tdist
+
+        from radeon_kernels.distributed.peer import PeerExchange
+
+        M, N, K = 16384, 57344, 8192
+        nb = N // g
+        a = seeded((M, K), 4, "uniform16", "bf16")
+        b = seeded((K, nb), 5 + dist.rank, "uniform16", "bf16")
+        c_local = torch.empty(M, nb, dtype=a.dtype, device="cuda")
+        exchange = PeerExchange((M, N), a.dtype)
+        staged = torch.empty(g * M, nb, dtype=a.dtype, device="cuda")
+        full = torch.empty(M, N, dtype=a.dtype, device="cuda")
+
+        def compute():
+            ext.gemm_out(a, b, c_local, 0)
+
+        def fused():
+            ext.gemm_allgather(a, b, exchange.output, exchange.out_ptrs, exchange.ctl_ptrs,
+                               exchange.rank, exchange.timeout_ns)
+
+        def nccl():
+            ext.gemm_out(a, b, c_local, 0)
+            tdist.all_gather_into_tensor(staged, c_local)
+            ext.gather_column_blocks(staged.view(g, M, nb), full)
+
+        def measure(fn):
+            fn()
+            torch.cuda.synchronize()
+            times = []
+            for _ in range(iters):
+                flush.zero_()  # L2 flush between timed launches
+                dist.barrier()
+                times.append(time_loop(lambda i: fn(), 1, stream))
+            dist.barrier()
+            return dist.max(statistics.median(times))
+
+        ms_compute = measure(compute)
+        cool_down()
+        ms_fused = measure(fused)
+        cool_down()
+        ms_nccl = measure(nccl)
+        flops = 2.0 * M * N * K
+        received = (g - 1) * M * nb * 2  # bytes of C each GPU receives from its peers
+        # Roofline of the fused kernel: the slower of the tensor work at the sustained GEMM
+        # peak and the bytes every GPU must receive at the measured 770 GB/s peer bandwidth.
+        t_tensor = flops / g / (peaks["bf16_tflops_sustained"] * 1e12)
+        t_link = received / 770e9
+        target_ms = max(t_tensor, t_link) * 1e3
+        results[name] = {
+            "unit": "TFLOP/s",
+            "value": round(flops / (ms_fused / 1e3) / 1e12, 1),
+            "compute_only": {"ms": round(ms_compute, 4), "value": round(flops / (ms_compute / 1e3) / 1e12, 1),
+                             "per_gpu": round(flops / g / (ms_compute / 1e3) / 1e12, 1),
+                             "roofline_frac": round(flops / g / (ms_compute / 1e3) / 1e12 / peaks["bf16_tflops"], 4)},
+            "with_gather_fused": {"ms": round(ms_fused, 4), "value": round(flops / (ms_fused / 1e3) / 1e12, 1),
+                                  "gather_ms": round(ms_fused - ms_compute, 4),
+                                  "nvlink_recv_gbs_per_gpu": round(received / (ms_fused / 1e3) / 1e9, 1),
+                                  "vs_compute_only": round(ms_compute / ms_fused, 4)},
+            "with_gather_nccl": {"ms": round(ms_nccl, 4), "value": round(flops / (ms_nccl / 1e3) / 1e12, 1),
+                                 "gather_ms": round(ms_nccl - ms_compute, 4)},
+            "roofline": {"bound": "nvlink" if t_link > t_tensor else "tensor", "target_ms": round(target_ms, 4),
+                         "frac": round(target_ms / ms_fused, 4),
+                         "basis": "max(2MNK/G / sustained bf16 peak, received bytes / 770 GB/s per GPU)"},
+            "scaling": "strong",
+            "shape": [M, N, K],
+            "n_per_gpu": nb,
+            "dtype": "bf16",
+            "timing": "single call, L2 flushed, median of %d, max over ranks" % iters,
+        }
+        exchange.close()
+        del a, b, c_local, staged, full, exchange
+
     def cool_down():
         # Let the power/clock state recover between long GEMM cases so one case's
         # power capping does not leak into the next measurement.
@@ -796,7 +1029,10 @@ def suite(args, dist: Dist, ext, peaks):
     if not args.quick:
         gemm_case("gemm_8192_bf16", 8192, 8192, 8192, "bf16", "uniform16", 7, 5)
         cool_down()
-    gemm_case(f"c5_gemm_large_bf16_shard{g}", 16384, 57344 // g, 8192, "bf16", "uniform16", 4, 3, scaling="strong")
+    if g == 1:
+        gemm_case("c5_gemm_large_bf16_shard1", 16384, 57344, 8192, "bf16", "uniform16", 4, 3, scaling="strong")
+    else:
+        c5_sharded_case(f"c5_gemm_large_bf16_shard{g}", 3)
     del flush
     return results
 
@@ -845,9 +1081,18 @@ def _cpu_model() -> str:
 
 
 def run_reference(args) -> int:
-    """--impl reference: the reference's CPU implementation on the host cores (rank 0 only)."""
+    """--impl reference: the reference's CPU implementation on the host cores (rank 0 only).
+
+    The reference's path for config 2 is ``torch.mm(x, W.T)`` on host tensors
+    (ops/gemv/reference.py:12-15, via oracle/reference_path.py) -- one call covers the whole
+    8192 x 8192 weight, whatever N.  The timed region spans about ``--cpu-seconds`` (the
+    window of the repo arm's ``cpu_baseline``): ``--steps`` steps of an equal number of
+    calls each, the count calibrated from the warm-up calls, so the denominator of the
+    driver's ratio is a stable sample rather than a few milliseconds.
+    """
 
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return 0
     import torch
@@ -859,36 +1104,39 @@ def run_reference(args) -> int:
     gen = torch.Generator().manual_seed(1)
     x = torch.randn((1, 8192), generator=gen).to(torch.bfloat16)
     w = (torch.randn((8192, 8192), generator=gen) / 8192**0.5).to(torch.bfloat16)
-    for _ in range(max(args.warmup, 3)):
-        reference_path.gemv_fallback(torch, x, w)
+    warm = max(args.warmup, 3)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(warm):
         reference_path.gemv_fallback(torch, x, w)
+    per_call = (time.perf_counter() - t0) / warm
+    steps = max(1, args.steps)
+    calls_per_step = max(1, int(round(args.cpu_seconds / steps / max(per_call, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for _ in range(calls_per_step):
+            reference_path.gemv_fallback(torch, x, w)
     elapsed = time.perf_counter() - t0
-    value = gemv_bytes(1, 8192, 8192) * args.steps / elapsed / 1e9
+    calls = steps * calls_per_step
+    value = gemv_bytes(1, 8192, 8192) * calls / elapsed / 1e9
+    sample = (f"{steps} steps x {calls_per_step} calls of torch.mm(x, W.T) on x[1,8192] @ W[8192,8192]^T bf16 "
+              f"(ops/gemv/reference.py:12-15 via oracle/reference_path.py), {elapsed:.1f} s, {cores} threads")
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": round(value, 2),
         "unit": "GB/s",
-        "n_gpus": args.gpus,
-        "steps": args.steps,
+        "n_gpus": args.gpus if args.gpus else world,
+        "steps": steps,
         "warmup": args.warmup,
-        "ms_per_step": round(elapsed / args.steps * 1e3, 4),
+        "ms_per_step": round(elapsed / calls * 1e3, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded torch.Generator, BASELINE config 2 distributions)",
-        "config": {"workload": "gemv-decode-bf16-m1-n8192-k8192 (BASELINE config 2)", "l2": "n/a (host CPU)"},
-        "cpu_baseline": {
-            "value": round(value, 2),
-            "unit": "GB/s",
-            "cores": cores,
-            "kind": "port",
-            "sample": f"{args.steps} calls of torch.mm(x, W.T) (ops/gemv/reference.py:12-15 via oracle/reference_path.py), host CPU",
-            "cpu": _cpu_model(),
-        },
+        "data": DATA,
+        "config": headline_config(max(1, args.gpus)),
+        "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": sample, "cpu": _cpu_model()},
         "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -977,7 +1225,7 @@ def main(argv=None) -> int:
     parser.add_argument("--profile", choices=sorted(PROFILE_CASES), default=None,
                         help="run --steps launches of one kernel only (the case ncu captures)")
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=40000)
+    parser.add_argument("--steps", type=int, default=4000)
     parser.add_argument("--warmup", type=int, default=20)
     parser.add_argument("--e2e-steps", type=int, default=2000)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -1007,12 +1255,14 @@ def main(argv=None) -> int:
         head = headline(args, dist, ext, peaks, peak_kind)
         end_to_end = e2e(args, dist)
         extra = {} if args.no_suite else suite(args, dist, ext, peaks)
-    traffic = load_traffic().get("gemv_decode_bf16_m1_n8192_k8192")  # bytes per launch (ncu)
-    head["roofline"]["traffic"] = traffic
+    traffic_key = "gemv_decode_bf16_m1_n8192_k8192" if dist.world == 1 else f"gemv_allgather_bf16_m1_n8192_k8192_w{dist.world}"
+    head["roofline"]["traffic"] = load_traffic().get(traffic_key)  # bytes per launch (ncu)
     cpu = cpu_baseline(args.cpu_seconds) if dist.rank == 0 and dist.world == 1 else None
     dist.close()
     if dist.rank != 0:
         return 0
+    config = headline_config(dist.world)
+    config["launch"] = head.pop("launch")
     line = {
         "metric": METRIC,
         "value": round(head["value"], 1),
@@ -1022,27 +1272,23 @@ def main(argv=None) -> int:
         "warmup": args.warmup,
         "ms_per_step": round(head["ms_per_step"], 6),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded torch.Generator, BASELINE config 2 distributions: x~N(0,1), W~N(0,1/8192))",
-        "config": {
-            "workload": "gemv-decode-bf16-m1-n8192-k8192 (BASELINE config 2), x @ W^T, N-row shards of 8192 rows per GPU",
-            "m": 1,
-            "n_per_gpu": 8192,
-            "k": 8192,
-            "l2": f"inputs larger than L2: {ROTATE} weight matrices x 128 MiB rotated per step",
-            "launch": "CUDA graph of 40 rk_gemv launches, replayed",
-            "parallelism": f"weight-row shards x{dist.world}",
-        },
+        "data": DATA,
+        "config": config,
         "roofline": head["roofline"],
         "e2e": end_to_end,
         "gpu_launches": head["steps"],
+        "gpu_launches_note": "per rank: one rk_gemv (N = 1) or rk_gemv_allgather (N > 1) launch per timed step",
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
         "suite": extra,
         "library_launches_host_counted": int(_native.library().rk_launch_count() - launches_before),
     }
+    for key in ("compute_only", "exchange_us_per_step", "weight_sets_per_rank"):
+        if key in head:
+            line[key] = head[key]
     print(json.dumps(line), flush=True)
     return 0
 

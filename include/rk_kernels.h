@@ -185,6 +185,76 @@ RK_API rk_status rk_gather_column_blocks(const void* blocks, void* out, int64_t 
                                   rk_stream_t stream);
 
 /*
+ * Multi-GPU: N-column sharding with the all-gather fused into the kernel.  No
+ * counterpart in the reference (it has no multi-GPU path).
+ *
+ * One process per GPU.  A group of `world` ranks shares, per rank, a full output
+ * buffer [M, world * N_block] and a control block of RK_PEER_CTL_BYTES (zeroed before
+ * the first call, 512-byte aligned), each mapped into every other rank's process with
+ * rk_ipc_export / rk_ipc_open.  Rank r owns the column block [r*N_block, (r+1)*N_block)
+ * of the result; its kernel computes that block and stores it with plain peer stores
+ * over NVLink into every rank's output while the rest of the block is still being
+ * computed.  When the call completes on a rank's stream, that rank's full output holds
+ * every rank's block.
+ *
+ * Rules: every rank of the group makes the same sequence of calls on one group, each
+ * rank on one stream; a rank's output may be read until that rank's next call on the
+ * group (the next call lets the other ranks overwrite it only after it has started on
+ * this rank, i.e. after everything queued before it on the stream completed).  Cross-GPU
+ * waits are bounded by `timeout_ns` (0: 10 s); a wait that runs out is reported by
+ * rk_device_status() as RK_ERR_TIMEOUT and the group must be rebuilt.
+ */
+#define RK_PEER_MAX 8
+#define RK_PEER_CTL_BYTES 512
+
+typedef struct rk_ipc_handle {
+  unsigned char bytes[64]; /* cudaIpcMemHandle_t of the allocation holding the pointer */
+  uint64_t offset;         /* pointer - allocation base */
+} rk_ipc_handle;
+
+typedef struct rk_peer_group {
+  int32_t rank;              /* this process's rank, 0 <= rank < world */
+  int32_t world;             /* ranks in the group, 1..RK_PEER_MAX */
+  void* out[RK_PEER_MAX];    /* out[j]: rank j's full output as mapped in this process */
+  void* ctl[RK_PEER_MAX];    /* ctl[j]: rank j's control block as mapped in this process */
+  uint64_t timeout_ns;       /* limit of each cross-GPU wait (0: 10 s) */
+} rk_peer_group;
+
+/* Handle to the device allocation holding `ptr` (any pointer into it, e.g. a PyTorch
+ * tensor's data_ptr()), for another process to map with rk_ipc_open. */
+RK_API rk_status rk_ipc_export(const void* ptr, rk_ipc_handle* handle);
+/* Maps another process's exported pointer into this process (current device); opening
+ * the same allocation again shares the mapping. */
+RK_API rk_status rk_ipc_open(const rk_ipc_handle* handle, void** ptr);
+/* Releases one rk_ipc_open of `handle`; the last release unmaps the allocation. */
+RK_API rk_status rk_ipc_close(const rk_ipc_handle* handle);
+
+/*
+ * out = x @ weight^T with the weight split by rows: weight_block holds rows
+ * [rank*N_block, (rank+1)*N_block) of the [world*N_block, K] weight; x [M, K] is the same
+ * on every rank.  The 128-bit streaming kernel of RK_GEMV_STREAM (identical results to
+ * rk_gemv with that variant on the unsplit weight) stores each output element into every
+ * rank's out[j] [M, world*N_block].  1 <= M <= 32; K % 8 == 0 and 16-byte-aligned x and
+ * weight (RK_ERR_UNSUPPORTED otherwise).
+ */
+RK_API rk_status rk_gemv_allgather(const void* x, const void* weight_block, int64_t M,
+                                   int64_t N_block, int64_t K, rk_dtype dt,
+                                   const rk_peer_group* group, rk_stream_t stream);
+
+/*
+ * C = A @ B with B split by columns: B_block is [K, N_block] (columns [rank*N_block,
+ * (rank+1)*N_block) of the [K, world*N_block] B, row-major), A [M, K] is the same on every
+ * rank.  The 2-SM tcgen05 kernel of RK_GEMM_TC_2SM (identical results to rk_gemm with that
+ * variant on the unsplit B) stages each finished 256 x 256 tile in shared memory and stores
+ * it, 128 contiguous bytes per row segment, into every rank's out[j] [M, world*N_block]
+ * while the next tile accumulates.  N_block % 8 == 0, K % 8 == 0, 16-byte-aligned operands
+ * and outputs (RK_ERR_UNSUPPORTED otherwise).
+ */
+RK_API rk_status rk_gemm_allgather(const void* A, const void* B_block, int64_t M,
+                                   int64_t N_block, int64_t K, rk_dtype dt,
+                                   const rk_peer_group* group, rk_stream_t stream);
+
+/*
  * Fused FFN-up projection with SwiGLU: C = silu(A @ B[:, :N]) * (A @ B[:, N:]).
  * A: [M,K] row-major; B: [K, 2N] row-major, the gate projection in columns [0, N) and the
  * up projection in columns [N, 2N) (torch.cat([w_gate, w_up], dim=1)); C: [M,N].  Both

@@ -49,7 +49,7 @@ NVCC_FLAGS = [
     f"-I{INCLUDE}",
     f"-I{CSRC}",
 ]
-KERNEL_SOURCES = ["rk_abi.cu", "gemm_tcgen05.cu", "gemm_tcgen05_2sm.cu", "gemm_simt.cu", "gemv.cu", "gemv_tcgen05.cu", "gather.cu", "llm_ops.cu", "llm_ops_backward.cu", "paged_attention.cu", "paged_attention_tc.cu", "sdpa_tcgen05.cu"]
+KERNEL_SOURCES = ["rk_abi.cu", "peer.cu", "gemm_tcgen05.cu", "gemm_tcgen05_2sm.cu", "gemm_simt.cu", "gemv.cu", "gemv_tcgen05.cu", "gather.cu", "llm_ops.cu", "llm_ops_backward.cu", "paged_attention.cu", "paged_attention_tc.cu", "sdpa_tcgen05.cu"]
 HEADERS = sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "rk_kernels.h"]
 
 EXT_SUFFIX = sysconfig.get_config_var("EXT_SUFFIX") or ".so"

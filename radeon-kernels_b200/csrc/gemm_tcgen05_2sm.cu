@@ -31,6 +31,7 @@
 
 #include "rk_device.cuh"
 #include "rk_internal.h"
+#include "rk_peer.cuh"
 #include "rk_tma.h"
 
 namespace rk {
@@ -61,6 +62,27 @@ struct __align__(8) Bars {
 };
 
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + int(sizeof(Bars));
+// PEERS form: a 32-row x 64-column staging tile per epilogue warp after the barriers.
+constexpr int PEER_STAGE_OFFSET = STAGES * STAGE_BYTES + 1024;
+constexpr int PEER_STAGE_WARP = 32 * 128;
+constexpr int SMEM_BYTES_PEERS = 1024 + PEER_STAGE_OFFSET + 4 * PEER_STAGE_WARP;
+static_assert(int(sizeof(Bars)) <= 1024, "barriers fit before the staging tiles");
+static_assert(SMEM_BYTES_PEERS <= 227 * 1024, "shared memory per CTA");
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, const uint4& v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
@@ -76,11 +98,21 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 // stages the tile's 128 gate columns and the odd CTA the matching 128 up columns, so
 // accumulator columns 0-127 hold gate and 128-255 up for the CTA's rows, and the
 // epilogue stores silu(gate) * up (N is the output width).
-template <typename T, bool SWIGLU = false, bool A_MN = false, bool B_K = false>
+//
+// PEERS: the fused all-gather form (rk_gemm_allgather).  B is this rank's column block
+// [K, N] and C is unused: each epilogue warp converts 64 accumulator columns of its 32 rows
+// into a swizzled staging tile in shared memory, releases the accumulator after the last
+// TMEM read of the tile, and then writes the staged rows -- 8 lanes per 128-byte row
+// segment -- into every rank's full output (peer.out[j], row stride peer.ldo) with plain
+// 16-byte stores, so each tile crosses NVLink while the next one accumulates.  The first
+// peer store waits until every rank has started this call; the exchange then completes as
+// rk_peer.cuh describes.
+template <typename T, bool SWIGLU = false, bool A_MN = false, bool B_K = false, bool PEERS = false>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M, int N,
-                    int K, KernelCtl ctl) {
+                    int K, KernelCtl ctl, const __grid_constant__ PeerOut<T> peer) {
+  static_assert(!(PEERS && (SWIGLU || A_MN || B_K)), "the fused all-gather GEMM takes the nn layout");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -124,6 +156,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   cluster_sync_all();  // both CTAs' barriers exist before either signals the other
   const uint32_t tmem_base = bars->tmem_base;
   pdl_begin();  // global memory is touched only after this
+  uint32_t epoch = 0;
+  if constexpr (PEERS) {
+    epoch = peer_call_epoch(peer);
+    if (blockIdx.x == 0 && threadIdx.x == 64) peer_announce(peer, epoch);
+  }
 
   if (warp == 0) {
     if (lane == 0) {
@@ -241,6 +278,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // --------------------------------------------------------------- epilogue
     const int quarter = warp & 3;
     int i = 0;
+    bool peers_checked = false;
     for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
       int mb, nb;
       tile_coords(t, num_m, num_n, mb, nb);
@@ -253,6 +291,63 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
+      if constexpr (PEERS) {
+        if (!peers_checked) {
+          int ok = 1;
+          if (lane == 0) ok = peer_wait_ready(peer, epoch) ? 1 : 0;
+          peers_checked = true;
+          if (__shfl_sync(0xffffffffu, ok, 0) == 0) {
+            *abort_flag = 1;  // a rank never started: stop every role, store nothing
+            break;
+          }
+        }
+        const int row0 = mb * BM + static_cast<int>(rank) * HALF + quarter * 32;
+        const uint32_t stage = smem_u32(smem + PEER_STAGE_OFFSET + quarter * PEER_STAGE_WARP);
+        const uint32_t tbase =
+            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+        const int unit = lane & 7;
+#pragma unroll 1
+        for (int c2 = 0; c2 < BN / 64; ++c2) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tbase + (2 * c2 + h) * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 v;
+              v.x = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+              v.y = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+              v.z = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+              v.w = Pack2<T>::from_floats(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+              // Row `lane`, 16-byte unit h*4+q; the unit index is XORed with the row so the
+              // eight lanes of each store phase hit eight different bank groups.
+              st_shared_v4(stage + lane * 128 + (((h * 4 + q) ^ (lane & 7)) << 4), v);
+            }
+          }
+          if (c2 == BN / 64 - 1) {
+            // Last TMEM read of this accumulator: hand it back before the stores.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&bars->tmem_empty[acc]), 0));
+          } else {
+            __syncwarp();
+          }
+          const int gcol = nb * BN + c2 * 64 + unit * 8;
+#pragma unroll 4
+          for (int it = 0; it < 8; ++it) {
+            const int rr = (lane >> 3) + 4 * it;  // lanes 8k..8k+7 cover one row's 128 bytes
+            const uint4 v = ld_shared_v4(stage + rr * 128 + ((unit ^ (rr & 7)) << 4));
+            const int grow = row0 + rr;
+            if (grow < M && gcol + 8 <= N) {
+              const size_t at = static_cast<size_t>(grow) * peer.ldo + gcol;
+              for (int j = 0; j < peer.world; ++j) *reinterpret_cast<uint4*>(peer.out[j] + at) = v;
+            }
+          }
+          __syncwarp();  // the staging tile is rewritten by the next column group
+        }
+        continue;
+      }
       const int row = mb * BM + static_cast<int>(rank) * HALF + quarter * 32 + lane;
       T* crow = C + static_cast<size_t>(row) * N;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
@@ -289,6 +384,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&bars->tmem_empty[acc]), 0));
     }
+    if constexpr (PEERS) __threadfence_system();  // this thread's peer stores, before the count
   }
 
   tc_fence_before();
@@ -297,6 +393,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+  if constexpr (PEERS) {
+    if (threadIdx.x == 0) peer_finish(peer, epoch, gridDim.x);
   }
 }
 
@@ -338,11 +437,65 @@ rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N
                                       dim3(static_cast<unsigned>(2 * pairs)),
                                       dim3(tc2::THREADS), tc2::SMEM_BYTES, s, 2, ta, tb,
                                       reinterpret_cast<T*>(C), static_cast<int>(M),
-                                      static_cast<int>(N), static_cast<int>(K), ctl);
+                                      static_cast<int>(N), static_cast<int>(K), ctl, PeerOut<T>{});
+  note_launch();
+  return cuda_status(e);
+}
+
+template <typename T>
+rk_status launch_tc2_peers(const void* A, const void* B, int64_t M, int64_t N, int64_t K,
+                           rk_dtype dt, const PeerTargets& t, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  rk_status st = make_tmap_2d(&ta, A, dt, K, M, 64, tc2::HALF);
+  if (st != RK_OK) return st;
+  st = make_tmap_2d(&tb, B, dt, N, K, 64, tc2::BK);
+  if (st != RK_OK) return st;
+  LaunchCtl lc;
+  if ((st = launch_ctl(&lc)) != RK_OK) return st;
+  // The roles' waits may include another rank's late start: give them the group's limit.
+  KernelCtl ctl{lc.status, lc.timeout_ns > t.timeout_ns ? lc.timeout_ns : t.timeout_ns, 0};
+  PeerOut<T> peer{};
+  for (int j = 0; j < t.world; ++j) {
+    peer.out[j] = static_cast<T*>(t.out[j]);
+    peer.ctl[j] = static_cast<PeerCtl*>(t.ctl[j]);
+  }
+  peer.ldo = t.ldo;
+  peer.rank = t.rank;
+  peer.world = t.world;
+  peer.timeout_ns = t.timeout_ns;
+  peer.status = lc.status;
+
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(tc2::gemm_tc2_kernel<T, false, false, false, true>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              tc2::SMEM_BYTES_PEERS);
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
+
+  const int64_t tiles = ((M + tc2::BM - 1) / tc2::BM) * ((N + tc2::BN - 1) / tc2::BN);
+  const int64_t pairs_max = device_sm_count() / 2;
+  const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
+  const cudaError_t e = launch_kernel(tc2::gemm_tc2_kernel<T, false, false, false, true>,
+                                      dim3(static_cast<unsigned>(2 * pairs)), dim3(tc2::THREADS),
+                                      tc2::SMEM_BYTES_PEERS, s, 2, ta, tb, static_cast<T*>(nullptr),
+                                      static_cast<int>(M), static_cast<int>(N),
+                                      static_cast<int>(K), ctl, peer);
   note_launch();
   return cuda_status(e);
 }
 }  // namespace
+
+rk_status gemm_tc2_allgather_launch(const void* A, const void* B, int64_t M, int64_t N_block,
+                                    int64_t K, rk_dtype dt, const PeerTargets& t, cudaStream_t s) {
+  if (!gemm_tc_supported(A, B, t.out[t.rank], M, N_block, K, RK_LAYOUT_NN)) return RK_ERR_UNSUPPORTED;
+  if (device_sm_count() < 2) return RK_ERR_UNSUPPORTED;
+  if (dt == RK_DTYPE_BF16) return launch_tc2_peers<__nv_bfloat16>(A, B, M, N_block, K, dt, t, s);
+  return launch_tc2_peers<__half>(A, B, M, N_block, K, dt, t, s);
+}
 
 template <typename T>
 rk_status launch_tc2_layout(const void* A, const void* B, void* C, int64_t M, int64_t N,

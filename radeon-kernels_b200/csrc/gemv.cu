@@ -34,6 +34,7 @@
 
 #include "rk_device.cuh"
 #include "rk_internal.h"
+#include "rk_peer.cuh"
 
 namespace rk {
 
@@ -139,10 +140,16 @@ struct Log2<1> {
 // its K-slice at a time with UNROLL 16-byte loads per row per lane in flight
 // (out-of-range vectors are predicated off, never loaded).  Per-warp partial
 // sums go to shared memory [KS][rows][MB] and are added in ks order.
-template <typename T, int MB, int ROWS, int KS>
+//
+// PEER: the fused all-gather form (rk_gemv_allgather).  W holds this rank's block of
+// weight rows; each output element is stored into every rank's full output
+// (peer.out[j], row stride peer.ldo) once the ranks have started this call, and the
+// exchange completes as rk_peer.cuh describes.  CTA 0 announces the call at the start.
+template <typename T, int MB, int ROWS, int KS, bool PEER = false>
 __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_stream_kernel(const T* __restrict__ x, const T* __restrict__ W, T* __restrict__ out,
-                       int M, int N, int K, int rows_base, int rows_rem, int rows_max) {
+                       int M, int N, int K, int rows_base, int rows_rem, int rows_max,
+                       const __grid_constant__ PeerOut<T> peer) {
   constexpr int RG = GEMV_WARPS / KS;
   constexpr int UNROLL = ROWS >= 4 ? 2 : 4;
   constexpr int V = MB * ROWS;
@@ -150,6 +157,11 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   extern __shared__ float red[];  // [KS][rows_max][MB]
 
   pdl_begin();
+  uint32_t epoch = 0;
+  if constexpr (PEER) {
+    epoch = peer_call_epoch(peer);
+    if (blockIdx.x == 0 && threadIdx.x == 0) peer_announce(peer, epoch);
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int cta = blockIdx.x;
@@ -216,12 +228,32 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     }
   }
   __syncthreads();
-  for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {
-    const int i = t / M, m = t % M;
-    float s = 0.f;
+  if constexpr (PEER) {
+    __shared__ int peers_ready;
+    if (threadIdx.x == 0) peers_ready = peer_wait_ready(peer, epoch) ? 1 : 0;
+    __syncthreads();
+    if (peers_ready) {
+      for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {
+        const int i = t / M, m = t % M;
+        float s = 0.f;
 #pragma unroll
-    for (int k = 0; k < KS; ++k) s += red[(k * rows_max + i) * MB + m];
-    out[static_cast<size_t>(m) * N + row_begin + i] = from_f32<T>(s);
+        for (int k = 0; k < KS; ++k) s += red[(k * rows_max + i) * MB + m];
+        const T v = from_f32<T>(s);
+        const size_t at = static_cast<size_t>(m) * peer.ldo + row_begin + i;
+        for (int j = 0; j < peer.world; ++j) peer.out[j][at] = v;
+      }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) peer_finish(peer, epoch, gridDim.x);
+  } else {
+    for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {
+      const int i = t / M, m = t % M;
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) s += red[(k * rows_max + i) * MB + m];
+      out[static_cast<size_t>(m) * N + row_begin + i] = from_f32<T>(s);
+    }
   }
 }
 
@@ -253,55 +285,74 @@ __global__ void __launch_bounds__(256)
 
 struct StreamLaunch {
   const void* kernel;
+  // `peer` is null for the plain kernel, the fused all-gather targets otherwise.
   void (*launch)(const void*, const void*, void*, int, int, int, int, int, int, int, size_t,
-                 cudaStream_t);
+                 cudaStream_t, const PeerTargets*, const LaunchCtl*);
 };
 
-template <typename T, int MB, int ROWS, int KS>
+template <typename T>
+PeerOut<T> peer_out(const PeerTargets* t, const LaunchCtl* lc) {
+  PeerOut<T> p{};
+  if (t != nullptr) {
+    for (int j = 0; j < t->world; ++j) {
+      p.out[j] = static_cast<T*>(t->out[j]);
+      p.ctl[j] = static_cast<PeerCtl*>(t->ctl[j]);
+    }
+    p.ldo = t->ldo;
+    p.rank = t->rank;
+    p.world = t->world;
+    p.timeout_ns = t->timeout_ns;
+    p.status = lc->status;
+  }
+  return p;
+}
+
+template <typename T, int MB, int ROWS, int KS, bool PEER>
 void launch_stream(const void* x, const void* W, void* out, int M, int N, int K, int grid,
-                   int rows_base, int rows_rem, int rows_max, size_t smem, cudaStream_t s) {
+                   int rows_base, int rows_rem, int rows_max, size_t smem, cudaStream_t s,
+                   const PeerTargets* peer, const LaunchCtl* lc) {
   // Launch errors are left for the caller's cudaGetLastError().
-  (void)launch_kernel(gemv_stream_kernel<T, MB, ROWS, KS>, dim3(grid), dim3(GEMV_THREADS), smem, s, 0,
-                      static_cast<const T*>(x), static_cast<const T*>(W), static_cast<T*>(out), M, N,
-                      K, rows_base, rows_rem, rows_max);
+  (void)launch_kernel(gemv_stream_kernel<T, MB, ROWS, KS, PEER>, dim3(grid), dim3(GEMV_THREADS), smem,
+                      s, 0, static_cast<const T*>(x), static_cast<const T*>(W), static_cast<T*>(out),
+                      M, N, K, rows_base, rows_rem, rows_max, peer_out<T>(peer, lc));
 }
 
-template <typename T, int MB, int ROWS, int KS>
+template <typename T, int MB, int ROWS, int KS, bool PEER>
 StreamLaunch make_stream() {
-  return {reinterpret_cast<const void*>(&gemv_stream_kernel<T, MB, ROWS, KS>),
-          &launch_stream<T, MB, ROWS, KS>};
+  return {reinterpret_cast<const void*>(&gemv_stream_kernel<T, MB, ROWS, KS, PEER>),
+          &launch_stream<T, MB, ROWS, KS, PEER>};
 }
 
-template <typename T, int MB, int ROWS>
+template <typename T, int MB, int ROWS, bool PEER>
 StreamLaunch pick_ks(int ks) {
   switch (ks) {
-    case 1: return make_stream<T, MB, ROWS, 1>();
-    case 2: return make_stream<T, MB, ROWS, 2>();
-    case 4: return make_stream<T, MB, ROWS, 4>();
-    default: return make_stream<T, MB, ROWS, 8>();
+    case 1: return make_stream<T, MB, ROWS, 1, PEER>();
+    case 2: return make_stream<T, MB, ROWS, 2, PEER>();
+    case 4: return make_stream<T, MB, ROWS, 4, PEER>();
+    default: return make_stream<T, MB, ROWS, 8, PEER>();
   }
 }
 
-template <typename T, int MB>
+template <typename T, int MB, bool PEER>
 StreamLaunch pick_rows(int rows, int ks) {
   if constexpr (MB <= 4) {
-    if (rows >= 4) return pick_ks<T, MB, 4>(ks);
+    if (rows >= 4) return pick_ks<T, MB, 4, PEER>(ks);
   }
   if constexpr (MB <= 16) {
-    if (rows >= 2) return pick_ks<T, MB, 2>(ks);
+    if (rows >= 2) return pick_ks<T, MB, 2, PEER>(ks);
   }
-  return pick_ks<T, MB, 1>(ks);
+  return pick_ks<T, MB, 1, PEER>(ks);
 }
 
-template <typename T>
+template <typename T, bool PEER = false>
 StreamLaunch pick(int mb, int rows, int ks) {
   switch (mb) {
-    case 1: return pick_rows<T, 1>(rows, ks);
-    case 2: return pick_rows<T, 2>(rows, ks);
-    case 4: return pick_rows<T, 4>(rows, ks);
-    case 8: return pick_rows<T, 8>(rows, ks);
-    case 16: return pick_rows<T, 16>(rows, ks);
-    default: return pick_rows<T, 32>(rows, ks);
+    case 1: return pick_rows<T, 1, PEER>(rows, ks);
+    case 2: return pick_rows<T, 2, PEER>(rows, ks);
+    case 4: return pick_rows<T, 4, PEER>(rows, ks);
+    case 8: return pick_rows<T, 8, PEER>(rows, ks);
+    case 16: return pick_rows<T, 16, PEER>(rows, ks);
+    default: return pick_rows<T, 32, PEER>(rows, ks);
   }
 }
 
@@ -349,9 +400,14 @@ bool gemv_stream_supported(const void* x, const void* W, const void* out, int64_
   return true;
 }
 
-rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,
-                             int64_t K, rk_dtype dt, cudaStream_t s) {
-  if (!gemv_stream_supported(x, W, out, M, N, K)) return RK_ERR_UNSUPPORTED;
+namespace {
+
+// The streaming launch shared by rk_gemv (peer == nullptr: out is [M, N]) and
+// rk_gemv_allgather (out unused: the kernel stores into every rank's output).  Both take
+// the same rows / K-split choice from (M, K), so every output element is reduced in the
+// same order and the fused form reproduces the plain kernel bit for bit.
+rk_status stream_run(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
+                     rk_dtype dt, cudaStream_t s, const PeerTargets* peer) {
   const int mb = bucket_m(M);
   int rows = g_gemv_rows_override.load();
   if (rows <= 0) rows = mb <= 2 ? 2 : (mb <= 4 ? 4 : (mb <= 16 ? 2 : 1));
@@ -378,7 +434,16 @@ rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M,
     }
   }
   ks = ks >= 8 ? 8 : (ks >= 4 ? 4 : (ks >= 2 ? 2 : 1));
-  StreamLaunch L = dt == RK_DTYPE_BF16 ? pick<__nv_bfloat16>(mb, rows, ks) : pick<__half>(mb, rows, ks);
+  StreamLaunch L = peer != nullptr
+                       ? (dt == RK_DTYPE_BF16 ? pick<__nv_bfloat16, true>(mb, rows, ks)
+                                              : pick<__half, true>(mb, rows, ks))
+                       : (dt == RK_DTYPE_BF16 ? pick<__nv_bfloat16>(mb, rows, ks)
+                                              : pick<__half>(mb, rows, ks));
+  LaunchCtl lc{};
+  if (peer != nullptr) {
+    const rk_status st = launch_ctl(&lc);
+    if (st != RK_OK) return st;
+  }
   // Grid: every resident CTA slot of the GPU, rows dealt out evenly; more CTAs only
   // when the per-CTA partial-sum buffer would exceed 32 KiB.
   const int rows_per_group = (GEMV_WARPS / ks) * rows;
@@ -395,9 +460,24 @@ rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M,
   const int rows_max = rows_base + (rows_rem ? 1 : 0);
   const size_t smem = static_cast<size_t>(ks) * rows_max * mb * sizeof(float);
   L.launch(x, W, out, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
-           static_cast<int>(grid), rows_base, rows_rem, rows_max, smem, s);
+           static_cast<int>(grid), rows_base, rows_rem, rows_max, smem, s, peer, &lc);
   note_launch();
   return cuda_status(cudaGetLastError());
+}
+
+}  // namespace
+
+rk_status gemv_stream_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,
+                             int64_t K, rk_dtype dt, cudaStream_t s) {
+  if (!gemv_stream_supported(x, W, out, M, N, K)) return RK_ERR_UNSUPPORTED;
+  return stream_run(x, W, out, M, N, K, dt, s, nullptr);
+}
+
+rk_status gemv_stream_allgather_launch(const void* x, const void* W, int64_t M, int64_t N_block,
+                                       int64_t K, rk_dtype dt, const PeerTargets& t,
+                                       cudaStream_t s) {
+  if (!gemv_stream_supported(x, W, nullptr, M, N_block, K)) return RK_ERR_UNSUPPORTED;
+  return stream_run(x, W, nullptr, M, N_block, K, dt, s, &t);
 }
 
 rk_status gemv_scalar_launch(const void* x, const void* W, void* out, int64_t M, int64_t N,

@@ -102,6 +102,8 @@ int device_cc_major() {
   return d ? d->cc_major : 0;
 }
 
+rk_status device_ready() { return current_device_info() != nullptr ? RK_OK : RK_ERR_NO_DEVICE; }
+
 rk_status launch_ctl(LaunchCtl* ctl) {
   DeviceInfo* d = current_device_info();
   if (d == nullptr) return RK_ERR_NO_DEVICE;

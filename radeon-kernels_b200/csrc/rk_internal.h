@@ -151,6 +151,25 @@ rk_status sdpa_launch(const void* q, const void* k, const void* v, void* out, in
 rk_status gather_column_blocks_launch(const void* blocks, void* out, int64_t G, int64_t M,
                                       int64_t N, rk_dtype dt, cudaStream_t s);
 
+// Host view of an rk_peer_group for one fused call: out[j] is rank j's full output
+// advanced to this rank's column block, ctl[j] rank j's control block.
+struct PeerTargets {
+  void* out[RK_PEER_MAX];
+  void* ctl[RK_PEER_MAX];
+  int64_t ldo;
+  int rank;
+  int world;
+  uint64_t timeout_ns;
+};
+// RK_OK when a usable device is current on this thread (binds its primary context).
+rk_status device_ready();
+// Fused compute + all-gather launchers (peer.cu validates; protocol in rk_peer.cuh).
+rk_status gemv_stream_allgather_launch(const void* x, const void* W, int64_t M, int64_t N_block,
+                                       int64_t K, rk_dtype dt, const PeerTargets& t,
+                                       cudaStream_t s);
+rk_status gemm_tc2_allgather_launch(const void* A, const void* B, int64_t M, int64_t N_block,
+                                    int64_t K, rk_dtype dt, const PeerTargets& t, cudaStream_t s);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace rk

@@ -1,0 +1,127 @@
+// rk_peer.cuh -- the exchange protocol of the fused compute + all-gather kernels
+// (rk_gemv_allgather, rk_gemm_allgather): every rank's kernel stores its column block of
+// the result straight into every rank's full output through peer pointers (CUDA IPC
+// mappings over NVLink / NVSwitch, plain st.global -- no TMA and no multicast touches
+// peer memory), and two flag rounds in each rank's control block order the calls:
+//
+//   ready[j]   written by rank j when its call e starts (after griddepcontrol.wait, so every
+//              earlier kernel of its stream -- the consumers of call e-1's output -- has
+//              completed): from then on the other ranks may overwrite rank j's output.
+//   arrive[j]  written by rank j once every store of its call e into this rank's output has
+//              been made visible (__threadfence_system by every storing thread, then a
+//              grid-wide count; the last CTA of the grid sends it).
+//   epoch      calls completed by this rank on this control block; written only by this
+//              rank, read at the start of the next call (which begins after it in stream
+//              order), so all ranks agree on the call number without host involvement and
+//              a captured CUDA graph replays correctly.
+//   done_ctas  CTAs of the running call that have finished storing; the last resets it.
+//
+// The last CTA of each rank waits until every rank's arrive[] reaches the call's epoch, so
+// when the kernel completes the local full output is complete.  Every wait is bounded (time
+// and iteration count); a wait that runs out sets RK_DEV_ERR_TIMEOUT_PEER in the status word
+// and the kernel finishes without the missing data (the group must then be rebuilt).
+#pragma once
+
+#include <cstdint>
+
+#include "rk_device.cuh"
+
+namespace rk {
+
+constexpr int kPeerMax = 8;
+constexpr uint32_t RK_DEV_ERR_TIMEOUT_PEER = 1u << 5;
+
+// One per rank, at the start of that rank's control allocation (RK_PEER_CTL_BYTES).
+struct __align__(256) PeerCtl {
+  uint32_t ready[kPeerMax];
+  uint32_t pad0[24];
+  uint32_t arrive[kPeerMax];
+  uint32_t pad1[24];
+  uint32_t epoch;
+  uint32_t done_ctas;
+  uint32_t pad2[62];
+};
+static_assert(sizeof(PeerCtl) == 512, "PeerCtl layout");
+
+// Kernel-side view of a group: out[j] is rank j's full output as mapped in this process,
+// already advanced to this rank's column block; ctl[j] rank j's control block.
+template <typename T>
+struct PeerOut {
+  T* out[kPeerMax];
+  PeerCtl* ctl[kPeerMax];
+  int64_t ldo;  // row stride of the full output (elements)
+  int rank;
+  int world;
+  uint64_t timeout_ns;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Epoch number of the call this kernel runs (1 for the first call on a control block).
+template <typename T>
+__device__ __forceinline__ uint32_t peer_call_epoch(const PeerOut<T>& p) {
+  return ld_relaxed_gpu(&p.ctl[p.rank]->epoch) + 1u;
+}
+
+// Tells every rank that this rank's call `e` has started (one thread).
+template <typename T>
+__device__ __forceinline__ void peer_announce(const PeerOut<T>& p, uint32_t e) {
+  for (int j = 0; j < p.world; ++j) st_release_sys(&p.ctl[j]->ready[p.rank], e);
+}
+
+// Bounded wait until flags[j] has reached `e` for every rank j < world (one thread).
+__device__ __forceinline__ bool peer_wait_all(const uint32_t* flags, int world, uint32_t e,
+                                              uint64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0; it < (1u << 30); ++it) {
+    bool all = true;
+    for (int j = 0; j < world; ++j)
+      all &= static_cast<int32_t>(ld_acquire_sys(&flags[j]) - e) >= 0;
+    if (all) return true;
+    if ((it & 15u) == 15u && globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+  return false;
+}
+
+// Bounded wait until every rank has started call `e` (one thread); afterwards this rank may
+// store into every rank's output.
+template <typename T>
+__device__ __forceinline__ bool peer_wait_ready(const PeerOut<T>& p, uint32_t e) {
+  const bool ok = peer_wait_all(p.ctl[p.rank]->ready, p.world, e, p.timeout_ns);
+  if (!ok) atomicOr(p.status, RK_DEV_ERR_TIMEOUT_PEER);
+  return ok;
+}
+
+// End of a CTA's part of call `e`: called by one thread after every thread of the CTA that
+// stored to a peer has executed __threadfence_system() and the CTA has synchronised.  The
+// last CTA of the grid publishes this rank's arrival to every rank, waits for every rank's,
+// and advances the epoch.
+template <typename T>
+__device__ __forceinline__ void peer_finish(const PeerOut<T>& p, uint32_t e, uint32_t grid_ctas) {
+  PeerCtl* mine = p.ctl[p.rank];
+  __threadfence_system();
+  const uint32_t before = atomicAdd(&mine->done_ctas, 1u);
+  if (before != grid_ctas - 1u) return;
+  __threadfence_system();  // acquire side of the count: every CTA's stores precede the flags
+  mine->done_ctas = 0u;    // the next call starts after this kernel completes
+  for (int j = 0; j < p.world; ++j) st_release_sys(&p.ctl[j]->arrive[p.rank], e);
+  if (!peer_wait_all(mine->arrive, p.world, e, p.timeout_ns)) atomicOr(p.status, RK_DEV_ERR_TIMEOUT_PEER);
+  *reinterpret_cast<volatile uint32_t*>(&mine->epoch) = e;
+}
+
+}  // namespace rk

@@ -17,6 +17,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/extension.h>
+#include <pybind11/stl.h>
 
 #include <map>
 #include <vector>
@@ -190,6 +191,7 @@ at::Tensor gather_column_blocks(const at::Tensor& blocks, at::Tensor out) {
   TORCH_CHECK(blocks.is_cuda() && blocks.dim() == 3 && blocks.is_contiguous(),
               "blocks must be a contiguous CUDA tensor [G, M, N/G]");
   check_matrix(out, "out");
+  TORCH_CHECK(blocks.device() == out.device(), "blocks and out must use the same device");
   TORCH_CHECK(out.scalar_type() == blocks.scalar_type(), "dtype mismatch");
   TORCH_CHECK(out.size(0) == blocks.size(1) && out.size(1) == blocks.size(0) * blocks.size(2),
               "out must be [M, G * N/G]");
@@ -198,6 +200,72 @@ at::Tensor gather_column_blocks(const at::Tensor& blocks, at::Tensor out) {
                                        out.size(0), out.size(1), dtype_of(out, "out"),
                                        current_stream(out)),
                "rk_gather_column_blocks");
+  return out;
+}
+
+// Fused compute + all-gather (rk_gemv_allgather / rk_gemm_allgather).  `out` is this rank's
+// full output (a view into its exchange buffer, entry `rank` of out_ptrs); out_ptrs and
+// ctl_ptrs list every rank's output and control block as mapped in this process.
+rk_peer_group peer_group(const at::Tensor& out, const std::vector<int64_t>& out_ptrs,
+                         const std::vector<int64_t>& ctl_ptrs, int64_t rank, int64_t timeout_ns) {
+  const int64_t world = static_cast<int64_t>(out_ptrs.size());
+  TORCH_CHECK(world >= 1 && world <= RK_PEER_MAX, "the group must have 1 to ", RK_PEER_MAX, " ranks");
+  TORCH_CHECK(static_cast<int64_t>(ctl_ptrs.size()) == world, "one control block per rank");
+  TORCH_CHECK(rank >= 0 && rank < world, "rank out of range");
+  TORCH_CHECK(out_ptrs[rank] == reinterpret_cast<int64_t>(out.data_ptr()),
+              "out must be this rank's entry of out_ptrs");
+  rk_peer_group g{};
+  g.rank = static_cast<int32_t>(rank);
+  g.world = static_cast<int32_t>(world);
+  for (int64_t j = 0; j < world; ++j) {
+    g.out[j] = reinterpret_cast<void*>(out_ptrs[j]);
+    g.ctl[j] = reinterpret_cast<void*>(ctl_ptrs[j]);
+  }
+  g.timeout_ns = static_cast<uint64_t>(timeout_ns);
+  return g;
+}
+
+at::Tensor gemv_allgather(const at::Tensor& x, const at::Tensor& weight_block, at::Tensor out,
+                          const std::vector<int64_t>& out_ptrs, const std::vector<int64_t>& ctl_ptrs,
+                          int64_t rank, int64_t timeout_ns) {
+  check_matrix(x, "input");
+  check_matrix(weight_block, "weight");
+  check_matrix(out, "out");
+  TORCH_CHECK(x.device() == weight_block.device() && out.device() == x.device(),
+              "input, weight and out must use the same device");
+  TORCH_CHECK(x.scalar_type() == weight_block.scalar_type() && out.scalar_type() == x.scalar_type(),
+              "input, weight and out must use the same dtype");
+  TORCH_CHECK(x.size(0) > 0 && x.size(0) <= 32, "input M must be in [1, 32]");
+  TORCH_CHECK(x.size(1) == weight_block.size(1), "input and weight must share K");
+  const rk_peer_group g = peer_group(out, out_ptrs, ctl_ptrs, rank, timeout_ns);
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == weight_block.size(0) * g.world,
+              "out must be [M, world * N_block]");
+  c10::cuda::CUDAGuard guard(x.device());
+  check_status(rk_gemv_allgather(x.data_ptr(), weight_block.data_ptr(), x.size(0),
+                                 weight_block.size(0), x.size(1), dtype_of(x, "input"), &g,
+                                 current_stream(x)),
+               "rk_gemv_allgather");
+  return out;
+}
+
+at::Tensor gemm_allgather(const at::Tensor& a, const at::Tensor& b_block, at::Tensor out,
+                          const std::vector<int64_t>& out_ptrs, const std::vector<int64_t>& ctl_ptrs,
+                          int64_t rank, int64_t timeout_ns) {
+  check_matrix(a, "a");
+  check_matrix(b_block, "b");
+  check_matrix(out, "out");
+  TORCH_CHECK(a.device() == b_block.device() && out.device() == a.device(),
+              "a, b and out must use the same device");
+  TORCH_CHECK(a.scalar_type() == b_block.scalar_type() && out.scalar_type() == a.scalar_type(),
+              "a, b and out must use the same dtype");
+  TORCH_CHECK(a.size(1) == b_block.size(0), "a and b must share K");
+  const rk_peer_group g = peer_group(out, out_ptrs, ctl_ptrs, rank, timeout_ns);
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == b_block.size(1) * g.world,
+              "out must be [M, world * N_block]");
+  c10::cuda::CUDAGuard guard(a.device());
+  check_status(rk_gemm_allgather(a.data_ptr(), b_block.data_ptr(), a.size(0), b_block.size(1),
+                                 a.size(1), dtype_of(a, "a"), &g, current_stream(a)),
+               "rk_gemm_allgather");
   return out;
 }
 
@@ -469,6 +537,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_stream", &gemv_stream, "128-bit weight-streaming GEMV (K % 8 == 0, 16B aligned)");
   m.def("gemv_scalar", &gemv_scalar, "generic GEMV (any K, any alignment)");
   m.def("gather_column_blocks", &gather_column_blocks, "[G,M,N/G] blocks -> row-major [M,N]");
+  m.def("gemv_allgather", &gemv_allgather,
+        "row-sharded x @ W.T with the output all-gather fused into the kernel (peer stores)",
+        py::arg("input"), py::arg("weight_block"), py::arg("out"), py::arg("out_ptrs"),
+        py::arg("ctl_ptrs"), py::arg("rank"), py::arg("timeout_ns") = 0);
+  m.def("gemm_allgather", &gemm_allgather,
+        "column-sharded A @ B with the output all-gather fused into the kernel (peer stores)",
+        py::arg("a"), py::arg("b_block"), py::arg("out"), py::arg("out_ptrs"),
+        py::arg("ctl_ptrs"), py::arg("rank"), py::arg("timeout_ns") = 0);
   m.def("paged_attention_decode", &paged_attention_decode, "decode attention over a paged K/V cache",
         py::arg("query"), py::arg("key_cache"), py::arg("value_cache"), py::arg("block_tables"),
         py::arg("context_lengths"), py::arg("scale"));
