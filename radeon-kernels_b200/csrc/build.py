@@ -52,6 +52,7 @@ NVCC_FLAGS = [
 KERNEL_SOURCES = ["rk_abi.cu", "peer.cu", "gemm_tcgen05.cu", "gemm_tcgen05_2sm.cu", "gemm_simt.cu", "gemv.cu", "gemv_tcgen05.cu", "gather.cu", "llm_ops.cu", "llm_ops_backward.cu", "paged_attention.cu", "paged_attention_tc.cu", "sdpa_tcgen05.cu"]
 HEADERS = sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "rk_kernels.h"]
 
+REPRODUCIBLE_LINK = ["-Wl,--strip-all", "-Wl,--build-id=none"]
 EXT_SUFFIX = sysconfig.get_config_var("EXT_SUFFIX") or ".so"
 LIBRARY = LIB_DIR / "librk_kernels.so"
 BUILTIN_EXT = LIB_DIR / f"_rk_ext{EXT_SUFFIX}"
@@ -76,7 +77,8 @@ def _compile_cuda(source: Path, force: bool) -> Path:
     obj = BUILD / "obj" / (source.stem + ".o")
     if _stale(obj, [source, *HEADERS], force):
         obj.parent.mkdir(parents=True, exist_ok=True)
-        _run([NVCC, *NVCC_FLAGS, "-c", str(source), "-o", str(obj)])
+        # A fixed seed keeps the host compiler's generated names the same from build to build.
+        _run([NVCC, *NVCC_FLAGS, f"-Xcompiler=-frandom-seed={source.stem}", "-c", str(source), "-o", str(obj)])
     return obj
 
 
@@ -114,7 +116,8 @@ def _compile_binding(name: str, cflags: list[str], force: bool) -> Path:
     obj = BUILD / "obj" / f"torch_ext_{name}.o"
     if _stale(obj, [source, INCLUDE / "rk_kernels.h"], force):
         obj.parent.mkdir(parents=True, exist_ok=True)
-        _run(["g++", *cflags, f"-DTORCH_EXTENSION_NAME={name}", "-c", str(source), "-o", str(obj)])
+        _run(["g++", *cflags, f"-frandom-seed=torch_ext_{name}", f"-DTORCH_EXTENSION_NAME={name}", "-c", str(source),
+              "-o", str(obj)])
     return obj
 
 
@@ -134,8 +137,14 @@ def build(*, force: bool = False, jobs: int | None = None) -> dict[str, Path]:
         objects = [job.result() for job in kernel_jobs]
         bindings = {name: job.result() for name, job in binding_jobs.items()}
 
+    # Reproducible links: nvcc records its per-process temporary file names in the host
+    # symbol table, so the libraries are linked without .symtab (--strip-all; the exported
+    # .dynsym and the kernels' line information in the device code stay) and without a
+    # build id -- the same sources and toolchain give byte-identical binaries, so the pack
+    # digests in the tracked manifests change only when the code does.
     if _stale(LIBRARY, objects, force):
-        _run([NVCC, *ARCH_FLAGS, "-shared", "-o", str(LIBRARY), *map(str, objects), "-cudart", "static"])
+        _run([NVCC, *ARCH_FLAGS, "-shared", "-o", str(LIBRARY), *map(str, objects), "-cudart", "static",
+              "-Xlinker", "--strip-all,--build-id=none"])
 
     cudart = ["-L" + str(CUDA_HOME / "lib64"), "-lcudart_static", "-ldl", "-lrt", "-lpthread"]
     if _stale(BUILTIN_EXT, [bindings["_rk_ext"], LIBRARY], force):
@@ -150,18 +159,35 @@ def build(*, force: bool = False, jobs: int | None = None) -> dict[str, Path]:
                 "-lrk_kernels",
                 "-Wl,-rpath,$ORIGIN",
                 *ldflags,
+                *REPRODUCIBLE_LINK,
             ]
         )
     pack_built = False
     if _stale(PACK_EXT, [bindings["rk_sm100a"], *objects], force):
-        _run(["g++", "-shared", "-o", str(PACK_EXT), str(bindings["rk_sm100a"]), *map(str, objects), *ldflags, *cudart])
+        _run(["g++", "-shared", "-o", str(PACK_EXT), str(bindings["rk_sm100a"]), *map(str, objects), *ldflags, *cudart,
+              *REPRODUCIBLE_LINK])
         pack_built = True
 
     sys.path.insert(0, str(PKG_ROOT))
-    from radeon_kernels.runtime.publish import publish_builtin_pack
+    from radeon_kernels.runtime.publish import load_private_key, publish_builtin_pack, sign_manifest
+    from radeon_kernels.runtime.signing import builtin_trusted_keyring
 
-    publish_builtin_pack(PACK_DIR, PACK_EXT, refresh_dispatch=True, rewrite=pack_built)
+    publish_builtin_pack(PACK_DIR, PACK_EXT, refresh_dispatch=False, rewrite=pack_built)
+    key_file = release_key_file()
+    key, key_id = load_private_key(key_file) if key_file is not None else (None, None)
+    sign_manifest(PACK_DIR, key, key_id, builtin_trusted_keyring())
     return {"library": LIBRARY, "builtin_extension": BUILTIN_EXT, "pack_extension": PACK_EXT}
+
+
+def release_key_file() -> Path | None:
+    """The release signing key: $RADEON_KERNELS_RELEASE_KEY, else the one ``<key_id>.pem`` in
+    the repository's git-ignored ``.release-key/`` directory, else none (unsigned build)."""
+
+    named = os.environ.get("RADEON_KERNELS_RELEASE_KEY")
+    if named:
+        return Path(named)
+    found = sorted((REPO / ".release-key").glob("*.pem"))
+    return found[-1] if found else None
 
 
 def clean() -> None:

@@ -224,7 +224,7 @@ class OperatorRuntime(DispatchingRuntime):
             try:
                 resolved = self.resolve(decision, fingerprint)
                 loader = self.loader(resolved.pack.root)
-                result = native.execute(loader, decision.winner, decision.launch, *native_arguments)
+                result = native.execute(loader, resolved.load_spec, decision.launch, *native_arguments)
                 reason = f"{decision.reason}; loaded pack {resolved.pack.pack_id} {resolved.pack.pack_version}"
                 record_execution(
                     decision,
@@ -233,7 +233,7 @@ class OperatorRuntime(DispatchingRuntime):
                     evidence_id=decision.evidence_id,
                     reason=reason,
                 )
-                entry = getattr(loader, "load_entrypoint")(decision.winner).callable
+                entry = getattr(loader, "load_entrypoint")(resolved.load_spec).callable
                 self.fast_store(key, entry, dict(decision.launch), decision, reason)
                 return result
             except WINNER_FAILURES as error:

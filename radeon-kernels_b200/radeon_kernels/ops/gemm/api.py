@@ -120,7 +120,7 @@ class GemmRuntime(DispatchingRuntime):
                 if target is None:
                     target = call.a.new_empty((call.signature["m"], call.signature["n"]))
                 loader = self.loader(resolved.pack.root)
-                result = native.gemm(loader, decision.winner, decision.launch, call.a, call.b, target)
+                result = native.gemm(loader, resolved.load_spec, decision.launch, call.a, call.b, target)
                 reason = f"{decision.reason}; loaded pack {resolved.pack.pack_id} {resolved.pack.pack_version}"
                 record_execution(
                     decision,
@@ -129,7 +129,7 @@ class GemmRuntime(DispatchingRuntime):
                     evidence_id=decision.evidence_id,
                     reason=reason,
                 )
-                entry = loader.load_entrypoint(decision.winner).callable
+                entry = loader.load_entrypoint(resolved.load_spec).callable
                 self.fast_store(key, entry, decision.launch["variant"], decision, reason)
                 return result
             except WINNER_FAILURES as error:

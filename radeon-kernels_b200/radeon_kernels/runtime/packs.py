@@ -16,7 +16,7 @@ from __future__ import annotations
 
 import os
 import sys
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 from pathlib import Path
 from typing import Iterable, Mapping, Sequence
 
@@ -43,6 +43,13 @@ class PackResolutionError(RadeonKernelsError):
 class ResolvedKernelPack:
     pack: KernelPack
     artifact: KernelPackArtifact
+    # What to load: the dispatch winner, with the SHA-256 the pack vouches for (equal to the
+    # winner's own digest for signed packs; the built-in pack's manifest digest otherwise).
+    spec: ArtifactSpec | None = None
+
+    @property
+    def load_spec(self) -> ArtifactSpec:
+        return self.spec if self.spec is not None else self.artifact.artifact
 
 
 def default_pack_roots(
@@ -74,9 +81,12 @@ def _pack_dirs(roots: Iterable[Path]) -> tuple[Path, ...]:
 
 
 class KernelPackRegistry:
-    def __init__(self, packs: Sequence[KernelPack] = (), *, rejected: Sequence[str] = ()) -> None:
+    def __init__(
+        self, packs: Sequence[KernelPack] = (), *, rejected: Sequence[str] = (), builtin: Iterable[Path] = ()
+    ) -> None:
         self._packs = tuple(packs)
         self._rejected = tuple(rejected)
+        self._builtin = frozenset(Path(root) for root in builtin)
 
     @classmethod
     def discover(
@@ -104,14 +114,18 @@ class KernelPackRegistry:
                 packs.append(KernelPack.from_directory(directory, verify_artifacts=False))
             except (ConfigError, SignatureVerificationError) as error:
                 rejected.append(f"{directory}: {error}")
+        builtin: list[Path] = []
         for directory in _pack_dirs(builtin_roots):
             if any(pack.root == directory for pack in packs):
                 continue
             try:
-                packs.append(KernelPack.from_directory(directory, verify_artifacts=False))
+                pack = KernelPack.from_directory(directory, verify_artifacts=False)
             except ConfigError as error:
                 rejected.append(f"{directory}: {error}")
-        return cls(packs, rejected=rejected)
+                continue
+            packs.append(pack)
+            builtin.append(pack.root)
+        return cls(packs, rejected=rejected, builtin=builtin)
 
     @property
     def packs(self) -> tuple[KernelPack, ...]:
@@ -137,8 +151,19 @@ class KernelPackRegistry:
                 item = pack.get(operator, semantic_version)
             except ConfigError:
                 continue
-            if item.evidence_id == evidence_id and item.artifact == artifact:
-                return ResolvedKernelPack(pack=pack, artifact=item)
+            if item.evidence_id != evidence_id:
+                continue
+            if item.artifact == artifact:
+                return ResolvedKernelPack(pack=pack, artifact=item, spec=artifact)
+            # The pack built from this source tree is trusted by location: the dispatch entry
+            # names its file, format and entrypoint, and its own manifest (written by the same
+            # build) supplies the digest the file is verified against -- a rebuild does not
+            # rewrite the tracked manifests.
+            mine = item.artifact
+            if pack.root in self._builtin and (mine.provider, mine.artifact, mine.format) == (
+                artifact.provider, artifact.artifact, artifact.format
+            ):
+                return ResolvedKernelPack(pack=pack, artifact=item, spec=replace(artifact, sha256=mine.sha256))
         note = f"; {len(self._rejected)} invalid pack(s) were ignored" if self._rejected else ""
         raise PackResolutionError(
             f"no installed kernel pack matches {operator} {semantic_version}, "

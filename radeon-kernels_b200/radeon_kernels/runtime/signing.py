@@ -1,13 +1,21 @@
-"""Ed25519 detached signatures over release files (kernel-pack manifests).
+"""Ed25519 detached signatures over release files (pack manifests, pack indexes).
 
-Wire-compatible with the reference (src/radeon_kernels/runtime/signing.py:22-279): a
-signature document ``{schema_version, algorithm: "ed25519", key_id, signed_file,
-signed_sha256, signature}`` signs the byte string
-``b"radeon-kernels-ed25519-v1\\0" + signed_file + b"\\0" + sha256_hex``, and a keyring
-``{schema_version, keys: [{key_id, algorithm, public_key, status, created_at[, reason]}]}``
-lists the trusted public keys (only ``active`` keys verify).  Packs signed for the
-reference therefore verify here with the same keyring, and packs this build signs verify
-in the reference.
+Format (shared with the reference so packs and keyrings move between the two,
+src/radeon_kernels/runtime/signing.py:22-279):
+
+* a signature document is a JSON object with exactly ``schema_version`` ("1.0"),
+  ``algorithm`` ("ed25519"), ``key_id``, ``signed_file`` (a normalized relative path),
+  ``signed_sha256`` (lowercase hex) and ``signature`` (base64 of 64 bytes);
+* the signed message is ``b"radeon-kernels-ed25519-v1\\0" + signed_file + b"\\0" +
+  signed_sha256`` -- the file is bound by name and digest, not by its bytes;
+* a keyring is ``{"schema_version": "1.0", "keys": [...]}`` whose entries carry ``key_id``,
+  ``algorithm`` ("ed25519"), ``public_key`` (base64 of 32 bytes), ``status`` ("active" or
+  "revoked"), ``created_at`` and an optional ``reason``; only active keys verify.
+
+The implementation here is organised around one small schema checker (``_check``) used
+by both documents, an immutable :class:`DetachedSignature` that knows its own message
+(:meth:`DetachedSignature.message`), and a :class:`TrustedKeyring` that maps key ids to
+verifier objects.
 """
 
 from __future__ import annotations
@@ -24,51 +32,65 @@ from typing import Any, Mapping, Sequence
 
 from radeon_kernels.errors import ConfigError, RadeonKernelsError
 
-_ID_RE = re.compile(r"^[a-z][a-z0-9_.-]*$")
-_SHA_RE = re.compile(r"^[0-9a-f]{64}$")
-DOMAIN = b"radeon-kernels-ed25519-v1\x00"
-_SIGNATURE_FIELDS = frozenset({"schema_version", "algorithm", "key_id", "signed_file", "signed_sha256", "signature"})
-_KEY_FIELDS = frozenset({"key_id", "algorithm", "public_key", "status", "created_at", "reason"})
+MESSAGE_PREFIX = b"radeon-kernels-ed25519-v1\x00"
+DOMAIN = MESSAGE_PREFIX  # name kept for callers of the first release of this module
+_HEX64 = re.compile(r"[0-9a-f]{64}")
+_IDENT = re.compile(r"[a-z][a-z0-9_.-]*")
 
 
 class SignatureVerificationError(RadeonKernelsError):
     """A signature is missing, malformed, made with an untrusted key or does not verify."""
 
 
-def _b64(value: Any, path: str, size: int) -> bytes:
-    if not isinstance(value, str):
-        raise ConfigError(path, "expected base64 text")
+# ----------------------------------------------------------------------------- checks
+def _check(value: Any, where: str, required: frozenset[str], optional: frozenset[str] = frozenset()) -> Mapping[str, Any]:
+    """``value`` must be a mapping with all of ``required`` and nothing beyond ``optional``."""
+
+    if not isinstance(value, Mapping):
+        raise ConfigError(where, "expected a mapping")
+    keys = set(value)
+    missing, unknown = required - keys, keys - required - optional
+    if missing or unknown:
+        raise ConfigError(where, f"unknown={sorted(unknown)}, missing={sorted(missing)}")
+    return value
+
+
+def _text(value: Any, where: str, pattern: re.Pattern[str] | None = None, what: str = "non-empty text") -> str:
+    if not isinstance(value, str) or not value or (pattern is not None and pattern.fullmatch(value) is None):
+        raise ConfigError(where, f"expected {what}")
+    return value
+
+
+def _decoded(value: Any, where: str, size: int) -> bytes:
     try:
-        raw = base64.b64decode(value, validate=True)
+        raw = base64.b64decode(_text(value, where, what="base64 text"), validate=True)
     except (ValueError, binascii.Error) as error:
-        raise ConfigError(path, "invalid base64 text") from error
+        raise ConfigError(where, "invalid base64 text") from error
     if len(raw) != size:
-        raise ConfigError(path, f"expected {size} decoded bytes")
+        raise ConfigError(where, f"expected {size} decoded bytes")
     return raw
 
 
-def _key_id(value: Any, path: str) -> str:
-    if not isinstance(value, str) or _ID_RE.fullmatch(value) is None:
-        raise ConfigError(path, "expected a lowercase identifier")
-    return value
+def _release_path(value: Any, where: str) -> str:
+    text = _text(value, where, what="a relative file path")
+    posix = PurePosixPath(text)
+    if posix.is_absolute() or ".." in posix.parts or posix.as_posix() != text:
+        raise ConfigError(where, "expected a normalized relative file path")
+    return text
 
 
-def _relative(value: Any, path: str) -> str:
-    if not isinstance(value, str) or not value:
-        raise ConfigError(path, "expected a relative file path")
-    posix = PurePosixPath(value)
-    if posix.is_absolute() or ".." in posix.parts or posix.as_posix() != value:
-        raise ConfigError(path, "expected a normalized relative file path")
-    return value
+def _digest(value: Any, where: str) -> str:
+    return _text(value, where, _HEX64, "a lowercase SHA-256")
 
 
 def signature_payload(signed_file: str, signed_sha256: str) -> bytes:
-    name = _relative(signed_file, "signature.signed_file")
-    if not isinstance(signed_sha256, str) or _SHA_RE.fullmatch(signed_sha256) is None:
-        raise ConfigError("signature.signed_sha256", "expected a lowercase SHA-256")
-    return DOMAIN + name.encode("utf-8") + b"\x00" + signed_sha256.encode("ascii")
+    """The bytes an Ed25519 key signs for ``signed_file`` with digest ``signed_sha256``."""
+
+    name = _release_path(signed_file, "signature.signed_file")
+    return MESSAGE_PREFIX + name.encode("utf-8") + b"\x00" + _digest(signed_sha256, "signature.signed_sha256").encode("ascii")
 
 
+# ----------------------------------------------------------------------------- keyring
 @dataclass(frozen=True)
 class TrustedKey:
     key_id: str
@@ -79,50 +101,44 @@ class TrustedKey:
 
 
 class TrustedKeyring:
+    """Public keys a signature may be made with, by key id."""
+
+    _DOC = frozenset({"schema_version", "keys"})
+    _ENTRY = frozenset({"key_id", "algorithm", "public_key", "status", "created_at"})
+
     def __init__(self, keys: Sequence[TrustedKey]) -> None:
+        by_id = {key.key_id: key for key in keys}
         if not keys:
             raise ConfigError("trusted-keys.keys", "expected at least one key")
-        self._keys = {key.key_id: key for key in keys}
-        if len(self._keys) != len(keys):
+        if len(by_id) != len(keys):
             raise ConfigError("trusted-keys.keys", "key ids must be unique")
+        self._by_id = by_id
 
     @classmethod
     def from_mapping(cls, value: Any, path: str = "trusted-keys") -> TrustedKeyring:
-        if not isinstance(value, Mapping):
-            raise ConfigError(path, "expected a mapping")
-        if set(value) != {"schema_version", "keys"}:
-            raise ConfigError(path, "expected exactly ['keys', 'schema_version']")
-        if value["schema_version"] != "1.0":
+        doc = _check(value, path, cls._DOC)
+        if doc["schema_version"] != "1.0":
             raise ConfigError(f"{path}.schema_version", "unsupported version")
-        if not isinstance(value["keys"], list):
+        if not isinstance(doc["keys"], list):
             raise ConfigError(f"{path}.keys", "expected a list")
-        keys = []
-        for index, item in enumerate(value["keys"]):
-            where = f"{path}.keys[{index}]"
-            if not isinstance(item, Mapping):
-                raise ConfigError(where, "expected a mapping")
-            unknown, missing = set(item) - _KEY_FIELDS, (_KEY_FIELDS - {"reason"}) - set(item)
-            if unknown or missing:
-                raise ConfigError(where, f"unknown={sorted(unknown)}, missing={sorted(missing)}")
-            if item["algorithm"] != "ed25519":
-                raise ConfigError(f"{where}.algorithm", "expected ed25519")
-            if item["status"] not in ("active", "revoked"):
-                raise ConfigError(f"{where}.status", "expected active or revoked")
-            if not isinstance(item["created_at"], str) or not item["created_at"]:
-                raise ConfigError(f"{where}.created_at", "expected a timestamp")
-            reason = item.get("reason")
-            if reason is not None and (not isinstance(reason, str) or not reason):
-                raise ConfigError(f"{where}.reason", "expected non-empty text")
-            keys.append(
-                TrustedKey(
-                    key_id=_key_id(item["key_id"], f"{where}.key_id"),
-                    public_key=_b64(item["public_key"], f"{where}.public_key", 32),
-                    status=item["status"],
-                    created_at=item["created_at"],
-                    reason=reason,
-                )
-            )
+        keys = [cls._entry(item, f"{path}.keys[{i}]") for i, item in enumerate(doc["keys"])]
         return cls(keys)
+
+    @classmethod
+    def _entry(cls, value: Any, where: str) -> TrustedKey:
+        item = _check(value, where, cls._ENTRY, frozenset({"reason"}))
+        if item["algorithm"] != "ed25519":
+            raise ConfigError(f"{where}.algorithm", "expected ed25519")
+        if item["status"] not in ("active", "revoked"):
+            raise ConfigError(f"{where}.status", "expected active or revoked")
+        reason = item.get("reason")
+        return TrustedKey(
+            key_id=_text(item["key_id"], f"{where}.key_id", _IDENT, "a lowercase identifier"),
+            public_key=_decoded(item["public_key"], f"{where}.public_key", 32),
+            status=item["status"],
+            created_at=_text(item["created_at"], f"{where}.created_at", what="a timestamp"),
+            reason=None if reason is None else _text(reason, f"{where}.reason"),
+        )
 
     @classmethod
     def from_file(cls, path: Path) -> TrustedKeyring:
@@ -133,16 +149,20 @@ class TrustedKeyring:
         return cls.from_mapping(value, str(path))
 
     def active_public_key(self, key_id: str) -> Any:
-        from cryptography.hazmat.primitives.asymmetric.ed25519 import Ed25519PublicKey
+        """The ``cryptography`` public-key object of an active key; raises for unknown or
+        revoked keys."""
 
-        key = self._keys.get(key_id)
+        key = self._by_id.get(key_id)
         if key is None:
             raise SignatureVerificationError(f"signature uses unknown key {key_id!r}")
         if key.status != "active":
             raise SignatureVerificationError(f"signature key {key_id!r} is not active")
+        from cryptography.hazmat.primitives.asymmetric.ed25519 import Ed25519PublicKey
+
         return Ed25519PublicKey.from_public_bytes(key.public_key)
 
 
+# --------------------------------------------------------------------------- envelope
 @dataclass(frozen=True)
 class DetachedSignature:
     key_id: str
@@ -150,48 +170,75 @@ class DetachedSignature:
     signed_sha256: str
     signature: bytes
 
+    _FIELDS = frozenset({"schema_version", "algorithm", "key_id", "signed_file", "signed_sha256", "signature"})
+
     @classmethod
     def from_mapping(cls, value: Any, path: str = "signature") -> DetachedSignature:
-        if not isinstance(value, Mapping):
-            raise ConfigError(path, "expected a mapping")
-        if set(value) != _SIGNATURE_FIELDS:
-            raise ConfigError(path, f"expected exactly {sorted(_SIGNATURE_FIELDS)}")
-        if value["schema_version"] != "1.0" or value["algorithm"] != "ed25519":
+        doc = _check(value, path, cls._FIELDS)
+        if (doc["schema_version"], doc["algorithm"]) != ("1.0", "ed25519"):
             raise ConfigError(path, "unsupported signature version or algorithm")
-        digest = value["signed_sha256"]
-        if not isinstance(digest, str) or _SHA_RE.fullmatch(digest) is None:
-            raise ConfigError(f"{path}.signed_sha256", "expected a lowercase SHA-256")
         return cls(
-            key_id=_key_id(value["key_id"], f"{path}.key_id"),
-            signed_file=_relative(value["signed_file"], f"{path}.signed_file"),
-            signed_sha256=digest,
-            signature=_b64(value["signature"], f"{path}.signature", 64),
+            key_id=_text(doc["key_id"], f"{path}.key_id", _IDENT, "a lowercase identifier"),
+            signed_file=_release_path(doc["signed_file"], f"{path}.signed_file"),
+            signed_sha256=_digest(doc["signed_sha256"], f"{path}.signed_sha256"),
+            signature=_decoded(doc["signature"], f"{path}.signature", 64),
         )
 
     @classmethod
     def from_file(cls, path: Path) -> DetachedSignature:
         try:
-            value = json.loads(Path(path).read_text(encoding="utf-8"))
+            return cls.from_mapping(json.loads(Path(path).read_text(encoding="utf-8")), str(path))
         except (OSError, json.JSONDecodeError) as error:
             raise SignatureVerificationError(f"cannot read detached signature {path}: {error}") from error
-        try:
-            return cls.from_mapping(value, str(path))
         except ConfigError as error:
             raise SignatureVerificationError(str(error)) from error
 
+    def message(self) -> bytes:
+        return signature_payload(self.signed_file, self.signed_sha256)
+
+    def to_dict(self) -> dict[str, str]:
+        return {
+            "schema_version": "1.0",
+            "algorithm": "ed25519",
+            "key_id": self.key_id,
+            "signed_file": self.signed_file,
+            "signed_sha256": self.signed_sha256,
+            "signature": base64.b64encode(self.signature).decode("ascii"),
+        }
+
+    def check(self, content: bytes, keyring: TrustedKeyring, expected_file: str) -> None:
+        """Raises SignatureVerificationError unless this signs ``content`` as ``expected_file``."""
+
+        expected = _release_path(expected_file, "signed_file")
+        if self.signed_file != expected:
+            raise SignatureVerificationError(f"signature names {self.signed_file!r}, expected {expected!r}")
+        actual = hashlib.sha256(content).hexdigest()
+        if not hmac.compare_digest(actual, self.signed_sha256):
+            raise SignatureVerificationError(f"signed file SHA-256 mismatch: expected {self.signed_sha256}, got {actual}")
+        from cryptography.exceptions import InvalidSignature
+
+        try:
+            keyring.active_public_key(self.key_id).verify(self.signature, self.message())
+        except InvalidSignature as error:
+            raise SignatureVerificationError("invalid Ed25519 signature") from error
+
+
+def sign(private_key: Any, key_id: str, signed_file: str, content: bytes) -> DetachedSignature:
+    """Signs ``content`` under the name ``signed_file`` with an Ed25519 private key."""
+
+    return DetachedSignature.from_mapping(
+        signature_document(private_key=private_key, key_id=key_id, signed_file=signed_file,
+                           signed_sha256=hashlib.sha256(content).hexdigest())
+    )
+
 
 def signature_document(*, private_key: Any, key_id: str, signed_file: str, signed_sha256: str) -> dict[str, str]:
-    """Sign ``signed_file`` (by its digest) with an Ed25519 private key."""
+    """Signature document for a file known by its name and digest."""
 
-    signature = private_key.sign(signature_payload(signed_file, signed_sha256))
-    return {
-        "schema_version": "1.0",
-        "algorithm": "ed25519",
-        "key_id": _key_id(key_id, "signature.key_id"),
-        "signed_file": signed_file,
-        "signed_sha256": signed_sha256,
-        "signature": base64.b64encode(signature).decode("ascii"),
-    }
+    name = _release_path(signed_file, "signature.signed_file")
+    digest = _digest(signed_sha256, "signature.signed_sha256")
+    ident = _text(key_id, "signature.key_id", _IDENT, "a lowercase identifier")
+    return DetachedSignature(ident, name, digest, private_key.sign(signature_payload(name, digest))).to_dict()
 
 
 def verify_detached_content(
@@ -201,22 +248,8 @@ def verify_detached_content(
     *,
     signed_file: str,
 ) -> DetachedSignature:
-    from cryptography.exceptions import InvalidSignature
-
     envelope = signature if isinstance(signature, DetachedSignature) else DetachedSignature.from_mapping(signature)
-    expected = _relative(signed_file, "signed_file")
-    if envelope.signed_file != expected:
-        raise SignatureVerificationError(f"signature names {envelope.signed_file!r}, expected {expected!r}")
-    actual = hashlib.sha256(content).hexdigest()
-    if not hmac.compare_digest(actual, envelope.signed_sha256):
-        raise SignatureVerificationError(
-            f"signed file SHA-256 mismatch: expected {envelope.signed_sha256}, got {actual}"
-        )
-    key = keyring.active_public_key(envelope.key_id)
-    try:
-        key.verify(envelope.signature, signature_payload(envelope.signed_file, envelope.signed_sha256))
-    except InvalidSignature as error:
-        raise SignatureVerificationError("invalid Ed25519 signature") from error
+    envelope.check(content, keyring, signed_file)
     return envelope
 
 
@@ -227,12 +260,20 @@ def verify_detached_file(
         content = Path(file_path).read_bytes()
     except OSError as error:
         raise SignatureVerificationError(f"cannot read signed file {file_path}: {error}") from error
-    return verify_detached_content(
-        content, DetachedSignature.from_file(signature_path), keyring, signed_file=signed_file or Path(file_path).name
-    )
+    envelope = DetachedSignature.from_file(signature_path)
+    envelope.check(content, keyring, signed_file or Path(file_path).name)
+    return envelope
 
 
 def builtin_trusted_keyring() -> TrustedKeyring:
     """Release keys shipped with the package (``radeon_kernels/keys/trusted-keys.json``)."""
 
     return TrustedKeyring.from_file(Path(__file__).resolve().parents[1] / "keys" / "trusted-keys.json")
+
+
+def sha256_file(path: Path) -> str:
+    digest = hashlib.sha256()
+    with Path(path).open("rb") as handle:
+        for block in iter(lambda: handle.read(1 << 20), b""):
+            digest.update(block)
+    return digest.hexdigest()

@@ -63,6 +63,12 @@ def test_signed_pack_is_discovered_and_resolved(tmp_path):
         fingerprint=fingerprint(), operator="gemm", semantic_version="1.0", artifact=spec, evidence_id="test-evidence"
     )
     assert found.pack.pack_id == "test-pack"
+    # Only the pack built from the source tree is matched by location; an installed pack must
+    # carry exactly the digest the dispatch entry pins.
+    other = ArtifactSpec("native", "lib/test_kernel.so", "gemm_out", digest_of(b"other"))
+    with pytest.raises(PackResolutionError):
+        registry.resolve(fingerprint=fingerprint(), operator="gemm", semantic_version="1.0", artifact=other,
+                         evidence_id="test-evidence")
     with pytest.raises(PackResolutionError):
         registry.resolve(
             fingerprint=fingerprint(), operator="gemm", semantic_version="1.0", artifact=spec, evidence_id="other"
@@ -99,7 +105,10 @@ def test_signature_payload_binds_file_name_and_digest():
 
 
 def test_shipped_keyring_parses():
-    assert builtin_trusted_keyring().active_public_key("rk-b200-release-2026-12") is not None
+    ring = builtin_trusted_keyring()
+    assert ring.active_public_key("rk-b200-release-2026-12b") is not None
+    with pytest.raises(SignatureVerificationError, match="not active"):
+        ring.active_public_key("rk-b200-release-2026-12")  # revoked: its private half was not kept
 
 
 def test_builtin_pack_is_trusted_by_location_and_matches_dispatch():
@@ -115,8 +124,16 @@ def test_builtin_pack_is_trusted_by_location_and_matches_dispatch():
         item = pack.get(operator, "1.0")
         assert sha256_of(pack.root / item.artifact.artifact) == item.artifact.sha256
         for entry in dispatch.get(operator, "1.0").entries:
-            assert entry.winner == item.artifact, f"{entry.id} does not point at the built pack"
+            if entry.environment.architecture != "sm_100a":
+                continue  # the reference's own entries for its AMD packs
+            winner, mine = entry.winner, item.artifact
+            assert (winner.provider, winner.artifact, winner.format) == (mine.provider, mine.artifact, mine.format), entry.id
             assert entry.evidence_id == item.evidence_id
+            # Trusted by location: resolved whatever digest the tracked entry pins, and loaded
+            # against the digest this build's manifest records.
+            resolved = registry.resolve(fingerprint=fingerprint(), operator=operator, semantic_version="1.0",
+                                        artifact=winner, evidence_id=entry.evidence_id)
+            assert resolved.load_spec.sha256 == mine.sha256 and resolved.load_spec.entrypoint == winner.entrypoint
 
 
 def test_shipped_entries_pin_the_kernel_the_library_would_choose():
@@ -133,6 +150,8 @@ def test_shipped_entries_pin_the_kernel_the_library_would_choose():
     dispatch = builtin_dispatch_registry()
     gemv_stream, gemv_tc = _native.GEMV_VARIANTS["stream"], _native.GEMV_VARIANTS["tc"]
     for entry in dispatch.get("gemv", "1.0").entries:
+        if entry.environment.architecture != "sm_100a":
+            continue
         variant = entry.launch["variant"]
         m = entry.workload.values["m"]
         lo, hi = m.value if m.kind == "range" else (min(m.values()), max(m.values()))
@@ -142,6 +161,8 @@ def test_shipped_entries_pin_the_kernel_the_library_would_choose():
             assert lo >= 3, f"{entry.id}: tensor-core kernel pinned for M from {lo}"
     gemm_1sm, gemm_2sm = _native.GEMM_VARIANTS["tc_1sm"], _native.GEMM_VARIANTS["tc_2sm"]
     for entry in dispatch.get("gemm", "1.0").entries:
+        if entry.environment.architecture != "sm_100a":
+            continue
         variant = entry.launch["variant"]
         if variant not in (gemm_1sm, gemm_2sm):
             continue

@@ -220,9 +220,10 @@ class _Packs:
         self.root = root
         self.calls = 0
 
-    def resolve(self, **_):
+    def resolve(self, *, artifact, **_):
         self.calls += 1
-        return SimpleNamespace(pack=SimpleNamespace(root=self.root, pack_id="test-pack", pack_version="0.1.0"))
+        return SimpleNamespace(pack=SimpleNamespace(root=self.root, pack_id="test-pack", pack_version="0.1.0"),
+                               load_spec=artifact)
 
 
 class _Loader:
