@@ -1,10 +1,11 @@
-"""Exact-match static dispatch: (operator, version, signature, fingerprint) -> decision.
+"""Static dispatch: (operator, version, signature, fingerprint) -> decision.
 
-Behaviour of the reference's ``Dispatcher.select`` (src/radeon_kernels/runtime/dispatcher.py:57-100):
-every entry whose environment and workload match is a candidate, the highest priority wins
-(the manifest validator guarantees it is unique), and a miss yields the manifest's
-``default_fallbacks``.  The decision is recorded for ``explain_last_dispatch`` before any
-kernel runs.  Selection is a linear scan: manifests hold a handful of entries.
+Semantics of the reference's ``Dispatcher.select`` (src/radeon_kernels/runtime/dispatcher.py:
+57-100): an entry is a candidate when its environment and workload both match; the
+highest-priority candidate wins (the manifest validator makes it unique); with no candidate
+the manifest's ``default_fallbacks`` apply.  The decision -- as the dictionary that
+``explain_last_dispatch`` renders -- is recorded before any kernel runs.  Manifests hold a
+handful of entries, so selection is one pass over them.
 """
 
 from __future__ import annotations
@@ -14,7 +15,9 @@ from typing import Any, Mapping
 
 from radeon_kernels.runtime.explain import record_dispatch
 from radeon_kernels.runtime.fingerprint import EnvironmentFingerprint
-from radeon_kernels.runtime.registry import ArtifactSpec, DispatchRegistry
+from radeon_kernels.runtime.registry import ArtifactSpec, DispatchEntry, DispatchRegistry
+
+NO_MATCH_REASON = "no compatible environment and workload region matched"
 
 
 @dataclass(frozen=True)
@@ -40,18 +43,27 @@ class DispatchDecision:
     def matched(self) -> bool:
         return self.winner is not None
 
+    @classmethod
+    def for_entry(cls, request: DispatchRequest, fingerprint: EnvironmentFingerprint, entry: DispatchEntry) -> DispatchDecision:
+        return cls(request.operator, request.semantic_version, fingerprint, entry.id, entry.winner, entry.launch,
+                   entry.fallbacks, entry.evidence_id, f"matched dispatch entry {entry.id!r} at priority {entry.priority}")
+
+    @classmethod
+    def unmatched(cls, request: DispatchRequest, fingerprint: EnvironmentFingerprint, fallbacks: tuple[str, ...]) -> DispatchDecision:
+        return cls(request.operator, request.semantic_version, fingerprint, None, None, {}, fallbacks, None, NO_MATCH_REASON)
+
     def to_dict(self) -> dict[str, Any]:
-        winner = self.winner
+        """The record ``get_last_dispatch()`` returns (keys callers parse)."""
+
+        env = self.fingerprint
+        chosen = self.winner
         return {
             "operator": self.operator,
             "semantic_version": self.semantic_version,
-            "architecture": self.fingerprint.architecture,
-            "rocm_abi": self.fingerprint.rocm_abi,
-            "python_abi": self.fingerprint.python_abi,
-            "pytorch_version": self.fingerprint.pytorch_version,
+            **{key: getattr(env, key) for key in ("architecture", "rocm_abi", "python_abi", "pytorch_version")},
             "entry_id": self.entry_id,
-            "selected": f"{winner.provider}/{winner.entrypoint}" if winner else None,
-            "artifact": winner.artifact if winner else None,
+            "selected": None if chosen is None else f"{chosen.provider}/{chosen.entrypoint}",
+            "artifact": None if chosen is None else chosen.artifact,
             "launch": dict(self.launch),
             "fallbacks": list(self.fallbacks),
             "evidence_id": self.evidence_id,
@@ -61,37 +73,14 @@ class DispatchDecision:
 
 class Dispatcher:
     def __init__(self, registry: DispatchRegistry) -> None:
-        self._registry = registry
+        self.registry = registry
 
     def select(self, request: DispatchRequest, fingerprint: EnvironmentFingerprint) -> DispatchDecision:
-        manifest = self._registry.get(request.operator, request.semantic_version)
-        best = None
-        for entry in manifest.entries:
-            if entry.matches(fingerprint, request.signature) and (best is None or entry.priority > best.priority):
-                best = entry
-        if best is not None:
-            decision = DispatchDecision(
-                operator=request.operator,
-                semantic_version=request.semantic_version,
-                fingerprint=fingerprint,
-                entry_id=best.id,
-                winner=best.winner,
-                launch=best.launch,
-                fallbacks=best.fallbacks,
-                evidence_id=best.evidence_id,
-                reason=f"matched dispatch entry {best.id!r} at priority {best.priority}",
-            )
+        manifest = self.registry.get(request.operator, request.semantic_version)
+        candidates = [entry for entry in manifest.entries if entry.matches(fingerprint, request.signature)]
+        if candidates:
+            decision = DispatchDecision.for_entry(request, fingerprint, max(candidates, key=lambda entry: entry.priority))
         else:
-            decision = DispatchDecision(
-                operator=request.operator,
-                semantic_version=request.semantic_version,
-                fingerprint=fingerprint,
-                entry_id=None,
-                winner=None,
-                launch={},
-                fallbacks=manifest.default_fallbacks,
-                evidence_id=None,
-                reason="no compatible environment and workload region matched",
-            )
+            decision = DispatchDecision.unmatched(request, fingerprint, manifest.default_fallbacks)
         record_dispatch(decision.to_dict())
         return decision

@@ -76,65 +76,102 @@ def _is_int(value: Any) -> bool:
 
 
 @dataclass(frozen=True)
+class _Span:
+    """Closed interval of positive integers."""
+
+    low: int
+    high: int
+
+
+def _tagged(items: Iterable[Any]) -> frozenset[tuple[type, Any]]:
+    # Values are compared type-exactly: True is not 1, 1 is not 1.0.
+    return frozenset((type(item), item) for item in items)
+
+
+def _domain(constraint: ValueConstraint) -> _Span | frozenset[tuple[type, Any]]:
+    if constraint.kind == "range":
+        return _Span(*constraint.value)
+    return _tagged(constraint.values())
+
+
+def _ints_of(members: frozenset[tuple[type, Any]]) -> list[int]:
+    return [value for kind, value in members if kind is int]
+
+
+def _intersects(a: _Span | frozenset, b: _Span | frozenset) -> bool:
+    if isinstance(a, _Span) and isinstance(b, _Span):
+        return max(a.low, b.low) <= min(a.high, b.high)
+    if isinstance(a, _Span) or isinstance(b, _Span):
+        span, members = (a, b) if isinstance(a, _Span) else (b, a)
+        return any(span.low <= value <= span.high for value in _ints_of(members))
+    return bool(a & b)
+
+
+def _within(a: _Span | frozenset, b: _Span | frozenset) -> bool:
+    """Every value admitted by ``a`` is admitted by ``b`` (a span inside a finite set only as a
+    single point: the manifest language never enumerates a whole span)."""
+
+    if isinstance(a, frozenset):
+        if isinstance(b, frozenset):
+            return a <= b
+        return all(kind is int and b.low <= value <= b.high for kind, value in a)
+    if isinstance(b, _Span):
+        return b.low <= a.low and a.high <= b.high
+    return a.low == a.high and (int, a.low) in b
+
+
+@dataclass(frozen=True)
 class ValueConstraint:
-    """One workload field: ``eq`` (scalar), ``range`` ((lo, hi) ints) or ``one_of`` (tuple)."""
+    """Admissible values of one workload field.
+
+    Manifest forms (schema 1.0): a bare scalar (``kind == "eq"``), ``[low, high]`` -- an
+    inclusive range of positive integers (``"range"``) -- or ``{"one_of": [...]}`` (``"one_of"``).
+    Matching, overlap and containment are computed on a common domain: a span of integers or
+    a finite set of type-tagged scalars.
+    """
 
     kind: str
     value: Any
 
     @classmethod
     def from_raw(cls, raw: Any, path: str) -> ValueConstraint:
-        if isinstance(raw, list):
-            if len(raw) != 2 or not all(_is_int(item) for item in raw) or raw[0] <= 0 or raw[1] < raw[0]:
-                raise ConfigError(path, "integer ranges must be [minimum, maximum]")
-            return cls("range", (raw[0], raw[1]))
         if isinstance(raw, Mapping):
             _check_fields(_require_mapping(raw, path), path, allowed={"one_of"}, required={"one_of"})
-            options = raw["one_of"]
-            if not isinstance(options, list) or not options:
+            listed = raw["one_of"]
+            if not isinstance(listed, list) or not listed:
                 raise ConfigError(f"{path}.one_of", "expected a non-empty list")
-            choices = tuple(_scalar(item, f"{path}.one_of") for item in options)
-            if len({(type(item), item) for item in choices}) != len(choices):
+            members = tuple(_scalar(item, f"{path}.one_of") for item in listed)
+            if len(_tagged(members)) != len(members):
                 raise ConfigError(f"{path}.one_of", "contains duplicate values")
-            return cls("one_of", choices)
+            return cls("one_of", members)
+        if isinstance(raw, list):
+            ends = raw if len(raw) == 2 and all(_is_int(end) for end in raw) else None
+            if ends is None or not 0 < ends[0] <= ends[1]:
+                raise ConfigError(path, "integer ranges must be [minimum, maximum]")
+            return cls("range", (ends[0], ends[1]))
         return cls("eq", _scalar(raw, path))
 
     def values(self) -> tuple[Any, ...]:
-        """Representative values: every value for eq/one_of, the endpoints for a range."""
+        """Representative values: all of them for eq/one_of, the ends of a range."""
 
-        if self.kind == "eq":
-            return (self.value,)
-        if self.kind == "one_of":
-            return self.value
-        low, high = self.value
-        return (low,) if low == high else (low, high)
+        if self.kind == "range":
+            return tuple(sorted(set(self.value)))
+        return self.value if self.kind == "one_of" else (self.value,)
 
     def matches(self, candidate: Any) -> bool:
-        if self.kind == "range":
-            return _is_int(candidate) and self.value[0] <= candidate <= self.value[1]
-        return any(_same(candidate, option) for option in self.values())
+        domain = _domain(self)
+        if isinstance(domain, _Span):
+            return _is_int(candidate) and domain.low <= candidate <= domain.high
+        return (type(candidate), candidate) in domain
 
     def overlaps(self, other: ValueConstraint) -> bool:
-        if self.kind == "range" and other.kind == "range":
-            return max(self.value[0], other.value[0]) <= min(self.value[1], other.value[1])
-        if self.kind == "range":
-            return any(self.matches(item) for item in other.values())
-        return any(other.matches(item) for item in self.values())
+        return _intersects(_domain(self), _domain(other))
 
     def is_subset_of(self, other: ValueConstraint) -> bool:
-        if self.kind != "range":
-            return all(other.matches(item) for item in self.values())
-        low, high = self.value
-        if other.kind == "range":
-            return other.value[0] <= low and high <= other.value[1]
-        return low == high and other.matches(low)
+        return _within(_domain(self), _domain(other))
 
     def to_raw(self) -> Any:
-        if self.kind == "range":
-            return [self.value[0], self.value[1]]
-        if self.kind == "one_of":
-            return {"one_of": list(self.value)}
-        return self.value
+        return {"range": list, "one_of": lambda v: {"one_of": list(v)}}.get(self.kind, lambda v: v)(self.value)
 
 
 @dataclass(frozen=True)

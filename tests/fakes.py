@@ -60,6 +60,8 @@ class FakeTorch:
     Tensor = FakeTensor
     float16 = "float16"
     bfloat16 = "bfloat16"
+    int32 = "int32"
+    int64 = "int64"
 
     def __init__(self):
         self.cuda = SimpleNamespace(current_device=lambda: 0)
