@@ -166,9 +166,12 @@ RK_API rk_status rk_gemv_workspace_size(int64_t M, int64_t N, int64_t K, rk_dtyp
  * that device current; make that first call before any stream capture.  All calls
  * on a device share the one array and each call re-zeroes the part that must start
  * at zero, so calls that may overlap on the GPU (different streams without ordering)
- * race and must not be issued.  Problems needing more scratch than the capacity are
- * rejected with RK_ERR_TOO_LARGE; shapes the tensor-core GEMV cannot run (K % 8 != 0,
- * unaligned pointers, non-sm_100 device) with RK_ERR_UNSUPPORTED.
+ * race and must not be issued.  The array holds one split-K ticket per 128-row tile of
+ * the weight (RK_GEMV_WORKSPACE_TICKET_BYTES of them: N <= 2,097,152) and the fp32
+ * partial tiles of as many stream-K CTAs as fit in the rest (up to the full grid of two
+ * per SM); taller weights are rejected with RK_ERR_TOO_LARGE, shapes the tensor-core
+ * GEMV cannot run (K % 8 != 0, unaligned pointers, non-sm_100 device) with
+ * RK_ERR_UNSUPPORTED.
  */
 RK_API rk_status rk_gemv_fixed_scratch(const void* x, const void* weight, void* out,
                                        int64_t M, int64_t N, int64_t K, rk_dtype dt,
@@ -413,6 +416,35 @@ RK_API const char* rk_status_string(rk_status status);
 /* Message of the last CUDA error seen by this thread's calls ("" if none). */
 RK_API const char* rk_last_error(void);
 
+/*
+ * Reads and clears the device-side status word of the current device after
+ * synchronising `stream`.  Returns RK_OK, RK_ERR_TIMEOUT when a kernel launched
+ * since the previous call gave up on a bounded wait, or RK_ERR_INVALID_ARGUMENT
+ * when one met an out-of-range index in device memory (a paged-attention block
+ * table entry) and skipped it.
+ */
+RK_API rk_status rk_device_status(rk_stream_t stream);
+
+/* Programmatic dependent launch (on by default; no counterpart in the reference,
+ * whose kernels launch one after another).  When enabled every kernel of this
+ * library is launched with programmatic stream serialisation: it may be scheduled
+ * while the previous kernel in the stream is still finishing, runs its set-up
+ * (barrier initialisation, tensor-memory allocation, descriptor prefetch), then waits
+ * in griddepcontrol.wait until every earlier kernel of the stream has completed and
+ * its writes are visible, before it reads or writes global memory.  Results are
+ * identical either way; 0 disables it (kernels then start only after the previous
+ * kernel completes).  Returns the previous setting.  Process-wide. */
+RK_API int rk_set_programmatic_launch(int enable);
+
+/*
+ * ---------------------------------------------------------------------------------
+ * Tuning and debugging hooks.  Process-wide settings read when a kernel is launched:
+ * they change the choices of every caller in the process, so they are for tests,
+ * benchmarks and tuning sweeps, not for concurrent production use.  None of them
+ * changes results beyond the documented reduction order of the variant it selects.
+ * No counterpart in the reference.
+ * ---------------------------------------------------------------------------------
+ */
 /* Tuning hook for RK_GEMV_STREAM: weight rows per warp (1, 2, 4) and in-CTA
  * K split (1, 2, 4, 8); 0 restores the built-in heuristic.  Process-wide. */
 RK_API void rk_gemv_set_tuning(int rows_per_warp, int ksplit);
@@ -443,26 +475,6 @@ RK_API void rk_norm_backward_set_ctas_per_sm(int ctas_per_sm);
  * split-K); 0 restores the built-in choice.  Process-wide. */
 RK_API void rk_gemv_tc_set_cluster(int cluster_size);
 
-/* Programmatic dependent launch (on by default; no counterpart in the reference,
- * whose kernels launch one after another).  When enabled every kernel of this
- * library is launched with programmatic stream serialisation: it may be scheduled
- * while the previous kernel in the stream is still finishing, runs its set-up
- * (barrier initialisation, tensor-memory allocation, descriptor prefetch), then waits
- * in griddepcontrol.wait until every earlier kernel of the stream has completed and
- * its writes are visible, before it reads or writes global memory.  Results are
- * identical either way; 0 disables it (kernels then start only after the previous
- * kernel completes).  Returns the previous setting.  Process-wide. */
-RK_API int rk_set_programmatic_launch(int enable);
-
-/*
- * Reads and clears the device-side status word of the current device after
- * synchronising `stream`.  Returns RK_OK, RK_ERR_TIMEOUT when a kernel launched
- * since the previous call gave up on a bounded wait, or RK_ERR_INVALID_ARGUMENT
- * when one met an out-of-range index in device memory (a paged-attention block
- * table entry) and skipped it.
- */
-RK_API rk_status rk_device_status(rk_stream_t stream);
-
 /* Sets the per-wait time limit (nanoseconds, default 1e9) used by kernels
  * launched after the call.  0 restores the default. */
 RK_API void rk_set_wait_timeout_ns(uint64_t ns);
@@ -471,6 +483,14 @@ RK_API void rk_set_wait_timeout_ns(uint64_t ns);
  * role wait on a barrier that nothing arrives on, so the bounded wait runs
  * out and the kernel reports RK_ERR_TIMEOUT.  Resets itself after one launch. */
 RK_API void rk_debug_inject_stall(int enable);
+
+/* Name of the last kernel this thread launched through the library ("gemv_tc_sk_kernel",
+ * "gemm_tc2_kernel", ...; "" before the first launch, "other" for unnamed ones). */
+RK_API const char* rk_debug_last_kernel(void);
+
+/* Test hook: fills the whole array behind rk_gemv_fixed_scratch on the current device
+ * with `byte` (stream-ordered), as an interrupted call could leave it. */
+RK_API rk_status rk_debug_fill_fixed_scratch(int byte, rk_stream_t stream);
 
 /* Human-readable name of a variant ("gemm:tc_1sm", "gemv:stream", ...). */
 RK_API const char* rk_variant_name(int op /* 0 = gemm, 1 = gemv */, int variant);

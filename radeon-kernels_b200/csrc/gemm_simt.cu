@@ -88,7 +88,7 @@ rk_status gemm_simt_launch(const void* A, const void* B, void* C, int64_t M, int
     e = launch_kernel(gemm_simt_kernel<__half>, grid, dim3(256), 0, s, 0,
                       static_cast<const __half*>(A), static_cast<const __half*>(B),
                       static_cast<__half*>(C), M, N, K, sam, sak, sbk, sbn);
-  note_launch();
+  note_launch("gemm_simt_kernel");
   return cuda_status(e);
 }
 

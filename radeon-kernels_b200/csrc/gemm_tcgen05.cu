@@ -364,7 +364,7 @@ rk_status launch_tc1(const void* A, const void* B, void* C, int64_t M, int64_t N
                                       smem, s, 0, ta, tb, reinterpret_cast<T*>(C),
                                       static_cast<int>(M), static_cast<int>(N),
                                       static_cast<int>(K), ctl);
-  note_launch();
+  note_launch("gemm_tc1_kernel");
   return cuda_status(e);
 }
 

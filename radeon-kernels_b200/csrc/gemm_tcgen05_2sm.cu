@@ -84,6 +84,14 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   return v;
 }
 
+// First tile that is split into two 128-column halves: the last partial wave, when it
+// occupies at most half of the pairs (then its 2x as many half units still fit one wave, which
+// takes half as long -- 896 tiles on 74 pairs: 12 waves + 8 tiles, the 13th wave 24 -> 12 us).
+inline int64_t tail_split_from(int64_t tiles, int64_t pairs) {
+  const int64_t left = pairs > 0 ? tiles % pairs : 0;
+  return (tiles > pairs && left > 0 && 2 * left <= pairs) ? tiles - left : tiles;
+}
+
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
   const int group = t / per_group;
@@ -92,6 +100,20 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   const int in_group = t - group * per_group;
   mb = first_m + in_group % gsize;
   nb = in_group / gsize;
+}
+
+// Work units of a launch: tiles [0, split_from) whole, every later tile as two 256 x 128
+// halves (half = 0, 1; -1 for a whole tile).  The host splits the last partial wave this way
+// when it fills at most half the SM pairs, so that wave takes half as long.
+__device__ __forceinline__ void unit_coords(int u, int split_from, int num_m, int num_n, int& mb,
+                                            int& nb, int& half) {
+  int t = u;
+  half = -1;
+  if (u >= split_from) {
+    t = split_from + ((u - split_from) >> 1);
+    half = (u - split_from) & 1;
+  }
+  tile_coords(t, num_m, num_n, mb, nb);
 }
 
 // SWIGLU: B is [K, 2N] = [gate | up]; a tile has 128 output columns, the even CTA
@@ -111,7 +133,7 @@ template <typename T, bool SWIGLU = false, bool A_MN = false, bool B_K = false, 
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, T* __restrict__ C, int M, int N,
-                    int K, KernelCtl ctl, const __grid_constant__ PeerOut<T> peer) {
+                    int K, int split_from, KernelCtl ctl, const __grid_constant__ PeerOut<T> peer) {
   static_assert(!(PEERS && (SWIGLU || A_MN || B_K)), "the fused all-gather GEMM takes the nn layout");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -128,6 +150,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int num_m = (M + BM - 1) / BM;
   const int num_n = SWIGLU ? (N + HALF - 1) / HALF : (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
+  // Half units exist only in the nn, non-SwiGLU forms (their B tile is two 64-column boxes).
+  const int split = (SWIGLU || A_MN || B_K) ? num_tiles : min(split_from, num_tiles);
+  const int num_units = split + 2 * (num_tiles - split);
   const int num_kb = (K + BK - 1) / BK;
   volatile int* abort_flag = &bars->abort;
 
@@ -167,9 +192,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ------------------------------------------------------------- producer
       uint32_t stage = 0, phase = 0, issued = 0, issued_parity = 0;
       bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-        int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+      for (int u = pair; u < num_units && ok; u += num_pairs) {
+        int mb, nb, half;
+        unit_coords(u, split, num_m, num_n, mb, nb, half);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(smem_u32(&bars->empty[stage]), phase ^ 1, ctl.timeout_ns,
                                  abort_flag)) {
@@ -178,7 +203,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           const uint32_t full_local = smem_u32(&bars->full[stage]);
           const uint32_t full_even = map_to_rank(full_local, 0);
-          if (rank == 0) mbar_arrive_expect_tx(full_local, 2 * STAGE_BYTES);
+          if (rank == 0) mbar_arrive_expect_tx(full_local, half < 0 ? 2 * STAGE_BYTES : 2 * (A_STAGE + B_BOX));
           const int arow = mb * BM + static_cast<int>(rank) * HALF;
           if constexpr (A_MN) {
 #pragma unroll
@@ -190,13 +215,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                              arow);
           }
           const int bcol = SWIGLU ? (rank == 0 ? nb * HALF : N + nb * HALF)
-                                  : nb * BN + static_cast<int>(rank) * HALF;
+                           : half < 0 ? nb * BN + static_cast<int>(rank) * HALF
+                                      : nb * BN + half * HALF + static_cast<int>(rank) * 64;
           if constexpr (B_K) {
             tma_load_2d_pair(smem_u32(smem_b + stage * B_STAGE), &tmap_b, full_even, kb * BK,
                              bcol);
           } else {
-#pragma unroll
-            for (int j = 0; j < HALF / 64; ++j)
+            const int boxes = half < 0 ? HALF / 64 : 1;  // a half unit's CTA stages 64 columns
+            for (int j = 0; j < boxes; ++j)
               tma_load_2d_pair(smem_u32(smem_b + stage * B_STAGE + j * B_BOX), &tmap_b,
                                full_even, bcol + j * 64, kb * BK);
           }
@@ -226,12 +252,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ------------------------------------------------ MMA issuer (even CTA only)
-      const uint32_t idesc =
+      const uint32_t idesc_whole =
           umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, BN, A_MN, !B_K);
+      const uint32_t idesc_half =
+          umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, BM, HALF, A_MN, !B_K);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       int i = 0;
-      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++i) {
+      for (int u = pair; u < num_units && ok; u += num_pairs, ++i) {
+        const uint32_t idesc = u < split ? idesc_whole : idesc_half;
         const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
         if (!mbar_wait_cluster_bounded(smem_u32(&bars->tmem_empty[acc]), acc_phase ^ 1,
                                        ctl.timeout_ns, abort_flag)) {
@@ -279,9 +308,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;
     int i = 0;
     bool peers_checked = false;
-    for (int t = pair; t < num_tiles; t += num_pairs, ++i) {
-      int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+    for (int u = pair; u < num_units; u += num_pairs, ++i) {
+      int mb, nb, half;
+      unit_coords(u, split, num_m, num_n, mb, nb, half);
+      const int cols = half < 0 ? BN : HALF;           // accumulator columns of this unit
+      const int col0 = nb * BN + (half < 0 ? 0 : half * HALF);
       const uint32_t acc = i & 1, acc_phase = (i >> 1) & 1;
       const bool got = mbar_wait_bounded(smem_u32(&bars->tmem_full[acc]), acc_phase,
                                          ctl.timeout_ns, abort_flag);
@@ -307,7 +338,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
         const int unit = lane & 7;
 #pragma unroll 1
-        for (int c2 = 0; c2 < BN / 64; ++c2) {
+        for (int c2 = 0; c2 < cols / 64; ++c2) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             uint32_t r[32];
@@ -325,7 +356,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               st_shared_v4(stage + lane * 128 + (((h * 4 + q) ^ (lane & 7)) << 4), v);
             }
           }
-          if (c2 == BN / 64 - 1) {
+          if (c2 == cols / 64 - 1) {
             // Last TMEM read of this accumulator: hand it back before the stores.
             tc_fence_before();
             __syncwarp();
@@ -333,7 +364,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           } else {
             __syncwarp();
           }
-          const int gcol = nb * BN + c2 * 64 + unit * 8;
+          const int gcol = col0 + c2 * 64 + unit * 8;
 #pragma unroll 4
           for (int it = 0; it < 8; ++it) {
             const int rr = (lane >> 3) + 4 * it;  // lanes 8k..8k+7 cover one row's 128 bytes
@@ -352,7 +383,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       T* crow = C + static_cast<size_t>(row) * N;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
 #pragma unroll 1
-      for (int c = 0; c < (SWIGLU ? HALF : BN) / 32; ++c) {
+      for (int c = 0; c < (SWIGLU ? HALF : cols) / 32; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tbase + c * 32, r);
         if (SWIGLU) {
@@ -365,7 +396,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         } else {
           tmem_ld_wait();
         }
-        const int n0 = (SWIGLU ? nb * HALF : nb * BN) + c * 32;
+        const int n0 = (SWIGLU ? nb * HALF : col0) + c * 32;
         if (row < M) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -384,7 +415,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&bars->tmem_empty[acc]), 0));
     }
-    if constexpr (PEERS) __threadfence_system();  // this thread's peer stores, before the count
   }
 
   tc_fence_before();
@@ -395,6 +425,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
   if constexpr (PEERS) {
+    // The CTA barrier above orders the epilogue warps' peer stores before thread 0's
+    // system-scope fence in peer_finish (the grid-synchronisation pattern).
     if (threadIdx.x == 0) peer_finish(peer, epoch, gridDim.x);
   }
 }
@@ -432,13 +464,15 @@ rk_status launch_tc2(const void* A, const void* B, void* C, int64_t M, int64_t N
   const int64_t tiles = ((M + tc2::BM - 1) / tc2::BM) * ((N + tile_n - 1) / tile_n);
   const int64_t pairs_max = device_sm_count() / 2;
   const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
+  const int64_t split_from = (SWIGLU || A_MN || B_K) ? tiles : tc2::tail_split_from(tiles, pairs);
 
   const cudaError_t e = launch_kernel(tc2::gemm_tc2_kernel<T, SWIGLU, A_MN, B_K>,
                                       dim3(static_cast<unsigned>(2 * pairs)),
                                       dim3(tc2::THREADS), tc2::SMEM_BYTES, s, 2, ta, tb,
                                       reinterpret_cast<T*>(C), static_cast<int>(M),
-                                      static_cast<int>(N), static_cast<int>(K), ctl, PeerOut<T>{});
-  note_launch();
+                                      static_cast<int>(N), static_cast<int>(K),
+                                      static_cast<int>(split_from), ctl, PeerOut<T>{});
+  note_launch("gemm_tc2_kernel");
   return cuda_status(e);
 }
 
@@ -483,8 +517,9 @@ rk_status launch_tc2_peers(const void* A, const void* B, int64_t M, int64_t N, i
                                       dim3(static_cast<unsigned>(2 * pairs)), dim3(tc2::THREADS),
                                       tc2::SMEM_BYTES_PEERS, s, 2, ta, tb, static_cast<T*>(nullptr),
                                       static_cast<int>(M), static_cast<int>(N),
-                                      static_cast<int>(K), ctl, peer);
-  note_launch();
+                                      static_cast<int>(K),
+                                      static_cast<int>(tc2::tail_split_from(tiles, pairs)), ctl, peer);
+  note_launch("gemm_tc2_kernel<PEERS>");
   return cuda_status(e);
 }
 }  // namespace

@@ -142,9 +142,10 @@ struct Log2<1> {
 // sums go to shared memory [KS][rows][MB] and are added in ks order.
 //
 // PEER: the fused all-gather form (rk_gemv_allgather).  W holds this rank's block of
-// weight rows; each output element is stored into every rank's full output
-// (peer.out[j], row stride peer.ldo) once the ranks have started this call, and the
-// exchange completes as rk_peer.cuh describes.  CTA 0 announces the call at the start.
+// weight rows; the output (peer.out[rank], row stride peer.ldo) is gathered into every
+// rank's full output at the end of the kernel as rk_peer.cuh describes, the push done by
+// the grid's last CTA (the block is at most 32 x N elements).  CTA 0 announces the call at
+// the start.
 template <typename T, int MB, int ROWS, int KS, bool PEER = false>
 __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_stream_kernel(const T* __restrict__ x, const T* __restrict__ W, T* __restrict__ out,
@@ -229,23 +230,60 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   }
   __syncthreads();
   if constexpr (PEER) {
-    __shared__ int peers_ready;
-    if (threadIdx.x == 0) peers_ready = peer_wait_ready(peer, epoch) ? 1 : 0;
-    __syncthreads();
-    if (peers_ready) {
-      for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {
-        const int i = t / M, m = t % M;
-        float s = 0.f;
+    // Every CTA stores its rows into this rank's own full output only; the last CTA of
+    // the grid (grid-wide count, GPU-scope fences) then pushes the rank's whole column
+    // block to every peer with 16-byte stores and runs the arrival round alone, so one
+    // CTA pays the system-scope fence and the NVLink round trip instead of every CTA.
+    T* const mine = peer.out[peer.rank];
+    for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {
+      const int i = t / M, m = t % M;
+      float s = 0.f;
 #pragma unroll
-        for (int k = 0; k < KS; ++k) s += red[(k * rows_max + i) * MB + m];
-        const T v = from_f32<T>(s);
-        const size_t at = static_cast<size_t>(m) * peer.ldo + row_begin + i;
-        for (int j = 0; j < peer.world; ++j) peer.out[j][at] = v;
+      for (int k = 0; k < KS; ++k) s += red[(k * rows_max + i) * MB + m];
+      mine[static_cast<size_t>(m) * peer.ldo + row_begin + i] = from_f32<T>(s);
+    }
+    __shared__ int role;  // 1: this CTA finished last; 2: ... and every rank has started
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      role = atomicAdd(&peer.ctl[peer.rank]->done_ctas, 1u) == gridDim.x - 1u ? 1 : 0;
+      if (role) {
+        __threadfence();
+        peer.ctl[peer.rank]->done_ctas = 0u;  // the next call starts after this kernel completes
+        if (peer_wait_ready(peer, epoch)) role = 2;
       }
     }
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) peer_finish(peer, epoch, gridDim.x);
+    if (role == 0) return;
+    if (role == 2) {
+      // The block is M rows of N contiguous elements at row stride ldo.
+      bool vec = (N % 8) == 0;
+      for (int j = 0; j < peer.world; ++j) vec &= (reinterpret_cast<uintptr_t>(peer.out[j]) & 15u) == 0;
+      if (vec) {
+        const int per_row = N / 8;
+        for (int t = threadIdx.x; t < M * per_row; t += GEMV_THREADS) {
+          const size_t at = static_cast<size_t>(t / per_row) * peer.ldo + static_cast<size_t>(t % per_row) * 8;
+          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(mine + at));
+          for (int j = 0; j < peer.world; ++j)
+            if (j != peer.rank) *reinterpret_cast<uint4*>(peer.out[j] + at) = v;
+        }
+      } else {
+        for (int t = threadIdx.x; t < M * N; t += GEMV_THREADS) {
+          const size_t at = static_cast<size_t>(t / N) * peer.ldo + t % N;
+          const T v = mine[at];
+          for (int j = 0; j < peer.world; ++j)
+            if (j != peer.rank) peer.out[j][at] = v;
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();  // every peer store of this CTA, before the arrival flags
+      for (int j = 0; j < peer.world; ++j) st_release_sys(&peer.ctl[j]->arrive[peer.rank], epoch);
+      if (!peer_wait_all(peer.ctl[peer.rank]->arrive, peer.world, epoch, peer.timeout_ns))
+        atomicOr(peer.status, RK_DEV_ERR_TIMEOUT_PEER);
+      *reinterpret_cast<volatile uint32_t*>(&peer.ctl[peer.rank]->epoch) = epoch;
+    }
   } else {
     for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {
       const int i = t / M, m = t % M;
@@ -461,7 +499,7 @@ rk_status stream_run(const void* x, const void* W, void* out, int64_t M, int64_t
   const size_t smem = static_cast<size_t>(ks) * rows_max * mb * sizeof(float);
   L.launch(x, W, out, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
            static_cast<int>(grid), rows_base, rows_rem, rows_max, smem, s, peer, &lc);
-  note_launch();
+  note_launch(peer != nullptr ? "gemv_stream_kernel<PEER>" : "gemv_stream_kernel");
   return cuda_status(cudaGetLastError());
 }
 
@@ -508,7 +546,7 @@ rk_status gemv_scalar_launch(const void* x, const void* W, void* out, int64_t M,
     default: return RK_ERR_INVALID_ARGUMENT;
   }
 #undef RK_SCALAR_CASE
-  note_launch();
+  note_launch("gemv_scalar_kernel");
   return cuda_status(cudaGetLastError());
 }
 

@@ -612,16 +612,20 @@ __global__ void __launch_bounds__(THREADS, 2)
 
 namespace {
 
-// Stream-K grid: two CTAs per SM, at most one per work unit, and at most 240 CTAs for
-// 32-wide accumulators so the partial slots of the largest case fit the 8 MiB fixed
-// scratch of rk_gemv_fixed_scratch.
+// Stream-K grid: two CTAs per SM, at most one per work unit.
 int sk_grid(int64_t M, int64_t N, int64_t K) {
+  (void)M;
   const int64_t units = ((N + gtc::BM - 1) / gtc::BM) * ((K + gtc::BK - 1) / gtc::BK);
   int64_t g = 2ll * device_sm_count();
-  if (M > 16 && g > 240) g = 240;
   if (g > 480) g = 480;
   if (g > units) g = units;
   return g < 1 ? 1 : static_cast<int>(g);
+}
+
+// Bytes of partial sums one stream-K CTA owns (two slots of a BM x MN fp32 tile).
+size_t sk_cta_bytes(int64_t M) {
+  const int mn = M <= 16 ? 16 : 32;
+  return static_cast<size_t>(2) * gtc::BM * mn * sizeof(float);
 }
 
 // Tickets live in the workspace's fixed ticket prefix (kept zero by every strategy).
@@ -636,8 +640,18 @@ bool sk_fits(int64_t N) {
 
 // Stream-K workspace bytes (ticket counters + two partial slots per CTA).
 size_t sk_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  const int mn = M <= 16 ? 16 : 32;
-  return sk_ticket_bytes(N) + static_cast<size_t>(sk_grid(M, N, K)) * 2 * gtc::BM * mn * sizeof(float);
+  return sk_ticket_bytes(N) + static_cast<size_t>(sk_grid(M, N, K)) * sk_cta_bytes(M);
+}
+
+// Stream-K CTAs a workspace of `bytes` holds partial slots for (0: not even one), capped
+// at the full grid.  A caller's workspace sized by rk_gemv_workspace_size gets the full
+// grid; the fixed array of rk_gemv_fixed_scratch gets as many CTAs as it has room for.
+int sk_grid_within(int64_t M, int64_t N, int64_t K, size_t bytes) {
+  const size_t tickets = sk_ticket_bytes(N);
+  if (bytes <= tickets) return 0;
+  const int64_t room = static_cast<int64_t>((bytes - tickets) / sk_cta_bytes(M));
+  const int full = sk_grid(M, N, K);
+  return room < full ? static_cast<int>(room) : full;
 }
 
 // Workspace the automatic strategy can use.  Measured on B200, cluster split-K beats
@@ -675,9 +689,11 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
 
   const int64_t tiles = (N + gtc::BM - 1) / gtc::BM;
   const int64_t num_kb = (K + gtc::BK - 1) / gtc::BK;
-  const size_t need = sk_workspace_bytes(M, N, K);
-  if ((stream_k || csize_override == -1) && sk_fits(N) && workspace != nullptr &&
-      workspace_bytes >= need) {
+  const int sk_ctas = workspace != nullptr ? sk_grid_within(M, N, K, workspace_bytes) : 0;
+  // A caller's workspace must hold the full grid's slots (rk_gemv_workspace_size); the fixed
+  // array (stream_k) runs with the CTAs it has room for.
+  if ((stream_k || csize_override == -1) && sk_fits(N) && sk_ctas >= 1 &&
+      (stream_k || sk_ctas == sk_grid(M, N, K))) {
     // Stream-K over all SMs, shared tiles meet in the caller's workspace.
     constexpr int sk_smem = gtc::sk_smem_bytes<MN>();
     static std::once_flag sk_once[64];
@@ -689,11 +705,11 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
     if (sk_err[dev & 63] != cudaSuccess) return cuda_status(sk_err[dev & 63]);
     int* ticket = static_cast<int*>(workspace);
     float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + sk_ticket_bytes(N));
-    const cudaError_t e = launch_kernel(gtc::gemv_tc_sk_kernel<T, MN>, dim3(sk_grid(M, N, K)),
+    const cudaError_t e = launch_kernel(gtc::gemv_tc_sk_kernel<T, MN>, dim3(sk_ctas),
                                         dim3(gtc::THREADS), sk_smem, s, 0, tw, tx,
                                         static_cast<T*>(out), static_cast<int>(M),
                                         static_cast<int>(N), static_cast<int>(K), part, ticket, ctl);
-    note_launch();
+    note_launch("gemv_tc_sk_kernel");
     return cuda_status(e);
   }
   // Split K over a thread-block cluster, reduced through DSMEM: the largest cluster of
@@ -701,8 +717,20 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   int csize = csize_override;
   if (csize <= 0) {
     // Measured on B200: 8-CTA clusters only pay off for very short weights (<= 12 row
-    // tiles); otherwise the largest of 1/2/4 keeping the grid within two CTAs per SM.
-    const int64_t target = 2ll * device_sm_count();
+    // tiles); otherwise the largest of 1/2/4 keeping the grid within one wave of the CTAs
+    // that fit an SM -- two with 16-wide accumulators, one with 32-wide ones (124 KiB of
+    // shared memory each): at M = 17..32, N = 8192 clusters of 4 would launch a second
+    // wave (36.5 us) where clusters of 2 take 28.5 us.
+    static std::once_flag occ_once[64];
+    static int occ[64];
+    std::call_once(occ_once[dev & 63], [&] {
+      int n = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gtc::gemv_tc_kernel<T, MN>, gtc::THREADS,
+                                                        smem) != cudaSuccess || n < 1)
+        n = 1;
+      occ[dev & 63] = n > 2 ? 2 : n;
+    });
+    const int64_t target = static_cast<int64_t>(occ[dev & 63]) * device_sm_count();
     const int cap = tiles <= 12 ? 8 : 4;
     csize = 1;
     while (csize < cap && tiles * csize * 2 <= target && csize * 2 <= num_kb) csize *= 2;
@@ -714,7 +742,7 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
                                       dim3(gtc::THREADS), smem, s, csize, tw, tx,
                                       static_cast<T*>(out), static_cast<int>(M),
                                       static_cast<int>(N), static_cast<int>(K), csize, ctl);
-  note_launch();
+  note_launch("gemv_tc_kernel");
   return cuda_status(e);
 }
 
@@ -772,12 +800,26 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_gemv_fixed_scratch[RK_GEMV_FIXED_SCRATCH_BYTES];
 
-struct FixedScratch {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
-  void* ptr = nullptr;
-};
-FixedScratch g_fixed_scratch[64];
+// Device address of the array, per device; looked up under the lock until a lookup
+// succeeds (a failed lookup -- say inside a stream capture -- is retried next call).
+std::mutex g_fixed_scratch_mu;
+void* g_fixed_scratch_ptr[64] = {};
+
+rk_status fixed_scratch_address(int dev, void** ptr) {
+  std::lock_guard<std::mutex> lock(g_fixed_scratch_mu);
+  if (g_fixed_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_gemv_fixed_scratch);
+    if (e != cudaSuccess) return rk::cuda_status(e);
+    if (p == nullptr) {
+      rk::note_error("cudaGetSymbolAddress returned no address for the fixed GEMV scratch");
+      return RK_ERR_CUDA;
+    }
+    g_fixed_scratch_ptr[dev] = p;
+  }
+  *ptr = g_fixed_scratch_ptr[dev];
+  return RK_OK;
+}
 
 }  // namespace
 
@@ -791,19 +833,28 @@ extern "C" rk_status rk_gemv_fixed_scratch(const void* x, const void* weight, vo
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RK_ERR_NO_DEVICE;
   if (!gemv_tc_supported(x, weight, out, M, N, K)) return RK_ERR_UNSUPPORTED;
-  FixedScratch& fs = g_fixed_scratch[dev];
-  std::call_once(fs.once, [&fs] { fs.err = cudaGetSymbolAddress(&fs.ptr, g_gemv_fixed_scratch); });
-  if (fs.err != cudaSuccess || fs.ptr == nullptr) return cuda_status(fs.err);
-  const size_t need = gemv_tc_stream_k_bytes(M, N, K);
-  if (need > RK_GEMV_FIXED_SCRATCH_BYTES) return RK_ERR_TOO_LARGE;
+  // One ticket per 128-row tile of the weight lives in the array's ticket prefix.
+  if (!sk_fits(N)) return RK_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  const rk_status found = fixed_scratch_address(dev, &scratch);
+  if (found != RK_OK) return found;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // The array keeps whatever the previous call left; the split-K tickets at its start
-  // must be zero when the kernel begins.
-  // (Weights taller than the ticket prefix covers run cluster split-K, which needs none.)
-  if (sk_fits(N)) {
-    const size_t used_tickets = ((N + gtc::BM - 1) / gtc::BM * sizeof(int) + 255) / 256 * 256;
-    const rk_status st = cuda_status(cudaMemsetAsync(fs.ptr, 0, used_tickets, s));
-    if (st != RK_OK) return st;
-  }
-  return gemv_tc_launch(x, weight, out, M, N, K, dt, s, fs.ptr, RK_GEMV_FIXED_SCRATCH_BYTES, true);
+  // must be zero when the kernel begins (the partial slots are written before read).
+  const size_t used_tickets = ((N + gtc::BM - 1) / gtc::BM * sizeof(int) + 255) / 256 * 256;
+  const rk_status st = cuda_status(cudaMemsetAsync(scratch, 0, used_tickets, s));
+  if (st != RK_OK) return st;
+  return gemv_tc_launch(x, weight, out, M, N, K, dt, s, scratch, RK_GEMV_FIXED_SCRATCH_BYTES, true);
+}
+
+// Test hook: fills the whole fixed array of the current device with `byte`, as a
+// previous call stopped midway could leave it (non-zero tickets, stale partial sums).
+extern "C" rk_status rk_debug_fill_fixed_scratch(int byte, rk_stream_t stream) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RK_ERR_NO_DEVICE;
+  void* scratch = nullptr;
+  const rk_status found = fixed_scratch_address(dev, &scratch);
+  if (found != RK_OK) return found;
+  return rk::cuda_status(cudaMemsetAsync(scratch, byte & 0xff, RK_GEMV_FIXED_SCRATCH_BYTES,
+                                         reinterpret_cast<cudaStream_t>(stream)));
 }

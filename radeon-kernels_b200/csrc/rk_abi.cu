@@ -83,7 +83,14 @@ rk_status cuda_status(cudaError_t e) {
 
 void note_error(const std::string& message) { g_last_error = message; }
 
-void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+namespace {
+thread_local const char* g_last_kernel = "";
+}  // namespace
+
+void note_launch(const char* kernel) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  g_last_kernel = kernel != nullptr ? kernel : "other";
+}
 
 namespace {
 std::atomic<bool> g_pdl{true};
@@ -154,6 +161,8 @@ const char* rk_last_error(void) { return g_last_error.c_str(); }
 int rk_abi_version(void) { return RK_ABI_VERSION; }
 
 uint64_t rk_launch_count(void) { return g_launches.load(); }
+
+const char* rk_debug_last_kernel(void) { return g_last_kernel; }
 
 void rk_set_wait_timeout_ns(uint64_t ns) { g_timeout_ns.store(ns ? ns : 1000000000ull); }
 

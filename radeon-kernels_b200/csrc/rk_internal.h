@@ -23,8 +23,9 @@ rk_status launch_ctl(LaunchCtl* ctl);
 // Cached per-device properties.
 int device_sm_count();
 int device_cc_major();
-// Counts one kernel launch (rk_launch_count()).
-void note_launch();
+// Counts one kernel launch (rk_launch_count()) and records the kernel's name for this
+// thread (rk_debug_last_kernel(); null: "other").
+void note_launch(const char* kernel = nullptr);
 // Programmatic dependent launch switch (rk_set_programmatic_launch()).
 bool programmatic_launch();
 bool set_programmatic_launch(bool enable);

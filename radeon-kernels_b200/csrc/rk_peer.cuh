@@ -8,16 +8,21 @@
 //              earlier kernel of its stream -- the consumers of call e-1's output -- has
 //              completed): from then on the other ranks may overwrite rank j's output.
 //   arrive[j]  written by rank j once every store of its call e into this rank's output has
-//              been made visible (__threadfence_system by every storing thread, then a
-//              grid-wide count; the last CTA of the grid sends it).
+//              been made visible (per CTA: a barrier, then one thread's system-scope fence
+//              and a grid-wide count -- the grid-synchronisation pattern; the last CTA of
+//              the grid sends it).
 //   epoch      calls completed by this rank on this control block; written only by this
 //              rank, read at the start of the next call (which begins after it in stream
 //              order), so all ranks agree on the call number without host involvement and
 //              a captured CUDA graph replays correctly.
 //   done_ctas  CTAs of the running call that have finished storing; the last resets it.
 //
-// The last CTA of each rank waits until every rank's arrive[] reaches the call's epoch, so
-// when the kernel completes the local full output is complete.  Every wait is bounded (time
+// Two ways to move the data: the GEMM (large blocks) stores every finished tile into every
+// rank's output from the CTA that made it, while the next tile accumulates, and ends with
+// peer_finish; the GEMV (a block of at most 32 x N elements) stores into its own output
+// only, and the grid's last CTA pushes the whole block to the peers and sends the arrival
+// flags itself.  Either way the last CTA of each rank waits until every rank's arrive[]
+// reaches the call's epoch, so when the kernel completes the local full output is complete.  Every wait is bounded (time
 // and iteration count); a wait that runs out sets RK_DEV_ERR_TIMEOUT_PEER in the status word
 // and the kernel finishes without the missing data (the group must then be rebuilt).
 #pragma once
@@ -107,10 +112,10 @@ __device__ __forceinline__ bool peer_wait_ready(const PeerOut<T>& p, uint32_t e)
   return ok;
 }
 
-// End of a CTA's part of call `e`: called by one thread after every thread of the CTA that
-// stored to a peer has executed __threadfence_system() and the CTA has synchronised.  The
-// last CTA of the grid publishes this rank's arrival to every rank, waits for every rank's,
-// and advances the epoch.
+// End of a CTA's part of call `e`: called by one thread after a CTA-wide barrier that follows
+// every peer store of the CTA; its system-scope fence makes those stores visible before the
+// count.  The last CTA of the grid publishes this rank's arrival to every rank, waits for
+// every rank's, and advances the epoch.
 template <typename T>
 __device__ __forceinline__ void peer_finish(const PeerOut<T>& p, uint32_t e, uint32_t grid_ctas) {
   PeerCtl* mine = p.ctl[p.rank];

@@ -535,6 +535,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv_out", &gemv_out, "out = x @ weight.T into the caller's output", py::arg("input"),
         py::arg("weight"), py::arg("out"), py::arg("variant") = 0);
   m.def("gemv_stream", &gemv_stream, "128-bit weight-streaming GEMV (K % 8 == 0, 16B aligned)");
+  // The reference pack's GEMV entrypoint names (benchmarks/gemv/native_gemv.hip:381-391):
+  // its dispatch entries launch gemv_wave1 / gemv_wave2 (one or two outputs per wavefront)
+  // with no arguments beyond (input, weight).  Here the outputs-per-wave choice has no
+  // counterpart -- the automatic kernel choice runs -- so a manifest naming either resolves.
+  m.def("gemv_wave1", [](const at::Tensor& x, const at::Tensor& w) { return gemv(x, w, RK_GEMV_AUTO); },
+        "out = x @ weight.T (reference entrypoint name)", py::arg("input"), py::arg("weight"));
+  m.def("gemv_wave2", [](const at::Tensor& x, const at::Tensor& w) { return gemv(x, w, RK_GEMV_AUTO); },
+        "out = x @ weight.T (reference entrypoint name)", py::arg("input"), py::arg("weight"));
   m.def("gemv_scalar", &gemv_scalar, "generic GEMV (any K, any alignment)");
   m.def("gather_column_blocks", &gather_column_blocks, "[G,M,N/G] blocks -> row-major [M,N]");
   m.def("gemv_allgather", &gemv_allgather,

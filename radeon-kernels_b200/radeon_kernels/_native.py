@@ -109,6 +109,14 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_add_rms_norm.restype = cint
     lib.rk_gemv_fixed_scratch.argtypes = [vp, vp, vp, i64, i64, i64, cint, vp]
     lib.rk_gemv_fixed_scratch.restype = cint
+    lib.rk_debug_fill_fixed_scratch.argtypes = [cint, vp]
+    lib.rk_debug_fill_fixed_scratch.restype = cint
+    lib.rk_debug_last_kernel.argtypes = []
+    lib.rk_debug_last_kernel.restype = ctypes.c_char_p
+    lib.rk_gemv_allgather.argtypes = [vp, vp, i64, i64, i64, cint, vp, vp]
+    lib.rk_gemv_allgather.restype = cint
+    lib.rk_gemm_allgather.argtypes = [vp, vp, i64, i64, i64, cint, vp, vp]
+    lib.rk_gemm_allgather.restype = cint
     lib.rk_gather_column_blocks.argtypes = [vp, vp, i64, i64, i64, cint, vp]
     lib.rk_gather_column_blocks.restype = cint
     lib.rk_status_string.argtypes = [cint]

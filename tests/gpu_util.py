@@ -117,24 +117,3 @@ def seeded(shape, seed: int, dist: str, dtype: str, generator=None):
     else:
         raise ValueError(dist)
     return x.to(torch_dtype(dtype))
-
-
-def seeded_device(shape, seed: int, dist: str, dtype: str):
-    """Same distribution drawn on the GPU (for sizes where CPU generation is too slow)."""
-
-    import torch
-
-    gen = torch.Generator(device="cuda").manual_seed(seed)
-    if dist == "uniform":
-        x = torch.rand(shape, generator=gen, device="cuda") * 2 - 1
-    elif dist == "uniform16":
-        x = (torch.rand(shape, generator=gen, device="cuda") * 2 - 1) / 16
-    elif dist == "normal64":
-        x = torch.randn(shape, generator=gen, device="cuda") / 64
-    elif dist == "normal":
-        x = torch.randn(shape, generator=gen, device="cuda")
-    elif dist.startswith("normal/"):
-        x = torch.randn(shape, generator=gen, device="cuda") / float(dist.split("/", 1)[1]) ** 0.5
-    else:
-        raise ValueError(dist)
-    return x.to(torch_dtype(dtype))
