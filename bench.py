@@ -522,8 +522,12 @@ def e2e(args, dist: Dist):
 
 
 def e2e_sharded(args, dist: Dist):
-    """N > 1: H2D copy, ShardedGemv(gather=True) (fused all-gather kernel), D2H copy of the
-    full output, one stream, 16 steps per CUDA graph, replayed."""
+    """N > 1: per step a pinned H2D copy of x, ``ShardedGemv(gather=True)`` (the fused
+    all-gather kernel) and a pinned D2H copy of the full output, 16 steps captured into one
+    CUDA graph and replayed.  As at N = 1 the input copies run ahead on a copy stream and each
+    output copy runs on a second stream right after its kernel; the operators rotate over the
+    weight sets, each with its own exchange buffer, and a step's kernel waits for the output
+    copy of the step that last used its buffer (the fused call rewrites it)."""
 
     import torch
 
@@ -532,23 +536,63 @@ def e2e_sharded(args, dist: Dist):
     m, n, k = HEAD_M, HEAD_N, HEAD_K
     weights = sharded_weights(dist)
     operators = [ShardedGemv(w, n_total=n) for w in weights]
+    R = len(operators)
     stream = torch.cuda.current_stream()
     G = E2E_GRAPH_STEPS
     xs_host = seeded((G, m, k), 2, "normal", "bf16", device="cpu").pin_memory()
     outs_host = torch.empty((G, m, n), dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty((m, k), dtype=torch.bfloat16, device="cuda")
+    xs_dev = torch.empty((G, m, k), dtype=torch.bfloat16, device="cuda")
+    h2d, d2h, cap = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
 
-    def step(i):
-        x_dev.copy_(xs_host[i % G], non_blocking=True)
-        y = operators[i % len(operators)](x_dev, gather=True)
-        outs_host[i % G].copy_(y, non_blocking=True)
-
-    for i in range(max(args.warmup, 3, len(operators))):
-        step(i)  # the first gathered call of each operator sets up its exchange (collective)
+    for i in range(max(args.warmup, 3, R)):
+        operators[i % R](xs_dev[i % G], gather=True)  # first call of each operator: collective set-up
     torch.cuda.synchronize()
-    graph = capture_graph(step, G, stream)
+
+    def graph_body():
+        here = torch.cuda.current_stream()
+        h2d.wait_stream(here)
+        d2h.wait_stream(here)
+        ready, copied = [], []
+        with torch.cuda.stream(h2d):
+            for i in range(G):
+                xs_dev[i].copy_(xs_host[i], non_blocking=True)
+                ready.append(torch.cuda.Event())
+                ready[-1].record(h2d)
+        for i in range(G):
+            here.wait_event(ready[i])
+            if i >= R:
+                here.wait_event(copied[i - R])  # buffer of operator i % R copied out
+            y = operators[i % R](xs_dev[i], gather=True)
+            done = torch.cuda.Event()
+            done.record(here)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                outs_host[i].copy_(y, non_blocking=True)
+                copied.append(torch.cuda.Event())
+                copied[-1].record(d2h)
+        here.wait_stream(h2d)
+        here.wait_stream(d2h)
+
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        graph_body()  # eager run of the same body
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=cap):
+        graph_body()
+    stream.wait_stream(cap)
+    torch.cuda.synchronize()
     graph.replay()
     torch.cuda.synchronize()
+    # Spot check: the replayed outputs equal the rank-local product on this rank's block.
+    rows = n // dist.world
+    from radeon_kernels import _native
+
+    ext = _native.extension()
+    for i in (0, G - 1):
+        local = ext.gemv_out(xs_dev[i], weights[i % R], torch.empty(m, rows, dtype=torch.bfloat16, device="cuda"), 2)
+        if not torch.equal(outs_host[i][:, dist.rank * rows:(dist.rank + 1) * rows], local.cpu()):
+            raise RuntimeError("e2e: gathered output differs from the local block product")
     replays = max(args.e2e_steps // G, 10)
     ms, _ = timed_region(lambda: [graph.replay() for _ in range(replays)], dist, stream)
     del graph
@@ -561,9 +605,9 @@ def e2e_sharded(args, dist: Dist):
         "d2h_bytes_per_step": m * n * 2,
         "value": round(gemv_bytes(m, n, k) * steps / (ms / 1e3) / 1e9, 1),
         "ms_per_step": round(ms / steps, 5),
-        "path": (f"CUDA graph of {G} captured steps on one stream: pinned H2D copy, "
-                 "radeon_kernels.distributed.ShardedGemv(gather=True) -> rk_gemv_allgather, "
-                 "pinned D2H copy of the full output"),
+        "path": (f"CUDA graph of {G} captured steps: pinned H2D copies (forked copy stream), "
+                 "radeon_kernels.distributed.ShardedGemv(gather=True) -> rk_gemv_allgather, pinned D2H "
+                 "copy of the full output (second stream); outputs spot-checked against the local block"),
     }
 
 
@@ -611,6 +655,14 @@ def suite(args, dist: Dist, ext, peaks):
         ms = dist.max(statistics.median(times))
         flops = 2.0 * m * n * k
         achieved = flops / (ms / 1e3) / 1e12
+        # The same product through torch.mm (cuBLAS), timed the same way: a reference point for
+        # the shape, not part of this library.
+        lib_times = []
+        if not graph:
+            torch.mm(a, b, out=c)
+            for _ in range(iters):
+                flush.zero_()
+                lib_times.append(time_loop(lambda i: torch.mm(a, b, out=c), 1, stream))
         results[name] = {
             "unit": "TFLOP/s",
             "value": round(achieved * dist.world, 1),
@@ -622,6 +674,9 @@ def suite(args, dist: Dist, ext, peaks):
             "dtype": dtype,
             "timing": "CUDA graph of 20 launches, L2-warm" if graph else "single launch, L2 flushed",
         }
+        if lib_times:
+            lib_ms = statistics.median(lib_times)
+            results[name]["torch_mm_cublas_tflops"] = round(flops / (lib_ms / 1e3) / 1e12, 1)
         del a, b, c
 
     def gemv_case(name, m, n, k, dtype, seed, iters):
