@@ -1042,6 +1042,9 @@ def suite(args, dist: Dist, ext, peaks):
         time.sleep(1.0)
 
     g = dist.world
+    # Config 1 first: a 7-10 us launch-bound case is sensitive to the clock state that the
+    # heavier cases below leave behind.
+    gemm_case("c1_gemm_1024_bf16", 1024, 1024, 1024, "bf16", "uniform", 0, 10, graph=True)
     for m in (1, 4, 16):
         gemv_case(f"c2_gemv_decode_bf16_m{m}", m, 8192, 8192, "bf16", 1, 400)
     for m in (1, 4, 16):
@@ -1075,8 +1078,6 @@ def suite(args, dist: Dist, ext, peaks):
     sdpa_case("sdpa_b1_mha16_s256_d64_full_bf16", 1, 16, 16, 256, 64, False, "bf16", 73)
     sdpa_case("sdpa_b2_gqa16x4_s256_d256_causal_bf16", 2, 16, 4, 256, 256, True, "bf16", 74)
     sdpa_case("sdpa_b4_gqa32x8_s4096_d128_causal_bf16", 4, 32, 8, 4096, 128, True, "bf16", 75)
-    gemm_case("c1_gemm_1024_bf16", 1024, 1024, 1024, "bf16", "uniform", 0, 10, graph=True)
-    cool_down()
     gemm_case("c4_gemm_ffn_up_fp16", 4096, 14336, 4096, "fp16", "normal64", 3, 10)
     cool_down()
     ffn_swiglu_case("c4_ffn_up_swiglu_fused_fp16", 4096, 14336, 4096, "fp16", 10)

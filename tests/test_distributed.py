@@ -43,6 +43,9 @@ def _worker(rank, world, port, results, mode):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
     try:
+        if mode == "decide":
+            results[rank] = _decide(rank, world)
+            return
         gen = torch.Generator().manual_seed(0)
         a = torch.randn(5, 16, generator=gen)
         b = torch.randn(16, 6 * world, generator=gen)
@@ -68,6 +71,42 @@ def _worker(rank, world, port, results, mode):
             dist.destroy_process_group()
         except Exception:
             pass
+
+
+def _decide(rank, world):
+    """The collective choice of the gather form on CPU ranks."""
+
+    import torch.distributed as dist
+
+    from radeon_kernels.distributed.peer import fused_path_available
+    from radeon_kernels.distributed.shard import ShardedGemv
+
+    out = {"available": fused_path_available(torch.zeros(2, 2))}  # CPU tensors: every rank declines
+    calls = []
+    original = dist.all_gather_object
+
+    def counting(*args, **kwargs):
+        calls.append(1)
+        return original(*args, **kwargs)
+
+    dist.all_gather_object = counting
+    try:
+        auto = ShardedGemv(torch.randn(4 * world, 8), compute=None, fused=None)
+        auto._compute = lambda p, q: p @ q.t()  # keep the NCCL form's plumbing on CPU
+        auto._permute = _permute_cpu
+        x = torch.randn(2, 8)
+        for _ in range(3):
+            auto(x, gather=True)
+        out["decided_once"] = len(calls) == 1 and auto._fused is False
+        required = ShardedGemv(torch.randn(4 * world, 8), fused=True)
+        try:
+            required(x, gather=True)
+            out["required"] = "ran"
+        except RuntimeError as error:
+            out["required"] = "refused" if "NVLink" in str(error) else str(error)
+    finally:
+        dist.all_gather_object = original
+    return out
 
 
 def _run(world, mode="ok"):
@@ -110,3 +149,11 @@ def test_a_failing_rank_surfaces_as_errors_not_a_hang():
     assert "error" in results[1]
     # rank 0 reaches the all-gather without its peer and fails on the short timeout
     assert "error" in results[0]
+
+
+def test_the_gather_form_is_decided_once_and_together():
+    """CPU ranks never take the fused peer-store path; the decision costs one collective call
+    on the first gathered call only, and fused=True is refused on every rank alike."""
+
+    results = _run(2, mode="decide")
+    assert results == {r: {"available": False, "decided_once": True, "required": "refused"} for r in range(2)}, results
