@@ -645,24 +645,22 @@ def suite(args, dist: Dist, ext, peaks):
             g.replay()
             torch.cuda.synchronize()
             times = [time_loop(lambda i: g.replay(), 1, stream) / 20 for _ in range(iters)]
+            lib_times = []
             del g
         else:
-            times = []
+            # Interleaved with the same product through torch.mm (cuBLAS), a reference point for
+            # the shape (not part of this library): both see the same clock and power state.
+            times, lib_times = [], []
+            torch.mm(a, b, out=c)
             for _ in range(iters):
                 flush.zero_()  # L2 flush between timed launches
                 times.append(time_loop(lambda i: ext.gemm_out(a, b, c, 0), 1, stream))
+                flush.zero_()
+                lib_times.append(time_loop(lambda i: torch.mm(a, b, out=c), 1, stream))
         dist.barrier()
         ms = dist.max(statistics.median(times))
         flops = 2.0 * m * n * k
         achieved = flops / (ms / 1e3) / 1e12
-        # The same product through torch.mm (cuBLAS), timed the same way: a reference point for
-        # the shape, not part of this library.
-        lib_times = []
-        if not graph:
-            torch.mm(a, b, out=c)
-            for _ in range(iters):
-                flush.zero_()
-                lib_times.append(time_loop(lambda i: torch.mm(a, b, out=c), 1, stream))
         results[name] = {
             "unit": "TFLOP/s",
             "value": round(achieved * dist.world, 1),
@@ -674,7 +672,7 @@ def suite(args, dist: Dist, ext, peaks):
             "dtype": dtype,
             "timing": "CUDA graph of 20 launches, L2-warm" if graph else "single launch, L2 flushed",
         }
-        if lib_times:
+        if not graph:
             lib_ms = statistics.median(lib_times)
             results[name]["torch_mm_cublas_tflops"] = round(flops / (lib_ms / 1e3) / 1e12, 1)
         del a, b, c
@@ -1078,6 +1076,7 @@ def suite(args, dist: Dist, ext, peaks):
     sdpa_case("sdpa_b1_mha16_s256_d64_full_bf16", 1, 16, 16, 256, 64, False, "bf16", 73)
     sdpa_case("sdpa_b2_gqa16x4_s256_d256_causal_bf16", 2, 16, 4, 256, 256, True, "bf16", 74)
     sdpa_case("sdpa_b4_gqa32x8_s4096_d128_causal_bf16", 4, 32, 8, 4096, 128, True, "bf16", 75)
+    cool_down()
     gemm_case("c4_gemm_ffn_up_fp16", 4096, 14336, 4096, "fp16", "normal64", 3, 10)
     cool_down()
     ffn_swiglu_case("c4_ffn_up_swiglu_fused_fp16", 4096, 14336, 4096, "fp16", 10)
