@@ -475,6 +475,15 @@ RK_API void rk_norm_backward_set_ctas_per_sm(int ctas_per_sm);
  * split-K); 0 restores the built-in choice.  Process-wide. */
 RK_API void rk_gemv_tc_set_cluster(int cluster_size);
 
+/* Tuning hook for RK_GEMV_TC's cluster split-K: how the cluster's partial sums reach its
+ * leader CTA -- 1 pulled (parked in each CTA's own ring, read by the leader through
+ * distributed shared memory; two CTAs per SM), 2 pushed (stored straight into a receive
+ * area of the leader's shared memory; one CTA per SM, an 8-stage ring, clusters of at most
+ * 4); 0 restores the built-in choice (pushed when every cluster of the grid is resident at
+ * once and the grid is no narrower).  For a given cluster size both forms add the same
+ * partial sums in the same order.  Process-wide. */
+RK_API void rk_gemv_tc_set_exchange(int mode);
+
 /* Sets the per-wait time limit (nanoseconds, default 1e9) used by kernels
  * launched after the call.  0 restores the default. */
 RK_API void rk_set_wait_timeout_ns(uint64_t ns);

@@ -10,16 +10,20 @@
 // Formulation (operands swapped so the tiny M becomes the UMMA N dimension):
 //   D[128 rows of W, MN] += W_tile[128, 64] (A, K-major) * x_tile[MN, 64]^T (B, K-major)
 // with MN = M rounded up to 16 or 32; x rows >= M are zero-filled by TMA.
-//   * warp 0: TMA producer -- a 5-stage ring of {W 128x64 (16 KiB), x MNx64} boxes,
+//   * warp 0: TMA producer -- a 6- or 8-stage ring of {W 128x64 (16 KiB), x MNx64} boxes,
 //     128-byte swizzle, completion on mbarriers;
 //   * warp 1: TMEM allocation (32 columns) and one thread issuing tcgen05.mma
 //     (M=128, N=MN, K=16), tcgen05.commit releases ring slots;
 //   * warps 2..5: epilogue, tcgen05.ld of the 128 x MN fp32 accumulator.
 // Split-K over a thread-block cluster of C CTAs (C = 1..8, one cluster per 128-row
-// tile, CTA rank r owns K blocks [r*KB/C, (r+1)*KB/C)): non-leader CTAs park their
-// partial accumulator in their own (now idle) ring memory and signal the leader's
-// mbarrier remotely; the leader reads the partials through distributed shared memory
-// (ld.shared::cluster) in rank order, adds them to its own, rounds once, and stores.
+// tile, CTA rank r owns K blocks [r*KB/C, (r+1)*KB/C)): the non-leader CTAs hand their
+// partial accumulators to the leader, which adds them to its own in rank order, rounds
+// once, and stores.  The hand-over is either pulled (a non-leader parks its partial in
+// its own idle ring and signals the leader's mbarrier remotely; the leader reads it
+// through distributed shared memory, ld.shared::cluster) or, for grids of at most one
+// CTA per SM, pushed (non-leaders store straight into a receive area of the leader's
+// shared memory, st.shared::cluster, and signal; the leader reads locally and its ring
+// is 8 stages deep).  Same additions in the same order either way.
 // Deterministic, no global workspace.  Every wait is bounded; the only unbounded
 // waits are the two cluster barriers every thread reaches unconditionally (after
 // barrier initialisation and before exit, so no CTA leaves while its shared memory
@@ -43,6 +47,8 @@ namespace rk {
 // Tuning override of the split-K strategy: 0 = automatic, 1/2/4/8 = cluster size,
 // -1 = stream-K through the workspace whenever one is supplied.
 static std::atomic<int> g_gemv_tc_cluster{0};
+// Tuning override of the cluster exchange: 0 = automatic, 1 = pulled, 2 = pushed.
+static std::atomic<int> g_gemv_tc_exchange{0};
 
 namespace gtc {
 
@@ -51,34 +57,48 @@ constexpr int BK = 64;
 constexpr int UMMA_K = 16;
 constexpr int W_STAGE = BM * BK * 2;  // 16 KiB
 constexpr int THREADS = 192;
-constexpr int STAGES = 6;
+constexpr int STAGES = 6;       // ring depth of the pulled exchange (two CTAs per SM)
+constexpr int PUSH_STAGES = 8;  // ring depth of the pushed exchange (one CTA per SM)
 constexpr int TMEM_COLS = 32;
 constexpr int MAX_CLUSTER = 8;
+constexpr int PUSH_MAX_CLUSTER = 4;
 
-template <int MN>
+// Two ways to combine a cluster's partial sums (the sum is the same, in the same order):
+//  * pulled -- each non-leader parks its partial in its own idle ring and arrives on the
+//    leader's barrier; the leader reads the partials through DSMEM.  No extra shared
+//    memory, so two 6-stage CTAs fit an SM.
+//  * pushed -- each non-leader stores its partial straight into a receive area of the
+//    leader's shared memory (st.shared::cluster) and arrives; the leader reads them
+//    locally.  The DSMEM round trips leave the leader's critical path, at the cost of
+//    (cluster - 1) partial tiles of shared memory, so one CTA per SM -- which also
+//    leaves room for an 8-stage ring.
+template <int MN, bool PUSH>
 struct Cfg {
+  static constexpr int NST = PUSH ? PUSH_STAGES : STAGES;
   static constexpr int X_STAGE = MN * BK * 2;
   static constexpr int STAGE = W_STAGE + X_STAGE;  // multiple of 1024
-  static constexpr int RING = STAGES * STAGE;
+  static constexpr int RING = NST * STAGE;
   static constexpr int SLOT = BM * MN * 4;  // one fp32 partial tile
+  static constexpr int RECV = PUSH ? (PUSH_MAX_CLUSTER - 1) * SLOT : 0;
   static_assert(STAGE % 1024 == 0, "stage bases stay 1024-byte aligned");
   static_assert(SLOT <= RING, "the partial tile is parked in the idle ring");
 };
 
+template <int NST>
 struct __align__(8) Bars {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[NST];
+  uint64_t empty[NST];
   uint64_t tmem_full;
   uint64_t drain;
   uint64_t partials;  // leader: one remote arrival per non-leader CTA
   uint32_t tmem_base;
   int abort;
-  int last;  // workspace split-K: this CTA is the last of its tile to finish
 };
 
-template <int MN>
+template <int MN, bool PUSH>
 constexpr int smem_bytes() {
-  return 1024 + Cfg<MN>::RING + int(sizeof(Bars));
+  using C = Cfg<MN, PUSH>;
+  return 1024 + C::RING + C::RECV + int(sizeof(Bars<C::NST>));
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() { return cluster_ctarank(); }
@@ -114,16 +134,22 @@ __device__ __forceinline__ void tmem_ld_cols<32>(uint32_t taddr, uint32_t (&r)[3
   tmem_ld_32x32b_x32(taddr, r);
 }
 
-template <typename T, int MN>
-__global__ void __launch_bounds__(THREADS, 2)
+template <typename T, int MN, bool PUSH>
+__global__ void __launch_bounds__(THREADS, PUSH ? 1 : 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x, T* __restrict__ out, int M, int N,
                    int K, int csize, KernelCtl ctl) {
-  using C = Cfg<MN>;
+  using C = Cfg<MN, PUSH>;
+  constexpr int NST = C::NST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(ring + C::RING);
+  float* recv = reinterpret_cast<float*>(ring + C::RING);  // pushed exchange only
+  auto* bars = reinterpret_cast<Bars<NST>*>(ring + C::RING + C::RECV);
+  if (PUSH && csize > PUSH_MAX_CLUSTER) {  // the receive area holds PUSH_MAX_CLUSTER - 1 slots
+    if (threadIdx.x == 0) atomicOr(ctl.status, RK_DEV_ERR_BAD_INDEX);
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const int tile = blockIdx.x / csize;
@@ -133,17 +159,23 @@ __global__ void __launch_bounds__(THREADS, 2)
   volatile int* abort_flag = &bars->abort;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(smem_u32(&bars->full[s]), 1);
       mbar_init(smem_u32(&bars->empty[s]), 1);
     }
     mbar_init(smem_u32(&bars->tmem_full), 1);
     mbar_init(smem_u32(&bars->drain), 1);
-    mbar_init(smem_u32(&bars->partials), csize > 1 ? csize - 1 : 1);
+    // Pulled: one arrival per non-leader CTA.  Pushed: one per epilogue thread of each
+    // non-leader, each releasing its own stores into the receive area.
+    mbar_init(smem_u32(&bars->partials), csize > 1 ? (PUSH ? 128 : 1) * (csize - 1) : 1);
     bars->abort = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_x);
+    // Warm L2 with the weight boxes of this CTA's first ring fill while the previous kernel
+    // of the stream drains (before the dependency wait: a prefetch has no result).  Only
+    // the weight: x is what the previous kernel typically produces.
+    for (int kb = kb0; kb < kb1 && kb < kb0 + NST; ++kb) tma_prefetch_l2_2d(&tmap_w, kb * BK, tile * BM);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(&bars->tmem_base), TMEM_COLS);
@@ -176,7 +208,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         tma_load_2d(smem_u32(base + W_STAGE), &tmap_x, full, kb * BK, 0);
         issued |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == STAGES) {
+        if (++stage == NST) {
           stage = 0;
           phase ^= 1;
         }
@@ -186,7 +218,7 @@ __global__ void __launch_bounds__(THREADS, 2)
         atomicOr(ctl.status, RK_DEV_ERR_TIMEOUT_PRODUCER);
       }
       int never = 0;
-      for (int s = 0; s < STAGES; ++s)
+      for (int s = 0; s < NST; ++s)
         if ((issued >> s) & 1u)
           if (!mbar_wait_bounded(smem_u32(&bars->full[s]), (issued_parity >> s) & 1u,
                                  ctl.timeout_ns, &never))
@@ -215,7 +247,7 @@ __global__ void __launch_bounds__(THREADS, 2)
           tc_mma_f16(tmem_base, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
         }
         tc_commit(smem_u32(&bars->empty[stage]));
-        if (++stage == STAGES) {
+        if (++stage == NST) {
           stage = 0;
           phase ^= 1;
         }
@@ -253,23 +285,32 @@ __global__ void __launch_bounds__(THREADS, 2)
     float* slot = reinterpret_cast<float*>(ring);  // the ring is idle once tmem_full fired
     cluster_wait();  // every CTA of the cluster has initialised its barriers
     if (rank != 0) {
-      if (ok) {
-        // The async proxy (TMA, MMA) is done with the ring; order our generic writes after it.
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      if constexpr (PUSH) {
+        // Into the leader's receive area, slot rank - 1 (zeros if this CTA failed: the
+        // leader still gets every slot and the status word carries the error).
+        const uint32_t dst = map_to_rank(smem_u32(recv + (rank - 1) * (BM * MN) + row_local * MN), 0);
 #pragma unroll
-        for (int j = 0; j < MN; j += 4)
-          *reinterpret_cast<float4*>(slot + row_local * MN + j) =
-              make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-      }
-      epilogue_bar_sync();
-      if (warp == 2 && lane == 0) {
-        asm volatile("fence.acq_rel.cluster;" ::: "memory");
-        remote_arrive(map_to_rank(smem_u32(&bars->partials), 0));
+        for (int j = 0; j < MN; j += 4) st_cluster_v4(dst + j * 4, acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        remote_arrive(map_to_rank(smem_u32(&bars->partials), 0));  // release.cluster: after the stores
+      } else {
+        if (ok) {
+          // The async proxy (TMA, MMA) is done with the ring; order our generic writes after it.
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+#pragma unroll
+          for (int j = 0; j < MN; j += 4)
+            *reinterpret_cast<float4*>(slot + row_local * MN + j) =
+                make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        }
+        epilogue_bar_sync();
+        if (warp == 2 && lane == 0) {
+          asm volatile("fence.acq_rel.cluster;" ::: "memory");
+          remote_arrive(map_to_rank(smem_u32(&bars->partials), 0));
+        }
       }
     } else {
       if (csize > 1) {
         bool ready = false;
-        if (ok) {
+        if (PUSH || ok) {
           const uint64_t t0 = globaltimer_ns();
           for (uint32_t it = 0;; ++it) {
             if (try_wait_cluster(smem_u32(&bars->partials), 0)) {
@@ -281,16 +322,30 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
         ready = __all_sync(0xffffffffu, ready);
         if (ready) {
-          const uint32_t mine = smem_u32(slot + row_local * MN);
-          for (int c = 1; c < csize; ++c) {
-            const uint32_t remote = map_to_rank(mine, static_cast<uint32_t>(c));
+          if constexpr (PUSH) {
+            const float* mine = recv + row_local * MN;
+            for (int c = 1; c < csize; ++c) {
 #pragma unroll
-            for (int j = 0; j < MN; j += 4) {
-              const float4 v = ld_cluster_v4(remote + j * 4);
-              acc[j] += v.x;
-              acc[j + 1] += v.y;
-              acc[j + 2] += v.z;
-              acc[j + 3] += v.w;
+              for (int j = 0; j < MN; j += 4) {
+                const float4 v = *reinterpret_cast<const float4*>(mine + (c - 1) * (BM * MN) + j);
+                acc[j] += v.x;
+                acc[j + 1] += v.y;
+                acc[j + 2] += v.z;
+                acc[j + 3] += v.w;
+              }
+            }
+          } else {
+            const uint32_t mine = smem_u32(slot + row_local * MN);
+            for (int c = 1; c < csize; ++c) {
+              const uint32_t remote = map_to_rank(mine, static_cast<uint32_t>(c));
+#pragma unroll
+              for (int j = 0; j < MN; j += 4) {
+                const float4 v = ld_cluster_v4(remote + j * 4);
+                acc[j] += v.x;
+                acc[j + 1] += v.y;
+                acc[j + 2] += v.z;
+                acc[j + 3] += v.w;
+              }
             }
           }
         } else if (lane == 0) {
@@ -313,7 +368,9 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
   tc_fence_before();
   __syncthreads();
-  // No CTA leaves while the leader may still read its parked partial.
+  // No CTA leaves while another may still touch its shared memory: the leader reading a
+  // parked partial (pulled), or a partial still landing in the leader's receive area
+  // (pushed: the stores are released before each non-leader's arrival here).
   cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
@@ -663,27 +720,67 @@ size_t workspace_bytes_for(int64_t M, int64_t N, int64_t K) {
   return g_gemv_tc_cluster.load() == -1 && sk_fits(N) ? sk_workspace_bytes(M, N, K) : 0;
 }
 
+// Clusters of `csize` CTAs of the pushed-exchange kernel that can be resident at once
+// (cudaOccupancyMaxActiveClusters; one CTA per SM, clusters confined to a GPC), per device.
+// The kernel's shared-memory attribute must be set before the first query.
+template <typename T, int MN>
+int push_capacity(int dev, int csize) {
+  static std::once_flag once[64][2];
+  static int capacity[64][2];
+  const int slot = csize == 2 ? 0 : 1;
+  std::call_once(once[dev & 63][slot], [&] {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(csize) * 64u);
+    cfg.blockDim = dim3(gtc::THREADS);
+    cfg.dynamicSmemBytes = gtc::smem_bytes<MN, true>();
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(csize);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gtc::gemv_tc_kernel<T, MN, true>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    capacity[dev & 63][slot] = n;
+  });
+  return capacity[dev & 63][slot];
+}
+
 template <typename T, int MN>
 rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int64_t N, int64_t K,
                          rk_dtype dt, cudaStream_t s, int csize_override, void* workspace,
                          size_t workspace_bytes, bool stream_k) {
   CUtensorMap tw, tx;
-  rk_status st = make_tmap_2d(&tw, W, dt, K, N, 64, gtc::BM);
-  if (st != RK_OK) return st;
-  st = make_tmap_2d(&tx, x, dt, K, M, 64, MN);
+  rk_status st = make_tmap_2d(&tx, x, dt, K, M, 64, MN);
   if (st != RK_OK) return st;
   LaunchCtl lc;
   if ((st = launch_ctl(&lc)) != RK_OK) return st;
   KernelCtl ctl{lc.status, lc.timeout_ns, 0};
 
-  constexpr int smem = gtc::smem_bytes<MN>();
+  constexpr int smem = gtc::smem_bytes<MN, false>();
+  constexpr int smem_push = gtc::smem_bytes<MN, true>();
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [&] {
-    attr_err[dev & 63] = cudaFuncSetAttribute(gtc::gemv_tc_kernel<T, MN>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(gtc::gemv_tc_kernel<T, MN, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gtc::gemv_tc_kernel<T, MN, true>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem_push);
+    // All of the SM's unified memory as shared memory: two pulled CTAs per SM.
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gtc::gemv_tc_kernel<T, MN, false>,
+                               cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gtc::gemv_tc_kernel<T, MN, true>,
+                               cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    attr_err[dev & 63] = e;
   });
   if (attr_err[dev & 63] != cudaSuccess) return cuda_status(attr_err[dev & 63]);
 
@@ -703,6 +800,7 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, sk_smem);
     });
     if (sk_err[dev & 63] != cudaSuccess) return cuda_status(sk_err[dev & 63]);
+    if ((st = make_tmap_2d(&tw, W, dt, K, N, 64, gtc::BM)) != RK_OK) return st;
     int* ticket = static_cast<int*>(workspace);
     float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + sk_ticket_bytes(N));
     const cudaError_t e = launch_kernel(gtc::gemv_tc_sk_kernel<T, MN>, dim3(sk_ctas),
@@ -712,23 +810,23 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
     note_launch("gemv_tc_sk_kernel");
     return cuda_status(e);
   }
-  // Split K over a thread-block cluster, reduced through DSMEM: the largest cluster of
-  // at most 4 CTAs (8-CTA clusters measured slower) keeping the grid within two CTAs per SM.
+  // Split K over a thread-block cluster, reduced through DSMEM.
   int csize = csize_override;
   if (csize <= 0) {
     // Measured on B200: 8-CTA clusters only pay off for very short weights (<= 12 row
-    // tiles); otherwise the largest of 1/2/4 keeping the grid within one wave of the CTAs
-    // that fit an SM -- two with 16-wide accumulators, one with 32-wide ones (124 KiB of
-    // shared memory each): at M = 17..32, N = 8192 clusters of 4 would launch a second
-    // wave (36.5 us) where clusters of 2 take 28.5 us.
+    // tiles); otherwise the largest of 1/2/4 keeping the grid within one wave of the pulled
+    // CTAs that fit an SM -- two with 16-wide accumulators (109 KiB of shared memory each),
+    // one with 32-wide ones (124 KiB): at M = 17..32, N = 8192 clusters of 4 would launch
+    // a second wave (36.5 us) where clusters of 2 take 28.5 us.
     static std::once_flag occ_once[64];
     static int occ[64];
     std::call_once(occ_once[dev & 63], [&] {
-      int n = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gtc::gemv_tc_kernel<T, MN>, gtc::THREADS,
-                                                        smem) != cudaSuccess || n < 1)
-        n = 1;
-      occ[dev & 63] = n > 2 ? 2 : n;
+      // Shared memory is what binds: the SM's over the CTA's plus its reservation.
+      int per_sm = 0, reserved = 0;
+      cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev);
+      const int n = per_sm / (smem + reserved);
+      occ[dev & 63] = n < 1 ? 1 : (n > 2 ? 2 : n);
     });
     const int64_t target = static_cast<int64_t>(occ[dev & 63]) * device_sm_count();
     const int cap = tiles <= 12 ? 8 : 4;
@@ -738,11 +836,40 @@ rk_status launch_gemv_tc(const void* x, const void* W, void* out, int64_t M, int
   if (csize > gtc::MAX_CLUSTER) csize = gtc::MAX_CLUSTER;
   while (csize > 1 && csize > num_kb) csize /= 2;
 
-  const cudaError_t e = launch_kernel(gtc::gemv_tc_kernel<T, MN>, dim3(static_cast<unsigned>(tiles * csize)),
-                                      dim3(gtc::THREADS), smem, s, csize, tw, tx,
-                                      static_cast<T*>(out), static_cast<int>(M),
-                                      static_cast<int>(N), static_cast<int>(K), csize, ctl);
-  note_launch("gemv_tc_kernel");
+  // Pushed exchange where every cluster of the grid is resident at once at one CTA per SM
+  // and the grid is no narrower than the pulled one: clusters of 2 or 4 (of the largest
+  // size that fits, when the size is automatic).  Measured on B200: [4096 x 14336] at
+  // M = 4 takes 23.3 us pushed against 24.4 us pulled (clusters of 4 either way), and
+  // shortening the row tiles to spread the weight over all 37 resident clusters instead
+  // of 32 gains nothing (DRAM, not the SM count, bounds the stream).
+  const int mode = g_gemv_tc_exchange.load();
+  bool push = false;
+  if (mode != 1 && csize > 1) {
+    const bool automatic = csize_override <= 0;
+    for (int c = automatic ? gtc::PUSH_MAX_CLUSTER : csize; c >= 2 && c >= csize; c /= 2) {
+      if (c > gtc::PUSH_MAX_CLUSTER || c > num_kb) continue;
+      const int resident = push_capacity<T, MN>(dev, c);
+      if (mode == 2 || tiles <= resident) {
+        csize = c;
+        push = true;
+        break;
+      }
+    }
+  }
+  if ((st = make_tmap_2d(&tw, W, dt, K, N, 64, gtc::BM)) != RK_OK) return st;
+  const unsigned grid = static_cast<unsigned>(tiles * csize);
+  cudaError_t e;
+  if (push) {
+    e = launch_kernel(gtc::gemv_tc_kernel<T, MN, true>, dim3(grid), dim3(gtc::THREADS), smem_push, s,
+                      csize, tw, tx, static_cast<T*>(out), static_cast<int>(M), static_cast<int>(N),
+                      static_cast<int>(K), csize, ctl);
+    note_launch("gemv_tc_kernel<push>");
+  } else {
+    e = launch_kernel(gtc::gemv_tc_kernel<T, MN, false>, dim3(grid), dim3(gtc::THREADS), smem, s,
+                      csize, tw, tx, static_cast<T*>(out), static_cast<int>(M), static_cast<int>(N),
+                      static_cast<int>(K), csize, ctl);
+    note_launch("gemv_tc_kernel");
+  }
   return cuda_status(e);
 }
 
@@ -752,6 +879,7 @@ size_t gemv_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) { return workspa
 size_t gemv_tc_stream_k_bytes(int64_t M, int64_t N, int64_t K) { return sk_workspace_bytes(M, N, K); }
 
 void gemv_tc_set_cluster(int c) { g_gemv_tc_cluster.store(c); }
+void gemv_tc_set_exchange(int mode) { g_gemv_tc_exchange.store(mode == 1 || mode == 2 ? mode : 0); }
 
 bool gemv_tc_supported(const void* x, const void* W, const void* out, int64_t M, int64_t N,
                        int64_t K) {

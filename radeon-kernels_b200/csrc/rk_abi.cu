@@ -15,6 +15,7 @@ namespace rk {
 void gemv_set_tuning(int rows, int ks);
 void gemm_set_tile_n(int bn);
 void gemv_tc_set_cluster(int c);
+void gemv_tc_set_exchange(int mode);
 }
 
 // One status word per device: kernels atomicOr RK_DEV_ERR_* bits into it when
@@ -173,6 +174,7 @@ void rk_gemv_set_tuning(int rows, int ksplit) { rk::gemv_set_tuning(rows, ksplit
 void rk_gemm_set_tile_n(int tile_n) { rk::gemm_set_tile_n(tile_n); }
 
 void rk_gemv_tc_set_cluster(int cluster_size) { rk::gemv_tc_set_cluster(cluster_size); }
+void rk_gemv_tc_set_exchange(int mode) { rk::gemv_tc_set_exchange(mode); }
 
 void rk_norm_set_threads(int threads_per_row) { rk::norm_set_threads(threads_per_row); }
 

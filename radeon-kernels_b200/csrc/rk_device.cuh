@@ -120,6 +120,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// Prefetch of a 2-D box into L2 (no shared-memory destination, no completion).  It has no
+// result, and L2 is coherent with every writer, so a kernel may issue it before its grid
+// dependency wait (pdl_begin) to overlap DRAM latency with the previous kernel's tail.
+// Same 16-byte rule on c0 as tma_load_2d.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 // 3-D form (c0 innermost, same 16-byte rule); out-of-range rows of a 3-D map read as zero
 // without spilling into the next matrix of the stack.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0,
@@ -334,6 +345,13 @@ __device__ __forceinline__ float4 ld_cluster_v4(uint32_t cluster_addr) {
                : "r"(cluster_addr)
                : "memory");
   return v;
+}
+
+// Stores into another CTA's shared memory (a shared::cluster address from map_to_rank).
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
 }
 
 __device__ __forceinline__ float ld_cluster_f32(uint32_t cluster_addr) {

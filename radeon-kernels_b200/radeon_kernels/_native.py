@@ -135,6 +135,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_gemm_set_tile_n.restype = None
     lib.rk_gemv_tc_set_cluster.argtypes = [cint]
     lib.rk_gemv_tc_set_cluster.restype = None
+    lib.rk_gemv_tc_set_exchange.argtypes = [cint]
+    lib.rk_gemv_tc_set_exchange.restype = None
     lib.rk_norm_set_threads.argtypes = [cint]
     lib.rk_norm_set_threads.restype = None
     lib.rk_set_programmatic_launch.argtypes = [cint]

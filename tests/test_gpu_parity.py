@@ -7,6 +7,8 @@ reference's own rounded output on every element not dominated by cancellation.
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -342,6 +344,44 @@ def test_gemv_tensor_core_cluster_split_k(cluster, m):
         lib.rk_gemv_tc_set_cluster(0)
     assert _guards_intact(buf)
     oracle.assert_parity(to_bits(out), o_bits, o32, "fp16")
+
+
+@pytest.mark.parametrize("m", [1, 5, 16, 17, 32])
+@pytest.mark.parametrize("n, k, cluster", [(1000, 4104, 2), (1000, 4104, 4), (4096, 14336, 0)])
+def test_gemv_tensor_core_pushed_and_pulled_exchange_agree(m, n, k, cluster):
+    """The cluster's partial sums reach the leader pulled (read through DSMEM) or pushed
+    (stored into its receive area): the same additions in the same order, so the outputs
+    agree bit for bit, and with the oracle.  cluster 0 is the automatic size (BASELINE
+    config 3's weight, where the automatic exchange is the pushed one when every cluster
+    of the grid fits at once)."""
+
+    import torch
+
+    gen = torch.Generator().manual_seed(17 + m + n)
+    x = seeded((m, k), 17, "normal", "bf16", gen)
+    w = seeded((n, k), 17, f"normal/{k}", "bf16", gen)
+    o_bits, o32 = oracle.gemv(to_bits(x), to_bits(w), "bf16")
+    lib = _native.library()
+    lib.rk_debug_last_kernel.restype = ctypes.c_char_p
+    outs, names = [], []
+    lib.rk_gemv_tc_set_cluster(cluster)
+    try:
+        for exchange in (1, 2, 0):
+            lib.rk_gemv_tc_set_exchange(exchange)
+            buf, out = _guarded(torch, m, n, "bf16")
+            assert abi_gemv(x.cuda(), w.cuda(), out, GEMV["tc"], "bf16") == _native.RK_OK
+            names.append(lib.rk_debug_last_kernel().decode())
+            torch.cuda.synchronize()
+            assert device_status() == _native.RK_OK
+            assert _guards_intact(buf)
+            outs.append(out)
+    finally:
+        lib.rk_gemv_tc_set_exchange(0)
+        lib.rk_gemv_tc_set_cluster(0)
+    assert names[:2] == ["gemv_tc_kernel", "gemv_tc_kernel<push>"], names
+    for other in outs[1:]:
+        assert torch.equal(outs[0].view(torch.int16), other.view(torch.int16))
+    oracle.assert_parity(to_bits(outs[1]), o_bits, o32, "bf16")
 
 
 @pytest.mark.parametrize("m", [3, 5, 16, 17, 32])
