@@ -157,12 +157,6 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   constexpr int LOGV = Log2<V>::value;
   extern __shared__ float red[];  // [KS][rows_max][MB]
 
-  pdl_begin();
-  uint32_t epoch = 0;
-  if constexpr (PEER) {
-    epoch = peer_call_epoch(peer);
-    if (blockIdx.x == 0 && threadIdx.x == 0) peer_announce(peer, epoch);
-  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp / KS, ks = warp % KS;
   const int cta = blockIdx.x;
@@ -171,6 +165,22 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   const int KV = K >> 3;  // 16-byte vectors per row
   const int v0 = static_cast<int>(static_cast<int64_t>(KV) * ks / KS);
   const int v1 = static_cast<int>(static_cast<int64_t>(KV) * (ks + 1) / KS);
+  // Warm L2 with this warp's first step of weight loads (ROWS rows x up to 32 x UNROLL
+  // vectors) while the previous kernel of the stream drains: a prefetch has no result and
+  // L2 is coherent, so it may precede the dependency wait.  The weight only.
+  if (lane < ROWS && rg * ROWS + lane < rows && v1 > v0) {
+    const int row = row_begin + rg * ROWS + lane;
+    const int vecs = min(v1 - v0, 32 * UNROLL);
+    prefetch_l2_bulk(W + static_cast<size_t>(row) * K + static_cast<size_t>(v0) * 8,
+                     static_cast<uint32_t>(vecs) * 16u);
+  }
+
+  pdl_begin();
+  uint32_t epoch = 0;
+  if constexpr (PEER) {
+    epoch = peer_call_epoch(peer);
+    if (blockIdx.x == 0 && threadIdx.x == 0) peer_announce(peer, epoch);
+  }
   const uint4* xrow = reinterpret_cast<const uint4*>(x);
 
   // Row chunks of ROWS rows are dealt to the RG row groups round-robin.

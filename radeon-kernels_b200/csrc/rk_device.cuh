@@ -131,6 +131,14 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t c0,
                : "memory");
 }
 
+// Untiled form: `bytes` (a multiple of 16) from `p` (16-byte aligned) into L2; same
+// reasoning as tma_prefetch_l2_2d for issuing it before pdl_begin.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p)),
+               "r"(bytes)
+               : "memory");
+}
+
 // 3-D form (c0 innermost, same 16-byte rule); out-of-range rows of a 3-D map read as zero
 // without spilling into the next matrix of the stack.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int32_t c0,
