@@ -218,6 +218,7 @@ def time_loop(fn, steps: int, stream) -> float:
 
 
 L2_BYTES = 126 * 1024 * 1024
+DRAM_INTERFACE_GBS = 8161.3  # ncu: 2048 B per DRAM cycle at 3.985 GHz (B200)
 HEAD_M, HEAD_N, HEAD_K = 1, 8192, 8192
 
 
@@ -368,6 +369,19 @@ def headline(args, dist: Dist, ext, peaks, peak_kind):
         compute = {"us_per_step": round(c_ms * 1e3 / steps, 3),
                    "what": "rk_gemv over the rank's row block alone (no exchange), same rotation"}
 
+    # Context for the roofline: one launch with nothing before it to overlap, so the L2
+    # prefetch each CTA issues before its dependency wait hides nothing.  The L2 flush
+    # (two 256 MiB writes, ~80 us of device time) is still running when the events and the
+    # launch are enqueued, so no host launch latency falls between the events.
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    isolated = []
+    for i in range(21):
+        flush.zero_()
+        flush.zero_()
+        isolated.append(time_loop(lambda j: compute_only(i), 1, stream))
+    del flush
+    torch.cuda.synchronize()
+
     bytes_step = gemv_bytes(m, HEAD_N, k)  # the whole logical problem, per step
     # Per-rank algorithmic HBM bytes of one launch: the weight block and x read, the full
     # output written into this rank's memory (its own block and every peer's).
@@ -387,6 +401,17 @@ def headline(args, dist: Dist, ext, peaks, peak_kind):
             "peak_source": peak_kind,
             "kernel": "gemv_stream_kernel" + ("<PEER> (rk_gemv_allgather)" if exchange is not None else " (rk_gemv)"),
             "bytes_per_launch": rank_bytes,
+            "isolated_launch": {
+                "us": round(statistics.median(isolated) * 1e3, 2),
+                "gbs": round(gemv_bytes(m, rows, k) / (statistics.median(isolated) / 1e3) / 1e9, 1),
+                "what": "rk_gemv of the rank's weight block alone, L2 flushed before it, median of 21",
+            },
+            "dram_interface": {
+                "gbs": DRAM_INTERFACE_GBS,
+                "frac": round(achieved / DRAM_INTERFACE_GBS, 4),
+                "what": "ncu dram__bytes.sum.peak_sustained (2048 B/cycle) x dram__cycles_elapsed.avg.per_second "
+                        "(3.985 GHz) on B200; the measured peak above is a copy (reads and writes)",
+            },
         },
         "bytes_per_step": bytes_step,
         "weight_sets_per_rank": len(weights),
