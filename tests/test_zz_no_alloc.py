@@ -66,7 +66,8 @@ def test_fixed_scratch_matches_the_oracle_and_the_workspace_entry_point(dtype, m
         m, n, k, code, _native.GEMV_VARIANTS["tc"], ctypes.c_void_p(workspace.data_ptr()), need.value, _stream(),
     )
     assert st == _native.RK_OK, _native.status_text(st)
-    assert lib.rk_debug_last_kernel() == b"gemv_tc_kernel"
+    # Cluster split-K, in either exchange form (pulled, or pushed into the leader CTA).
+    assert lib.rk_debug_last_kernel() in (b"gemv_tc_kernel", b"gemv_tc_kernel<push>")
 
     if dirty:
         assert lib.rk_debug_fill_fixed_scratch(0xA7, _stream()) == _native.RK_OK
