@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     __syncthreads();
     if (threadIdx.x == 0) {
       __threadfence_system();  // every peer store of this CTA, before the arrival flags
-      for (int j = 0; j < peer.world; ++j) st_release_sys(&peer.ctl[j]->arrive[peer.rank], epoch);
+      peer_publish_arrival(peer, epoch);
       if (!peer_wait_all(peer.ctl[peer.rank]->arrive, peer.world, epoch, peer.timeout_ns))
         atomicOr(peer.status, RK_DEV_ERR_TIMEOUT_PEER);
       *reinterpret_cast<volatile uint32_t*>(&peer.ctl[peer.rank]->epoch) = epoch;

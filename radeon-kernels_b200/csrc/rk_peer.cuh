@@ -61,8 +61,15 @@ struct PeerOut {
   uint32_t* status;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Relaxed system-scope store: after a fence it forms the release pattern (fence, then a
+// morally strong store), so the ranks' flags go out back to back instead of each waiting
+// for the previous remote store to be acknowledged, as a release store per flag would.
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
@@ -83,10 +90,21 @@ __device__ __forceinline__ uint32_t peer_call_epoch(const PeerOut<T>& p) {
   return ld_relaxed_gpu(&p.ctl[p.rank]->epoch) + 1u;
 }
 
-// Tells every rank that this rank's call `e` has started (one thread).
+// Tells every rank that this rank's call `e` has started (one thread): one fence, then the
+// flags.  Nothing of this call precedes it that the others read; what the flag stands for --
+// every earlier reader of this rank's output has finished -- holds before the kernel passed
+// its dependency wait.
 template <typename T>
 __device__ __forceinline__ void peer_announce(const PeerOut<T>& p, uint32_t e) {
-  for (int j = 0; j < p.world; ++j) st_release_sys(&p.ctl[j]->ready[p.rank], e);
+  fence_acq_rel_sys();
+  for (int j = 0; j < p.world; ++j) st_relaxed_sys(&p.ctl[j]->ready[p.rank], e);
+}
+
+// Publishes this rank's arrival for call `e` to every rank (one thread, after a system-scope
+// fence that follows every store of the call into the peers' outputs).
+template <typename T>
+__device__ __forceinline__ void peer_publish_arrival(const PeerOut<T>& p, uint32_t e) {
+  for (int j = 0; j < p.world; ++j) st_relaxed_sys(&p.ctl[j]->arrive[p.rank], e);
 }
 
 // Bounded wait until flags[j] has reached `e` for every rank j < world (one thread).
@@ -124,7 +142,7 @@ __device__ __forceinline__ void peer_finish(const PeerOut<T>& p, uint32_t e, uin
   if (before != grid_ctas - 1u) return;
   __threadfence_system();  // acquire side of the count: every CTA's stores precede the flags
   mine->done_ctas = 0u;    // the next call starts after this kernel completes
-  for (int j = 0; j < p.world; ++j) st_release_sys(&p.ctl[j]->arrive[p.rank], e);
+  peer_publish_arrival(p, e);
   if (!peer_wait_all(mine->arrive, p.world, e, p.timeout_ns)) atomicOr(p.status, RK_DEV_ERR_TIMEOUT_PEER);
   *reinterpret_cast<volatile uint32_t*>(&mine->epoch) = e;
 }
