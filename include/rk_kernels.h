@@ -236,13 +236,21 @@ RK_API rk_status rk_ipc_close(const rk_ipc_handle* handle);
  * out = x @ weight^T with the weight split by rows: weight_block holds rows
  * [rank*N_block, (rank+1)*N_block) of the [world*N_block, K] weight; x [M, K] is the same
  * on every rank.  The 128-bit streaming kernel of RK_GEMV_STREAM (identical results to
- * rk_gemv with that variant on the unsplit weight) stores each output element into every
- * rank's out[j] [M, world*N_block].  1 <= M <= 32; K % 8 == 0 and 16-byte-aligned x and
- * weight (RK_ERR_UNSUPPORTED otherwise).
+ * rk_gemv with that variant on the unsplit weight) computes the rank's block, and every
+ * rank's out[j] [M, world*N_block] receives it.  The block crosses NVLink as 8-byte packets
+ * that carry the call number, written into a staging area that follows each rank's control
+ * block, so no fence or flag round trip is paid per call: ctl[j] must span
+ * rk_gemv_allgather_ctl_bytes(M, N_block, world) bytes, zeroed before the first call.
+ * 1 <= M <= 32; K % 8 == 0 and 16-byte-aligned x and weight (RK_ERR_UNSUPPORTED otherwise).
  */
 RK_API rk_status rk_gemv_allgather(const void* x, const void* weight_block, int64_t M,
                                    int64_t N_block, int64_t K, rk_dtype dt,
                                    const rk_peer_group* group, rk_stream_t stream);
+
+/* Bytes of the control area each rank needs for rk_gemv_allgather with these sizes: the
+ * RK_PEER_CTL_BYTES control block followed by the packet staging area (2 x world x M x
+ * N_block packets of 8 bytes).  No counterpart in the reference. */
+RK_API rk_status rk_gemv_allgather_ctl_bytes(int64_t M, int64_t N_block, int32_t world, size_t* bytes);
 
 /*
  * C = A @ B with B split by columns: B_block is [K, N_block] (columns [rank*N_block,

@@ -240,59 +240,68 @@ __global__ void __launch_bounds__(GEMV_THREADS)
   }
   __syncthreads();
   if constexpr (PEER) {
-    // Every CTA stores its rows into this rank's own full output only; the last CTA of
-    // the grid (grid-wide count, GPU-scope fences) then pushes the rank's whole column
-    // block to every peer with 16-byte stores and runs the arrival round alone, so one
-    // CTA pays the system-scope fence and the NVLink round trip instead of every CTA.
-    T* const mine = peer.out[peer.rank];
+    // Every CTA stores its rows into this rank's own full output and sends them to every
+    // other rank as packets {value bits, call number} in that rank's staging slot of this
+    // call's parity (rk_peer.cuh); then it polls its rows of every other rank's block from
+    // this rank's staging and writes them into the local output.
+    const int W = peer.world, R = peer.rank;
+    T* const mine = peer.out[R];  // this rank's block inside its own full output
+    const uint32_t par = epoch & 1u;
+    const size_t sect = static_cast<size_t>(M) * N;  // packets per (parity, source rank)
+    __shared__ int may_send;
+    if (threadIdx.x == 0) {
+      may_send = (W == 1 || peer_wait_all(peer.ctl[R]->ready, W, epoch - 1u, peer.timeout_ns)) ? 1 : 0;
+      if (!may_send) atomicOr(peer.status, RK_DEV_ERR_TIMEOUT_PEER);
+    }
+    __syncthreads();
     for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {
       const int i = t / M, m = t % M;
       float s = 0.f;
 #pragma unroll
       for (int k = 0; k < KS; ++k) s += red[(k * rows_max + i) * MB + m];
-      mine[static_cast<size_t>(m) * peer.ldo + row_begin + i] = from_f32<T>(s);
+      const T v = from_f32<T>(s);
+      mine[static_cast<size_t>(m) * peer.ldo + row_begin + i] = v;
+      if (may_send) {
+        const uint64_t pkt = (static_cast<uint64_t>(epoch) << 32) | bits_of(v);
+        const size_t at = (par * W + R) * sect + static_cast<size_t>(m) * N + row_begin + i;
+        for (int j = 0; j < W; ++j)
+          if (j != R) st_relaxed_sys_u64(peer_stage(peer.ctl[j]) + at, pkt);
+      }
     }
-    __shared__ int role;  // 1: this CTA finished last; 2: ... and every rank has started
+    const uint64_t* stage = peer_stage(peer.ctl[R]);
+    const int per_peer = rows * M;
+    bool timed_out = false;
+    for (int t = threadIdx.x; t < (W - 1) * per_peer && !timed_out; t += GEMV_THREADS) {
+      const int jj = t / per_peer, rem = t - jj * per_peer;
+      const int j = jj + (jj >= R ? 1 : 0);
+      const int i = rem / M, m = rem - i * M;
+      const uint64_t* src = stage + (par * W + j) * sect + static_cast<size_t>(m) * N + row_begin + i;
+      uint64_t pkt = ld_relaxed_sys_u64(src);
+      if (static_cast<uint32_t>(pkt >> 32) != epoch) {
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t it = 0;; ++it) {
+          pkt = ld_relaxed_sys_u64(src);
+          if (static_cast<uint32_t>(pkt >> 32) == epoch) break;
+          if ((it & 15u) == 15u && (globaltimer_ns() - t0 > peer.timeout_ns || it >= (1u << 30))) {
+            timed_out = true;
+            break;
+          }
+        }
+      }
+      // Rank j's block of this rank's full output: columns [j N, (j + 1) N).
+      if (!timed_out)
+        mine[static_cast<ptrdiff_t>(m) * peer.ldo + static_cast<ptrdiff_t>(j - R) * N + row_begin + i] =
+            from_bits<T>(static_cast<uint32_t>(pkt));
+    }
+    if (timed_out) atomicOr(peer.status, RK_DEV_ERR_TIMEOUT_PEER);
+    // The call number advances once every CTA has read it: the grid's last CTA to finish.
     __syncthreads();
     if (threadIdx.x == 0) {
       __threadfence();
-      role = atomicAdd(&peer.ctl[peer.rank]->done_ctas, 1u) == gridDim.x - 1u ? 1 : 0;
-      if (role) {
-        __threadfence();
-        peer.ctl[peer.rank]->done_ctas = 0u;  // the next call starts after this kernel completes
-        if (peer_wait_ready(peer, epoch)) role = 2;
+      if (atomicAdd(&peer.ctl[R]->done_ctas, 1u) == gridDim.x - 1u) {
+        peer.ctl[R]->done_ctas = 0u;  // the next call starts after this kernel completes
+        *reinterpret_cast<volatile uint32_t*>(&peer.ctl[R]->epoch) = epoch;
       }
-    }
-    __syncthreads();
-    if (role == 0) return;
-    if (role == 2) {
-      // The block is M rows of N contiguous elements at row stride ldo.
-      bool vec = (N % 8) == 0;
-      for (int j = 0; j < peer.world; ++j) vec &= (reinterpret_cast<uintptr_t>(peer.out[j]) & 15u) == 0;
-      if (vec) {
-        const int per_row = N / 8;
-        for (int t = threadIdx.x; t < M * per_row; t += GEMV_THREADS) {
-          const size_t at = static_cast<size_t>(t / per_row) * peer.ldo + static_cast<size_t>(t % per_row) * 8;
-          const uint4 v = __ldcg(reinterpret_cast<const uint4*>(mine + at));
-          for (int j = 0; j < peer.world; ++j)
-            if (j != peer.rank) *reinterpret_cast<uint4*>(peer.out[j] + at) = v;
-        }
-      } else {
-        for (int t = threadIdx.x; t < M * N; t += GEMV_THREADS) {
-          const size_t at = static_cast<size_t>(t / N) * peer.ldo + t % N;
-          const T v = mine[at];
-          for (int j = 0; j < peer.world; ++j)
-            if (j != peer.rank) peer.out[j][at] = v;
-        }
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();  // every peer store of this CTA, before the arrival flags
-      peer_publish_arrival(peer, epoch);
-      if (!peer_wait_all(peer.ctl[peer.rank]->arrive, peer.world, epoch, peer.timeout_ns))
-        atomicOr(peer.status, RK_DEV_ERR_TIMEOUT_PEER);
-      *reinterpret_cast<volatile uint32_t*>(&peer.ctl[peer.rank]->epoch) = epoch;
     }
   } else {
     for (int t = threadIdx.x; t < rows * M; t += GEMV_THREADS) {

@@ -135,6 +135,16 @@ rk_status rk_ipc_close(const rk_ipc_handle* handle) {
   return RK_OK;
 }
 
+rk_status rk_gemv_allgather_ctl_bytes(int64_t M, int64_t N_block, int32_t world, size_t* bytes) {
+  if (bytes == nullptr) return RK_ERR_INVALID_ARGUMENT;
+  *bytes = 0;
+  if (M < 1 || M > 32 || N_block < 1 || world < 1 || world > RK_PEER_MAX) return RK_ERR_INVALID_ARGUMENT;
+  // Control block, then 8-byte packets [call parity 2][source rank][M][N_block] (rk_peer.cuh).
+  const uint64_t packets = 2ull * static_cast<uint64_t>(world) * static_cast<uint64_t>(M) * static_cast<uint64_t>(N_block);
+  *bytes = static_cast<size_t>(RK_PEER_CTL_BYTES + packets * 8ull);
+  return RK_OK;
+}
+
 rk_status rk_gemv_allgather(const void* x, const void* weight_block, int64_t M, int64_t N_block,
                             int64_t K, rk_dtype dt, const rk_peer_group* group,
                             rk_stream_t stream) {

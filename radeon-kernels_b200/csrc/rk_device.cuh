@@ -534,6 +534,19 @@ __device__ __forceinline__ __half from_f32<__half>(float v) {
   return __float2half_rn(v);
 }
 
+// The 16 bits of a 16-bit float, and back.
+template <typename T>
+__device__ __forceinline__ uint32_t bits_of(T v) {
+  static_assert(sizeof(T) == 2, "16-bit types");
+  return *reinterpret_cast<const uint16_t*>(&v);
+}
+template <typename T>
+__device__ __forceinline__ T from_bits(uint32_t b) {
+  static_assert(sizeof(T) == 2, "16-bit types");
+  const uint16_t h = static_cast<uint16_t>(b);
+  return *reinterpret_cast<const T*>(&h);
+}
+
 // Streaming 128-bit global load that bypasses L1 allocation (weights are read once).
 __device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
   uint4 r;

@@ -17,14 +17,19 @@
 //              a captured CUDA graph replays correctly.
 //   done_ctas  CTAs of the running call that have finished storing; the last resets it.
 //
-// Two ways to move the data: the GEMM (large blocks) stores every finished tile into every
+// Two ways to move the data.  The GEMM (large blocks) stores every finished tile into every
 // rank's output from the CTA that made it, while the next tile accumulates, and ends with
-// peer_finish; the GEMV (a block of at most 32 x N elements) stores into its own output
-// only, and the grid's last CTA pushes the whole block to the peers and sends the arrival
-// flags itself.  Either way the last CTA of each rank waits until every rank's arrive[]
-// reaches the call's epoch, so when the kernel completes the local full output is complete.  Every wait is bounded (time
-// and iteration count); a wait that runs out sets RK_DEV_ERR_TIMEOUT_PEER in the status word
-// and the kernel finishes without the missing data (the group must then be rebuilt).
+// peer_finish: the last CTA of each rank waits until every rank's arrive[] reaches the call's
+// epoch.  The GEMV (a block of at most 32 x N elements, a few microseconds of work) cannot
+// afford that fence and flag round trip: every CTA sends its rows to the peers as 8-byte
+// packets that carry the call number (peer_stage), and polls its rows of every peer's block
+// from its own staging area, so data and "arrived" travel in one store and no fence is
+// needed.  Its slots alternate by call parity: a peer's slot of parity e & 1 was last read
+// in that peer's call e - 2, so a rank may send once every peer has started call e - 1
+// (ready[]), which in steady state holds already.  Either way, when the kernel completes the
+// local full output is complete.  Every wait is bounded (time and iteration count); a wait
+// that runs out sets RK_DEV_ERR_TIMEOUT_PEER in the status word and the kernel finishes
+// without the missing data (the group must then be rebuilt).
 #pragma once
 
 #include <cstdint>
@@ -76,6 +81,25 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+
+// 8-byte packets of the GEMV exchange: a single naturally aligned 64-bit access, so a reader
+// sees either the old packet or the new one whole.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// rk_gemv_allgather's staging area, right after a rank's control block: 8-byte packets
+// [call parity 2][source rank world][M][N_block], each {value bits (low 32), call number
+// (high 32)}.
+__device__ __forceinline__ uint64_t* peer_stage(PeerCtl* ctl) {
+  return reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(ctl) + sizeof(PeerCtl));
 }
 
 __device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {

@@ -75,6 +75,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.rk_gemm.restype = cint
     lib.rk_gemm_layout.argtypes = [vp, vp, vp, i64, i64, i64, cint, cint, cint, vp]
     lib.rk_gemm_layout.restype = cint
+    lib.rk_gemv_allgather_ctl_bytes.argtypes = [i64, i64, ctypes.c_int32, ctypes.POINTER(ctypes.c_size_t)]
+    lib.rk_gemv_allgather_ctl_bytes.restype = cint
     lib.rk_sdpa.argtypes = [vp] * 4 + [i64] * 5 + [cint, ctypes.c_float, cint, vp]
     lib.rk_sdpa.restype = cint
     lib.rk_silu_mul_backward.argtypes = [vp] * 5 + [i64, i64, cint, vp]

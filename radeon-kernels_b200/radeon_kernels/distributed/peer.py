@@ -2,8 +2,9 @@
 
 No counterpart in the reference (it is single-GPU).  A :class:`PeerExchange` is created
 collectively by every rank of a process group (one process per GPU).  Each rank allocates
-one device buffer -- a control block of ``RK_PEER_CTL_BYTES`` followed by its full output
-``[M, N]`` -- exports it with ``rk_ipc_export``, and maps every other rank's buffer with
+one device buffer -- a control region (the ``RK_PEER_CTL_BYTES`` control block and, for the
+GEMV's packet exchange, the staging area ``rk_gemv_allgather_ctl_bytes`` sizes) followed by
+its full output ``[M, N]`` -- exports it with ``rk_ipc_export``, and maps every other rank's buffer with
 ``rk_ipc_open`` (CUDA IPC; NVLink / NVSwitch peer access).  The kernels behind
 ``rk_gemv_allgather`` / ``rk_gemm_allgather`` then store every rank's column block straight
 into every rank's output and order the calls through the control blocks, so a gathered
@@ -23,7 +24,8 @@ from typing import Any
 
 RK_PEER_MAX = 8
 RK_PEER_CTL_BYTES = 512
-CTL_REGION = 4096  # control block region at the start of each buffer (keeps the output 4 KiB aligned)
+CTL_REGION = 4096  # smallest control region at the start of each buffer (keeps the output 4 KiB aligned)
+GEMV_MAX_M = 32  # rk_gemv_allgather's row limit: shapes above it never need the staging area
 
 
 class _IpcHandle(ctypes.Structure):
@@ -48,6 +50,23 @@ def _lib() -> ctypes.CDLL:
     lib = _native.library()
     _declare(lib)
     return lib
+
+
+def control_region_bytes(shape: tuple[int, int], world: int) -> int:
+    """Bytes in front of each rank's output: the control block, plus, for shapes that
+    ``rk_gemv_allgather`` can run (M <= 32), its packet staging area; a multiple of 4 KiB."""
+
+    from radeon_kernels import _native
+
+    m, n = int(shape[0]), int(shape[1])
+    need = RK_PEER_CTL_BYTES
+    if 1 <= m <= GEMV_MAX_M and world >= 1 and n % world == 0:
+        size = ctypes.c_size_t(0)
+        status = _lib().rk_gemv_allgather_ctl_bytes(m, n // world, world, ctypes.byref(size))
+        if status != _native.RK_OK:
+            raise RuntimeError(f"rk_gemv_allgather_ctl_bytes failed: {_native.status_text(status)}")
+        need = int(size.value)
+    return max(CTL_REGION, -(-need // CTL_REGION) * CTL_REGION)
 
 
 def export_handle(ptr: int) -> bytes:
@@ -125,8 +144,9 @@ class PeerExchange:
         self.timeout_ns = int(timeout_s * 1e9)
         device = torch.device("cuda", torch.cuda.current_device())
         nbytes = math.prod(self.shape) * torch.empty((), dtype=dtype).element_size()
-        self._storage = torch.zeros(CTL_REGION + nbytes, dtype=torch.uint8, device=device)
-        self.output = self._storage[CTL_REGION:].view(dtype).view(self.shape)
+        self.ctl_region = control_region_bytes(self.shape, self.world)
+        self._storage = torch.zeros(self.ctl_region + nbytes, dtype=torch.uint8, device=device)
+        self.output = self._storage[self.ctl_region:].view(dtype).view(self.shape)
         # The zeroed control block must be in memory before any rank's kernel can write it.
         torch.cuda.current_stream(device).synchronize()
         base = self._storage.data_ptr()
@@ -150,7 +170,7 @@ class PeerExchange:
             self._opened = []
             raise PeerMappingError(f"peer mapping failed on {len(failures)} rank(s): {failures[0]}")
         self.ctl_ptrs = bases
-        self.out_ptrs = [b + CTL_REGION for b in bases]
+        self.out_ptrs = [b + self.ctl_region for b in bases]
         dist.barrier(group=group)
 
     def close(self) -> None:
@@ -188,4 +208,4 @@ def fused_path_available(device_tensor: Any, *, group: Any = None) -> bool:
     return len(set(uuids)) == len(uuids)
 
 
-__all__ = ["CTL_REGION", "PeerExchange", "PeerMappingError", "RK_PEER_CTL_BYTES", "RK_PEER_MAX", "export_handle", "fused_path_available", "open_handle"]
+__all__ = ["CTL_REGION", "PeerExchange", "control_region_bytes", "PeerMappingError", "RK_PEER_CTL_BYTES", "RK_PEER_MAX", "export_handle", "fused_path_available", "open_handle"]

@@ -21,15 +21,16 @@ from radeon_kernels import _native
 
 pytestmark = pytest.mark.gpu
 
-CTL = 4096  # control region in front of each output, as radeon_kernels.distributed.peer lays it out
-
-
 def _exchange(torch, m, n, dtype, ranks=1):
-    """Per rank: one zeroed [CTL | m x n] buffer; returns (buffers, outputs, out_ptrs, ctl_ptrs)."""
+    """Per rank: one zeroed [control region | m x n] buffer laid out as
+    radeon_kernels.distributed.peer does; returns (buffers, outputs, out_ptrs, ctl_ptrs)."""
 
+    from radeon_kernels.distributed.peer import control_region_bytes
+
+    ctl = control_region_bytes((m, n), ranks)
     esize = torch.empty((), dtype=dtype).element_size()
-    bufs = [torch.zeros(CTL + m * n * esize, dtype=torch.uint8, device="cuda") for _ in range(ranks)]
-    outs = [b[CTL:].view(dtype).view(m, n) for b in bufs]
+    bufs = [torch.zeros(ctl + m * n * esize, dtype=torch.uint8, device="cuda") for _ in range(ranks)]
+    outs = [b[ctl:].view(dtype).view(m, n) for b in bufs]
     return bufs, outs, [o.data_ptr() for o in outs], [b.data_ptr() for b in bufs]
 
 
