@@ -194,11 +194,14 @@ RK_API rk_status rk_gather_column_blocks(const void* blocks, void* out, int64_t 
  * One process per GPU.  A group of `world` ranks shares, per rank, a full output
  * buffer [M, world * N_block] and a control block of RK_PEER_CTL_BYTES (zeroed before
  * the first call, 512-byte aligned), each mapped into every other rank's process with
- * rk_ipc_export / rk_ipc_open.  Rank r owns the column block [r*N_block, (r+1)*N_block)
- * of the result; its kernel computes that block and stores it with plain peer stores
- * over NVLink into every rank's output while the rest of the block is still being
- * computed.  When the call completes on a rank's stream, that rank's full output holds
- * every rank's block.
+ * rk_ipc_export / rk_ipc_open (rk_gemv_allgather needs a larger control area, sized by
+ * rk_gemv_allgather_ctl_bytes).  Rank r owns the column block [r*N_block, (r+1)*N_block)
+ * of the result.  Its kernel computes that block and sends it over NVLink with plain peer
+ * stores while the rest of the block is still being computed.  The GEMM stores finished
+ * tiles straight into every rank's output.  The GEMV sends 8-byte packets that carry the
+ * call number into each rank's staging area, and each rank copies them into its own
+ * output.  When the call completes on a rank's stream, that rank's full output holds every
+ * rank's block.
  *
  * Rules: every rank of the group makes the same sequence of calls on one group, each
  * rank on one stream; a rank's output may be read until that rank's next call on the
