@@ -425,7 +425,8 @@ def headline(args, dist: Dist, ext, peaks, peak_kind):
     return result
 
 
-E2E_GRAPH_STEPS = 16  # independent steps captured in one CUDA graph (multiple of ROTATE)
+E2E_GRAPH_STEPS = 64  # independent steps captured in one CUDA graph (multiple of ROTATE and E2E_COPY_GROUP)
+E2E_COPY_GROUP = 8  # N = 1: input copies issued per group, a group ahead of the kernels that read them
 
 
 def e2e(args, dist: Dist):
@@ -434,10 +435,14 @@ def e2e(args, dist: Dist):
     Every step copies its activation host->device from pinned memory, calls the public API
     (validation, dispatch, pack winner) and copies the full result back into pinned memory.
     N = 1: ``radeon_kernels.gemv``; the reported value comes from a CUDA graph captured from
-    those calls: 16 independent steps, H2D copies on a forked copy stream and each D2H on a
-    second stream right after its kernel, so copy-engine latency overlaps neighbouring
-    kernels; ``eager_serial`` is the same step issued eagerly with copy, kernel and copy
-    serialised on one stream (the per-call latency).  N > 1: ``ShardedGemv(..., gather=True)``
+    those calls: 64 independent steps, each with its own H2D copy and its own D2H copy.  The
+    H2D copies run on a forked copy stream in groups of 8, which it works through in order, so
+    a group's copies run while the kernels of the group before it run; one join precedes the
+    group's first kernel.  Each D2H runs on
+    a second stream right after its kernel.  A join in front of every kernel measured 2.7-3 us
+    more per step (the kernel then cannot start early on its predecessor's tail).
+    ``eager_serial`` is the same step issued eagerly with copy, kernel and copy serialised on
+    one stream (the per-call latency).  N > 1: ``ShardedGemv(..., gather=True)``
     (the fused all-gather kernel), copy in, kernel and copy out on one stream -- the gathered
     output buffer is rewritten by the next call, so its copy must finish first -- captured
     into a CUDA graph of 16 steps.
@@ -494,12 +499,15 @@ def e2e(args, dist: Dist):
         d2h.wait_stream(here)
         ready = []
         with torch.cuda.stream(h2d):
-            for i in range(G):
-                xs_dev[i].copy_(xs_host[i], non_blocking=True)
+            # Every step's input is copied separately; a group's copies complete on one event.
+            for g0 in range(0, G, E2E_COPY_GROUP):
+                for i in range(g0, g0 + E2E_COPY_GROUP):
+                    xs_dev[i].copy_(xs_host[i], non_blocking=True)
                 ready.append(torch.cuda.Event())
                 ready[-1].record(h2d)
         for i in range(G):
-            here.wait_event(ready[i])
+            if i % E2E_COPY_GROUP == 0:
+                here.wait_event(ready[i // E2E_COPY_GROUP])
             y = rk.gemv(xs_dev[i], weights[i % ROTATE])
             kept.append(y)
             done = torch.cuda.Event()
@@ -538,7 +546,8 @@ def e2e(args, dist: Dist):
     result.update({
         "value": rate(ms, steps),
         "ms_per_step": round(ms / steps, 5),
-        "path": (f"CUDA graph of {G} captured steps: pinned H2D copy (forked copy stream), "
+        "path": (f"CUDA graph of {G} captured steps: pinned H2D copy per step (forked copy stream, "
+                 f"groups of {E2E_COPY_GROUP} issued a group ahead), "
                  f"radeon_kernels.gemv -> {selected}, pinned D2H copy (second stream); "
                  "outputs checked equal to eager calls"),
         "eager_serial": eager,
