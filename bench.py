@@ -442,10 +442,10 @@ def e2e(args, dist: Dist):
     a second stream right after its kernel.  A join in front of every kernel measured 2.7-3 us
     more per step (the kernel then cannot start early on its predecessor's tail).
     ``eager_serial`` is the same step issued eagerly with copy, kernel and copy serialised on
-    one stream (the per-call latency).  N > 1: ``ShardedGemv(..., gather=True)``
-    (the fused all-gather kernel), copy in, kernel and copy out on one stream -- the gathered
-    output buffer is rewritten by the next call, so its copy must finish first -- captured
-    into a CUDA graph of 16 steps.
+    one stream (the per-call latency).  N > 1: ``ShardedGemv(..., gather=True)`` (the fused
+    all-gather kernel) in the same graph of 64 steps, in groups no larger than the number of
+    exchange buffers: a gathered output buffer is rewritten by the next call on it, so its
+    copy must finish first, and one join per group covers that too.
     """
 
     if dist.world > 1:
@@ -582,28 +582,37 @@ def e2e_sharded(args, dist: Dist):
         operators[i % R](xs_dev[i % G], gather=True)  # first call of each operator: collective set-up
     torch.cuda.synchronize()
 
+    # Steps in groups of at most R (one exchange buffer per operator): a group's inputs are
+    # copied in while the group before it runs, and before its first kernel one join on its
+    # inputs and one on the output copy that frees the last buffer it reuses (the copy stream
+    # works in order, so that covers the group's other buffers too).
+    gsz = min(E2E_COPY_GROUP, R)
+    groups = [range(g0, min(g0 + gsz, G)) for g0 in range(0, G, gsz)]
+
     def graph_body():
         here = torch.cuda.current_stream()
         h2d.wait_stream(here)
         d2h.wait_stream(here)
         ready, copied = [], []
         with torch.cuda.stream(h2d):
-            for i in range(G):
-                xs_dev[i].copy_(xs_host[i], non_blocking=True)
+            for grp in groups:
+                for i in grp:
+                    xs_dev[i].copy_(xs_host[i], non_blocking=True)
                 ready.append(torch.cuda.Event())
                 ready[-1].record(h2d)
-        for i in range(G):
-            here.wait_event(ready[i])
-            if i >= R:
-                here.wait_event(copied[i - R])  # buffer of operator i % R copied out
-            y = operators[i % R](xs_dev[i], gather=True)
-            done = torch.cuda.Event()
-            done.record(here)
-            d2h.wait_event(done)
-            with torch.cuda.stream(d2h):
-                outs_host[i].copy_(y, non_blocking=True)
-                copied.append(torch.cuda.Event())
-                copied[-1].record(d2h)
+        for gi, grp in enumerate(groups):
+            here.wait_event(ready[gi])
+            if grp.stop - 1 - R >= 0:
+                here.wait_event(copied[grp.stop - 1 - R])  # every buffer of this group copied out
+            for i in grp:
+                y = operators[i % R](xs_dev[i], gather=True)
+                done = torch.cuda.Event()
+                done.record(here)
+                d2h.wait_event(done)
+                with torch.cuda.stream(d2h):
+                    outs_host[i].copy_(y, non_blocking=True)
+                    copied.append(torch.cuda.Event())
+                    copied[-1].record(d2h)
         here.wait_stream(h2d)
         here.wait_stream(d2h)
 
@@ -639,7 +648,8 @@ def e2e_sharded(args, dist: Dist):
         "d2h_bytes_per_step": m * n * 2,
         "value": round(gemv_bytes(m, n, k) * steps / (ms / 1e3) / 1e9, 1),
         "ms_per_step": round(ms / steps, 5),
-        "path": (f"CUDA graph of {G} captured steps: pinned H2D copies (forked copy stream), "
+        "path": (f"CUDA graph of {G} captured steps: pinned H2D copy per step (forked copy stream, "
+                 f"groups of {gsz} issued a group ahead), "
                  "radeon_kernels.distributed.ShardedGemv(gather=True) -> rk_gemv_allgather, pinned D2H "
                  "copy of the full output (second stream); outputs spot-checked against the local block"),
     }
