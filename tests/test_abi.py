@@ -87,6 +87,28 @@ def test_arguments_are_validated_before_any_device_work():
     assert lib.rk_gemv_ex(null, null, null, 1, 4, 4, 0, 0, null, 0, null) == _native.RK_ERR_INVALID_ARGUMENT
 
 
+def test_gemv_allgather_control_area_size():
+    """rk_gemv_allgather's control area: the control block, then 2 x world x M x N_block
+    8-byte packets; radeon_kernels.distributed.peer rounds it up to whole 4 KiB pages in front
+    of each output, and GEMM-only shapes (M > 32) keep the 4 KiB minimum."""
+
+    from radeon_kernels.distributed.peer import CTL_REGION, RK_PEER_CTL_BYTES, control_region_bytes
+
+    lib = _native.library()
+    size = ctypes.c_size_t(0)
+    assert lib.rk_gemv_allgather_ctl_bytes(1, 1024, 8, ctypes.byref(size)) == _native.RK_OK
+    assert size.value == RK_PEER_CTL_BYTES + 2 * 8 * 1 * 1024 * 8
+    assert lib.rk_gemv_allgather_ctl_bytes(32, 4096, 2, ctypes.byref(size)) == _native.RK_OK
+    assert size.value == RK_PEER_CTL_BYTES + 2 * 2 * 32 * 4096 * 8
+    for bad in ((0, 8, 2), (33, 8, 2), (1, 0, 2), (1, 8, 0), (1, 8, 9)):
+        assert lib.rk_gemv_allgather_ctl_bytes(*bad, ctypes.byref(size)) == _native.RK_ERR_INVALID_ARGUMENT
+        assert size.value == 0
+    assert lib.rk_gemv_allgather_ctl_bytes(1, 8, 2, None) == _native.RK_ERR_INVALID_ARGUMENT
+    assert control_region_bytes((1, 8192), 8) == 135168  # 512 + 131072 bytes -> 33 pages
+    assert control_region_bytes((1, 16), 2) == CTL_REGION
+    assert control_region_bytes((16384, 57344), 8) == CTL_REGION  # M > 32: the GEMM's exchange
+
+
 def test_missing_binary_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_native, "_library", None)
     monkeypatch.setattr(_native, "LIBRARY_PATH", tmp_path / "librk_kernels.so")
